@@ -1,0 +1,146 @@
+/*
+ * pa_kernels.h - C ABI of the B200 (sm_100a) attention-block kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (pa_stream_t is a cudaStream_t; NULL = legacy default stream), enqueues its
+ * kernels on that stream and returns a pa_status. Nothing here allocates
+ * device memory: scratch space is passed in by the caller (query the size with
+ * the matching *_workspace_size function). Calls never throw and never print.
+ *
+ * Kernels whose waits are bounded record a timeout in a per-device status
+ * word instead of hanging; pa_device_status() reads (and optionally clears) it.
+ *
+ * Layouts follow the Pure-Attention boundary:
+ *   q, k, v, o, dO, dq, dk, dv : [B, L, H, D] row-major (heads interleaved
+ *                                along E = H*D, the reference's [N, L, E])
+ *   lse                        : [B*H, L] fp32, natural-log log-sum-exp
+ *   delta                      : [B, L, H] fp32
+ *   matrices                   : row-major
+ */
+#ifndef PA_KERNELS_H
+#define PA_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PA_ABI_VERSION 1
+
+typedef enum pa_status {
+  PA_OK = 0,
+  PA_ERR_SHAPE = 1,       /* sizes are inconsistent or zero where not allowed */
+  PA_ERR_DTYPE = 2,       /* dtype not supported by this entry point */
+  PA_ERR_ALIGN = 3,       /* a pointer or stride breaks the 16-byte TMA rule */
+  PA_ERR_UNSUPPORTED = 4, /* e.g. head_dim outside {32, 64, 128} */
+  PA_ERR_LAUNCH = 5,      /* the CUDA launch itself failed */
+  PA_ERR_TIMEOUT = 6,     /* a kernel's bounded wait ran out (device status) */
+  PA_ERR_WORKSPACE = 7,   /* workspace missing or too small */
+  PA_ERR_NULL = 8,        /* a required pointer is NULL */
+  PA_ERR_DEVICE = 9       /* no sm_100 device current, or a CUDA runtime error */
+} pa_status;
+
+typedef enum pa_dtype { PA_F32 = 0, PA_BF16 = 1 } pa_dtype;
+
+typedef void* pa_stream_t; /* cudaStream_t */
+
+typedef struct pa_attn_desc {
+  int32_t batch;       /* B (the reference calls it N) */
+  int32_t seq_len;     /* L */
+  int32_t num_heads;   /* H */
+  int32_t head_dim;    /* D = E / H */
+  int32_t dtype;       /* pa_dtype of q, k, v, o, dO, dq, dk, dv */
+  float softmax_scale; /* <= 0 selects 1/sqrt(head_dim) */
+} pa_attn_desc;
+
+/* Library information and status. */
+int pa_abi_version(void);
+const char* pa_status_string(int status);
+/* Synchronises `stream`, returns PA_OK or the first error recorded by a kernel
+ * on the current device (PA_ERR_TIMEOUT), and resets the word when clear != 0. */
+int pa_device_status(pa_stream_t stream, int clear);
+
+/* ---------------------------------------------------------------- attention */
+
+/* Flash-attention forward: o = softmax(q k^T * scale) v, lse = row log-sum-exp.
+ * Replaces launch_flash_attention (include/backend/Launchers.cuh:159-167).
+ * bf16: head_dim 64 or 128. f32: head_dim 32, 64 or 128. */
+int pa_attn_fwd(const pa_attn_desc* desc, const void* q, const void* k, const void* v, void* o,
+                float* lse, pa_stream_t stream);
+
+/* Bytes of workspace pa_attn_bwd needs for this shape. */
+size_t pa_attn_bwd_workspace_size(const pa_attn_desc* desc);
+
+/* Flash-attention backward from the saved lse: dq, dk, dv (overwritten, or
+ * added to when accumulate != 0). Replaces launch_flash_backward
+ * (include/backend/Launchers.cuh:169-174), which allocated its scratch itself. */
+int pa_attn_bwd(const pa_attn_desc* desc, const void* q, const void* k, const void* v,
+                const void* o, const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                int accumulate, void* workspace, size_t workspace_bytes, pa_stream_t stream);
+
+/* delta = rowsum(dO * o) as [B, L, H] fp32. Replaces compute_delta_kernel
+ * (include/backend/Kernels.cuh:132, launched inside launch_flash_backward). */
+int pa_attn_delta(const pa_attn_desc* desc, const void* dO, const void* o, float* delta,
+                  pa_stream_t stream);
+
+/* ---------------------------------------------------------------- layer norm */
+
+/* y = gamma * (x - mean) * rstd + beta over rows of length N; saves mean, rstd.
+ * Replaces launch_layer_norm_forward (include/backend/Launchers.cuh:178-189). */
+int pa_layer_norm_fwd(const float* x, const float* gamma, const float* beta, float* y,
+                      float* mean, float* rstd, uint32_t M, uint32_t N, float epsilon,
+                      pa_stream_t stream);
+
+size_t pa_layer_norm_bwd_workspace_size(uint32_t M, uint32_t N);
+
+/* dx (overwritten), dgamma and dbeta (accumulated); a NULL output is skipped.
+ * Replaces launch_layer_norm_backward (include/backend/Launchers.cuh:191-203). */
+int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                      const float* gamma, float* dx, float* dgamma, float* dbeta, uint32_t M,
+                      uint32_t N, void* workspace, size_t workspace_bytes, pa_stream_t stream);
+
+/* ---------------------------------------------------------------- matmul */
+
+/* C[M,N] = A[M,K] B[K,N]. Replaces launch_matmul_tiled (Launchers.cuh:15-23). */
+int pa_matmul(const float* A, const float* B, float* C, int M, int N, int K, pa_stream_t stream);
+
+/* dX[M,N] += dY[M,K] W[N,K]^T. Replaces launch_matmul_grad_X (Launchers.cuh:64-72). */
+int pa_matmul_grad_x(const float* dY, const float* W, float* dX, int M, int N, int K,
+                     pa_stream_t stream);
+
+/* dW[N,K] += X[M,N]^T dY[M,K]. Replaces launch_matmul_grad_W (Launchers.cuh:74-82). */
+int pa_matmul_grad_w(const float* X, const float* dY, float* dW, int M, int N, int K,
+                     pa_stream_t stream);
+
+/* ---------------------------------------------------------------- elementwise */
+
+/* out[M,N] = A[M,N] + bias[N]. Replaces launch_matadd_tiled (Launchers.cuh:25-32). */
+int pa_bias_add(const float* A, const float* bias, float* out, int M, int N, pa_stream_t stream);
+
+/* out = a + b elementwise over n values (same-shape residual add). */
+int pa_add(const float* a, const float* b, float* out, size_t n, pa_stream_t stream);
+
+/* dst += src over n values. Replaces launch_tensor_add_grad (Launchers.cuh:84-89). */
+int pa_grad_accumulate(const float* src, float* dst, size_t n, pa_stream_t stream);
+
+/* db[N] += column sums of dY[M,N]. Replaces launch_sum_rows_grad (Launchers.cuh:91-97). */
+int pa_bias_grad(const float* dY, float* db, int M, int N, pa_stream_t stream);
+
+/* Split [rows, parts*width] along the last dimension into `parts` arrays of
+ * [rows, width]; outs is a HOST array of `parts` device pointers (parts <= 8).
+ * Replaces launch_split_forward (Launchers.cuh:139-147). */
+int pa_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
+                      uint32_t width, pa_stream_t stream);
+
+/* grad_in[rows, parts*width] += concatenation of part_grads (NULL parts are
+ * treated as zero). Replaces launch_concat_backward (Launchers.cuh:149-157). */
+int pa_concat_last_dim_grad(const float* const* part_grads, float* grad_in, uint32_t parts,
+                            uint32_t rows, uint32_t width, pa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PA_KERNELS_H */

@@ -1,0 +1,512 @@
+// Flash-attention backward for sm_100a: bf16 inputs, fp32 accumulation.
+//
+// Restates the reference's backward (flash_attn_backward_kernel.cu:25-41 for
+// Delta, :153-197 for the per-tile math, doc/flash_backward.md section 5):
+//   P  = exp(S * scale - LSE)        recomputed from the saved row LSE
+//   dP = dO V^T,  Delta = rowsum(dO * O)
+//   dS = P * (dP - Delta) * scale
+//   dV = P^T dO,  dK = dS^T Q,  dQ = dS K
+// with the reference's dQ stub (:182-191) replaced by the real product.
+//
+// Three kernels:
+//   attn_bwd_prep_kernel : Delta and LSE*log2(e) per query row, laid out
+//                          [B*H, Lp] (Lp = L rounded up to 128, padded rows
+//                          get LSE = +inf so their P is exactly 0).
+//   attn_bwd_kernel      : one CTA per (batch, head, 128-key tile), looping
+//                          over 128-query tiles:
+//       warp 0     TMA producer (K, V once; Q, dO, LSE, Delta per query tile)
+//       warp 1     TMEM allocator + tcgen05.mma issuer
+//       warps 4-7  P / dS elementwise (thread = one key row), dK/dV epilogue
+//       warps 8-11 dQ readout: TMEM -> swizzled shared tile -> TMA tensor
+//                  reduce-add into an fp32 dQ accumulator in the workspace
+//     MMAs per query tile (M = 128, K-major unless noted):
+//       S^T  = K Q^T            (SS)        -> TMEM S
+//       dP^T = V dO^T           (SS)        -> TMEM dP
+//       dV  += P^T dO           (TS, dO MN-major)
+//       dK  += dS^T Q           (TS, Q MN-major)
+//       dQ   = dS K             (SS, dS and K MN-major; dS staged in shared)
+//     P^T and dS^T (bf16) are written over the first 64 columns of S and dP.
+//   attn_dq_convert_kernel : fp32 dQ accumulator -> dq in the boundary layout.
+#include "host_launchers.h"
+
+namespace pa {
+
+template <int D>
+struct BwdCfg {
+  static constexpr int KCH = D / 64;
+  static constexpr int STAGES = (D == 64) ? 2 : 1;
+  static constexpr int DQB = (D == 64) ? 2 : 1;      // dQ staging buffers
+  static constexpr int CHUNK = 128 * 128;
+  static constexpr int KV_BYTES = 128 * D * 2;
+  static constexpr int QT_BYTES = 128 * D * 2;
+  static constexpr int STAGE_BYTES = 2 * QT_BYTES + 1024;  // Q, dO, LSE2[128], Delta[128]
+  static constexpr int DS_BYTES = 128 * 128 * 2;
+  static constexpr int DQ_BYTES = 128 * D * 4;
+  static constexpr int SMEM = 2 * KV_BYTES + STAGES * STAGE_BYTES + DS_BYTES + DQB * DQ_BYTES + 1024;
+  static constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
+  static constexpr uint32_t T_DQ = (D == 64) ? 384 : 0;  // D=128: dQ reuses S's columns
+};
+
+// ---------------------------------------------------------------- prep
+// G = D/8 threads per (b, l, h) row, each reading 8 bf16 of dO and O.
+template <int D>
+__global__ void __launch_bounds__(256)
+    attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dO, const __nv_bfloat16* __restrict__ O,
+                         const float* __restrict__ lse, float* __restrict__ lse2_t,
+                         float* __restrict__ delta_t, float* __restrict__ delta_ref, int B, int L,
+                         int Lp, int H) {
+  constexpr int G = D / 8;
+  const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t rowi = gt / G;  // over B * Lp * H, ordered (b, l, h)
+  const int g = static_cast<int>(gt % G);
+  const size_t nrows = static_cast<size_t>(B) * Lp * H;
+  const bool in_range = rowi < nrows;
+  const int h = in_range ? static_cast<int>(rowi % H) : 0;
+  const int l = in_range ? static_cast<int>((rowi / H) % Lp) : 0;
+  const int b = in_range ? static_cast<int>(rowi / (static_cast<size_t>(H) * Lp)) : 0;
+  float acc = 0.f;
+  const bool real = in_range && l < L;
+  if (real) {
+    const size_t off = ((static_cast<size_t>(b) * L + l) * H + h) * D + g * 8;
+    const uint4 a = *reinterpret_cast<const uint4*>(dO + off);
+    const uint4 c = *reinterpret_cast<const uint4*>(O + off);
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 fa = __bfloat1622float2(a2[i]);
+      const float2 fc = __bfloat1622float2(c2[i]);
+      acc = fmaf(fa.x, fc.x, acc);
+      acc = fmaf(fa.y, fc.y, acc);
+    }
+  }
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (in_range && g == 0) {
+    const size_t bh = static_cast<size_t>(b) * H + h;
+    if (lse2_t) lse2_t[bh * Lp + l] = real ? lse[bh * L + l] * kLog2e : INFINITY;
+    if (delta_t) delta_t[bh * Lp + l] = real ? acc : 0.f;
+    if (delta_ref && real) delta_ref[(static_cast<size_t>(b) * L + l) * H + h] = acc;
+  }
+}
+
+// ---------------------------------------------------------------- main
+template <int D>
+__global__ void __launch_bounds__(384, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                    const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapdO,
+                    const __grid_constant__ CUtensorMap mapDQ,
+                    __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                    const float* __restrict__ lse2_t, const float* __restrict__ delta_t, int L, int Lp, int H, float scale, float scale_log2,
+                    int accumulate, uint32_t* status) {
+  using C = BwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bars[16];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  if (cta_aborted(status, &abort_flag)) return;
+
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::KV_BYTES;
+  uint8_t* sStage = sV + C::KV_BYTES;
+  uint8_t* sdS = sStage + C::STAGES * C::STAGE_BYTES;
+  uint8_t* sDQ = sdS + C::DS_BYTES;
+
+  const uint32_t kv_full = smem_u32(&bars[0]);
+  auto q_full = [&](int s) { return smem_u32(&bars[1 + s]); };
+  auto q_empty = [&](int s) { return smem_u32(&bars[3 + s]); };
+  const uint32_t sd_full = smem_u32(&bars[5]);
+  const uint32_t p_full = smem_u32(&bars[6]);
+  const uint32_t dq_full = smem_u32(&bars[7]);
+  const uint32_t dq_empty = smem_u32(&bars[8]);
+  const uint32_t kv_done = smem_u32(&bars[9]);
+
+  const int warp = warp_id();
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int k0 = blockIdx.x * 128;
+  const int n_q = Lp / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(q_full(s), 1);
+      mbar_init(q_empty(s), 1);
+    }
+    mbar_init(sd_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(kv_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      tma_prefetch_desc(&mapQ);
+      tma_prefetch_desc(&mapdO);
+      mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
+      for (int c = 0; c < C::KCH; ++c) {
+        tma_load_4d(smem_u32(sK + c * C::CHUNK), &mapK, kv_full, c * 64, h, k0, b);
+        tma_load_4d(smem_u32(sV + c * C::CHUNK), &mapV, kv_full, c * 64, h, k0, b);
+      }
+      for (int j = 0; j < n_q; ++j) {
+        const int s = j % C::STAGES;
+        if (j >= C::STAGES && !mbar_wait(q_empty(s), ((j / C::STAGES) - 1) & 1, status)) break;
+        uint8_t* st = sStage + s * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(q_full(s), 2 * C::QT_BYTES + 1024);
+        for (int c = 0; c < C::KCH; ++c) {
+          tma_load_4d(smem_u32(st + c * C::CHUNK), &mapQ, q_full(s), c * 64, h, j * 128, b);
+          tma_load_4d(smem_u32(st + C::QT_BYTES + c * C::CHUNK), &mapdO, q_full(s), c * 64, h,
+                      j * 128, b);
+        }
+        const size_t voff = static_cast<size_t>(bh) * Lp + j * 128;
+        bulk_load(smem_u32(st + 2 * C::QT_BYTES), lse2_t + voff, 512, q_full(s));
+        bulk_load(smem_u32(st + 2 * C::QT_BYTES + 512), delta_t + voff, 512, q_full(s));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idSP = make_idesc(128, 128, 1, false, false);
+      constexpr uint32_t idKV = make_idesc(128, D, 1, false, true);
+      constexpr uint32_t idQ = make_idesc(128, D, 1, true, true);
+      const uint32_t kA = smem_u32(sK), vA = smem_u32(sV), dsA = smem_u32(sdS);
+      bool ok = mbar_wait(kv_full, 0, status);
+      for (int j = 0; ok && j < n_q; ++j) {
+        const int s = j % C::STAGES;
+        const uint32_t qA = smem_u32(sStage + s * C::STAGE_BYTES);
+        const uint32_t doA = qA + C::QT_BYTES;
+        if (!(ok = mbar_wait(q_full(s), (j / C::STAGES) & 1, status))) break;
+        if (C::T_DQ == 0 && j > 0 && !(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k / 4) * C::CHUNK + (k % 4) * 32;
+          umma_f16_ss(tmem + C::T_S, make_sdesc(kA + off, 16, 1024), make_sdesc(qA + off, 16, 1024),
+                      idSP, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k / 4) * C::CHUNK + (k % 4) * 32;
+          umma_f16_ss(tmem + C::T_DP, make_sdesc(vA + off, 16, 1024),
+                      make_sdesc(doA + off, 16, 1024), idSP, k > 0);
+        }
+        umma_commit(sd_full);
+        if (!(ok = mbar_wait(p_full, j & 1, status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(tmem + C::T_DV, tmem + C::T_S + k * 8,
+                      make_sdesc(doA + k * 2048, C::CHUNK, 1024), idKV, (j > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + k * 8,
+                      make_sdesc(qA + k * 2048, C::CHUNK, 1024), idKV, (j > 0 || k > 0) ? 1u : 0u);
+        if (C::T_DQ != 0 && j > 0) {
+          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ss(tmem + C::T_DQ, make_sdesc(dsA + k * 2048, C::CHUNK, 1024),
+                      make_sdesc(kA + k * 2048, C::CHUNK, 1024), idQ, k > 0);
+        umma_commit(dq_full);
+        umma_commit(q_empty(s));
+      }
+      if (ok) umma_commit(kv_done);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ P / dS
+    const int kr = threadIdx.x - 128;  // key row within the tile == TMEM lane
+    const int key = k0 + kr;
+    const bool valid = key < L;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + C::T_S + lane_base;
+    const uint32_t tdP = tmem + C::T_DP + lane_base;
+    bool ok = true;
+    for (int j = 0; j < n_q; ++j) {
+      const int s = j % C::STAGES;
+      if (!(ok = mbar_wait_warp(sd_full, j & 1, status))) break;
+      if (!(ok = mbar_wait_warp(q_full(s), (j / C::STAGES) & 1, status))) break;
+      tc_fence_after();
+      const float* lse2s = reinterpret_cast<const float*>(sStage + s * C::STAGE_BYTES + 2 * C::QT_BYTES);
+      const float* dels = lse2s + 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dpv[32];
+        tmem_ld32(tS + c * 32, sv);
+        tmem_ld32(tdP + c * 32, dpv);
+        tmem_ld_wait();
+        uint32_t pk[16], dk2[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int q = c * 32 + 2 * i;
+          const float2 ls = *reinterpret_cast<const float2*>(lse2s + q);
+          const float2 de = *reinterpret_cast<const float2*>(dels + q);
+          float p0 = ex2(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -ls.x));
+          float p1 = ex2(fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -ls.y));
+          if (!valid) p0 = p1 = 0.f;
+          const float ds0 = p0 * (__uint_as_float(dpv[2 * i]) - de.x) * scale;
+          const float ds1 = p1 * (__uint_as_float(dpv[2 * i + 1]) - de.y) * scale;
+          pk[i] = pack_bf16x2(p0, p1);
+          dk2[i] = pack_bf16x2(ds0, ds1);
+        }
+        PA_TMEM_ST_X8(tS + c * 16, pk);
+        PA_TMEM_ST_X8(tS + c * 16 + 8, (pk + 8));
+        PA_TMEM_ST_X8(tdP + c * 16, dk2);
+        PA_TMEM_ST_X8(tdP + c * 16 + 8, (dk2 + 8));
+        // dS row of this key into the MN-major dS tile: queries c*32..c*32+31
+        uint8_t* region = sdS + (c >> 1) * C::CHUNK;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t cc = (c & 1) * 4 + u;
+          *reinterpret_cast<uint4*>(region + sw128_offset(kr, cc * 16)) =
+              make_uint4(dk2[4 * u], dk2[4 * u + 1], dk2[4 * u + 2], dk2[4 * u + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait_warp(kv_done, 0, status)) {
+      tc_fence_after();
+      const size_t roff = ((static_cast<size_t>(b) * L + key) * H + h) * D;
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {
+        __nv_bfloat16* dst = (part == 0 ? dv : dk) + roff;
+        const uint32_t tsrc = tmem + (part == 0 ? C::T_DV : C::T_DK) + lane_base;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tsrc + c * 32, o);
+          tmem_ld_wait();
+          if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * u + e]);
+              if (accumulate) {
+                const uint4 prev = d4[u];
+                const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&prev);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 pf = __bfloat1622float2(p2[e]);
+                  f[2 * e] += pf.x;
+                  f[2 * e + 1] += pf.y;
+                }
+              }
+              d4[u] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                 pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            }
+          }
+        }
+      }
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dQ readout
+    const int qr = threadIdx.x - 256;  // query row within the tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tdQ = tmem + C::T_DQ + lane_base;
+    // The loop never exits early: the named barriers below need all 128
+    // threads every iteration, so a failed wait only skips the work.
+    bool ok = true;
+    for (int j = 0; j < n_q; ++j) {
+      const int buf = j % C::DQB;
+      if (j >= C::DQB) {
+        if (qr == 0) bulk_wait_read<C::DQB - 1>();
+        named_bar_sync(1, 128);
+      }
+      ok = ok && mbar_wait_warp(dq_full, j & 1, status);
+      if (ok) {
+        tc_fence_after();
+        // Staging tile = D/32 boxes of 128 rows x 32 fp32 (128 B), 128B-swizzled
+        // like the TMA map over dq_acc, so stores are conflict-free.
+        uint8_t* sdq = sDQ + buf * C::DQ_BYTES;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tdQ + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(sdq + c * C::CHUNK + sw128_offset(qr, u * 16)) =
+                make_uint4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+        }
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+        fence_proxy_async_smem();
+      }
+      named_bar_sync(1, 128);
+      if (qr == 0 && !aborted(status)) {
+        for (int c = 0; c < D / 32; ++c)
+          tma_reduce_add_2d(&mapDQ, smem_u32(sDQ + buf * C::DQ_BYTES + c * C::CHUNK), c * 32,
+                            bh * Lp + j * 128);
+        tma_store_commit();
+      }
+    }
+    if (qr == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------- dQ convert
+// dq[b, l, h, :] (=|+=) dq_acc[b*H + h, l, :]; 8 values per thread.
+template <int D, typename OutT>
+__global__ void __launch_bounds__(256)
+    attn_dq_convert_kernel(const float* __restrict__ dq_acc, OutT* __restrict__ dq, int B, int L,
+                           int Lp, int H, int accumulate) {
+  const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t total = static_cast<size_t>(B) * L * H * (D / 8);
+  if (gt >= total) return;
+  const int g = static_cast<int>(gt % (D / 8));
+  const size_t rowi = gt / (D / 8);  // (b, l, h)
+  const int h = static_cast<int>(rowi % H);
+  const int l = static_cast<int>((rowi / H) % L);
+  const int b = static_cast<int>(rowi / (static_cast<size_t>(H) * L));
+  const float* src = dq_acc + ((static_cast<size_t>(b) * H + h) * Lp + l) * D + g * 8;
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  const float4 c = *reinterpret_cast<const float4*>(src + 4);
+  float f[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  OutT* dst = dq + rowi * D + g * 8;
+  if constexpr (sizeof(OutT) == 2) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    if (accumulate) {
+      const uint4 prev = *d4;
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&prev);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 pf = __bfloat1622float2(p2[e]);
+        f[2 * e] += pf.x;
+        f[2 * e + 1] += pf.y;
+      }
+    }
+    *d4 = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                     pack_bf16x2(f[6], f[7]));
+  } else {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    if (accumulate) {
+      const float4 p0 = d4[0], p1 = d4[1];
+      f[0] += p0.x; f[1] += p0.y; f[2] += p0.z; f[3] += p0.w;
+      f[4] += p1.x; f[5] += p1.y; f[6] += p1.z; f[7] += p1.w;
+    }
+    d4[0] = make_float4(f[0], f[1], f[2], f[3]);
+    d4[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+// ---------------------------------------------------------------- host
+size_t attn_bwd_workspace_bytes(const AttnShape& sh) {
+  const size_t Lp = static_cast<size_t>((sh.L + 127) / 128) * 128;
+  const size_t bh = static_cast<size_t>(sh.B) * sh.H;
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  return up(bh * Lp * 4) * 2 + up(bh * Lp * sh.D * 4);
+}
+
+template <int D>
+static int launch_prep(const AttnShape& sh, const void* dO, const void* o, const float* lse,
+                       float* lse2, float* delta_t, float* delta_ref, int Lp, cudaStream_t stream) {
+  const size_t rows = static_cast<size_t>(sh.B) * Lp * sh.H;
+  const size_t threads = rows * (D / 8);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  attn_bwd_prep_kernel<D><<<blocks, 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(dO), static_cast<const __nv_bfloat16*>(o), lse, lse2,
+      delta_t, delta_ref, sh.B, sh.L, Lp, sh.H);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+int launch_attn_delta_bf16(const AttnShape& sh, const void* dO, const void* o, float* delta,
+                           cudaStream_t stream) {
+  if (sh.D == 64) return launch_prep<64>(sh, dO, o, nullptr, nullptr, nullptr, delta, sh.L, stream);
+  if (sh.D == 128) return launch_prep<128>(sh, dO, o, nullptr, nullptr, nullptr, delta, sh.L, stream);
+  return PA_ERR_UNSUPPORTED;
+}
+
+template <int D>
+static int launch_bwd_impl(const AttnShape& sh, const void* q, const void* k, const void* v,
+                           const void* o, const void* dO, const float* lse, void* dq, void* dk,
+                           void* dv, int accumulate, void* ws, uint32_t* status,
+                           cudaStream_t stream) {
+  using C = BwdCfg<D>;
+  const int Lp = (sh.L + 127) / 128 * 128;
+  const size_t bh = static_cast<size_t>(sh.B) * sh.H;
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  float* lse2 = reinterpret_cast<float*>(w);
+  float* delta_t = reinterpret_cast<float*>(w + up(bh * Lp * 4));
+  float* dq_acc = reinterpret_cast<float*>(w + 2 * up(bh * Lp * 4));
+
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_qkv_map(&mq, q, sh, 128) || !make_qkv_map(&mk, k, sh, 128) ||
+      !make_qkv_map(&mv, v, sh, 128) || !make_qkv_map(&mdo, dO, sh, 128))
+    return PA_ERR_ALIGN;
+  // dQ accumulator [B*H*Lp, D] fp32, reduced into by 128-row x 32-column boxes.
+  CUtensorMap mdq;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(D), bh * Lp};
+    const uint64_t strides[1] = {static_cast<uint64_t>(D) * 4};
+    const uint32_t box[2] = {32, 128};
+    if (!make_tmap(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return PA_ERR_ALIGN;
+  }
+  if (cudaMemsetAsync(dq_acc, 0, bh * Lp * D * sizeof(float), stream) != cudaSuccess)
+    return PA_ERR_LAUNCH;
+  int st = launch_prep<D>(sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream);
+  if (st != PA_OK) return st;
+
+  static uint64_t attr = 0;
+  ensure_smem_attr(attn_bwd_kernel<D>, C::SMEM, attr);
+  dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
+  attn_bwd_kernel<D><<<grid, 384, C::SMEM, stream>>>(
+      mq, mk, mv, mdo, mdq, static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv), lse2,
+      delta_t, sh.L, Lp, sh.H, sh.scale, sh.scale * kLog2e, accumulate, status);
+  if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
+
+  const size_t threads = static_cast<size_t>(sh.B) * sh.L * sh.H * (D / 8);
+  attn_dq_convert_kernel<D, __nv_bfloat16><<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
+                                             stream>>>(dq_acc, static_cast<__nv_bfloat16*>(dq),
+                                                       sh.B, sh.L, Lp, sh.H, accumulate);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+int launch_attn_bwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v,
+                         const void* o, const void* dO, const float* lse, void* dq, void* dk,
+                         void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream) {
+  if (sh.D == 64)
+    return launch_bwd_impl<64>(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, ws, status, stream);
+  if (sh.D == 128)
+    return launch_bwd_impl<128>(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, ws, status, stream);
+  return PA_ERR_UNSUPPORTED;
+}
+
+size_t attn_bwd_workspace_bytes_f32(const AttnShape& sh) { return attn_bwd_workspace_bytes(sh); }
+int launch_attn_bwd_f32(const AttnShape&, const void*, const void*, const void*, const void*,
+                        const void*, const float*, void*, void*, void*, int, void*, uint32_t*,
+                        cudaStream_t) {
+  return PA_ERR_UNSUPPORTED;
+}
+int launch_attn_delta_f32(const AttnShape&, const void*, const void*, float*, cudaStream_t) {
+  return PA_ERR_UNSUPPORTED;
+}
+
+}  // namespace pa

@@ -1,0 +1,308 @@
+// Flash-attention forward for sm_100a: bf16 Q/K/V, fp32 accumulation in TMEM.
+//
+// Computes, per (batch, head) and query row, the reference's forward
+// (flash_attn_forward_kernel.cu:80-185): S = Q K^T * scale, online softmax,
+// O = softmax(S) V and LSE = rowmax + log(rowsum) (natural log). Unlike the
+// reference, O is divided by the row sum exactly (no +1e-6).
+//
+// One CTA = one (batch, head) and two 128-row query tiles (256 rows).
+//   warp 0      : TMA producer (Q once, K/V ring of STAGES stages)
+//   warp 1      : TMEM allocator + tcgen05.mma issuer (single elected lane)
+//   warps 4-7   : softmax of query tile 0   (thread = one query row)
+//   warps 8-11  : softmax of query tile 1
+// The two softmax warpgroups ping-pong so the tensor core computes one tile's
+// S or P*V while the other tile's softmax runs.
+//
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D,256+2D).
+// P (bf16 pairs) is written over the first 64 columns of its S tile and feeds
+// the P*V MMA directly from TMEM. tcgen05.mma ops issued by one thread run in
+// issue order, so the next S MMA (which overwrites P) is issued only after the
+// P*V MMA that reads it.
+//
+// The row max is kept in the log2 domain and only raised when a new tile's max
+// exceeds it by more than 8 (a factor 256): O and the row sum are rescaled
+// then, and otherwise P entries may reach 2^8, which fp32/bf16 hold exactly.
+#include "host_launchers.h"
+
+namespace pa {
+
+template <int D>
+struct FwdCfg {
+  static constexpr int BM = 128;                 // query rows per tile
+  static constexpr int BN = 128;                 // keys per KV tile
+  static constexpr int KCH = D / 64;             // 128-byte column chunks per row
+  static constexpr int STAGES = (D == 64) ? 3 : 2;
+  static constexpr int CHUNK = 128 * 128;        // bytes of one 128-row x 128-byte box
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int SMEM = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 1024;
+  static constexpr int THREADS = 384;
+};
+
+template <int D>
+__global__ void __launch_bounds__(384, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                    const __grid_constant__ CUtensorMap mapV, __nv_bfloat16* __restrict__ O,
+                    float* __restrict__ lse, int L, int H, float scale_log2, uint32_t* status) {
+  using C = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bars[16];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  if (cta_aborted(status, &abort_flag)) return;
+
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;                                // 2 tiles
+  uint8_t* sK = smem + 2 * C::Q_BYTES;               // STAGES tiles
+  uint8_t* sV = sK + C::STAGES * C::KV_BYTES;        // STAGES tiles
+
+  const uint32_t q_full = smem_u32(&bars[0]);
+  auto kv_full = [&](int s) { return smem_u32(&bars[1 + s]); };
+  auto kv_empty = [&](int s) { return smem_u32(&bars[4 + s]); };
+  auto s_full = [&](int t) { return smem_u32(&bars[7 + t]); };
+  auto p_full = [&](int t) { return smem_u32(&bars[9 + t]); };
+  auto o_done = [&](int t) { return smem_u32(&bars[11 + t]); };
+
+  const int warp = warp_id();
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int q0 = blockIdx.x * 256;
+  const int n_kv = (L + C::BN - 1) / C::BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(p_full(t), 128);
+      mbar_init(o_done(t), 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      tma_prefetch_desc(&mapQ);
+      tma_prefetch_desc(&mapK);
+      tma_prefetch_desc(&mapV);
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(smem_u32(sQ + t * C::Q_BYTES + c * C::CHUNK), &mapQ, q_full, c * 64, h,
+                      q0 + t * C::BM, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % C::STAGES;
+        if (j >= C::STAGES && !mbar_wait(kv_empty(s), ((j / C::STAGES) - 1) & 1, status)) break;
+        mbar_arrive_expect_tx(kv_full(s), 2 * C::KV_BYTES);
+        for (int c = 0; c < C::KCH; ++c) {
+          tma_load_4d(smem_u32(sK + s * C::KV_BYTES + c * C::CHUNK), &mapK, kv_full(s), c * 64, h,
+                      j * C::BN, b);
+          tma_load_4d(smem_u32(sV + s * C::KV_BYTES + c * C::CHUNK), &mapV, kv_full(s), c * 64, h,
+                      j * C::BN, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idS = make_idesc(128, 128, 1, false, false);
+      constexpr uint32_t idO = make_idesc(128, D, 1, false, true);
+      const uint32_t tS[2] = {tmem, tmem + 128};
+      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+      auto issue_S = [&](int t, int j) {
+        const uint32_t qa = smem_u32(sQ + t * C::Q_BYTES);
+        const uint32_t ka = smem_u32(sK + (j % C::STAGES) * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k / 4) * C::CHUNK + (k % 4) * 32;
+          umma_f16_ss(tS[t], make_sdesc(qa + off, 16, 1024), make_sdesc(ka + off, 16, 1024), idS,
+                      k > 0);
+        }
+      };
+      auto issue_PV = [&](int t, int j) {
+        const uint32_t va = smem_u32(sV + (j % C::STAGES) * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BN / 16; ++k)
+          umma_f16_ts(tO[t], tS[t] + k * 8, make_sdesc(va + k * 2048, C::CHUNK, 1024), idO,
+                      (j > 0 || k > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, status) && mbar_wait(kv_full(0), 0, status);
+      if (ok) {
+        tc_fence_after();
+        issue_S(0, 0);
+        umma_commit(s_full(0));
+        issue_S(1, 0);
+        umma_commit(s_full(1));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % C::STAGES;
+        const bool more = j + 1 < n_kv;
+        if (!(ok = mbar_wait(p_full(0), j & 1, status))) break;
+        tc_fence_after();
+        issue_PV(0, j);
+        if (more) {
+          if (!(ok = mbar_wait(kv_full((j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1, status)))
+            break;
+          tc_fence_after();
+          issue_S(0, j + 1);
+          umma_commit(s_full(0));
+        } else {
+          umma_commit(o_done(0));
+        }
+        if (!(ok = mbar_wait(p_full(1), j & 1, status))) break;
+        tc_fence_after();
+        issue_PV(1, j);
+        umma_commit(kv_empty(s));
+        if (more) {
+          issue_S(1, j + 1);
+          umma_commit(s_full(1));
+        } else {
+          umma_commit(o_done(1));
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int t = (warp - 4) / 4;                 // query tile of this warpgroup
+    const int r = threadIdx.x - 128 * (t + 1);    // row within the tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_base;
+    const uint32_t tO = tmem + 256 + t * D + lane_base;
+    const int row = q0 + t * C::BM + r;
+    float m = -INFINITY;  // running max of S * scale * log2(e)
+    float l = 0.f;        // running row sum (relative to m)
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!(ok = mbar_wait_warp(s_full(t), j & 1, status))) break;
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      tmem_ld_wait();
+      const int kv_left = L - j * C::BN;
+      if (kv_left < C::BN) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= kv_left) s[i] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      const float m_new = fmaxf(m, mx * scale_log2);
+      const bool need = m_new > m + 8.f;
+      const bool warp_need = __any_sync(0xffffffffu, need);
+      const float alpha = need ? ex2(m - m_new) : 1.f;
+      if (need) {
+        l *= alpha;
+        m = m_new;
+      }
+      // P = exp2(S * scale * log2(e) - m), packed to bf16 pairs over S's columns.
+      const float neg_m = -m;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float p0 = ex2(fmaf(s[c * 16 + 2 * i], scale_log2, neg_m));
+          const float p1 = ex2(fmaf(s[c * 16 + 2 * i + 1], scale_log2, neg_m));
+          sum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        PA_TMEM_ST_X8(tS + c * 8, pk);
+      }
+      l += sum;
+      // Rescale this tile's O rows when the running max moved (P*V of the
+      // previous tile has completed: it was issued before this tile's S MMA).
+      if (warp_need && j > 0) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full(t));
+    }
+    if (ok && mbar_wait_warp(o_done(t), 0, status)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      __nv_bfloat16* orow = O + ((static_cast<size_t>(b) * L + row) * H + h) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+        uint32_t pkd[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pkd[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+        if (row < L) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+        }
+      }
+      if (row < L) lse[static_cast<size_t>(bh) * L + row] = (m + __log2f(l)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Host launcher. q/k/v/o are [B, L, H, D] bf16, lse is [B*H, L] fp32.
+int launch_attn_fwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
+                         float* lse, uint32_t* status, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv;
+  if (!make_qkv_map(&mq, q, sh, 128) || !make_qkv_map(&mk, k, sh, 128) ||
+      !make_qkv_map(&mv, v, sh, 128))
+    return PA_ERR_ALIGN;
+  const float scale_log2 = sh.scale * kLog2e;
+  dim3 grid((sh.L + 255) / 256, sh.B * sh.H);
+  if (sh.D == 64) {
+    using C = FwdCfg<64>;
+    static uint64_t attr = 0;
+    ensure_smem_attr(attn_fwd_kernel<64>, C::SMEM, attr);
+    attn_fwd_kernel<64><<<grid, C::THREADS, C::SMEM, stream>>>(
+        mq, mk, mv, static_cast<__nv_bfloat16*>(o), lse, sh.L, sh.H, scale_log2, status);
+  } else if (sh.D == 128) {
+    using C = FwdCfg<128>;
+    static uint64_t attr = 0;
+    ensure_smem_attr(attn_fwd_kernel<128>, C::SMEM, attr);
+    attn_fwd_kernel<128><<<grid, C::THREADS, C::SMEM, stream>>>(
+        mq, mk, mv, static_cast<__nv_bfloat16*>(o), lse, sh.L, sh.H, scale_log2, status);
+  } else {
+    return PA_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+int launch_attn_fwd_f32(const AttnShape&, const void*, const void*, const void*, void*, float*,
+                        uint32_t*, cudaStream_t) {
+  return PA_ERR_UNSUPPORTED;
+}
+
+}  // namespace pa

@@ -1,0 +1,239 @@
+// extern "C" entry points of libpa_kernels.so (declared in include/pa_kernels.h).
+// Validation, status mapping and dispatch only; the kernels live in the other
+// translation units.
+#include <cmath>
+#include <cstdio>
+#include "attn_common.cuh"
+#include "host_launchers.h"
+
+namespace {
+
+// First error recorded by a bounded wait in any kernel on this device.
+__device__ uint32_t g_pa_status = 0;
+
+uint32_t* status_word() {
+  static uint32_t* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_pa_status) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<uint32_t*>(p);
+  }
+  return ptrs[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Validates an attention descriptor; fills `sh`.
+int check_attn(const pa_attn_desc* d, pa::AttnShape* sh) {
+  if (!d) return PA_ERR_NULL;
+  if (d->batch <= 0 || d->seq_len <= 0 || d->num_heads <= 0 || d->head_dim <= 0)
+    return PA_ERR_SHAPE;
+  if (d->dtype != PA_BF16 && d->dtype != PA_F32) return PA_ERR_DTYPE;
+  if (d->dtype == PA_BF16 && d->head_dim != 64 && d->head_dim != 128) return PA_ERR_UNSUPPORTED;
+  if (d->dtype == PA_F32 && d->head_dim != 32 && d->head_dim != 64 && d->head_dim != 128)
+    return PA_ERR_UNSUPPORTED;
+  const long long Lp = (static_cast<long long>(d->seq_len) + 127) / 128 * 128;
+  if (static_cast<long long>(d->batch) * d->num_heads * Lp > 0x7fffffffLL) return PA_ERR_SHAPE;
+  sh->B = d->batch;
+  sh->L = d->seq_len;
+  sh->H = d->num_heads;
+  sh->D = d->head_dim;
+  sh->scale = d->softmax_scale > 0.f ? d->softmax_scale
+                                     : 1.0f / std::sqrt(static_cast<float>(d->head_dim));
+  return PA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pa_abi_version(void) { return PA_ABI_VERSION; }
+
+const char* pa_status_string(int s) {
+  switch (s) {
+    case PA_OK: return "ok";
+    case PA_ERR_SHAPE: return "invalid shape";
+    case PA_ERR_DTYPE: return "unsupported dtype";
+    case PA_ERR_ALIGN: return "pointer or stride not 16-byte aligned";
+    case PA_ERR_UNSUPPORTED: return "unsupported configuration (head dimension)";
+    case PA_ERR_LAUNCH: return "kernel launch failed";
+    case PA_ERR_TIMEOUT: return "a kernel wait timed out";
+    case PA_ERR_WORKSPACE: return "workspace missing or too small";
+    case PA_ERR_NULL: return "required pointer is NULL";
+    case PA_ERR_DEVICE: return "CUDA device error";
+    default: return "unknown status";
+  }
+}
+
+int pa_device_status(pa_stream_t stream, int clear) {
+  uint32_t* w = status_word();
+  if (!w) return PA_ERR_DEVICE;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return PA_ERR_DEVICE;
+  uint32_t v = 0;
+  if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return PA_ERR_DEVICE;
+  if (clear && v != 0 && cudaMemset(w, 0, sizeof(v)) != cudaSuccess) return PA_ERR_DEVICE;
+  return v == 0 ? PA_OK : PA_ERR_TIMEOUT;
+}
+
+int pa_attn_fwd(const pa_attn_desc* desc, const void* q, const void* k, const void* v, void* o,
+                float* lse, pa_stream_t stream) {
+  pa::AttnShape sh;
+  int st = check_attn(desc, &sh);
+  if (st != PA_OK) return st;
+  if (!q || !k || !v || !o || !lse) return PA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return PA_ERR_ALIGN;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (desc->dtype == PA_BF16) return pa::launch_attn_fwd_bf16(sh, q, k, v, o, lse, status, s);
+  return pa::launch_attn_fwd_f32(sh, q, k, v, o, lse, status, s);
+}
+
+size_t pa_attn_bwd_workspace_size(const pa_attn_desc* desc) {
+  pa::AttnShape sh;
+  if (check_attn(desc, &sh) != PA_OK) return 0;
+  return desc->dtype == PA_BF16 ? pa::attn_bwd_workspace_bytes(sh)
+                                : pa::attn_bwd_workspace_bytes_f32(sh);
+}
+
+int pa_attn_bwd(const pa_attn_desc* desc, const void* q, const void* k, const void* v,
+                const void* o, const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                int accumulate, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  pa::AttnShape sh;
+  int st = check_attn(desc, &sh);
+  if (st != PA_OK) return st;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv) return PA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dO) ||
+      !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
+    return PA_ERR_ALIGN;
+  const size_t need = pa_attn_bwd_workspace_size(desc);
+  if (!workspace || workspace_bytes < need) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PA_ERR_ALIGN;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (desc->dtype == PA_BF16)
+    return pa::launch_attn_bwd_bf16(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, workspace,
+                                    status, s);
+  return pa::launch_attn_bwd_f32(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, workspace,
+                                 status, s);
+}
+
+int pa_attn_delta(const pa_attn_desc* desc, const void* dO, const void* o, float* delta,
+                  pa_stream_t stream) {
+  pa::AttnShape sh;
+  int st = check_attn(desc, &sh);
+  if (st != PA_OK) return st;
+  if (!dO || !o || !delta) return PA_ERR_NULL;
+  if (!aligned16(dO) || !aligned16(o)) return PA_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (desc->dtype == PA_BF16) return pa::launch_attn_delta_bf16(sh, dO, o, delta, s);
+  return pa::launch_attn_delta_f32(sh, dO, o, delta, s);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ layer norm, matmul, elementwise
+namespace {
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+extern "C" {
+
+int pa_layer_norm_fwd(const float* x, const float* gamma, const float* beta, float* y,
+                      float* mean, float* rstd, uint32_t M, uint32_t N, float epsilon,
+                      pa_stream_t stream) {
+  if (!x || !gamma || !beta || !y || !mean || !rstd) return PA_ERR_NULL;
+  if (M == 0 || N == 0) return PA_ERR_SHAPE;
+  if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
+  if (!al16(x) || !al16(gamma) || !al16(beta) || !al16(y)) return PA_ERR_ALIGN;
+  return pa::launch_layer_norm_fwd(x, gamma, beta, y, mean, rstd, M, N, epsilon,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+size_t pa_layer_norm_bwd_workspace_size(uint32_t M, uint32_t N) {
+  return pa::layer_norm_bwd_workspace_bytes(M, N);
+}
+
+int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                      const float* gamma, float* dx, float* dgamma, float* dbeta, uint32_t M,
+                      uint32_t N, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  if (!dy || !x || !mean || !rstd || !gamma) return PA_ERR_NULL;
+  if (M == 0 || N == 0) return PA_ERR_SHAPE;
+  if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
+  if (!al16(dy) || !al16(x) || !al16(gamma) || (dx && !al16(dx))) return PA_ERR_ALIGN;
+  if ((dgamma || dbeta) &&
+      (!workspace || workspace_bytes < pa::layer_norm_bwd_workspace_bytes(M, N)))
+    return PA_ERR_WORKSPACE;
+  return pa::launch_layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, M, N,
+                                   static_cast<float*>(workspace),
+                                   static_cast<cudaStream_t>(stream));
+}
+
+int pa_matmul(const float* A, const float* B, float* C, int M, int N, int K, pa_stream_t stream) {
+  if (!A || !B || !C) return PA_ERR_NULL;
+  if (M <= 0 || N <= 0 || K <= 0) return PA_ERR_SHAPE;
+  return pa::launch_gemm_f32(0, A, B, C, M, N, K, status_word(), static_cast<cudaStream_t>(stream));
+}
+
+int pa_matmul_grad_x(const float* dY, const float* W, float* dX, int M, int N, int K,
+                     pa_stream_t stream) {
+  if (!dY || !W || !dX) return PA_ERR_NULL;
+  if (M <= 0 || N <= 0 || K <= 0) return PA_ERR_SHAPE;
+  return pa::launch_gemm_f32(1, dY, W, dX, M, N, K, status_word(),
+                             static_cast<cudaStream_t>(stream));
+}
+
+int pa_matmul_grad_w(const float* X, const float* dY, float* dW, int M, int N, int K,
+                     pa_stream_t stream) {
+  if (!X || !dY || !dW) return PA_ERR_NULL;
+  if (M <= 0 || N <= 0 || K <= 0) return PA_ERR_SHAPE;
+  return pa::launch_gemm_f32(2, X, dY, dW, M, N, K, status_word(),
+                             static_cast<cudaStream_t>(stream));
+}
+
+int pa_bias_add(const float* A, const float* bias, float* out, int M, int N, pa_stream_t stream) {
+  if (!A || !bias || !out) return PA_ERR_NULL;
+  if (M <= 0 || N <= 0) return PA_ERR_SHAPE;
+  return pa::launch_bias_add(A, bias, out, M, N, static_cast<cudaStream_t>(stream));
+}
+
+int pa_add(const float* a, const float* b, float* out, size_t n, pa_stream_t stream) {
+  if (!a || !b || !out) return PA_ERR_NULL;
+  if (n == 0) return PA_OK;
+  return pa::launch_add(a, b, out, n, static_cast<cudaStream_t>(stream));
+}
+
+int pa_grad_accumulate(const float* src, float* dst, size_t n, pa_stream_t stream) {
+  if (!src || !dst) return PA_ERR_NULL;
+  if (n == 0) return PA_OK;
+  return pa::launch_add(src, dst, dst, n, static_cast<cudaStream_t>(stream));
+}
+
+int pa_bias_grad(const float* dY, float* db, int M, int N, pa_stream_t stream) {
+  if (!dY || !db) return PA_ERR_NULL;
+  if (M <= 0 || N <= 0) return PA_ERR_SHAPE;
+  return pa::launch_bias_grad(dY, db, M, N, static_cast<cudaStream_t>(stream));
+}
+
+int pa_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
+                      uint32_t width, pa_stream_t stream) {
+  if (!in || !outs) return PA_ERR_NULL;
+  if (parts == 0 || parts > 8 || rows == 0 || width == 0) return PA_ERR_SHAPE;
+  for (uint32_t i = 0; i < parts; ++i)
+    if (!outs[i]) return PA_ERR_NULL;
+  return pa::launch_split_last_dim(in, outs, parts, rows, width,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+int pa_concat_last_dim_grad(const float* const* part_grads, float* grad_in, uint32_t parts,
+                            uint32_t rows, uint32_t width, pa_stream_t stream) {
+  if (!part_grads || !grad_in) return PA_ERR_NULL;
+  if (parts == 0 || parts > 8 || rows == 0 || width == 0) return PA_ERR_SHAPE;
+  return pa::launch_concat_last_dim_grad(part_grads, grad_in, parts, rows, width,
+                                         static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,165 @@
+// Elementwise and reduction kernels of the attention block (fp32, HBM-bound):
+//   bias add          matadd_kernel.cu:4-12        out[i,j] = a[i,j] + bias[j]
+//   add               (same-shape residual add; the reference's pa.add only
+//                      broadcast row 0, matadd_kernel.cu:10)
+//   grad accumulate   tensor_add_grad_kernel.cu:4-9  dst += src
+//   bias grad         sum_rows_grad_kernel.cu:4-13   db[j] += sum_i dY[i,j]
+//   split / concat    split_forward_kernel.cu:4-21, split_backward_kernel.cu:4-22
+// Vectorised with 16-byte accesses where the sizes allow; grids are sized in
+// multiples of the SM count with grid-stride loops.
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "host_launchers.h"
+
+namespace pa {
+
+namespace {
+
+int sm_count() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev] > 0 ? sms[dev] : 148;
+}
+
+unsigned grid_for(size_t work, int threads) {
+  const size_t want = (work + threads - 1) / threads;
+  const size_t cap = static_cast<size_t>(sm_count()) * 8;
+  return static_cast<unsigned>(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+__global__ void bias_add_vec_kernel(const float4* __restrict__ a, const float4* __restrict__ bias,
+                                    float4* __restrict__ out, size_t n4, uint32_t n4_row) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 x = a[i], b = bias[i % n4_row];
+    out[i] = make_float4(x.x + b.x, x.y + b.y, x.z + b.z, x.w + b.w);
+  }
+}
+__global__ void bias_add_kernel(const float* __restrict__ a, const float* __restrict__ bias,
+                                float* __restrict__ out, size_t n, uint32_t N) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = a[i] + bias[i % N];
+}
+
+// out = a + b (beta == 1) or out += a (b == out).
+__global__ void add_vec_kernel(const float4* __restrict__ a, const float4* b, float4* out,
+                               size_t n4) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 x = a[i], y = b[i];
+    out[i] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+  }
+}
+__global__ void add_kernel(const float* __restrict__ a, const float* b, float* out, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = a[i] + b[i];
+}
+
+// Column sums: CTA = 32 columns x 32 row lanes; fixed-order reduction, then db += .
+__global__ void __launch_bounds__(1024)
+    bias_grad_kernel(const float* __restrict__ dy, float* __restrict__ db, uint32_t M, uint32_t N) {
+  __shared__ float part[32][33];
+  const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const uint32_t col = blockIdx.x * 32 + tx;
+  float acc = 0.f;
+  if (col < N)
+    for (uint32_t r = ty; r < M; r += 32) acc += dy[static_cast<size_t>(r) * N + col];
+  part[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && col < N) {
+    float s = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) s += part[k][tx];
+    db[col] += s;
+  }
+}
+
+struct PtrPack {
+  float* p[8];
+};
+
+// in[rows, parts*width] -> outs[p][rows, width]
+__global__ void split_kernel(const float* __restrict__ in, PtrPack outs, uint32_t parts,
+                             uint32_t width, size_t total) {
+  const size_t inner = static_cast<size_t>(parts) * width;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t row = i / inner;
+    const uint32_t col = static_cast<uint32_t>(i % inner);
+    const uint32_t p = col / width, c = col % width;
+    outs.p[p][row * width + c] = in[i];
+  }
+}
+// grad_in[rows, parts*width] += part_grads[p][rows, width]
+__global__ void concat_grad_kernel(PtrPack grads, float* __restrict__ grad_in, uint32_t parts,
+                                   uint32_t width, size_t total) {
+  const size_t inner = static_cast<size_t>(parts) * width;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t row = i / inner;
+    const uint32_t col = static_cast<uint32_t>(i % inner);
+    const uint32_t p = col / width, c = col % width;
+    const float* g = grads.p[p];
+    if (g) grad_in[i] += g[row * width + c];
+  }
+}
+
+int done() { return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH; }
+
+}  // namespace
+
+int launch_bias_add(const float* a, const float* bias, float* out, uint32_t M, uint32_t N,
+                    cudaStream_t s) {
+  const size_t n = static_cast<size_t>(M) * N;
+  if (N % 4 == 0 && al16(a) && al16(bias) && al16(out)) {
+    bias_add_vec_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(bias),
+        reinterpret_cast<float4*>(out), n / 4, N / 4);
+  } else {
+    bias_add_kernel<<<grid_for(n, 256), 256, 0, s>>>(a, bias, out, n, N);
+  }
+  return done();
+}
+
+int launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t s) {
+  if (n % 4 == 0 && al16(a) && al16(b) && al16(out)) {
+    add_vec_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(reinterpret_cast<const float4*>(a),
+                                                        reinterpret_cast<const float4*>(b),
+                                                        reinterpret_cast<float4*>(out), n / 4);
+  } else {
+    add_kernel<<<grid_for(n, 256), 256, 0, s>>>(a, b, out, n);
+  }
+  return done();
+}
+
+int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStream_t s) {
+  bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(dy, db, M, N);
+  return done();
+}
+
+int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
+                          uint32_t width, cudaStream_t s) {
+  PtrPack pk{};
+  for (uint32_t i = 0; i < parts; ++i) pk.p[i] = outs[i];
+  const size_t total = static_cast<size_t>(rows) * parts * width;
+  split_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, pk, parts, width, total);
+  return done();
+}
+
+int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint32_t parts,
+                                uint32_t rows, uint32_t width, cudaStream_t s) {
+  PtrPack pk{};
+  for (uint32_t i = 0; i < parts; ++i) pk.p[i] = const_cast<float*>(grads[i]);
+  const size_t total = static_cast<size_t>(rows) * parts * width;
+  concat_grad_kernel<<<grid_for(total, 256), 256, 0, s>>>(pk, grad_in, parts, width, total);
+  return done();
+}
+
+}  // namespace pa

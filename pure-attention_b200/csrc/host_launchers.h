@@ -1,0 +1,59 @@
+// Host launchers behind the C ABI (one definition per kernel translation unit).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "attn_common.cuh"
+
+namespace pa {
+
+// attn_fwd.cu
+int launch_attn_fwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
+                         float* lse, uint32_t* status, cudaStream_t stream);
+int launch_attn_fwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
+                        float* lse, uint32_t* status, cudaStream_t stream);
+
+// attn_bwd.cu
+size_t attn_bwd_workspace_bytes(const AttnShape& sh);
+size_t attn_bwd_workspace_bytes_f32(const AttnShape& sh);
+int launch_attn_bwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v,
+                         const void* o, const void* dO, const float* lse, void* dq, void* dk,
+                         void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream);
+int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v,
+                        const void* o, const void* dO, const float* lse, void* dq, void* dk,
+                        void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream);
+int launch_attn_delta_bf16(const AttnShape& sh, const void* dO, const void* o, float* delta,
+                           cudaStream_t stream);
+int launch_attn_delta_f32(const AttnShape& sh, const void* dO, const void* o, float* delta,
+                          cudaStream_t stream);
+
+}  // namespace pa
+
+namespace pa {
+
+// layernorm.cu
+int launch_layer_norm_fwd(const float* x, const float* g, const float* b, float* y, float* mu,
+                          float* rs, uint32_t M, uint32_t N, float eps, cudaStream_t s);
+size_t layer_norm_bwd_workspace_bytes(uint32_t M, uint32_t N);
+int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, const float* rs,
+                          const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,
+                          float* part, cudaStream_t s);
+
+// elementwise.cu
+int launch_bias_add(const float* a, const float* bias, float* out, uint32_t M, uint32_t N,
+                    cudaStream_t s);
+int launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
+int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStream_t s);
+int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
+                          uint32_t width, cudaStream_t s);
+int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint32_t parts,
+                                uint32_t rows, uint32_t width, cudaStream_t s);
+
+// gemm.cu: C (=|+=) op(A) op(B), fp32 in/out.
+//   mode 0: C[M,N]  = A[M,K] B[K,N]
+//   mode 1: C[M,N] += A[M,K] B[N,K]^T   (grad X: A = dY, B = W)
+//   mode 2: C[N,K] += A[M,N]^T B[M,K]   (grad W: A = X,  B = dY)
+int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, int N, int K,
+                    uint32_t* status, cudaStream_t s);
+
+}  // namespace pa

@@ -1,0 +1,230 @@
+"""ctypes binding of libpa_kernels.so (the C ABI in include/pa_kernels.h).
+
+This is the Python face of the drop-in boundary: the functions take torch CUDA
+tensors (or raw device pointers), call the extern "C" entry points on the
+current CUDA stream and raise on any non-zero status. There is no fallback: a
+missing library or a missing GPU raises immediately.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpa_kernels.so")
+
+PA_F32, PA_BF16 = 0, 1
+
+STATUS = {
+    0: "PA_OK", 1: "PA_ERR_SHAPE", 2: "PA_ERR_DTYPE", 3: "PA_ERR_ALIGN",
+    4: "PA_ERR_UNSUPPORTED", 5: "PA_ERR_LAUNCH", 6: "PA_ERR_TIMEOUT",
+    7: "PA_ERR_WORKSPACE", 8: "PA_ERR_NULL", 9: "PA_ERR_DEVICE",
+}
+
+# Every symbol include/pa_kernels.h declares.
+EXPORTS = [
+    "pa_abi_version", "pa_status_string", "pa_device_status",
+    "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_delta",
+    "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
+    "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
+    "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
+    "pa_split_last_dim", "pa_concat_last_dim_grad",
+]
+
+
+class PaError(RuntimeError):
+    def __init__(self, fn, status):
+        self.status = status
+        super().__init__(f"{fn} failed: {STATUS.get(status, status)}")
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seq_len", ctypes.c_int32),
+                ("num_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("dtype", ctypes.c_int32), ("softmax_scale", ctypes.c_float)]
+
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_u32 = ctypes.c_uint32
+_int = ctypes.c_int
+_flt = ctypes.c_float
+
+_SIGS = {
+    "pa_abi_version": (_int, []),
+    "pa_status_string": (ctypes.c_char_p, [_int]),
+    "pa_device_status": (_int, [_vp, _int]),
+    "pa_attn_fwd": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
+    "pa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
+    "pa_attn_bwd": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp, _sz, _vp]),
+    "pa_attn_delta": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp]),
+    "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
+    "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
+    "pa_layer_norm_bwd": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
+    "pa_matmul": (_int, [_vp] * 3 + [_int] * 3 + [_vp]),
+    "pa_matmul_grad_x": (_int, [_vp] * 3 + [_int] * 3 + [_vp]),
+    "pa_matmul_grad_w": (_int, [_vp] * 3 + [_int] * 3 + [_vp]),
+    "pa_bias_add": (_int, [_vp] * 3 + [_int] * 2 + [_vp]),
+    "pa_add": (_int, [_vp] * 3 + [_sz, _vp]),
+    "pa_grad_accumulate": (_int, [_vp] * 2 + [_sz, _vp]),
+    "pa_bias_grad": (_int, [_vp] * 2 + [_int] * 2 + [_vp]),
+    "pa_split_last_dim": (_int, [_vp, ctypes.POINTER(_vp), _u32, _u32, _u32, _vp]),
+    "pa_concat_last_dim_grad": (_int, [ctypes.POINTER(_vp), _vp, _u32, _u32, _u32, _vp]),
+}
+
+_lib = None
+
+
+def load(path=LIB_PATH):
+    """Load the library and bind every declared symbol (no GPU needed)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built; run pure-attention_b200/build.py")
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _check(fn, st):
+    if st != 0:
+        raise PaError(fn, st)
+
+
+def _dtype_code(t):
+    import torch
+    if t.dtype == torch.bfloat16:
+        return PA_BF16
+    if t.dtype == torch.float32:
+        return PA_F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def attn_desc(q, num_heads=None, scale=0.0):
+    """Descriptor for q of shape [B, L, H, D] (or [B, L, E] with num_heads)."""
+    if q.dim() == 4:
+        B, L, H, D = q.shape
+    else:
+        B, L, E = q.shape
+        H = num_heads
+        D = E // H
+    return AttnDesc(B, L, H, D, _dtype_code(q), float(scale))
+
+
+def attn_fwd(q, k, v, o, lse, desc=None, stream=None):
+    d = desc or attn_desc(q)
+    st = load().pa_attn_fwd(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse),
+                            _stream() if stream is None else stream)
+    _check("pa_attn_fwd", st)
+
+
+def attn_bwd_workspace_size(desc):
+    return load().pa_attn_bwd_workspace_size(ctypes.byref(desc))
+
+
+def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, workspace, accumulate=False, desc=None,
+             stream=None):
+    d = desc or attn_desc(q)
+    ws_bytes = workspace.numel() * workspace.element_size()
+    st = load().pa_attn_bwd(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO),
+                            _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), int(bool(accumulate)),
+                            _ptr(workspace), ws_bytes, _stream() if stream is None else stream)
+    _check("pa_attn_bwd", st)
+
+
+def attn_delta(dO, o, delta, desc=None, stream=None):
+    d = desc or attn_desc(o)
+    st = load().pa_attn_delta(ctypes.byref(d), _ptr(dO), _ptr(o), _ptr(delta),
+                              _stream() if stream is None else stream)
+    _check("pa_attn_delta", st)
+
+
+def device_status(clear=True, stream=None):
+    """Synchronise and return the device status word (0 = no kernel timed out)."""
+    return load().pa_device_status(_stream() if stream is None else stream, int(clear))
+
+
+def layer_norm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5, stream=None):
+    M = x.numel() // x.shape[-1]
+    N = x.shape[-1]
+    st = load().pa_layer_norm_fwd(_ptr(x), _ptr(gamma), _ptr(beta), _ptr(y), _ptr(mean),
+                                  _ptr(rstd), M, N, float(eps),
+                                  _stream() if stream is None else stream)
+    _check("pa_layer_norm_fwd", st)
+
+
+def layer_norm_bwd_workspace_size(M, N):
+    return load().pa_layer_norm_bwd_workspace_size(M, N)
+
+
+def layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, workspace, stream=None):
+    M = x.numel() // x.shape[-1]
+    N = x.shape[-1]
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = load().pa_layer_norm_bwd(_ptr(dy), _ptr(x), _ptr(mean), _ptr(rstd), _ptr(gamma),
+                                  _ptr(dx), _ptr(dgamma), _ptr(dbeta), M, N, _ptr(workspace),
+                                  ws_bytes, _stream() if stream is None else stream)
+    _check("pa_layer_norm_bwd", st)
+
+
+def matmul(a, b, c, M, N, K, stream=None):
+    _check("pa_matmul", load().pa_matmul(_ptr(a), _ptr(b), _ptr(c), M, N, K,
+                                         _stream() if stream is None else stream))
+
+
+def matmul_grad_x(dy, w, dx, M, N, K, stream=None):
+    _check("pa_matmul_grad_x", load().pa_matmul_grad_x(_ptr(dy), _ptr(w), _ptr(dx), M, N, K,
+                                                       _stream() if stream is None else stream))
+
+
+def matmul_grad_w(x, dy, dw, M, N, K, stream=None):
+    _check("pa_matmul_grad_w", load().pa_matmul_grad_w(_ptr(x), _ptr(dy), _ptr(dw), M, N, K,
+                                                       _stream() if stream is None else stream))
+
+
+def bias_add(a, bias, out, M, N, stream=None):
+    _check("pa_bias_add", load().pa_bias_add(_ptr(a), _ptr(bias), _ptr(out), M, N,
+                                             _stream() if stream is None else stream))
+
+
+def add(a, b, out, n, stream=None):
+    _check("pa_add", load().pa_add(_ptr(a), _ptr(b), _ptr(out), n,
+                                   _stream() if stream is None else stream))
+
+
+def grad_accumulate(src, dst, n, stream=None):
+    _check("pa_grad_accumulate", load().pa_grad_accumulate(_ptr(src), _ptr(dst), n,
+                                                           _stream() if stream is None else stream))
+
+
+def bias_grad(dy, db, M, N, stream=None):
+    _check("pa_bias_grad", load().pa_bias_grad(_ptr(dy), _ptr(db), M, N,
+                                               _stream() if stream is None else stream))
+
+
+def split_last_dim(inp, outs, rows, width, stream=None):
+    arr = (_vp * len(outs))(*[_ptr(o) for o in outs])
+    _check("pa_split_last_dim", load().pa_split_last_dim(_ptr(inp), arr, len(outs), rows, width,
+                                                         _stream() if stream is None else stream))
+
+
+def concat_last_dim_grad(part_grads, grad_in, rows, width, stream=None):
+    arr = (_vp * len(part_grads))(*[_ptr(o) for o in part_grads])
+    _check("pa_concat_last_dim_grad",
+           load().pa_concat_last_dim_grad(arr, _ptr(grad_in), len(part_grads), rows, width,
+                                          _stream() if stream is None else stream))

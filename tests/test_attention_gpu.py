@@ -1,0 +1,179 @@
+"""Parity of the sm_100a flash-attention kernels (through the C ABI) with the
+float64 oracle on the same seeded, bf16-rounded inputs.
+
+Tolerance (bf16 path): norm-wise relative error <= 2e-2 on O, dQ, dK, dV;
+LSE within 2e-3 absolute."""
+import numpy as np
+import pytest
+
+from conftest import rel_err, seeded_normal
+
+BF16_TOL = 2e-2
+LSE_TOL = 2e-3
+
+torch = pytest.importorskip("torch")
+
+
+def _bf16(x):
+    """Round a float32 numpy array to bf16; returns (torch bf16 on cuda, float64 numpy)."""
+    t = torch.from_numpy(x).to(torch.bfloat16)
+    return t.cuda(), t.float().numpy().astype(np.float64)
+
+
+def _run(B, L, H, D, seed, scale_in=0.5, accumulate=False):
+    import pa_capi
+    shape = (B, L, H, D)
+    q, qn = _bf16(seeded_normal(seed, shape, scale_in))
+    k, kn = _bf16(seeded_normal(seed + 1000, shape, scale_in))
+    v, vn = _bf16(seeded_normal(seed + 2000, shape, scale_in))
+    g, gn = _bf16(seeded_normal(seed + 3000, shape, scale_in))
+    o = torch.empty_like(q)
+    lse = torch.empty(B * H, L, dtype=torch.float32, device="cuda")
+    pa_capi.attn_fwd(q, k, v, o, lse)
+    d = pa_capi.attn_desc(q)
+    ws = torch.empty(pa_capi.attn_bwd_workspace_size(d), dtype=torch.uint8, device="cuda")
+    if accumulate:
+        dq = torch.ones_like(q)
+        dk = torch.ones_like(q)
+        dv = torch.ones_like(q)
+    else:
+        dq, dk, dv = (torch.full_like(q, float("nan")) for _ in range(3))
+    pa_capi.attn_bwd(q, k, v, o, g, lse, dq, dk, dv, ws, accumulate=accumulate)
+    assert pa_capi.device_status() == 0
+    torch.cuda.synchronize()
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)
+    return (qn, kn, vn, gn), (f(o), lse.cpu().numpy().astype(np.float64), f(dq), f(dk), f(dv))
+
+
+def _check(inputs, outs, heads=None, accumulate=False):
+    import oracle
+    qn, kn, vn, gn = inputs
+    o, lse, dq, dk, dv = outs
+    B, L, H, D = qn.shape
+    sel = heads or [(b, h) for b in range(B) for h in range(H)]
+    for (b, h) in sel:
+        sl = (slice(b, b + 1), slice(None), slice(h, h + 1), slice(None))
+        ro, rl = oracle.attn_fwd(qn[sl], kn[sl], vn[sl])
+        # the oracle's dO path uses the kernel-independent exact O
+        rdq, rdk, rdv, _ = oracle.attn_bwd(qn[sl], kn[sl], vn[sl], ro, gn[sl], rl)
+        off = 1.0 if accumulate else 0.0
+        errs = {
+            "o": rel_err(o[sl], ro),
+            "dq": rel_err(dq[sl] - off, rdq),
+            "dk": rel_err(dk[sl] - off, rdk),
+            "dv": rel_err(dv[sl] - off, rdv),
+        }
+        lse_err = float(np.max(np.abs(lse[b * H + h] - rl[0])))
+        print(f"(b={b},h={h}) L={L} D={D} rel errs {errs} lse max abs {lse_err:.2e}")
+        for name, e in errs.items():
+            assert e <= BF16_TOL, (name, e)
+        assert lse_err <= LSE_TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,H,D", [
+    (1, 128, 1, 64),     # one query tile pair / one KV tile
+    (2, 512, 2, 64),
+    (1, 256, 3, 128),
+    (1, 200, 2, 64),     # ragged: partial query and key tiles
+    (1, 333, 1, 128),    # ragged, d = 128
+    (1, 1024, 2, 64),    # several KV tiles, exercises the stage ring
+    (1, 64, 2, 64),      # shorter than one tile
+])
+def test_attention_bf16_matches_oracle(B, L, H, D):
+    inputs, outs = _run(B, L, H, D, seed=B * 131 + L * 7 + H * 3 + D)
+    _check(inputs, outs)
+
+
+@pytest.mark.gpu
+def test_attention_bf16_accumulate_adds_into_grads():
+    """accumulate=1 adds into dq/dk/dv: a second call onto the first call's
+    result doubles it (grads of the same magnitude, so bf16 keeps them)."""
+    import pa_capi
+    B, L, H, D = 1, 256, 2, 64
+    q, k, v, g = (_bf16(seeded_normal(s, (B, L, H, D), 0.5))[0] for s in (11, 12, 13, 14))
+    o = torch.empty_like(q)
+    lse = torch.empty(B * H, L, device="cuda")
+    pa_capi.attn_fwd(q, k, v, o, lse)
+    ws = torch.empty(pa_capi.attn_bwd_workspace_size(pa_capi.attn_desc(q)), dtype=torch.uint8,
+                     device="cuda")
+    grads = [torch.empty_like(q) for _ in range(3)]
+    pa_capi.attn_bwd(q, k, v, o, g, lse, *grads, ws)
+    first = [t.float().cpu().numpy() for t in grads]
+    pa_capi.attn_bwd(q, k, v, o, g, lse, *grads, ws, accumulate=True)
+    torch.cuda.synchronize()
+    for f, t in zip(first, grads):
+        assert rel_err(t.float().cpu().numpy(), 2.0 * f) < 5e-3
+
+
+@pytest.mark.gpu
+def test_attention_bf16_headline_shape_slices():
+    """B=8, H=16, L=4096, d=64 (the headline shape): two (b, h) slices against the oracle."""
+    inputs, outs = _run(8, 4096, 16, 64, seed=3)
+    _check(inputs, outs, heads=[(0, 0), (7, 15)])
+
+
+@pytest.mark.gpu
+def test_attention_bf16_d128_two_heads_oracle():
+    """d = 128 at L = 2048 (all heads) against the oracle."""
+    inputs, outs = _run(1, 2048, 2, 128, seed=4)
+    _check(inputs, outs)
+
+
+@pytest.mark.gpu
+def test_attention_bf16_long_sequence_d128_properties():
+    """B=2, H=16, L=16384, d=128 (long-sequence shape), checked through exact
+    identities of the math that hold at any size:
+      sum_j dV_j = sum_i dO_i   (rows of P sum to 1)
+      sum_j dK_j = 0            (rows of dS sum to 0)
+      O rows lie in the range of V's columns (convex combinations)."""
+    (qn, kn, vn, gn), (o, lse, dq, dk, dv) = _run(2, 16384, 16, 128, seed=4)
+    sdv = dv.sum(axis=1)           # [B, H, D]
+    sdo = gn.sum(axis=1)
+    assert rel_err(sdv, sdo) < 2e-2
+    sdk = np.abs(dk.sum(axis=1)).max()
+    scale = np.abs(dk).sum(axis=1).max()
+    assert sdk <= 2e-2 * scale
+    assert np.all(o <= vn.max(axis=1, keepdims=True) + 1e-2)
+    assert np.all(o >= vn.min(axis=1, keepdims=True) - 1e-2)
+    assert np.all(np.isfinite(dq)) and np.all(np.isfinite(lse))
+
+
+@pytest.mark.gpu
+def test_attention_deterministic_forward():
+    _, a = _run(1, 512, 2, 64, seed=5)
+    _, b = _run(1, 512, 2, 64, seed=5)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+    # dK / dV are accumulated in TMEM in a fixed order: bitwise equal as well
+    np.testing.assert_array_equal(a[3], b[3])
+    np.testing.assert_array_equal(a[4], b[4])
+
+
+@pytest.mark.gpu
+def test_attention_delta_matches_oracle():
+    import oracle
+    import pa_capi
+    B, L, H, D = 2, 300, 3, 64
+    o, on = _bf16(seeded_normal(21, (B, L, H, D)))
+    g, gn = _bf16(seeded_normal(22, (B, L, H, D)))
+    delta = torch.zeros(B, L, H, dtype=torch.float32, device="cuda")
+    pa_capi.attn_delta(g, o, delta)
+    torch.cuda.synchronize()
+    ref = np.einsum("blhd,blhd->blh", gn, on)
+    assert rel_err(delta.cpu().numpy(), ref) < 1e-5
+
+
+@pytest.mark.gpu
+def test_attention_rejects_bad_arguments():
+    import pa_capi
+    q = torch.zeros(1, 128, 1, 96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(pa_capi.PaError) as e:
+        pa_capi.attn_fwd(q, q, q, q, torch.zeros(128, device="cuda"))
+    assert e.value.status == 4  # PA_ERR_UNSUPPORTED
+    q = torch.zeros(1, 128, 1, 64, dtype=torch.bfloat16, device="cuda")
+    d = pa_capi.attn_desc(q)
+    small = torch.empty(16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(pa_capi.PaError) as e:
+        pa_capi.attn_bwd(q, q, q, q, q, torch.zeros(128, device="cuda"), q, q, q, small)
+    assert e.value.status == 7  # PA_ERR_WORKSPACE

@@ -1,0 +1,72 @@
+"""The C-ABI library loads, exports every symbol include/pa_kernels.h declares,
+and rejects invalid arguments with the documented status codes before any
+device work (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+
+def _declared_symbols():
+    hdr = open(os.path.join(REPO, "include", "pa_kernels.h")).read()
+    hdr = re.sub(r"/\*.*?\*/", "", hdr, flags=re.S)
+    return sorted(set(re.findall(r"\b(pa_[a-z0-9_]+)\s*\(", hdr)))
+
+
+def test_header_and_binding_agree():
+    import pa_capi
+    assert sorted(pa_capi.EXPORTS) == _declared_symbols()
+
+
+def test_library_exports_every_declared_symbol():
+    import pa_capi
+    lib = pa_capi.load()
+    for name in _declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_status_strings():
+    import pa_capi
+    lib = pa_capi.load()
+    assert lib.pa_abi_version() == 1
+    for code in range(10):
+        assert lib.pa_status_string(code)
+
+
+def test_attention_argument_validation_without_gpu():
+    import pa_capi
+    lib = pa_capi.load()
+    fwd = lib.pa_attn_fwd
+    assert fwd(None, None, None, None, None, None, None) == 8          # PA_ERR_NULL
+    d = pa_capi.AttnDesc(1, 128, 1, 96, pa_capi.PA_BF16, 0.0)
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None) == 4         # head_dim 96
+    d = pa_capi.AttnDesc(0, 128, 1, 64, pa_capi.PA_BF16, 0.0)
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None) == 1         # batch 0
+    d = pa_capi.AttnDesc(1, 128, 1, 64, 7, 0.0)
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None) == 2         # dtype
+    d = pa_capi.AttnDesc(1, 128, 1, 64, pa_capi.PA_BF16, 0.0)
+    assert fwd(ctypes.byref(d), 16, 17, 16, 16, 16, None) == 3         # misaligned k
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, None, None) == 8       # lse NULL
+    ws = lib.pa_attn_bwd_workspace_size(ctypes.byref(d))
+    assert ws >= 128 * 64 * 4
+    bwd = lib.pa_attn_bwd
+    assert bwd(ctypes.byref(d), *([16] * 9), 0, None, 0, None) == 7   # no workspace
+    assert bwd(ctypes.byref(d), *([16] * 9), 0, 256, ws - 1, None) == 7
+    assert bwd(ctypes.byref(d), *([16] * 9), 0, 260, ws, None) == 3   # misaligned workspace
+
+
+def test_layer_norm_and_matmul_validation_without_gpu():
+    import pa_capi
+    lib = pa_capi.load()
+    assert lib.pa_layer_norm_fwd(None, None, None, None, None, None, 4, 8, 1e-5, None) == 8
+    assert lib.pa_layer_norm_fwd(16, 16, 16, 16, 16, 16, 0, 8, 1e-5, None) == 1
+    assert lib.pa_layer_norm_fwd(16, 16, 16, 16, 16, 16, 4, 6, 1e-5, None) == 4
+    assert lib.pa_layer_norm_bwd(16, 16, 16, 16, 16, 16, 16, 16, 4, 8, None, 0, None) == 7
+    assert lib.pa_matmul(16, 16, 16, 0, 4, 4, None) == 1
+    assert lib.pa_matmul_grad_x(None, 16, 16, 4, 4, 4, None) == 8
+    assert lib.pa_split_last_dim(16, None, 3, 4, 4, None) == 8
+    arr = (ctypes.c_void_p * 9)(*([16] * 9))
+    assert lib.pa_split_last_dim(16, arr, 9, 4, 4, None) == 1          # more than 8 parts
