@@ -1,0 +1,361 @@
+"""Benchmark of the attention training hot path on B200.
+
+Workload: flash-attention forward + backward, bf16 inputs with fp32
+accumulation, non-causal, B=8 H=16 L=4096 d=64 per GPU (the headline shape).
+One step = pa_attn_fwd + pa_attn_bwd over one batch of seeded synthetic
+inputs. Multi-GPU runs shard along batch x heads with no collective on the data
+path: every rank owns its own B=8 x H=16 units (weak scaling), and `value` is
+the FLOPs of all ranks over the slowest rank's device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0). FLOPs follow the FlashAttention convention:
+fwd 4*B*H*L^2*d + bwd 10*B*H*L^2*d (the backward recomputes S), exp excluded.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "pure-attention_b200")
+sys.path.insert(0, PKG)
+
+B, H, L, D = 8, 16, 4096, 64
+FLOPS_FWD = 4 * B * H * L * L * D
+FLOPS_BWD = 10 * B * H * L * L * D
+FLOPS_STEP = FLOPS_FWD + FLOPS_BWD
+METRIC = "attn fwd+bwd TFLOPS/GPU (B8 H16 N4096 d64 bf16) and % of dense tensor peak"
+WORKLOAD = "flash-attention fwd+bwd, bf16 in / fp32 accumulate, non-causal, B8 H16 L4096 d64 per GPU"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p.get("bf16_tflops_sustained"), p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def traffic_from_profile():
+    """DRAM bytes per backward launch from the committed ncu summary, or None."""
+    path = os.path.join(REPO, "profiles", "attn_bwd_kernel_B8H16L4096d64.md")
+    try:
+        for ln in open(path):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                return float(ln.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def make_inputs(torch, seed, device):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    ts = [(torch.randn(B, L, H, D, generator=g) * 0.5).to(torch.bfloat16) for _ in range(4)]
+    return [t.to(device) for t in ts], ts
+
+
+def cpu_baseline(budget_s=12.0):
+    """Time the multithreaded fp32 CPU attention (oracle/libcpuattn.so) on a
+    bounded sample of the same workload: whole (batch, head) units at L=4096,
+    d=64, one unit per thread, repeated until ~budget_s of CPU work."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # noqa: E402  (CPU baseline leg only)
+    nth = oracle.cpu().cpu_hardware_threads()
+    units = max(1, nth)
+    rng = np.random.default_rng(0)
+    Bs = units
+    q, k, v, g = ((rng.standard_normal((Bs, L, 1, D)) * 0.5).astype(np.float32) for _ in range(4))
+    outs = (np.zeros((Bs, L, 1, D), np.float32), np.zeros((Bs, L), np.float32),
+            np.zeros((Bs, L, 1, D), np.float32), np.zeros((Bs, L, 1, D), np.float32),
+            np.zeros((Bs, L, 1, D), np.float32))
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        *_, used = oracle.cpu_attn_fwd_bwd(q, k, v, g, nthreads=nth, outs=outs)
+        reps += 1
+        if time.perf_counter() - t0 > budget_s / 2 or reps >= 8:
+            break
+    dt = time.perf_counter() - t0
+    flops = 14.0 * reps * units * L * L * D
+    return {"value": flops / dt / 1e12, "unit": "TFLOPS", "cores": int(used), "kind": "port",
+            "sample": f"{reps} x {units} (batch, head) units of L=4096 d=64 fwd+bwd, fp32, "
+                      f"{dt:.1f} s wall on {used} threads"}
+
+
+def run_reference_arm(args):
+    """--impl reference: the multithreaded CPU implementation of the same
+    fwd+bwd on the host cores (the reference's own path is CUDA-only)."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # noqa: E402  (reference arm)
+    nth = oracle.cpu().cpu_hardware_threads()
+    rng = np.random.default_rng(1)
+    Bs = max(1, nth)
+    q, k, v, g = ((rng.standard_normal((Bs, L, 1, D)) * 0.5).astype(np.float32) for _ in range(4))
+    outs = (np.zeros((Bs, L, 1, D), np.float32), np.zeros((Bs, L), np.float32),
+            np.zeros((Bs, L, 1, D), np.float32), np.zeros((Bs, L, 1, D), np.float32),
+            np.zeros((Bs, L, 1, D), np.float32))
+    for _ in range(min(args.warmup, 1)):
+        oracle.cpu_attn_fwd_bwd(q, k, v, g, nthreads=nth, outs=outs)
+    times = []
+    used = nth
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        *_, used = oracle.cpu_attn_fwd_bwd(q, k, v, g, nthreads=nth, outs=outs)
+        times.append(time.perf_counter() - t0)
+    dt = sum(times)
+    flops = 14.0 * Bs * L * L * D * args.steps
+    val = flops / dt / 1e12
+    sample = (f"each step: {Bs} (batch, head) units of L=4096 d=64 fwd+bwd (1/{B * H // Bs} of "
+              f"the B8 H16 step), fp32 on {used} threads")
+    line = {"metric": METRIC, "value": val, "unit": "TFLOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": B * args.gpus, "seq_len": L,
+                       "heads": H, "head_dim": D, "parallelism": f"dp{args.gpus} (rank 0 only)"},
+            "cpu_baseline": {"value": val, "unit": "TFLOPS", "cores": int(used), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": val, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    import torch
+    import pa_capi
+    rank, world, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+    pa_capi.load()
+    peak, peak_sus, hbm, peak_src = peaks()
+    stream = torch.cuda.current_stream()
+
+    (q, k, v, g), host = make_inputs(torch, 1234 + rank, dev)
+    o = torch.empty_like(q)
+    lse = torch.empty(B * H, L, dtype=torch.float32, device=dev)
+    desc = pa_capi.attn_desc(q)
+    ws = torch.empty(pa_capi.attn_bwd_workspace_size(desc), dtype=torch.uint8, device=dev)
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+
+    def step():
+        pa_capi.attn_fwd(q, k, v, o, lse, desc)
+        pa_capi.attn_bwd(q, k, v, o, g, lse, dq, dk, dv, ws, desc=desc)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if pa_capi.device_status() != 0:
+        raise SystemExit("device status reports a timed-out wait during warm-up")
+
+    # ---------------- device-timed region: K steps, per-kernel events on the launch stream
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.25)
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_begin.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        pa_capi.attn_fwd(q, k, v, o, lse, desc)
+        ev[i][1].record(stream)
+        pa_capi.attn_bwd(q, k, v, o, g, lse, dq, dk, dv, ws, desc=desc)
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if pg:
+        pg.barrier()
+    elapsed_ms = t_begin.elapsed_time(t_end)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    if pg:
+        t = torch.tensor([elapsed_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    status = pa_capi.device_status()
+
+    # ---------------- end to end through the C ABI with host buffers
+    pinned = [t.pin_memory() for t in host]
+    outs_h = [torch.empty(B, L, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    e2e_steps = max(3, args.steps // 2)
+
+    def e2e_step():
+        for src, dst in zip(pinned, (q, k, v, g)):
+            dst.copy_(src, non_blocking=True)
+        step()
+        for src, dst in zip((dq, dk, dv), outs_h):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if pg:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(t.numel() * t.element_size() for t in pinned)
+    d2h = sum(t.numel() * t.element_size() for t in outs_h)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    ms_step = elapsed_ms / args.steps
+    value = world * FLOPS_STEP / (ms_step * 1e-3) / 1e12
+    per_gpu = value / world
+    e2e_val = world * FLOPS_STEP * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    bwd_tflops = FLOPS_BWD / (bwd_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1)*0.5 per rank)",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": L, "heads": H,
+                   "head_dim": D, "parallelism": f"dp{world} (batch x head shards, no collective)",
+                   "l2": "inputs (4 x 64 MiB bf16) exceed the 126 MB L2; no flush"},
+        "per_gpu_tflops": round(per_gpu, 2),
+        "frac_of_dense_peak": {"measured_bf16": round(per_gpu / peak, 4),
+                               "datasheet_2250": round(per_gpu / 2250.0, 4)},
+        "fwd_ms": round(fwd_ms, 4),
+        "bwd_ms": round(bwd_ms, 4),
+        "roofline": {"bound": "tensor", "kernel": "attn_bwd (pa_attn_bwd span: prep + main + dQ convert)",
+                     "achieved": round(bwd_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(bwd_tflops / peak, 4), "traffic": traffic_from_profile(),
+                     "peak_source": f"{peak_src} burst bf16 (cuBLAS)",
+                     "algorithmic_flops_per_launch": FLOPS_BWD},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_val, 2), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 4)},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clk,
+        "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
