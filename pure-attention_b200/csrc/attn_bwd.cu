@@ -14,18 +14,21 @@
 //                          get LSE = +inf so their P is exactly 0).
 //   attn_bwd_kernel      : one CTA per (batch, head, 128-key tile), looping
 //                          over 128-query tiles:
-//       warp 0     TMA producer (K, V once; Q, dO, LSE, Delta per query tile)
-//       warp 1     TMEM allocator + tcgen05.mma issuer
-//       warps 4-7  P / dS elementwise (thread = one key row), dK/dV epilogue
-//       warps 8-11 dQ readout: TMEM -> swizzled shared tile -> TMA tensor
-//                  reduce-add into an fp32 dQ accumulator in the workspace
+//       warp 0      TMA producer (K, V once; Q, dO, LSE, Delta per query tile)
+//       warp 1      TMEM allocator + tcgen05.mma issuer
+//       warps 4-11  P / dS elementwise, thread = one key row and one half of
+//                   the 128 queries (two warpgroups); dK/dV epilogue
+//       warps 12-15 dQ readout: TMEM -> swizzled shared tile -> TMA tensor
+//                   reduce-add into an fp32 dQ accumulator in the workspace
 //     MMAs per query tile (M = 128, K-major unless noted):
 //       S^T  = K Q^T            (SS)        -> TMEM S
 //       dP^T = V dO^T           (SS)        -> TMEM dP
 //       dV  += P^T dO           (TS, dO MN-major)
 //       dK  += dS^T Q           (TS, Q MN-major)
 //       dQ   = dS K             (SS, dS and K MN-major; dS staged in shared)
-//     P^T and dS^T (bf16) are written over the first 64 columns of S and dP.
+//     P^T and dS^T (bf16) are written over the S and dP columns their
+//     warpgroup has already read. dS is kept without the softmax scale; the
+//     scale is applied once in the dK epilogue and in the dQ convert.
 //   attn_dq_convert_kernel : fp32 dQ accumulator -> dq in the boundary layout.
 #include "host_launchers.h"
 
@@ -35,14 +38,19 @@ template <int D>
 struct BwdCfg {
   static constexpr int KCH = D / 64;
   static constexpr int STAGES = (D == 64) ? 2 : 1;
-  static constexpr int DQB = (D == 64) ? 2 : 1;      // dQ staging buffers
+  static constexpr int DQB = 1;                      // dQ staging buffers
+  // d = 64: dS tile double-buffered and the next tile's S/dP MMAs issued before
+  // this tile's dQ MMA (dQ has its own TMEM columns). d = 128: dQ reuses S's
+  // TMEM columns, so dQ is issued before the next S.
+  static constexpr bool EARLY_S = (D == 64);
+  static constexpr int DSB = EARLY_S ? 2 : 1;
   static constexpr int CHUNK = 128 * 128;
   static constexpr int KV_BYTES = 128 * D * 2;
   static constexpr int QT_BYTES = 128 * D * 2;
   static constexpr int STAGE_BYTES = 2 * QT_BYTES + 1024;  // Q, dO, LSE2[128], Delta[128]
   static constexpr int DS_BYTES = 128 * 128 * 2;
   static constexpr int DQ_BYTES = 128 * D * 4;
-  static constexpr int SMEM = 2 * KV_BYTES + STAGES * STAGE_BYTES + DS_BYTES + DQB * DQ_BYTES + 1024;
+  static constexpr int SMEM = 2 * KV_BYTES + STAGES * STAGE_BYTES + DSB * DS_BYTES + DQB * DQ_BYTES + 1024;
   static constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
   static constexpr uint32_t T_DQ = (D == 64) ? 384 : 0;  // D=128: dQ reuses S's columns
 };
@@ -91,14 +99,20 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------- main
+// TMEM column of the k-th 16-query K-step of P^T / dS^T: each elementwise
+// warpgroup packs its 64 queries (32 columns of bf16 pairs) at the start of
+// the 64 fp32 columns it read, so queries [0,64) sit in columns [0,32) and
+// queries [64,128) in columns [64,96) of the S (or dP) tile.
+__device__ __forceinline__ uint32_t packed_col(int k) { return (k < 4) ? k * 8 : 64 + (k - 4) * 8; }
+
 template <int D>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapdO,
                     const __grid_constant__ CUtensorMap mapDQ,
                     __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
-                    const float* __restrict__ lse2_t, const float* __restrict__ delta_t, int L, int Lp, int H, float scale, float scale_log2,
-                    int accumulate, uint32_t* status) {
+                    const float* __restrict__ lse2_t, const float* __restrict__ delta_t, int L,
+                    int Lp, int H, float scale, float scale_log2, int accumulate, uint32_t* status) {
   using C = BwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[16];
@@ -111,7 +125,7 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* sV = sK + C::KV_BYTES;
   uint8_t* sStage = sV + C::KV_BYTES;
   uint8_t* sdS = sStage + C::STAGES * C::STAGE_BYTES;
-  uint8_t* sDQ = sdS + C::DS_BYTES;
+  uint8_t* sDQ = sdS + C::DSB * C::DS_BYTES;
 
   const uint32_t kv_full = smem_u32(&bars[0]);
   auto q_full = [&](int s) { return smem_u32(&bars[1 + s]); };
@@ -135,7 +149,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(q_empty(s), 1);
     }
     mbar_init(sd_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(kv_done, 1);
@@ -181,144 +195,202 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t idSP = make_idesc(128, 128, 1, false, false);
       constexpr uint32_t idKV = make_idesc(128, D, 1, false, true);
       constexpr uint32_t idQ = make_idesc(128, D, 1, true, true);
-      const uint32_t kA = smem_u32(sK), vA = smem_u32(sV), dsA = smem_u32(sdS);
-      bool ok = mbar_wait(kv_full, 0, status);
+      // Descriptor bases; offsets are added to the 16-byte address field.
+      const uint64_t dK_K = make_sdesc(smem_u32(sK), 16, 1024);              // K, K-major
+      const uint64_t dV_K = make_sdesc(smem_u32(sV), 16, 1024);              // V, K-major
+      const uint64_t dK_MN = make_sdesc(smem_u32(sK), C::CHUNK, 1024);       // K, MN-major
+      const uint64_t dSt_K = make_sdesc(smem_u32(sStage), 16, 1024);         // Q / dO, K-major
+      const uint64_t dSt_MN = make_sdesc(smem_u32(sStage), C::CHUNK, 1024);  // Q / dO, MN-major
+      const uint64_t dDS_MN = make_sdesc(smem_u32(sdS), C::CHUNK, 1024);     // dS, MN-major
+      auto issue_SdP = [&](int j) {
+        const uint32_t so = ((j % C::STAGES) * C::STAGE_BYTES) >> 4;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
+          umma_f16_ss(tmem + C::T_S, dK_K + off, dSt_K + so + off, idSP, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
+          umma_f16_ss(tmem + C::T_DP, dV_K + off, dSt_K + so + (C::QT_BYTES >> 4) + off, idSP,
+                      k > 0);
+        }
+      };
+      auto issue_dVdK = [&](int j) {
+        const uint32_t so = ((j % C::STAGES) * C::STAGE_BYTES) >> 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(tmem + C::T_DV, tmem + C::T_S + packed_col(k),
+                      dSt_MN + so + (C::QT_BYTES >> 4) + ((k * 2048) >> 4), idKV,
+                      (j > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + packed_col(k),
+                      dSt_MN + so + ((k * 2048) >> 4), idKV, (j > 0 || k > 0) ? 1u : 0u);
+      };
+      auto issue_dQ = [&](int j) {
+        const uint32_t bo = ((j % C::DSB) * C::DS_BYTES) >> 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ss(tmem + C::T_DQ, dDS_MN + bo + ((k * 2048) >> 4), dK_MN + ((k * 2048) >> 4),
+                      idQ, k > 0);
+      };
+      bool ok = mbar_wait(kv_full, 0, status) && mbar_wait(q_full(0), 0, status);
+      if (ok) {
+        tc_fence_after();
+        issue_SdP(0);
+        umma_commit(sd_full);
+      }
       for (int j = 0; ok && j < n_q; ++j) {
         const int s = j % C::STAGES;
-        const uint32_t qA = smem_u32(sStage + s * C::STAGE_BYTES);
-        const uint32_t doA = qA + C::QT_BYTES;
-        if (!(ok = mbar_wait(q_full(s), (j / C::STAGES) & 1, status))) break;
-        if (C::T_DQ == 0 && j > 0 && !(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k / 4) * C::CHUNK + (k % 4) * 32;
-          umma_f16_ss(tmem + C::T_S, make_sdesc(kA + off, 16, 1024), make_sdesc(qA + off, 16, 1024),
-                      idSP, k > 0);
-        }
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k / 4) * C::CHUNK + (k % 4) * 32;
-          umma_f16_ss(tmem + C::T_DP, make_sdesc(vA + off, 16, 1024),
-                      make_sdesc(doA + off, 16, 1024), idSP, k > 0);
-        }
-        umma_commit(sd_full);
+        const bool more = j + 1 < n_q;
         if (!(ok = mbar_wait(p_full, j & 1, status))) break;
         tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ts(tmem + C::T_DV, tmem + C::T_S + k * 8,
-                      make_sdesc(doA + k * 2048, C::CHUNK, 1024), idKV, (j > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + k * 8,
-                      make_sdesc(qA + k * 2048, C::CHUNK, 1024), idKV, (j > 0 || k > 0) ? 1u : 0u);
-        if (C::T_DQ != 0 && j > 0) {
-          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
-          tc_fence_after();
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ss(tmem + C::T_DQ, make_sdesc(dsA + k * 2048, C::CHUNK, 1024),
-                      make_sdesc(kA + k * 2048, C::CHUNK, 1024), idQ, k > 0);
-        umma_commit(dq_full);
+        issue_dVdK(j);
         umma_commit(q_empty(s));
+        if (C::EARLY_S) {
+          if (more) {
+            if (!(ok = mbar_wait(q_full((j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1, status)))
+              break;
+            tc_fence_after();
+            issue_SdP(j + 1);
+            umma_commit(sd_full);
+          }
+          if (j > 0) {
+            if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
+            tc_fence_after();
+          }
+          issue_dQ(j);
+          umma_commit(dq_full);
+        } else {
+          // dQ overwrites S's columns: after dV, before the next S.
+          if (j > 0) {
+            if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
+            tc_fence_after();
+          }
+          issue_dQ(j);
+          umma_commit(dq_full);
+          if (more) {
+            if (!(ok = mbar_wait(q_full((j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1, status)))
+              break;
+            if (!(ok = mbar_wait(dq_empty, j & 1, status))) break;
+            tc_fence_after();
+            issue_SdP(j + 1);
+            umma_commit(sd_full);
+          }
+        }
       }
       if (ok) umma_commit(kv_done);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ P / dS
-    const int kr = threadIdx.x - 128;  // key row within the tile == TMEM lane
+    // Two warpgroups: grp 0 handles queries [0,64) of each tile, grp 1 [64,128).
+    const int grp = (warp - 4) >> 2;
+    const int kr = ((warp & 3) << 5) + static_cast<int>(lane_id());  // key row == TMEM lane
     const int key = k0 + kr;
     const bool valid = key < L;
+    const bool full_tile = k0 + 128 <= L;  // CTA-uniform: no key masking needed
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + C::T_S + lane_base;
-    const uint32_t tdP = tmem + C::T_DP + lane_base;
+    const uint32_t tS = tmem + C::T_S + lane_base + grp * 64;
+    const uint32_t tdP = tmem + C::T_DP + lane_base + grp * 64;
     bool ok = true;
     for (int j = 0; j < n_q; ++j) {
       const int s = j % C::STAGES;
       if (!(ok = mbar_wait_warp(sd_full, j & 1, status))) break;
       if (!(ok = mbar_wait_warp(q_full(s), (j / C::STAGES) & 1, status))) break;
       tc_fence_after();
-      const float* lse2s = reinterpret_cast<const float*>(sStage + s * C::STAGE_BYTES + 2 * C::QT_BYTES);
+      uint8_t* dsrow = sdS + (j % C::DSB) * C::DS_BYTES + grp * C::CHUNK;  // MN-major dS tile
+      const float* lse2s =
+          reinterpret_cast<const float*>(sStage + s * C::STAGE_BYTES + 2 * C::QT_BYTES) + grp * 64;
       const float* dels = lse2s + 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld32(tS + c * 32, sv);
-        tmem_ld32(tdP + c * 32, dpv);
-        tmem_ld_wait();
-        uint32_t pk[16], dk2[16];
+      uint32_t sv[2][16], dpv[2][16];
+      tmem_ld16(tS, sv[0]);
+      tmem_ld16(tdP, dpv[0]);
+      tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int q = c * 32 + 2 * i;
-          const float2 ls = *reinterpret_cast<const float2*>(lse2s + q);
-          const float2 de = *reinterpret_cast<const float2*>(dels + q);
-          float p0 = ex2(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -ls.x));
-          float p1 = ex2(fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -ls.y));
-          if (!valid) p0 = p1 = 0.f;
-          const float ds0 = p0 * (__uint_as_float(dpv[2 * i]) - de.x) * scale;
-          const float ds1 = p1 * (__uint_as_float(dpv[2 * i + 1]) - de.y) * scale;
-          pk[i] = pack_bf16x2(p0, p1);
-          dk2[i] = pack_bf16x2(ds0, ds1);
+      for (int sc = 0; sc < 4; ++sc) {
+        const int cur = sc & 1;
+        if (sc < 3) {
+          tmem_ld16(tS + (sc + 1) * 16, sv[cur ^ 1]);
+          tmem_ld16(tdP + (sc + 1) * 16, dpv[cur ^ 1]);
         }
-        PA_TMEM_ST_X8(tS + c * 16, pk);
-        PA_TMEM_ST_X8(tS + c * 16 + 8, (pk + 8));
-        PA_TMEM_ST_X8(tdP + c * 16, dk2);
-        PA_TMEM_ST_X8(tdP + c * 16 + 8, (dk2 + 8));
-        // dS row of this key into the MN-major dS tile: queries c*32..c*32+31
-        uint8_t* region = sdS + (c >> 1) * C::CHUNK;
+        float ls[16], de[16];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const uint32_t cc = (c & 1) * 4 + u;
-          *reinterpret_cast<uint4*>(region + sw128_offset(kr, cc * 16)) =
-              make_uint4(dk2[4 * u], dk2[4 * u + 1], dk2[4 * u + 2], dk2[4 * u + 3]);
+          *reinterpret_cast<float4*>(&ls[4 * u]) =
+              *reinterpret_cast<const float4*>(lse2s + sc * 16 + 4 * u);
+          *reinterpret_cast<float4*>(&de[4 * u]) =
+              *reinterpret_cast<const float4*>(dels + sc * 16 + 4 * u);
         }
+        uint32_t pk[8], dk2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float p[2], d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int el = 2 * i + e;
+            p[e] = ex2(fmaf(__uint_as_float(sv[cur][el]), scale_log2, -ls[el]));
+            d2[e] = p[e] * (__uint_as_float(dpv[cur][el]) - de[el]);
+          }
+          pk[i] = pack_bf16x2(p[0], p[1]);
+          dk2[i] = pack_bf16x2(d2[0], d2[1]);
+        }
+        if (!full_tile && !valid) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pk[i] = dk2[i] = 0u;
+        }
+        PA_TMEM_ST_X8(tS + sc * 8, pk);
+        PA_TMEM_ST_X8(tdP + sc * 8, dk2);
+        // queries grp*64 + sc*16 .. +16 -> 32 bytes of this key's row in the dS tile
+        *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, (2 * sc) * 16)) =
+            make_uint4(dk2[0], dk2[1], dk2[2], dk2[3]);
+        *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, (2 * sc + 1) * 16)) =
+            make_uint4(dk2[4], dk2[5], dk2[6], dk2[7]);
+        if (sc < 3) tmem_ld_wait();
       }
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
+    // dK (x scale) and dV epilogue: group 0 writes dV, group 1 writes dK.
     if (ok && mbar_wait_warp(kv_done, 0, status)) {
       tc_fence_after();
       const size_t roff = ((static_cast<size_t>(b) * L + key) * H + h) * D;
+      __nv_bfloat16* dst = (grp == 0 ? dv : dk) + roff;
+      const uint32_t tsrc = tmem + (grp == 0 ? C::T_DV : C::T_DK) + lane_base;
+      const float mul = grp == 0 ? 1.f : scale;
 #pragma unroll 1
-      for (int part = 0; part < 2; ++part) {
-        __nv_bfloat16* dst = (part == 0 ? dv : dk) + roff;
-        const uint32_t tsrc = tmem + (part == 0 ? C::T_DV : C::T_DK) + lane_base;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tsrc + c * 32, o);
-          tmem_ld_wait();
-          if (valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tsrc + c * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float f[8];
+          for (int u = 0; u < 4; ++u) {
+            float f[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * u + e]);
-              if (accumulate) {
-                const uint4 prev = d4[u];
-                const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&prev);
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * u + e]) * mul;
+            if (accumulate) {
+              const uint4 prev = d4[u];
+              const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&prev);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 pf = __bfloat1622float2(p2[e]);
-                  f[2 * e] += pf.x;
-                  f[2 * e + 1] += pf.y;
-                }
+              for (int e = 0; e < 4; ++e) {
+                const float2 pf = __bfloat1622float2(p2[e]);
+                f[2 * e] += pf.x;
+                f[2 * e + 1] += pf.y;
               }
-              d4[u] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                 pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
             }
+            d4[u] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                               pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
           }
         }
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 12) {
     // ------------------------------------------------------------ dQ readout
-    const int qr = threadIdx.x - 256;  // query row within the tile == TMEM lane
+    const int qr = threadIdx.x - 384;  // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tdQ = tmem + C::T_DQ + lane_base;
     // The loop never exits early: the named barriers below need all 128
@@ -370,11 +442,11 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 // ---------------------------------------------------------------- dQ convert
-// dq[b, l, h, :] (=|+=) dq_acc[b*H + h, l, :]; 8 values per thread.
+// dq[b, l, h, :] (=|+=) scale * dq_acc[b*H + h, l, :]; 8 values per thread.
 template <int D, typename OutT>
 __global__ void __launch_bounds__(256)
     attn_dq_convert_kernel(const float* __restrict__ dq_acc, OutT* __restrict__ dq, int B, int L,
-                           int Lp, int H, int accumulate) {
+                           int Lp, int H, float scale, int accumulate) {
   const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t total = static_cast<size_t>(B) * L * H * (D / 8);
   if (gt >= total) return;
@@ -386,7 +458,8 @@ __global__ void __launch_bounds__(256)
   const float* src = dq_acc + ((static_cast<size_t>(b) * H + h) * Lp + l) * D + g * 8;
   const float4 a = *reinterpret_cast<const float4*>(src);
   const float4 c = *reinterpret_cast<const float4*>(src + 4);
-  float f[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  float f[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                c.x * scale, c.y * scale, c.z * scale, c.w * scale};
   OutT* dst = dq + rowi * D + g * 8;
   if constexpr (sizeof(OutT) == 2) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -477,7 +550,7 @@ static int launch_bwd_impl(const AttnShape& sh, const void* q, const void* k, co
   static uint64_t attr = 0;
   ensure_smem_attr(attn_bwd_kernel<D>, C::SMEM, attr);
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
-  attn_bwd_kernel<D><<<grid, 384, C::SMEM, stream>>>(
+  attn_bwd_kernel<D><<<grid, 512, C::SMEM, stream>>>(
       mq, mk, mv, mdo, mdq, static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv), lse2,
       delta_t, sh.L, Lp, sh.H, sh.scale, sh.scale * kLog2e, accumulate, status);
   if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
@@ -485,7 +558,8 @@ static int launch_bwd_impl(const AttnShape& sh, const void* q, const void* k, co
   const size_t threads = static_cast<size_t>(sh.B) * sh.L * sh.H * (D / 8);
   attn_dq_convert_kernel<D, __nv_bfloat16><<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
                                              stream>>>(dq_acc, static_cast<__nv_bfloat16*>(dq),
-                                                       sh.B, sh.L, Lp, sh.H, accumulate);
+                                                       sh.B, sh.L, Lp, sh.H, sh.scale,
+                                                       accumulate);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

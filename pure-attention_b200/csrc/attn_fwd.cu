@@ -13,11 +13,13 @@
 // The two softmax warpgroups ping-pong so the tensor core computes one tile's
 // S or P*V while the other tile's softmax runs.
 //
-// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D,256+2D).
-// P (bf16 pairs) is written over the first 64 columns of its S tile and feeds
-// the P*V MMA directly from TMEM. tcgen05.mma ops issued by one thread run in
-// issue order, so the next S MMA (which overwrites P) is issued only after the
-// P*V MMA that reads it.
+// TMEM columns (d = 64): S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
+// P0 [384,448) P1 [448,512). P has its own columns, so a softmax warpgroup
+// releases S (s_free) as soon as it has loaded it into registers and the next
+// tile's S = Q K^T runs while it computes the exponentials.
+// (d = 128: O takes 128 columns each, so P (bf16 pairs) is written over the
+// first 64 columns of its own S tile; the next S MMA is then issued after the
+// P*V MMA that reads P - tcgen05.mma ops of one thread execute in order.)
 //
 // The row max is kept in the log2 domain and only raised when a new tile's max
 // exceeds it by more than 8 (a factor 256): O and the row sum are rescaled
@@ -37,6 +39,9 @@ struct FwdCfg {
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int SMEM = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 1024;
   static constexpr int THREADS = 384;
+  static constexpr bool SEP_P = (D == 64);        // P in its own TMEM columns
+  static constexpr uint32_t T_S = 0, T_O = 256;
+  static constexpr uint32_t T_P = SEP_P ? 384 : 0;
 };
 
 template <int D>
@@ -46,7 +51,7 @@ __global__ void __launch_bounds__(384, 1)
                     float* __restrict__ lse, int L, int H, float scale_log2, uint32_t* status) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bars[16];
+  __shared__ uint64_t bars[24];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   if (cta_aborted(status, &abort_flag)) return;
@@ -62,6 +67,8 @@ __global__ void __launch_bounds__(384, 1)
   auto s_full = [&](int t) { return smem_u32(&bars[7 + t]); };
   auto p_full = [&](int t) { return smem_u32(&bars[9 + t]); };
   auto o_done = [&](int t) { return smem_u32(&bars[11 + t]); };
+  auto s_free = [&](int t) { return smem_u32(&bars[13 + t]); };
+  auto pv_done = [&](int t) { return smem_u32(&bars[15 + t]); };
 
   const int warp = warp_id();
   const int bh = blockIdx.y;
@@ -79,6 +86,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(s_full(t), 1);
       mbar_init(p_full(t), 128);
       mbar_init(o_done(t), 1);
+      mbar_init(s_free(t), 128);
+      mbar_init(pv_done(t), 1);
     }
     fence_mbar_init();
   }
@@ -119,23 +128,25 @@ __global__ void __launch_bounds__(384, 1)
     if (elect_one()) {
       constexpr uint32_t idS = make_idesc(128, 128, 1, false, false);
       constexpr uint32_t idO = make_idesc(128, D, 1, false, true);
-      const uint32_t tS[2] = {tmem, tmem + 128};
-      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+      // Descriptor bases; per-K-step offsets are added to the 16-byte address field.
+      const uint64_t dQ0 = make_sdesc(smem_u32(sQ), 16, 1024);
+      const uint64_t dK0 = make_sdesc(smem_u32(sK), 16, 1024);
+      const uint64_t dV0 = make_sdesc(smem_u32(sV), C::CHUNK, 1024);
       auto issue_S = [&](int t, int j) {
-        const uint32_t qa = smem_u32(sQ + t * C::Q_BYTES);
-        const uint32_t ka = smem_u32(sK + (j % C::STAGES) * C::KV_BYTES);
+        const uint64_t qd = dQ0 + ((t * C::Q_BYTES) >> 4);
+        const uint64_t kd = dK0 + (((j % C::STAGES) * C::KV_BYTES) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k / 4) * C::CHUNK + (k % 4) * 32;
-          umma_f16_ss(tS[t], make_sdesc(qa + off, 16, 1024), make_sdesc(ka + off, 16, 1024), idS,
-                      k > 0);
+          const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
+          umma_f16_ss(tmem + C::T_S + t * 128, qd + off, kd + off, idS, k > 0);
         }
       };
       auto issue_PV = [&](int t, int j) {
-        const uint32_t va = smem_u32(sV + (j % C::STAGES) * C::KV_BYTES);
+        const uint64_t vd = dV0 + (((j % C::STAGES) * C::KV_BYTES) >> 4);
+        const uint32_t tp = C::SEP_P ? (tmem + C::T_P + t * 64) : (tmem + C::T_S + t * 128);
 #pragma unroll
         for (int k = 0; k < C::BN / 16; ++k)
-          umma_f16_ts(tO[t], tS[t] + k * 8, make_sdesc(va + k * 2048, C::CHUNK, 1024), idO,
+          umma_f16_ts(tmem + C::T_O + t * D, tp + k * 8, vd + ((k * 2048) >> 4), idO,
                       (j > 0 || k > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, status) && mbar_wait(kv_full(0), 0, status);
@@ -149,27 +160,35 @@ __global__ void __launch_bounds__(384, 1)
       for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % C::STAGES;
         const bool more = j + 1 < n_kv;
-        if (!(ok = mbar_wait(p_full(0), j & 1, status))) break;
-        tc_fence_after();
-        issue_PV(0, j);
-        if (more) {
-          if (!(ok = mbar_wait(kv_full((j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1, status)))
-            break;
-          tc_fence_after();
-          issue_S(0, j + 1);
-          umma_commit(s_full(0));
-        } else {
-          umma_commit(o_done(0));
-        }
-        if (!(ok = mbar_wait(p_full(1), j & 1, status))) break;
-        tc_fence_after();
-        issue_PV(1, j);
-        umma_commit(kv_empty(s));
-        if (more) {
-          issue_S(1, j + 1);
-          umma_commit(s_full(1));
-        } else {
-          umma_commit(o_done(1));
+        if (more && !(ok = mbar_wait(kv_full((j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1,
+                                     status)))
+          break;
+        for (int t = 0; t < 2; ++t) {
+          if (C::SEP_P) {
+            // next S first (its columns were released by s_free), then P*V
+            if (more) {
+              if (!(ok = mbar_wait(s_free(t), j & 1, status))) break;
+              tc_fence_after();
+              issue_S(t, j + 1);
+              umma_commit(s_full(t));
+            }
+            if (!(ok = mbar_wait(p_full(t), j & 1, status))) break;
+            tc_fence_after();
+            issue_PV(t, j);
+            umma_commit(pv_done(t));
+          } else {
+            // P lives in S's columns: P*V first, then the next S overwrites them
+            if (!(ok = mbar_wait(p_full(t), j & 1, status))) break;
+            tc_fence_after();
+            issue_PV(t, j);
+            umma_commit(pv_done(t));
+            if (more) {
+              issue_S(t, j + 1);
+              umma_commit(s_full(t));
+            }
+          }
+          if (t == 1) umma_commit(kv_empty(s));
+          if (!more) umma_commit(o_done(t));
         }
       }
     }
@@ -178,8 +197,9 @@ __global__ void __launch_bounds__(384, 1)
     const int t = (warp - 4) / 4;                 // query tile of this warpgroup
     const int r = threadIdx.x - 128 * (t + 1);    // row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + t * 128 + lane_base;
-    const uint32_t tO = tmem + 256 + t * D + lane_base;
+    const uint32_t tS = tmem + C::T_S + t * 128 + lane_base;
+    const uint32_t tO = tmem + C::T_O + t * D + lane_base;
+    const uint32_t tP = C::SEP_P ? (tmem + C::T_P + t * 64 + lane_base) : tS;
     const int row = q0 + t * C::BM + r;
     float m = -INFINITY;  // running max of S * scale * log2(e)
     float l = 0.f;        // running row sum (relative to m)
@@ -191,6 +211,10 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_ld_wait();
+      if (C::SEP_P) {
+        tc_fence_before();
+        mbar_arrive(s_free(t));  // S may now be overwritten by the next tile's MMA
+      }
       const int kv_left = L - j * C::BN;
       if (kv_left < C::BN) {
 #pragma unroll
@@ -208,7 +232,13 @@ __global__ void __launch_bounds__(384, 1)
         l *= alpha;
         m = m_new;
       }
-      // P = exp2(S * scale * log2(e) - m), packed to bf16 pairs over S's columns.
+      // P of the previous tile and O are read / accumulated by its P*V MMA:
+      // wait for it before overwriting P or rescaling O (normally long done).
+      if (C::SEP_P && j > 0) {
+        if (!(ok = mbar_wait_warp(pv_done(t), (j - 1) & 1, status))) break;
+        tc_fence_after();
+      }
+      // P = exp2(S * scale * log2(e) - m), packed to bf16 pairs, 16 columns at a time.
       const float neg_m = -m;
       float sum = 0.f;
 #pragma unroll
@@ -221,11 +251,9 @@ __global__ void __launch_bounds__(384, 1)
           sum += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
-        PA_TMEM_ST_X8(tS + c * 8, pk);
+        PA_TMEM_ST_X8(tP + c * 8, pk);
       }
       l += sum;
-      // Rescale this tile's O rows when the running max moved (P*V of the
-      // previous tile has completed: it was issued before this tile's S MMA).
       if (warp_need && j > 0) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
