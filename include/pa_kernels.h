@@ -80,6 +80,22 @@ int pa_attn_bwd(const pa_attn_desc* desc, const void* q, const void* k, const vo
                 const void* o, const void* dO, const float* lse, void* dq, void* dk, void* dv,
                 int accumulate, void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
+/* Backward without a caller workspace, for callers that cannot allocate device
+ * memory (e.g. plugins whose host framework owns all GPU memory, or runtimes
+ * that forbid allocations once a model is resident). No counterpart in the
+ * reference, which allocated its scratch inside the call.
+ * Same arguments and results as pa_attn_bwd minus the workspace: the scratch
+ * is a fixed PA_ATTN_BWD_NOALLOC_MAX_WORKSPACE-byte array in the library's
+ * device memory, held on every GPU that loads the library until exit. Shapes
+ * whose pa_attn_bwd_workspace_size exceeds it return PA_ERR_WORKSPACE. All
+ * calls on a device share that array: calls that overlap on the GPU race and
+ * must be serialised. The first call on each device looks up the array's
+ * device address; make it before any stream capture on that device. */
+#define PA_ATTN_BWD_NOALLOC_MAX_WORKSPACE (32u << 20)
+int pa_attn_bwd_noalloc(const pa_attn_desc* desc, const void* q, const void* k, const void* v,
+                        const void* o, const void* dO, const float* lse, void* dq, void* dk,
+                        void* dv, int accumulate, pa_stream_t stream);
+
 /* delta = rowsum(dO * o) as [B, L, H] fp32. Replaces compute_delta_kernel
  * (include/backend/Kernels.cuh:132, launched inside launch_flash_backward). */
 int pa_attn_delta(const pa_attn_desc* desc, const void* dO, const void* o, float* delta,

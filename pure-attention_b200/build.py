@@ -29,6 +29,7 @@ KERNEL_SOURCES = [
     "elementwise.cu",
     "gemm.cu",
     "capi.cu",
+    "attn_bwd_noalloc.cu",
 ]
 
 LIB = os.path.join(HERE, "libpa_kernels.so")

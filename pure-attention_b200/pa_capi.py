@@ -22,7 +22,8 @@ STATUS = {
 # Every symbol include/pa_kernels.h declares.
 EXPORTS = [
     "pa_abi_version", "pa_status_string", "pa_device_status",
-    "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_delta",
+    "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
+    "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
     "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
@@ -55,6 +56,7 @@ _SIGS = {
     "pa_attn_fwd": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
     "pa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
     "pa_attn_bwd": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp, _sz, _vp]),
+    "pa_attn_bwd_noalloc": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp]),
     "pa_attn_delta": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp]),
     "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
     "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
@@ -145,6 +147,20 @@ def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, workspace, accumulate=False, desc=
                             _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), int(bool(accumulate)),
                             _ptr(workspace), ws_bytes, _stream() if stream is None else stream)
     _check("pa_attn_bwd", st)
+
+
+# Scratch limit of pa_attn_bwd_noalloc (PA_ATTN_BWD_NOALLOC_MAX_WORKSPACE).
+NOALLOC_MAX_WORKSPACE = 32 << 20
+
+
+def attn_bwd_noalloc(q, k, v, o, dO, lse, dq, dk, dv, accumulate=False, desc=None, stream=None):
+    """Backward using the library's built-in scratch instead of a caller
+    workspace (for callers that cannot allocate device memory)."""
+    d = desc or attn_desc(q)
+    st = load().pa_attn_bwd_noalloc(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                    _ptr(dO), _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv),
+                                    int(bool(accumulate)), _stream() if stream is None else stream)
+    _check("pa_attn_bwd_noalloc", st)
 
 
 def attn_delta(dO, o, delta, desc=None, stream=None):
