@@ -64,11 +64,16 @@ int pa_device_status(pa_stream_t stream, int clear);
 
 /* ---------------------------------------------------------------- attention */
 
+/* Bytes of workspace pa_attn_fwd needs for this shape (0 for bf16; the fp32
+ * path keeps bf16 hi/lo planes of q, k, v there). */
+size_t pa_attn_fwd_workspace_size(const pa_attn_desc* desc);
+
 /* Flash-attention forward: o = softmax(q k^T * scale) v, lse = row log-sum-exp.
  * Replaces launch_flash_attention (include/backend/Launchers.cuh:159-167).
- * bf16: head_dim 64 or 128. f32: head_dim 32, 64 or 128. */
+ * bf16: head_dim 64 or 128 (workspace may be NULL). f32: head_dim 32 or 64,
+ * computed as bf16 hi/lo splits (three tensor-core products per GEMM). */
 int pa_attn_fwd(const pa_attn_desc* desc, const void* q, const void* k, const void* v, void* o,
-                float* lse, pa_stream_t stream);
+                float* lse, void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
 /* Bytes of workspace pa_attn_bwd needs for this shape. */
 size_t pa_attn_bwd_workspace_size(const pa_attn_desc* desc);

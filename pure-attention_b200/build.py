@@ -25,6 +25,7 @@ NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler"
 KERNEL_SOURCES = [
     "attn_fwd.cu",
     "attn_bwd.cu",
+    "fp32_split.cu",
     "layernorm.cu",
     "elementwise.cu",
     "gemm.cu",

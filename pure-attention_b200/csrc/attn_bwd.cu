@@ -30,36 +30,43 @@
 //     warpgroup has already read. dS is kept without the softmax scale; the
 //     scale is applied once in the dK epilogue and in the dQ convert.
 //   attn_dq_convert_kernel : fp32 dQ accumulator -> dq in the boundary layout.
+//
+// fp32 path (SPLIT): Q, K, V, dO arrive as bf16 hi/lo planes (fp32_split.cu,
+// head dim padded to 64) and every product is hi*hi + hi*lo + lo*hi, three
+// chained MMAs; P and dS are split the same way. In TMEM the hi and lo halves
+// of each 16-query K-step sit in adjacent 8-column groups (16k, 16k + 8).
 #include "host_launchers.h"
 
 namespace pa {
 
-template <int D>
+template <int D, bool SPLIT>
 struct BwdCfg {
+  static constexpr int NP = SPLIT ? 2 : 1;  // operand planes (hi, lo)
   static constexpr int KCH = D / 64;
-  static constexpr int STAGES = (D == 64) ? 2 : 1;
+  static constexpr int STAGES = (D == 64 && !SPLIT) ? 2 : 1;
   static constexpr int DQB = 1;                      // dQ staging buffers
   // d = 64: dS tile double-buffered and the next tile's S/dP MMAs issued before
   // this tile's dQ MMA (dQ has its own TMEM columns). d = 128: dQ reuses S's
   // TMEM columns, so dQ is issued before the next S.
-  static constexpr bool EARLY_S = (D == 64);
+  static constexpr bool EARLY_S = (D == 64 && !SPLIT);
   static constexpr int DSB = EARLY_S ? 2 : 1;
   static constexpr int CHUNK = 128 * 128;
   static constexpr int KV_BYTES = 128 * D * 2;
   static constexpr int QT_BYTES = 128 * D * 2;
-  static constexpr int STAGE_BYTES = 2 * QT_BYTES + 1024;  // Q, dO, LSE2[128], Delta[128]
+  static constexpr int STAGE_BYTES = NP * 2 * QT_BYTES + 1024;  // Q, dO planes, LSE2[128], Delta[128]
   static constexpr int DS_BYTES = 128 * 128 * 2;
   static constexpr int DQ_BYTES = 128 * D * 4;
-  static constexpr int SMEM = 2 * KV_BYTES + STAGES * STAGE_BYTES + DSB * DS_BYTES + DQB * DQ_BYTES + 1024;
+  static constexpr int SMEM =
+      NP * 2 * KV_BYTES + STAGES * STAGE_BYTES + DSB * NP * DS_BYTES + DQB * DQ_BYTES + 1024;
   static constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
   static constexpr uint32_t T_DQ = (D == 64) ? 384 : 0;  // D=128: dQ reuses S's columns
 };
 
 // ---------------------------------------------------------------- prep
-// G = D/8 threads per (b, l, h) row, each reading 8 bf16 of dO and O.
-template <int D>
+// G = D/8 threads per (b, l, h) row, each reading 8 values of dO and O.
+template <int D, typename InT>
 __global__ void __launch_bounds__(256)
-    attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dO, const __nv_bfloat16* __restrict__ O,
+    attn_bwd_prep_kernel(const InT* __restrict__ dO, const InT* __restrict__ O,
                          const float* __restrict__ lse, float* __restrict__ lse2_t,
                          float* __restrict__ delta_t, float* __restrict__ delta_ref, int B, int L,
                          int Lp, int H) {
@@ -76,16 +83,25 @@ __global__ void __launch_bounds__(256)
   const bool real = in_range && l < L;
   if (real) {
     const size_t off = ((static_cast<size_t>(b) * L + l) * H + h) * D + g * 8;
-    const uint4 a = *reinterpret_cast<const uint4*>(dO + off);
-    const uint4 c = *reinterpret_cast<const uint4*>(O + off);
-    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-    const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+    if constexpr (sizeof(InT) == 2) {
+      const uint4 a = *reinterpret_cast<const uint4*>(dO + off);
+      const uint4 c = *reinterpret_cast<const uint4*>(O + off);
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 fa = __bfloat1622float2(a2[i]);
-      const float2 fc = __bfloat1622float2(c2[i]);
-      acc = fmaf(fa.x, fc.x, acc);
-      acc = fmaf(fa.y, fc.y, acc);
+      for (int i = 0; i < 4; ++i) {
+        const float2 fa = __bfloat1622float2(a2[i]);
+        const float2 fc = __bfloat1622float2(c2[i]);
+        acc = fmaf(fa.x, fc.x, acc);
+        acc = fmaf(fa.y, fc.y, acc);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float4 fa = *reinterpret_cast<const float4*>(dO + off + 4 * i);
+        const float4 fc = *reinterpret_cast<const float4*>(O + off + 4 * i);
+        acc = fmaf(fa.x, fc.x, fmaf(fa.y, fc.y, fmaf(fa.z, fc.z, fmaf(fa.w, fc.w, acc))));
+      }
     }
   }
 #pragma unroll
@@ -104,16 +120,24 @@ __global__ void __launch_bounds__(256)
 // the 64 fp32 columns it read, so queries [0,64) sit in columns [0,32) and
 // queries [64,128) in columns [64,96) of the S (or dP) tile.
 __device__ __forceinline__ uint32_t packed_col(int k) { return (k < 4) ? k * 8 : 64 + (k - 4) * 8; }
+// SPLIT: hi and lo halves of K-step k in columns 16k and 16k + 8.
+template <bool SPLIT>
+__device__ __forceinline__ uint32_t step_col(int k, int plane) {
+  return SPLIT ? static_cast<uint32_t>(16 * k + 8 * plane) : packed_col(k);
+}
 
-template <int D>
+// OutT: __nv_bfloat16 (bf16 path) or float (SPLIT); d_out = head dim of dk/dv.
+template <int D, bool SPLIT, typename OutT>
 __global__ void __launch_bounds__(512, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapdO,
-                    const __grid_constant__ CUtensorMap mapDQ,
-                    __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
-                    const float* __restrict__ lse2_t, const float* __restrict__ delta_t, int L,
-                    int Lp, int H, float scale, float scale_log2, int accumulate, uint32_t* status) {
-  using C = BwdCfg<D>;
+                    const __grid_constant__ CUtensorMap mapQl, const __grid_constant__ CUtensorMap mapKl,
+                    const __grid_constant__ CUtensorMap mapVl, const __grid_constant__ CUtensorMap mapdOl,
+                    const __grid_constant__ CUtensorMap mapDQ, OutT* __restrict__ dk,
+                    OutT* __restrict__ dv, const float* __restrict__ lse2_t,
+                    const float* __restrict__ delta_t, int L, int Lp, int H, int d_out, float scale,
+                    float scale_log2, int accumulate, uint32_t* status) {
+  using C = BwdCfg<D, SPLIT>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[16];
   __shared__ uint32_t tmem_slot;
@@ -121,11 +145,13 @@ __global__ void __launch_bounds__(512, 1)
   if (cta_aborted(status, &abort_flag)) return;
 
   uint8_t* smem = align1024(smem_raw);
+  // K / V: NP planes each. Stage s: Q planes, dO planes, LSE2, Delta.
+  // dS: DSB buffers of NP planes. Plane p of K at sK + p * KV_BYTES, etc.
   uint8_t* sK = smem;
-  uint8_t* sV = sK + C::KV_BYTES;
-  uint8_t* sStage = sV + C::KV_BYTES;
+  uint8_t* sV = sK + C::NP * C::KV_BYTES;
+  uint8_t* sStage = sV + C::NP * C::KV_BYTES;
   uint8_t* sdS = sStage + C::STAGES * C::STAGE_BYTES;
-  uint8_t* sDQ = sdS + C::DSB * C::DS_BYTES;
+  uint8_t* sDQ = sdS + C::DSB * C::NP * C::DS_BYTES;
 
   const uint32_t kv_full = smem_u32(&bars[0]);
   auto q_full = [&](int s) { return smem_u32(&bars[1 + s]); };
@@ -169,24 +195,29 @@ __global__ void __launch_bounds__(512, 1)
     if (elect_one()) {
       tma_prefetch_desc(&mapQ);
       tma_prefetch_desc(&mapdO);
-      mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
-      for (int c = 0; c < C::KCH; ++c) {
-        tma_load_4d(smem_u32(sK + c * C::CHUNK), &mapK, kv_full, c * 64, h, k0, b);
-        tma_load_4d(smem_u32(sV + c * C::CHUNK), &mapV, kv_full, c * 64, h, k0, b);
-      }
+      mbar_arrive_expect_tx(kv_full, C::NP * 2 * C::KV_BYTES);
+      for (int p = 0; p < C::NP; ++p)
+        for (int c = 0; c < C::KCH; ++c) {
+          tma_load_4d(smem_u32(sK + p * C::KV_BYTES + c * C::CHUNK), p ? &mapKl : &mapK, kv_full,
+                      c * 64, h, k0, b);
+          tma_load_4d(smem_u32(sV + p * C::KV_BYTES + c * C::CHUNK), p ? &mapVl : &mapV, kv_full,
+                      c * 64, h, k0, b);
+        }
       for (int j = 0; j < n_q; ++j) {
         const int s = j % C::STAGES;
         if (j >= C::STAGES && !mbar_wait(q_empty(s), ((j / C::STAGES) - 1) & 1, status)) break;
         uint8_t* st = sStage + s * C::STAGE_BYTES;
-        mbar_arrive_expect_tx(q_full(s), 2 * C::QT_BYTES + 1024);
-        for (int c = 0; c < C::KCH; ++c) {
-          tma_load_4d(smem_u32(st + c * C::CHUNK), &mapQ, q_full(s), c * 64, h, j * 128, b);
-          tma_load_4d(smem_u32(st + C::QT_BYTES + c * C::CHUNK), &mapdO, q_full(s), c * 64, h,
-                      j * 128, b);
-        }
+        mbar_arrive_expect_tx(q_full(s), C::NP * 2 * C::QT_BYTES + 1024);
+        for (int p = 0; p < C::NP; ++p)
+          for (int c = 0; c < C::KCH; ++c) {
+            tma_load_4d(smem_u32(st + p * C::QT_BYTES + c * C::CHUNK), p ? &mapQl : &mapQ,
+                        q_full(s), c * 64, h, j * 128, b);
+            tma_load_4d(smem_u32(st + (C::NP + p) * C::QT_BYTES + c * C::CHUNK),
+                        p ? &mapdOl : &mapdO, q_full(s), c * 64, h, j * 128, b);
+          }
         const size_t voff = static_cast<size_t>(bh) * Lp + j * 128;
-        bulk_load(smem_u32(st + 2 * C::QT_BYTES), lse2_t + voff, 512, q_full(s));
-        bulk_load(smem_u32(st + 2 * C::QT_BYTES + 512), delta_t + voff, 512, q_full(s));
+        bulk_load(smem_u32(st + 2 * C::NP * C::QT_BYTES), lse2_t + voff, 512, q_full(s));
+        bulk_load(smem_u32(st + 2 * C::NP * C::QT_BYTES + 512), delta_t + voff, 512, q_full(s));
       }
     }
   } else if (warp == 1) {
@@ -202,38 +233,63 @@ __global__ void __launch_bounds__(512, 1)
       const uint64_t dSt_K = make_sdesc(smem_u32(sStage), 16, 1024);         // Q / dO, K-major
       const uint64_t dSt_MN = make_sdesc(smem_u32(sStage), C::CHUNK, 1024);  // Q / dO, MN-major
       const uint64_t dDS_MN = make_sdesc(smem_u32(sdS), C::CHUNK, 1024);     // dS, MN-major
+      // SPLIT: product terms (A plane, B plane) = (hi,hi), (hi,lo), (lo,hi)
+      constexpr int NTERM = SPLIT ? 3 : 1;
+      constexpr uint32_t KVP = C::KV_BYTES >> 4, QTP = C::QT_BYTES >> 4, DSP = C::DS_BYTES >> 4;
       auto issue_SdP = [&](int j) {
         const uint32_t so = ((j % C::STAGES) * C::STAGE_BYTES) >> 4;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
-          umma_f16_ss(tmem + C::T_S, dK_K + off, dSt_K + so + off, idSP, k > 0);
+        for (int term = 0; term < NTERM; ++term) {
+          const uint32_t pa = term == 2, pb = term == 1;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
+            umma_f16_ss(tmem + C::T_S, dK_K + pa * KVP + off, dSt_K + so + pb * QTP + off, idSP,
+                        (term > 0 || k > 0) ? 1u : 0u);
+          }
         }
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
-          umma_f16_ss(tmem + C::T_DP, dV_K + off, dSt_K + so + (C::QT_BYTES >> 4) + off, idSP,
-                      k > 0);
+        for (int term = 0; term < NTERM; ++term) {
+          const uint32_t pa = term == 2, pb = term == 1;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
+            umma_f16_ss(tmem + C::T_DP, dV_K + pa * KVP + off,
+                        dSt_K + so + (C::NP + pb) * QTP + off, idSP, (term > 0 || k > 0) ? 1u : 0u);
+          }
         }
       };
       auto issue_dVdK = [&](int j) {
         const uint32_t so = ((j % C::STAGES) * C::STAGE_BYTES) >> 4;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ts(tmem + C::T_DV, tmem + C::T_S + packed_col(k),
-                      dSt_MN + so + (C::QT_BYTES >> 4) + ((k * 2048) >> 4), idKV,
-                      (j > 0 || k > 0) ? 1u : 0u);
+        for (int term = 0; term < NTERM; ++term) {
+          const int pa = term == 2, pb = term == 1;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + packed_col(k),
-                      dSt_MN + so + ((k * 2048) >> 4), idKV, (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 8; ++k)
+            umma_f16_ts(tmem + C::T_DV, tmem + C::T_S + step_col<SPLIT>(k, pa),
+                        dSt_MN + so + (C::NP + pb) * QTP + ((k * 2048) >> 4), idKV,
+                        (j > 0 || term > 0 || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int term = 0; term < NTERM; ++term) {
+          const int pa = term == 2, pb = term == 1;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + step_col<SPLIT>(k, pa),
+                        dSt_MN + so + pb * QTP + ((k * 2048) >> 4), idKV,
+                        (j > 0 || term > 0 || k > 0) ? 1u : 0u);
+        }
       };
       auto issue_dQ = [&](int j) {
-        const uint32_t bo = ((j % C::DSB) * C::DS_BYTES) >> 4;
+        const uint32_t bo = ((j % C::DSB) * C::NP * C::DS_BYTES) >> 4;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ss(tmem + C::T_DQ, dDS_MN + bo + ((k * 2048) >> 4), dK_MN + ((k * 2048) >> 4),
-                      idQ, k > 0);
+        for (int term = 0; term < NTERM; ++term) {
+          const uint32_t pa = term == 2, pb = term == 1;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            umma_f16_ss(tmem + C::T_DQ, dDS_MN + bo + pa * DSP + ((k * 2048) >> 4),
+                        dK_MN + pb * KVP + ((k * 2048) >> 4), idQ, (term > 0 || k > 0) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(kv_full, 0, status) && mbar_wait(q_full(0), 0, status);
       if (ok) {
@@ -299,9 +355,10 @@ __global__ void __launch_bounds__(512, 1)
       if (!(ok = mbar_wait_warp(sd_full, j & 1, status))) break;
       if (!(ok = mbar_wait_warp(q_full(s), (j / C::STAGES) & 1, status))) break;
       tc_fence_after();
-      uint8_t* dsrow = sdS + (j % C::DSB) * C::DS_BYTES + grp * C::CHUNK;  // MN-major dS tile
-      const float* lse2s =
-          reinterpret_cast<const float*>(sStage + s * C::STAGE_BYTES + 2 * C::QT_BYTES) + grp * 64;
+      // MN-major dS tile (hi plane; lo plane DS_BYTES further)
+      uint8_t* dsrow = sdS + (j % C::DSB) * C::NP * C::DS_BYTES + grp * C::CHUNK;
+      const float* lse2s = reinterpret_cast<const float*>(sStage + s * C::STAGE_BYTES +
+                                                          2 * C::NP * C::QT_BYTES) + grp * 64;
       const float* dels = lse2s + 128;
       uint32_t sv[2][16], dpv[2][16];
       tmem_ld16(tS, sv[0]);
@@ -322,7 +379,7 @@ __global__ void __launch_bounds__(512, 1)
           *reinterpret_cast<float4*>(&de[4 * u]) =
               *reinterpret_cast<const float4*>(dels + sc * 16 + 4 * u);
         }
-        uint32_t pk[8], dk2[8];
+        uint32_t pk[8], dk2[8], pl[8], dl2[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float p[2], d2[2];
@@ -334,18 +391,37 @@ __global__ void __launch_bounds__(512, 1)
           }
           pk[i] = pack_bf16x2(p[0], p[1]);
           dk2[i] = pack_bf16x2(d2[0], d2[1]);
+          if (SPLIT) {
+            pl[i] = pack_bf16x2(p[0] - __uint_as_float(pk[i] << 16),
+                                p[1] - __uint_as_float(pk[i] & 0xffff0000u));
+            dl2[i] = pack_bf16x2(d2[0] - __uint_as_float(dk2[i] << 16),
+                                 d2[1] - __uint_as_float(dk2[i] & 0xffff0000u));
+          }
         }
         if (!full_tile && !valid) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) pk[i] = dk2[i] = 0u;
+          for (int i = 0; i < 8; ++i) pk[i] = dk2[i] = pl[i] = dl2[i] = 0u;
         }
-        PA_TMEM_ST_X8(tS + sc * 8, pk);
-        PA_TMEM_ST_X8(tdP + sc * 8, dk2);
+        if (SPLIT) {
+          PA_TMEM_ST_X8(tS + sc * 16, pk);
+          PA_TMEM_ST_X8(tS + sc * 16 + 8, pl);
+          PA_TMEM_ST_X8(tdP + sc * 16, dk2);
+          PA_TMEM_ST_X8(tdP + sc * 16 + 8, dl2);
+        } else {
+          PA_TMEM_ST_X8(tS + sc * 8, pk);
+          PA_TMEM_ST_X8(tdP + sc * 8, dk2);
+        }
         // queries grp*64 + sc*16 .. +16 -> 32 bytes of this key's row in the dS tile
         *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, (2 * sc) * 16)) =
             make_uint4(dk2[0], dk2[1], dk2[2], dk2[3]);
         *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, (2 * sc + 1) * 16)) =
             make_uint4(dk2[4], dk2[5], dk2[6], dk2[7]);
+        if (SPLIT) {
+          *reinterpret_cast<uint4*>(dsrow + C::DS_BYTES + sw128_offset(kr, (2 * sc) * 16)) =
+              make_uint4(dl2[0], dl2[1], dl2[2], dl2[3]);
+          *reinterpret_cast<uint4*>(dsrow + C::DS_BYTES + sw128_offset(kr, (2 * sc + 1) * 16)) =
+              make_uint4(dl2[4], dl2[5], dl2[6], dl2[7]);
+        }
         if (sc < 3) tmem_ld_wait();
       }
       tmem_st_wait();
@@ -356,8 +432,8 @@ __global__ void __launch_bounds__(512, 1)
     // dK (x scale) and dV epilogue: group 0 writes dV, group 1 writes dK.
     if (ok && mbar_wait_warp(kv_done, 0, status)) {
       tc_fence_after();
-      const size_t roff = ((static_cast<size_t>(b) * L + key) * H + h) * D;
-      __nv_bfloat16* dst = (grp == 0 ? dv : dk) + roff;
+      const size_t roff = ((static_cast<size_t>(b) * L + key) * H + h) * d_out;
+      OutT* dst = (grp == 0 ? dv : dk) + roff;
       const uint32_t tsrc = tmem + (grp == 0 ? C::T_DV : C::T_DK) + lane_base;
       const float mul = grp == 0 ? 1.f : scale;
 #pragma unroll 1
@@ -365,7 +441,22 @@ __global__ void __launch_bounds__(512, 1)
         uint32_t o[32];
         tmem_ld32(tsrc + c * 32, o);
         tmem_ld_wait();
-        if (valid) {
+        if constexpr (SPLIT) {
+          if (valid && c * 32 < d_out) {
+            float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              float4 f = make_float4(__uint_as_float(o[4 * u]) * mul, __uint_as_float(o[4 * u + 1]) * mul,
+                                     __uint_as_float(o[4 * u + 2]) * mul,
+                                     __uint_as_float(o[4 * u + 3]) * mul);
+              if (accumulate) {
+                const float4 pv = d4[u];
+                f.x += pv.x; f.y += pv.y; f.z += pv.z; f.w += pv.w;
+              }
+              d4[u] = f;
+            }
+          }
+        } else if (valid) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -443,15 +534,17 @@ __global__ void __launch_bounds__(512, 1)
 
 // ---------------------------------------------------------------- dQ convert
 // dq[b, l, h, :] (=|+=) scale * dq_acc[b*H + h, l, :]; 8 values per thread.
+// D = row width of dq_acc; d_out (<= D, multiple of 8) = head dim of dq.
 template <int D, typename OutT>
 __global__ void __launch_bounds__(256)
     attn_dq_convert_kernel(const float* __restrict__ dq_acc, OutT* __restrict__ dq, int B, int L,
-                           int Lp, int H, float scale, int accumulate) {
+                           int Lp, int H, int d_out, float scale, int accumulate) {
   const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t total = static_cast<size_t>(B) * L * H * (D / 8);
+  const int G = d_out / 8;
+  const size_t total = static_cast<size_t>(B) * L * H * G;
   if (gt >= total) return;
-  const int g = static_cast<int>(gt % (D / 8));
-  const size_t rowi = gt / (D / 8);  // (b, l, h)
+  const int g = static_cast<int>(gt % G);
+  const size_t rowi = gt / G;  // (b, l, h)
   const int h = static_cast<int>(rowi % H);
   const int l = static_cast<int>((rowi / H) % L);
   const int b = static_cast<int>(rowi / (static_cast<size_t>(H) * L));
@@ -460,7 +553,7 @@ __global__ void __launch_bounds__(256)
   const float4 c = *reinterpret_cast<const float4*>(src + 4);
   float f[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
                 c.x * scale, c.y * scale, c.z * scale, c.w * scale};
-  OutT* dst = dq + rowi * D + g * 8;
+  OutT* dst = dq + rowi * d_out + g * 8;
   if constexpr (sizeof(OutT) == 2) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
     if (accumulate) {
@@ -488,99 +581,145 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------- host
-size_t attn_bwd_workspace_bytes(const AttnShape& sh) {
+namespace {
+size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// LSE2 [B*H, Lp], Delta [B*H, Lp], fp32 dQ accumulator [B*H*Lp, Dacc].
+size_t stats_bytes(const AttnShape& sh, int Dacc) {
   const size_t Lp = static_cast<size_t>((sh.L + 127) / 128) * 128;
   const size_t bh = static_cast<size_t>(sh.B) * sh.H;
-  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-  return up(bh * Lp * 4) * 2 + up(bh * Lp * sh.D * 4);
+  return up256(bh * Lp * 4) * 2 + up256(bh * Lp * Dacc * 4);
 }
 
-template <int D>
-static int launch_prep(const AttnShape& sh, const void* dO, const void* o, const float* lse,
-                       float* lse2, float* delta_t, float* delta_ref, int Lp, cudaStream_t stream) {
+// Delta (and LSE2) prep over rows of `Dreal` values of type InT.
+template <int Dreal, typename InT>
+int launch_prep(const AttnShape& sh, const void* dO, const void* o, const float* lse, float* lse2,
+                float* delta_t, float* delta_ref, int Lp, cudaStream_t stream) {
   const size_t rows = static_cast<size_t>(sh.B) * Lp * sh.H;
-  const size_t threads = rows * (D / 8);
+  const size_t threads = rows * (Dreal / 8);
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  attn_bwd_prep_kernel<D><<<blocks, 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(dO), static_cast<const __nv_bfloat16*>(o), lse, lse2,
-      delta_t, delta_ref, sh.B, sh.L, Lp, sh.H);
+  attn_bwd_prep_kernel<Dreal, InT><<<blocks, 256, 0, stream>>>(
+      static_cast<const InT*>(dO), static_cast<const InT*>(o), lse, lse2, delta_t, delta_ref, sh.B,
+      sh.L, Lp, sh.H);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
-int launch_attn_delta_bf16(const AttnShape& sh, const void* dO, const void* o, float* delta,
-                           cudaStream_t stream) {
-  if (sh.D == 64) return launch_prep<64>(sh, dO, o, nullptr, nullptr, nullptr, delta, sh.L, stream);
-  if (sh.D == 128) return launch_prep<128>(sh, dO, o, nullptr, nullptr, nullptr, delta, sh.L, stream);
-  return PA_ERR_UNSUPPORTED;
+template <typename InT>
+int prep_any(int Dreal, const AttnShape& sh, const void* dO, const void* o, const float* lse,
+             float* lse2, float* delta_t, float* delta_ref, int Lp, cudaStream_t stream) {
+  switch (Dreal) {
+    case 32: return launch_prep<32, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, Lp, stream);
+    case 64: return launch_prep<64, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, Lp, stream);
+    case 128: return launch_prep<128, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, Lp, stream);
+    default: return PA_ERR_UNSUPPORTED;
+  }
 }
 
-template <int D>
-static int launch_bwd_impl(const AttnShape& sh, const void* q, const void* k, const void* v,
-                           const void* o, const void* dO, const float* lse, void* dq, void* dk,
-                           void* dv, int accumulate, void* ws, uint32_t* status,
-                           cudaStream_t stream) {
-  using C = BwdCfg<D>;
+// Runs prep + main + dQ convert. m[0..3] = hi (or only) maps of q, k, v, dO;
+// m[4..7] = lo maps (SPLIT). sh.D = d_out (true head dim); D = MMA head dim.
+template <int D, bool SPLIT, typename T>
+int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void* dO,
+            const float* lse, void* dq, void* dk, void* dv, int accumulate, uint8_t* stats,
+            uint32_t* status, cudaStream_t stream) {
+  using C = BwdCfg<D, SPLIT>;
   const int Lp = (sh.L + 127) / 128 * 128;
   const size_t bh = static_cast<size_t>(sh.B) * sh.H;
-  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-  uint8_t* w = static_cast<uint8_t*>(ws);
-  float* lse2 = reinterpret_cast<float*>(w);
-  float* delta_t = reinterpret_cast<float*>(w + up(bh * Lp * 4));
-  float* dq_acc = reinterpret_cast<float*>(w + 2 * up(bh * Lp * 4));
-
-  CUtensorMap mq, mk, mv, mdo;
-  if (!make_qkv_map(&mq, q, sh, 128) || !make_qkv_map(&mk, k, sh, 128) ||
-      !make_qkv_map(&mv, v, sh, 128) || !make_qkv_map(&mdo, dO, sh, 128))
-    return PA_ERR_ALIGN;
+  float* lse2 = reinterpret_cast<float*>(stats);
+  float* delta_t = reinterpret_cast<float*>(stats + up256(bh * Lp * 4));
+  float* dq_acc = reinterpret_cast<float*>(stats + 2 * up256(bh * Lp * 4));
   // dQ accumulator [B*H*Lp, D] fp32, reduced into by 128-row x 32-column boxes.
   CUtensorMap mdq;
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(D), bh * Lp};
-    const uint64_t strides[1] = {static_cast<uint64_t>(D) * 4};
-    const uint32_t box[2] = {32, 128};
-    if (!make_tmap(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
-      return PA_ERR_ALIGN;
-  }
+  const uint64_t dims[2] = {static_cast<uint64_t>(D), bh * Lp};
+  const uint64_t strides[1] = {static_cast<uint64_t>(D) * 4};
+  const uint32_t box[2] = {32, 128};
+  if (!make_tmap(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return PA_ERR_ALIGN;
   if (cudaMemsetAsync(dq_acc, 0, bh * Lp * D * sizeof(float), stream) != cudaSuccess)
     return PA_ERR_LAUNCH;
-  int st = launch_prep<D>(sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream);
+  int st = prep_any<T>(sh.D, sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream);
   if (st != PA_OK) return st;
 
   static uint64_t attr = 0;
-  ensure_smem_attr(attn_bwd_kernel<D>, C::SMEM, attr);
+  ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr);
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
-  attn_bwd_kernel<D><<<grid, 512, C::SMEM, stream>>>(
-      mq, mk, mv, mdo, mdq, static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv), lse2,
-      delta_t, sh.L, Lp, sh.H, sh.scale, sh.scale * kLog2e, accumulate, status);
+  attn_bwd_kernel<D, SPLIT, T><<<grid, 512, C::SMEM, stream>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], mdq, static_cast<T*>(dk),
+      static_cast<T*>(dv), lse2, delta_t, sh.L, Lp, sh.H, sh.D, sh.scale, sh.scale * kLog2e,
+      accumulate, status);
   if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
 
-  const size_t threads = static_cast<size_t>(sh.B) * sh.L * sh.H * (D / 8);
-  attn_dq_convert_kernel<D, __nv_bfloat16><<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
-                                             stream>>>(dq_acc, static_cast<__nv_bfloat16*>(dq),
-                                                       sh.B, sh.L, Lp, sh.H, sh.scale,
-                                                       accumulate);
+  const size_t threads = static_cast<size_t>(sh.B) * sh.L * sh.H * (sh.D / 8);
+  attn_dq_convert_kernel<D, T><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      dq_acc, static_cast<T*>(dq), sh.B, sh.L, Lp, sh.H, sh.D, sh.scale, accumulate);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+}  // namespace
+
+size_t attn_bwd_workspace_bytes(const AttnShape& sh) { return stats_bytes(sh, sh.D); }
+
+int launch_attn_delta_bf16(const AttnShape& sh, const void* dO, const void* o, float* delta,
+                           cudaStream_t stream) {
+  if (sh.D != 64 && sh.D != 128) return PA_ERR_UNSUPPORTED;
+  return prep_any<__nv_bfloat16>(sh.D, sh, dO, o, nullptr, nullptr, nullptr, delta, sh.L, stream);
 }
 
 int launch_attn_bwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v,
                          const void* o, const void* dO, const float* lse, void* dq, void* dk,
                          void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream) {
+  CUtensorMap m[8];
+  if (!make_qkv_map(&m[0], q, sh, 128) || !make_qkv_map(&m[1], k, sh, 128) ||
+      !make_qkv_map(&m[2], v, sh, 128) || !make_qkv_map(&m[3], dO, sh, 128))
+    return PA_ERR_ALIGN;
+  for (int i = 0; i < 4; ++i) m[4 + i] = m[i];
+  uint8_t* w = static_cast<uint8_t*>(ws);
   if (sh.D == 64)
-    return launch_bwd_impl<64>(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, ws, status, stream);
+    return run_bwd<64, false, __nv_bfloat16>(sh, m, o, dO, lse, dq, dk, dv, accumulate, w, status,
+                                              stream);
   if (sh.D == 128)
-    return launch_bwd_impl<128>(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, ws, status, stream);
+    return run_bwd<128, false, __nv_bfloat16>(sh, m, o, dO, lse, dq, dk, dv, accumulate, w, status,
+                                               stream);
   return PA_ERR_UNSUPPORTED;
 }
 
-size_t attn_bwd_workspace_bytes_f32(const AttnShape& sh) { return attn_bwd_workspace_bytes(sh); }
-int launch_attn_bwd_f32(const AttnShape&, const void*, const void*, const void*, const void*,
-                        const void*, const float*, void*, void*, void*, int, void*, uint32_t*,
-                        cudaStream_t) {
-  return PA_ERR_UNSUPPORTED;
+// fp32 path: bf16 hi/lo planes of q, k, v, dO (head dim padded to 64), then
+// the statistics block.
+size_t attn_bwd_workspace_bytes_f32(const AttnShape& sh) {
+  const int Dp = f32_plane_dim(sh.D);
+  if (Dp < 0) return 0;
+  const size_t plane = up256(static_cast<size_t>(sh.B) * sh.L * sh.H * Dp * 2);
+  return 8 * plane + stats_bytes(sh, Dp);
 }
-int launch_attn_delta_f32(const AttnShape&, const void*, const void*, float*, cudaStream_t) {
-  return PA_ERR_UNSUPPORTED;
+
+int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v,
+                        const void* o, const void* dO, const float* lse, void* dq, void* dk,
+                        void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream) {
+  const int Dp = f32_plane_dim(sh.D);
+  if (Dp != 64) return PA_ERR_UNSUPPORTED;
+  const size_t rows = static_cast<size_t>(sh.B) * sh.L * sh.H;
+  const size_t plane = up256(rows * Dp * 2);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const float* src[4] = {static_cast<const float*>(q), static_cast<const float*>(k),
+                         static_cast<const float*>(v), static_cast<const float*>(dO)};
+  AttnShape ps = sh;
+  ps.D = Dp;
+  CUtensorMap m[8];
+  for (int i = 0; i < 4; ++i) {
+    uint8_t* hi = w + (2 * i) * plane;
+    uint8_t* lo = w + (2 * i + 1) * plane;
+    const int st = launch_split_planes(src[i], hi, lo, rows, sh.D, Dp, stream);
+    if (st != PA_OK) return st;
+    if (!make_qkv_map(&m[i], hi, ps, 128) || !make_qkv_map(&m[4 + i], lo, ps, 128))
+      return PA_ERR_ALIGN;
+  }
+  return run_bwd<64, true, float>(sh, m, o, dO, lse, dq, dk, dv, accumulate, w + 8 * plane, status,
+                                  stream);
+}
+
+int launch_attn_delta_f32(const AttnShape& sh, const void* dO, const void* o, float* delta,
+                          cudaStream_t stream) {
+  if (sh.D != 32 && sh.D != 64) return PA_ERR_UNSUPPORTED;
+  return prep_any<float>(sh.D, sh, dO, o, nullptr, nullptr, nullptr, delta, sh.L, stream);
 }
 
 }  // namespace pa

@@ -21,6 +21,12 @@
 // first 64 columns of its own S tile; the next S MMA is then issued after the
 // P*V MMA that reads P - tcgen05.mma ops of one thread execute in order.)
 //
+// fp32 path (SPLIT): Q, K, V arrive as bf16 hi/lo planes (fp32_split.cu) and
+// every product is taken as hi*hi + hi*lo + lo*hi, three chained MMAs into the
+// same TMEM accumulator; P is split the same way and stored as hi (columns
+// [0,64)) and lo ([64,128)) over its S tile. Head dims 32 and 64 run as 64
+// (zero-padded planes); O is written in fp32 with the true head dim.
+//
 // The row max is kept in the log2 domain and only raised when a new tile's max
 // exceeds it by more than 8 (a factor 256): O and the row sum are rescaled
 // then, and otherwise P entries may reach 2^8, which fp32/bf16 hold exactly.
@@ -28,28 +34,32 @@
 
 namespace pa {
 
-template <int D>
+template <int D, bool SPLIT>
 struct FwdCfg {
+  static constexpr int NP = SPLIT ? 2 : 1;      // operand planes (hi, lo)
   static constexpr int BM = 128;                 // query rows per tile
   static constexpr int BN = 128;                 // keys per KV tile
   static constexpr int KCH = D / 64;             // 128-byte column chunks per row
-  static constexpr int STAGES = (D == 64) ? 3 : 2;
+  static constexpr int STAGES = (D == 64 && !SPLIT) ? 3 : 2;
   static constexpr int CHUNK = 128 * 128;        // bytes of one 128-row x 128-byte box
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int SMEM = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 1024;
+  static constexpr int SMEM = NP * (2 * Q_BYTES + STAGES * 2 * KV_BYTES) + 1024;
   static constexpr int THREADS = 384;
-  static constexpr bool SEP_P = (D == 64);        // P in its own TMEM columns
+  static constexpr bool SEP_P = (D == 64 && !SPLIT);  // P in its own TMEM columns
   static constexpr uint32_t T_S = 0, T_O = 256;
   static constexpr uint32_t T_P = SEP_P ? 384 : 0;
 };
 
-template <int D>
+// OutT: __nv_bfloat16 (bf16 path) or float (SPLIT). d_out: head dim of O.
+template <int D, bool SPLIT, typename OutT>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
-                    const __grid_constant__ CUtensorMap mapV, __nv_bfloat16* __restrict__ O,
-                    float* __restrict__ lse, int L, int H, float scale_log2, uint32_t* status) {
-  using C = FwdCfg<D>;
+                    const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapQl,
+                    const __grid_constant__ CUtensorMap mapKl, const __grid_constant__ CUtensorMap mapVl,
+                    OutT* __restrict__ O, float* __restrict__ lse, int L, int H, int d_out,
+                    float scale_log2, uint32_t* status) {
+  using C = FwdCfg<D, SPLIT>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[24];
   __shared__ uint32_t tmem_slot;
@@ -57,9 +67,10 @@ __global__ void __launch_bounds__(384, 1)
   if (cta_aborted(status, &abort_flag)) return;
 
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sQ = smem;                                // 2 tiles
-  uint8_t* sK = smem + 2 * C::Q_BYTES;               // STAGES tiles
-  uint8_t* sV = sK + C::STAGES * C::KV_BYTES;        // STAGES tiles
+  // plane p of query tile t at sQ + (t * NP + p) * Q_BYTES; K/V likewise per stage
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + C::NP * 2 * C::Q_BYTES;
+  uint8_t* sV = sK + C::NP * C::STAGES * C::KV_BYTES;
 
   const uint32_t q_full = smem_u32(&bars[0]);
   auto kv_full = [&](int s) { return smem_u32(&bars[1 + s]); };
@@ -106,21 +117,23 @@ __global__ void __launch_bounds__(384, 1)
       tma_prefetch_desc(&mapQ);
       tma_prefetch_desc(&mapK);
       tma_prefetch_desc(&mapV);
-      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+      mbar_arrive_expect_tx(q_full, C::NP * 2 * C::Q_BYTES);
       for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(smem_u32(sQ + t * C::Q_BYTES + c * C::CHUNK), &mapQ, q_full, c * 64, h,
-                      q0 + t * C::BM, b);
+        for (int p = 0; p < C::NP; ++p)
+          for (int c = 0; c < C::KCH; ++c)
+            tma_load_4d(smem_u32(sQ + (t * C::NP + p) * C::Q_BYTES + c * C::CHUNK),
+                        p ? &mapQl : &mapQ, q_full, c * 64, h, q0 + t * C::BM, b);
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % C::STAGES;
         if (j >= C::STAGES && !mbar_wait(kv_empty(s), ((j / C::STAGES) - 1) & 1, status)) break;
-        mbar_arrive_expect_tx(kv_full(s), 2 * C::KV_BYTES);
-        for (int c = 0; c < C::KCH; ++c) {
-          tma_load_4d(smem_u32(sK + s * C::KV_BYTES + c * C::CHUNK), &mapK, kv_full(s), c * 64, h,
-                      j * C::BN, b);
-          tma_load_4d(smem_u32(sV + s * C::KV_BYTES + c * C::CHUNK), &mapV, kv_full(s), c * 64, h,
-                      j * C::BN, b);
-        }
+        mbar_arrive_expect_tx(kv_full(s), C::NP * 2 * C::KV_BYTES);
+        for (int p = 0; p < C::NP; ++p)
+          for (int c = 0; c < C::KCH; ++c) {
+            tma_load_4d(smem_u32(sK + (s * C::NP + p) * C::KV_BYTES + c * C::CHUNK),
+                        p ? &mapKl : &mapK, kv_full(s), c * 64, h, j * C::BN, b);
+            tma_load_4d(smem_u32(sV + (s * C::NP + p) * C::KV_BYTES + c * C::CHUNK),
+                        p ? &mapVl : &mapV, kv_full(s), c * 64, h, j * C::BN, b);
+          }
       }
     }
   } else if (warp == 1) {
@@ -132,22 +145,32 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t dQ0 = make_sdesc(smem_u32(sQ), 16, 1024);
       const uint64_t dK0 = make_sdesc(smem_u32(sK), 16, 1024);
       const uint64_t dV0 = make_sdesc(smem_u32(sV), C::CHUNK, 1024);
+      // SPLIT: product terms (A plane, B plane) = (hi,hi), (hi,lo), (lo,hi)
+      constexpr int NTERM = SPLIT ? 3 : 1;
       auto issue_S = [&](int t, int j) {
-        const uint64_t qd = dQ0 + ((t * C::Q_BYTES) >> 4);
-        const uint64_t kd = dK0 + (((j % C::STAGES) * C::KV_BYTES) >> 4);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
-          umma_f16_ss(tmem + C::T_S + t * 128, qd + off, kd + off, idS, k > 0);
+        for (int term = 0; term < NTERM; ++term) {
+          const int pa = term == 2 ? 1 : 0, pb = term == 1 ? 1 : 0;
+          const uint64_t qd = dQ0 + (((t * C::NP + pa) * C::Q_BYTES) >> 4);
+          const uint64_t kd = dK0 + ((((j % C::STAGES) * C::NP + pb) * C::KV_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
+            umma_f16_ss(tmem + C::T_S + t * 128, qd + off, kd + off, idS, (term > 0 || k > 0) ? 1u : 0u);
+          }
         }
       };
       auto issue_PV = [&](int t, int j) {
-        const uint64_t vd = dV0 + (((j % C::STAGES) * C::KV_BYTES) >> 4);
         const uint32_t tp = C::SEP_P ? (tmem + C::T_P + t * 64) : (tmem + C::T_S + t * 128);
 #pragma unroll
-        for (int k = 0; k < C::BN / 16; ++k)
-          umma_f16_ts(tmem + C::T_O + t * D, tp + k * 8, vd + ((k * 2048) >> 4), idO,
-                      (j > 0 || k > 0) ? 1u : 0u);
+        for (int term = 0; term < NTERM; ++term) {
+          const int pa = term == 2 ? 1 : 0, pb = term == 1 ? 1 : 0;
+          const uint64_t vd = dV0 + ((((j % C::STAGES) * C::NP + pb) * C::KV_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < C::BN / 16; ++k)
+            umma_f16_ts(tmem + C::T_O + t * D, tp + pa * 64 + k * 8, vd + ((k * 2048) >> 4), idO,
+                        (j > 0 || term > 0 || k > 0) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(q_full, 0, status) && mbar_wait(kv_full(0), 0, status);
       if (ok) {
@@ -243,15 +266,19 @@ __global__ void __launch_bounds__(384, 1)
       float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        uint32_t pk[8];
+        uint32_t pk[8], pl[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float p0 = ex2(fmaf(s[c * 16 + 2 * i], scale_log2, neg_m));
           const float p1 = ex2(fmaf(s[c * 16 + 2 * i + 1], scale_log2, neg_m));
           sum += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
+          if (SPLIT)
+            pl[i] = pack_bf16x2(p0 - __uint_as_float(pk[i] << 16),
+                                p1 - __uint_as_float(pk[i] & 0xffff0000u));
         }
         PA_TMEM_ST_X8(tP + c * 8, pk);
+        if (SPLIT) PA_TMEM_ST_X8(tP + 64 + c * 8, pl);
       }
       l += sum;
       if (warp_need && j > 0) {
@@ -272,21 +299,31 @@ __global__ void __launch_bounds__(384, 1)
     if (ok && mbar_wait_warp(o_done(t), 0, status)) {
       tc_fence_after();
       const float inv_l = 1.f / l;
-      __nv_bfloat16* orow = O + ((static_cast<size_t>(b) * L + row) * H + h) * D;
+      OutT* orow = O + ((static_cast<size_t>(b) * L + row) * H + h) * d_out;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(tO + c * 32, o);
         tmem_ld_wait();
-        uint32_t pkd[16];
+        if constexpr (SPLIT) {
+          if (row < L && c * 32 < d_out) {
+            float4* dst = reinterpret_cast<float4*>(orow + c * 32);
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pkd[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
-        if (row < L) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                                   __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
+          }
+        } else {
+          uint32_t pkd[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          for (int i = 0; i < 16; ++i)
+            pkd[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+          if (row < L) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          }
         }
       }
       if (row < L) lse[static_cast<size_t>(bh) * L + row] = (m + __log2f(l)) * kLn2;
@@ -301,36 +338,71 @@ __global__ void __launch_bounds__(384, 1)
   }
 }
 
-// Host launcher. q/k/v/o are [B, L, H, D] bf16, lse is [B*H, L] fp32.
-int launch_attn_fwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
-                         float* lse, uint32_t* status, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv;
-  if (!make_qkv_map(&mq, q, sh, 128) || !make_qkv_map(&mk, k, sh, 128) ||
-      !make_qkv_map(&mv, v, sh, 128))
-    return PA_ERR_ALIGN;
-  const float scale_log2 = sh.scale * kLog2e;
-  dim3 grid((sh.L + 255) / 256, sh.B * sh.H);
-  if (sh.D == 64) {
-    using C = FwdCfg<64>;
-    static uint64_t attr = 0;
-    ensure_smem_attr(attn_fwd_kernel<64>, C::SMEM, attr);
-    attn_fwd_kernel<64><<<grid, C::THREADS, C::SMEM, stream>>>(
-        mq, mk, mv, static_cast<__nv_bfloat16*>(o), lse, sh.L, sh.H, scale_log2, status);
-  } else if (sh.D == 128) {
-    using C = FwdCfg<128>;
-    static uint64_t attr = 0;
-    ensure_smem_attr(attn_fwd_kernel<128>, C::SMEM, attr);
-    attn_fwd_kernel<128><<<grid, C::THREADS, C::SMEM, stream>>>(
-        mq, mk, mv, static_cast<__nv_bfloat16*>(o), lse, sh.L, sh.H, scale_log2, status);
-  } else {
-    return PA_ERR_UNSUPPORTED;
-  }
+template <int D, bool SPLIT, typename OutT>
+static int launch_fwd(const AttnShape& shp, const CUtensorMap* m, void* o, float* lse, int d_out,
+                      uint32_t* status, cudaStream_t stream) {
+  using C = FwdCfg<D, SPLIT>;
+  static uint64_t attr = 0;
+  ensure_smem_attr(attn_fwd_kernel<D, SPLIT, OutT>, C::SMEM, attr);
+  dim3 grid((shp.L + 255) / 256, shp.B * shp.H);
+  attn_fwd_kernel<D, SPLIT, OutT><<<grid, C::THREADS, C::SMEM, stream>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], static_cast<OutT*>(o), lse, shp.L, shp.H, d_out,
+      shp.scale * kLog2e, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
-int launch_attn_fwd_f32(const AttnShape&, const void*, const void*, const void*, void*, float*,
-                        uint32_t*, cudaStream_t) {
+// Host launcher. q/k/v/o are [B, L, H, D] bf16, lse is [B*H, L] fp32.
+int launch_attn_fwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
+                         float* lse, uint32_t* status, cudaStream_t stream) {
+  CUtensorMap m[6];
+  if (!make_qkv_map(&m[0], q, sh, 128) || !make_qkv_map(&m[1], k, sh, 128) ||
+      !make_qkv_map(&m[2], v, sh, 128))
+    return PA_ERR_ALIGN;
+  m[3] = m[0];
+  m[4] = m[1];
+  m[5] = m[2];
+  if (sh.D == 64) return launch_fwd<64, false, __nv_bfloat16>(sh, m, o, lse, 64, status, stream);
+  if (sh.D == 128) return launch_fwd<128, false, __nv_bfloat16>(sh, m, o, lse, 128, status, stream);
   return PA_ERR_UNSUPPORTED;
+}
+
+// Padded head dim of the fp32 path's bf16 planes.
+int f32_plane_dim(int D) { return D <= 64 ? 64 : -1; }
+
+size_t attn_fwd_workspace_bytes_f32(const AttnShape& sh) {
+  const int Dp = f32_plane_dim(sh.D);
+  if (Dp < 0) return 0;
+  const size_t plane = static_cast<size_t>(sh.B) * sh.L * sh.H * Dp * 2;
+  const size_t up = (plane + 255) & ~static_cast<size_t>(255);
+  return 6 * up;
+}
+
+// fp32 q/k/v/o [B, L, H, D], D in {32, 64}: split into bf16 hi/lo planes in
+// the workspace, then the SPLIT kernel.
+int launch_attn_fwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
+                        float* lse, void* ws, uint32_t* status, cudaStream_t stream) {
+  const int Dp = f32_plane_dim(sh.D);
+  if (Dp < 0) return PA_ERR_UNSUPPORTED;
+  const size_t rows = static_cast<size_t>(sh.B) * sh.L * sh.H;
+  const size_t plane = rows * Dp * 2;
+  const size_t up = (plane + 255) & ~static_cast<size_t>(255);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const float* src[3] = {static_cast<const float*>(q), static_cast<const float*>(k),
+                         static_cast<const float*>(v)};
+  for (int i = 0; i < 3; ++i) {
+    const int st = launch_split_planes(src[i], w + (2 * i) * up, w + (2 * i + 1) * up, rows, sh.D,
+                                       Dp, stream);
+    if (st != PA_OK) return st;
+  }
+  AttnShape ps = sh;
+  ps.D = Dp;
+  CUtensorMap m[6];
+  // m[0..2] = hi planes of q, k, v; m[3..5] = lo planes
+  for (int i = 0; i < 3; ++i)
+    if (!make_qkv_map(&m[i], w + (2 * i) * up, ps, 128) ||
+        !make_qkv_map(&m[3 + i], w + (2 * i + 1) * up, ps, 128))
+      return PA_ERR_ALIGN;
+  return launch_fwd<64, true, float>(ps, m, o, lse, sh.D, status, stream);
 }
 
 }  // namespace pa

@@ -32,8 +32,7 @@ int check_attn(const pa_attn_desc* d, pa::AttnShape* sh) {
     return PA_ERR_SHAPE;
   if (d->dtype != PA_BF16 && d->dtype != PA_F32) return PA_ERR_DTYPE;
   if (d->dtype == PA_BF16 && d->head_dim != 64 && d->head_dim != 128) return PA_ERR_UNSUPPORTED;
-  if (d->dtype == PA_F32 && d->head_dim != 32 && d->head_dim != 64 && d->head_dim != 128)
-    return PA_ERR_UNSUPPORTED;
+  if (d->dtype == PA_F32 && d->head_dim != 32 && d->head_dim != 64) return PA_ERR_UNSUPPORTED;
   const long long Lp = (static_cast<long long>(d->seq_len) + 127) / 128 * 128;
   if (static_cast<long long>(d->batch) * d->num_heads * Lp > 0x7fffffffLL) return PA_ERR_SHAPE;
   sh->B = d->batch;
@@ -77,18 +76,29 @@ int pa_device_status(pa_stream_t stream, int clear) {
   return v == 0 ? PA_OK : PA_ERR_TIMEOUT;
 }
 
+size_t pa_attn_fwd_workspace_size(const pa_attn_desc* desc) {
+  pa::AttnShape sh;
+  if (check_attn(desc, &sh) != PA_OK) return 0;
+  return desc->dtype == PA_BF16 ? 0 : pa::attn_fwd_workspace_bytes_f32(sh);
+}
+
 int pa_attn_fwd(const pa_attn_desc* desc, const void* q, const void* k, const void* v, void* o,
-                float* lse, pa_stream_t stream) {
+                float* lse, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
   pa::AttnShape sh;
   int st = check_attn(desc, &sh);
   if (st != PA_OK) return st;
   if (!q || !k || !v || !o || !lse) return PA_ERR_NULL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return PA_ERR_ALIGN;
+  if (desc->dtype == PA_F32) {
+    const size_t need = pa_attn_fwd_workspace_size(desc);
+    if (!workspace || workspace_bytes < need) return PA_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PA_ERR_ALIGN;
+  }
   uint32_t* status = status_word();
   if (!status) return PA_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (desc->dtype == PA_BF16) return pa::launch_attn_fwd_bf16(sh, q, k, v, o, lse, status, s);
-  return pa::launch_attn_fwd_f32(sh, q, k, v, o, lse, status, s);
+  return pa::launch_attn_fwd_f32(sh, q, k, v, o, lse, workspace, status, s);
 }
 
 size_t pa_attn_bwd_workspace_size(const pa_attn_desc* desc) {

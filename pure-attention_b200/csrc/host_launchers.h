@@ -11,7 +11,13 @@ namespace pa {
 int launch_attn_fwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
                          float* lse, uint32_t* status, cudaStream_t stream);
 int launch_attn_fwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
-                        float* lse, uint32_t* status, cudaStream_t stream);
+                        float* lse, void* ws, uint32_t* status, cudaStream_t stream);
+size_t attn_fwd_workspace_bytes_f32(const AttnShape& sh);
+int f32_plane_dim(int D);  // padded head dim of the fp32 path's bf16 planes (-1: unsupported)
+
+// fp32_split.cu: x [rows, D] fp32 -> hi, lo [rows, Dp] bf16 (zero-padded).
+int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
+                        cudaStream_t s);
 
 // attn_bwd.cu
 size_t attn_bwd_workspace_bytes(const AttnShape& sh);

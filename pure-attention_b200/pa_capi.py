@@ -22,7 +22,7 @@ STATUS = {
 # Every symbol include/pa_kernels.h declares.
 EXPORTS = [
     "pa_abi_version", "pa_status_string", "pa_device_status",
-    "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
+    "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
     "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
@@ -53,7 +53,8 @@ _SIGS = {
     "pa_abi_version": (_int, []),
     "pa_status_string": (ctypes.c_char_p, [_int]),
     "pa_device_status": (_int, [_vp, _int]),
-    "pa_attn_fwd": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp, _vp, _vp]),
+    "pa_attn_fwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
+    "pa_attn_fwd": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "pa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
     "pa_attn_bwd": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp, _sz, _vp]),
     "pa_attn_bwd_noalloc": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp]),
@@ -128,10 +129,22 @@ def attn_desc(q, num_heads=None, scale=0.0):
     return AttnDesc(B, L, H, D, _dtype_code(q), float(scale))
 
 
-def attn_fwd(q, k, v, o, lse, desc=None, stream=None):
+def attn_fwd_workspace_size(desc):
+    return load().pa_attn_fwd_workspace_size(ctypes.byref(desc))
+
+
+def attn_fwd(q, k, v, o, lse, desc=None, stream=None, workspace=None):
+    """Forward. bf16 needs no workspace; for fp32 one is allocated here with
+    torch unless `workspace` is given."""
     d = desc or attn_desc(q)
+    if workspace is None:
+        need = attn_fwd_workspace_size(d)
+        if need:
+            import torch
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     st = load().pa_attn_fwd(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse),
-                            _stream() if stream is None else stream)
+                            _ptr(workspace), ws_bytes, _stream() if stream is None else stream)
     _check("pa_attn_fwd", st)
 
 

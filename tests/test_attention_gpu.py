@@ -177,3 +177,62 @@ def test_attention_rejects_bad_arguments():
     with pytest.raises(pa_capi.PaError) as e:
         pa_capi.attn_bwd(q, q, q, q, q, torch.zeros(128, device="cuda"), q, q, q, small)
     assert e.value.status == 7  # PA_ERR_WORKSPACE
+
+
+# ---------------------------------------------------------------- fp32 path
+F32_TOL = 1e-3  # norm-wise relative error on O, dQ, dK, dV (fp32 path)
+
+
+def _run_f32(q, k, v, g, accumulate=False):
+    import pa_capi
+    B, L, H, D = q.shape
+    tq, tk, tv, tg = (torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+                      for x in (q, k, v, g))
+    o = torch.empty_like(tq)
+    lse = torch.empty(B * H, L, device="cuda")
+    pa_capi.attn_fwd(tq, tk, tv, o, lse)
+    d = pa_capi.attn_desc(tq)
+    ws = torch.empty(pa_capi.attn_bwd_workspace_size(d), dtype=torch.uint8, device="cuda")
+    dq, dk, dv = (torch.full_like(tq, float("nan")) for _ in range(3))
+    pa_capi.attn_bwd(tq, tk, tv, o, tg, lse, dq, dk, dv, ws)
+    assert pa_capi.device_status() == 0
+    torch.cuda.synchronize()
+    f = lambda t: t.cpu().numpy().astype(np.float64)
+    return f(o), f(lse), f(dq), f(dk), f(dv)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,H,D,heads", [
+    (1, 128, 1, 32, None),     # single-head C1 shape
+    (2, 256, 2, 64, None),
+    (1, 200, 3, 32, None),     # ragged tiles, d = 32 (padded planes)
+    (8, 1024, 8, 64, [(0, 0), (3, 5), (7, 7)]),  # the pre-LN block's attention shape
+])
+def test_attention_f32_matches_oracle(B, L, H, D, heads):
+    import oracle
+    shape = (B, L, H, D)
+    q, k, v, g = (seeded_normal(s, shape) for s in (B + L, B + L + 1, B + L + 2, B + L + 3))
+    o, lse, dq, dk, dv = _run_f32(q, k, v, g)
+    for (b, h) in heads or [(b, h) for b in range(B) for h in range(H)]:
+        sl = (slice(b, b + 1), slice(None), slice(h, h + 1), slice(None))
+        ro, rl = oracle.attn_fwd(q[sl], k[sl], v[sl])
+        rdq, rdk, rdv, _ = oracle.attn_bwd(q[sl], k[sl], v[sl], ro, g[sl], rl)
+        errs = {"o": rel_err(o[sl], ro), "dq": rel_err(dq[sl], rdq), "dk": rel_err(dk[sl], rdk),
+                "dv": rel_err(dv[sl], rdv)}
+        print(f"f32 (b={b},h={h}) L={L} D={D} rel errs {errs}")
+        for name, e in errs.items():
+            assert e <= F32_TOL, (name, e)
+        assert np.max(np.abs(lse[b * H + h] - rl[0])) < 1e-4
+
+
+@pytest.mark.gpu
+def test_attention_f32_matches_reference_golden_c1():
+    """fp32 path on the exact inputs of the golden fixture produced by the
+    reference's own kernels (B=1, H=1, L=128, d=32): O, LSE, dK, dV."""
+    import os
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_c1_attention.npz"))
+    o, lse, dq, dk, dv = _run_f32(z["q"], z["k"], z["v"], z["dO"])
+    assert rel_err(o, z["o"]) < F32_TOL
+    assert np.max(np.abs(lse - z["lse"])) < 1e-4
+    assert rel_err(dk, z["dk"]) < F32_TOL
+    assert rel_err(dv, z["dv"]) < F32_TOL

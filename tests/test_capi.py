@@ -40,16 +40,22 @@ def test_attention_argument_validation_without_gpu():
     import pa_capi
     lib = pa_capi.load()
     fwd = lib.pa_attn_fwd
-    assert fwd(None, None, None, None, None, None, None) == 8          # PA_ERR_NULL
+    assert fwd(None, None, None, None, None, None, None, 0, None) == 8  # PA_ERR_NULL
     d = pa_capi.AttnDesc(1, 128, 1, 96, pa_capi.PA_BF16, 0.0)
-    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None) == 4         # head_dim 96
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None, 0, None) == 4  # head_dim 96
     d = pa_capi.AttnDesc(0, 128, 1, 64, pa_capi.PA_BF16, 0.0)
-    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None) == 1         # batch 0
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None, 0, None) == 1  # batch 0
     d = pa_capi.AttnDesc(1, 128, 1, 64, 7, 0.0)
-    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None) == 2         # dtype
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, 16, None, 0, None) == 2  # dtype
     d = pa_capi.AttnDesc(1, 128, 1, 64, pa_capi.PA_BF16, 0.0)
-    assert fwd(ctypes.byref(d), 16, 17, 16, 16, 16, None) == 3         # misaligned k
-    assert fwd(ctypes.byref(d), 16, 16, 16, 16, None, None) == 8       # lse NULL
+    assert fwd(ctypes.byref(d), 16, 17, 16, 16, 16, None, 0, None) == 3  # misaligned k
+    assert fwd(ctypes.byref(d), 16, 16, 16, 16, None, None, 0, None) == 8  # lse NULL
+    assert lib.pa_attn_fwd_workspace_size(ctypes.byref(d)) == 0          # bf16: none
+    d32 = pa_capi.AttnDesc(1, 128, 1, 32, pa_capi.PA_F32, 0.0)
+    assert lib.pa_attn_fwd_workspace_size(ctypes.byref(d32)) >= 6 * 128 * 64 * 2
+    assert fwd(ctypes.byref(d32), 16, 16, 16, 16, 16, None, 0, None) == 7  # f32 needs workspace
+    d128 = pa_capi.AttnDesc(1, 128, 1, 128, pa_capi.PA_F32, 0.0)
+    assert fwd(ctypes.byref(d128), 16, 16, 16, 16, 16, None, 0, None) == 4  # f32 d=128
     ws = lib.pa_attn_bwd_workspace_size(ctypes.byref(d))
     assert ws >= 128 * 64 * 4
     bwd = lib.pa_attn_bwd
