@@ -124,16 +124,23 @@ int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const 
 
 /* ---------------------------------------------------------------- matmul */
 
+/* fp32 GEMMs on the tensor cores: operands are split into bf16 hi/lo planes
+ * in the workspace and each product is hi*hi + hi*lo + lo*hi (fp32-level
+ * accuracy). Bytes of workspace any of the three calls below needs for these
+ * M, N, K: */
+size_t pa_matmul_workspace_size(int M, int N, int K);
+
 /* C[M,N] = A[M,K] B[K,N]. Replaces launch_matmul_tiled (Launchers.cuh:15-23). */
-int pa_matmul(const float* A, const float* B, float* C, int M, int N, int K, pa_stream_t stream);
+int pa_matmul(const float* A, const float* B, float* C, int M, int N, int K, void* workspace,
+              size_t workspace_bytes, pa_stream_t stream);
 
 /* dX[M,N] += dY[M,K] W[N,K]^T. Replaces launch_matmul_grad_X (Launchers.cuh:64-72). */
 int pa_matmul_grad_x(const float* dY, const float* W, float* dX, int M, int N, int K,
-                     pa_stream_t stream);
+                     void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
 /* dW[N,K] += X[M,N]^T dY[M,K]. Replaces launch_matmul_grad_W (Launchers.cuh:74-82). */
 int pa_matmul_grad_w(const float* X, const float* dY, float* dW, int M, int N, int K,
-                     pa_stream_t stream);
+                     void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
 /* ---------------------------------------------------------------- elementwise */
 

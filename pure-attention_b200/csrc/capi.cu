@@ -182,26 +182,35 @@ int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const 
                                    static_cast<cudaStream_t>(stream));
 }
 
-int pa_matmul(const float* A, const float* B, float* C, int M, int N, int K, pa_stream_t stream) {
+size_t pa_matmul_workspace_size(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return pa::gemm_workspace_bytes(M, N, K);
+}
+
+static int gemm_call(int mode, const float* A, const float* B, float* C, int M, int N, int K,
+                     void* ws, size_t ws_bytes, pa_stream_t stream) {
   if (!A || !B || !C) return PA_ERR_NULL;
   if (M <= 0 || N <= 0 || K <= 0) return PA_ERR_SHAPE;
-  return pa::launch_gemm_f32(0, A, B, C, M, N, K, status_word(), static_cast<cudaStream_t>(stream));
+  if (!ws || ws_bytes < pa::gemm_workspace_bytes(M, N, K)) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return PA_ERR_ALIGN;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  return pa::launch_gemm_f32(mode, A, B, C, M, N, K, ws, status, static_cast<cudaStream_t>(stream));
+}
+
+int pa_matmul(const float* A, const float* B, float* C, int M, int N, int K, void* workspace,
+              size_t workspace_bytes, pa_stream_t stream) {
+  return gemm_call(0, A, B, C, M, N, K, workspace, workspace_bytes, stream);
 }
 
 int pa_matmul_grad_x(const float* dY, const float* W, float* dX, int M, int N, int K,
-                     pa_stream_t stream) {
-  if (!dY || !W || !dX) return PA_ERR_NULL;
-  if (M <= 0 || N <= 0 || K <= 0) return PA_ERR_SHAPE;
-  return pa::launch_gemm_f32(1, dY, W, dX, M, N, K, status_word(),
-                             static_cast<cudaStream_t>(stream));
+                     void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  return gemm_call(1, dY, W, dX, M, N, K, workspace, workspace_bytes, stream);
 }
 
 int pa_matmul_grad_w(const float* X, const float* dY, float* dW, int M, int N, int K,
-                     pa_stream_t stream) {
-  if (!X || !dY || !dW) return PA_ERR_NULL;
-  if (M <= 0 || N <= 0 || K <= 0) return PA_ERR_SHAPE;
-  return pa::launch_gemm_f32(2, X, dY, dW, M, N, K, status_word(),
-                             static_cast<cudaStream_t>(stream));
+                     void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  return gemm_call(2, X, dY, dW, M, N, K, workspace, workspace_bytes, stream);
 }
 
 int pa_bias_add(const float* A, const float* bias, float* out, int M, int N, pa_stream_t stream) {

@@ -14,7 +14,7 @@ namespace pa {
 
 namespace {
 
-// One thread per 4 output columns of one row.
+// One thread per 4 output columns of one row (D % 4 == 0, 16-byte aligned x).
 __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
                                     __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp) {
   const int groups = Dp / 4;
@@ -40,14 +40,37 @@ __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* 
   }
 }
 
+// Any D: one thread per output element.
+__global__ void split_planes_scalar_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
+                                           __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < rows * Dp;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / Dp;
+    const int c = static_cast<int>(i % Dp);
+    const float v = c < D ? x[r * D + c] : 0.f;
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
 }  // namespace
 
 int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
                         cudaStream_t s) {
-  if (D % 4 != 0 || Dp % 4 != 0 || D > Dp) return PA_ERR_SHAPE;
+  if (D > Dp || D <= 0) return PA_ERR_SHAPE;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (D % 4 != 0 || Dp % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
+    const size_t n = rows * Dp;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > static_cast<size_t>(sms) * 16) blocks = static_cast<size_t>(sms) * 16;
+    if (blocks == 0) blocks = 1;
+    split_planes_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp);
+    return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+  }
   const size_t work = rows * (Dp / 4);
   size_t blocks = (work + 255) / 256;
   if (blocks > static_cast<size_t>(sms) * 16) blocks = static_cast<size_t>(sms) * 16;

@@ -1,11 +1,233 @@
-// tcgen05 GEMM for the projection forward and the matmul gradients (fp32 I/O).
+// tcgen05 GEMM for the projection forward and the matmul gradients (fp32 in/out).
+//
+// Restates the reference's three tiled fp32 GEMMs:
+//   mode 0  C[M,N]   = A[M,K] B[K,N]      matmul_kernel.cu:4-50
+//   mode 1  dX[M,N] += dY[M,K] W[N,K]^T   matmul_backward_X_kernel.cu:5-54
+//   mode 2  dW[N,K] += X[M,N]^T dY[M,K]   matmul_backward_W_kernel.cu:5-55
+// on the bf16 tensor cores at fp32-level accuracy: each fp32 operand is split
+// into bf16 hi/lo planes in the caller's workspace (fp32_split.cu) and every
+// product is hi*hi + hi*lo + lo*hi, three MMAs into one fp32 TMEM accumulator.
+//
+// The transposes of the gradients cost nothing: a row-major operand whose
+// reduction index is the row index is simply fed as an MN-major tcgen05
+// operand, so each mode reads its inputs in place.
+//
+// One CTA = one 128 x 128 output tile; K in blocks of 64 through a 3-stage
+// TMA ring (hi and lo planes of both operands per stage).
+//   warp 0     TMA producer
+//   warp 1     TMEM allocator + MMA issuer
+//   warps 4-7  epilogue: TMEM -> registers -> C (thread = one output row)
+#include <cuda_bf16.h>
 #include "host_launchers.h"
 
 namespace pa {
 
-int launch_gemm_f32(int, const float*, const float*, float*, int, int, int, uint32_t*,
-                    cudaStream_t) {
-  return PA_ERR_UNSUPPORTED;
+namespace {
+
+constexpr int GB = 128;          // output tile (rows and columns)
+constexpr int GK = 64;           // K block (one 128-byte swizzle row of bf16)
+constexpr int GSTAGES = 3;
+constexpr int PLANE_TILE = GB * GK * 2;       // 16 KB: one operand plane of one stage
+constexpr int STAGE = 4 * PLANE_TILE;         // A hi, A lo, B hi, B lo
+constexpr int GSMEM = GSTAGES * STAGE + 1024;
+
+// A_MN / B_MN: the operand is stored with its reduction index as the row index
+// (MN-major for tcgen05); otherwise the reduction index is contiguous (K-major).
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(256, 1)
+    gemm_split_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                      const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
+                      float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
+                      uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bars[2 * GSTAGES + 1];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  if (cta_aborted(status, &abort_flag)) return;
+  uint8_t* smem = align1024(smem_raw);
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[GSTAGES + s]); };
+  const uint32_t acc_full = smem_u32(&bars[2 * GSTAGES]);
+  const int warp = warp_id();
+  const int m0 = blockIdx.y * GB, n0 = blockIdx.x * GB;
+  const int nk = (Kred + GK - 1) / GK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GSTAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      const CUtensorMap* maps[4] = {&mAh, &mAl, &mBh, &mBl};
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % GSTAGES;
+        if (kb >= GSTAGES && !mbar_wait(empty(s), ((kb / GSTAGES) - 1) & 1, status)) break;
+        mbar_arrive_expect_tx(full(s), STAGE);
+        uint8_t* st = smem + s * STAGE;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const bool mn = p < 2 ? A_MN : B_MN;
+          const int r0 = p < 2 ? m0 : n0;
+          const uint32_t dst = smem_u32(st + p * PLANE_TILE);
+          if (mn) {
+            // two 64-wide groups along M/N, 64 K rows each
+            tma_load_2d(dst, maps[p], full(s), r0, kb * GK);
+            tma_load_2d(dst + PLANE_TILE / 2, maps[p], full(s), r0 + 64, kb * GK);
+          } else {
+            tma_load_2d(dst, maps[p], full(s), kb * GK, r0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc(128, 128, 1, A_MN, B_MN);
+      const uint64_t base = make_sdesc(smem_u32(smem), 16, 1024);
+      const uint64_t base_mn = make_sdesc(smem_u32(smem), PLANE_TILE / 2, 1024);
+      bool ok = true;
+      for (int kb = 0; ok && kb < nk; ++kb) {
+        const int s = kb % GSTAGES;
+        if (!(ok = mbar_wait(full(s), (kb / GSTAGES) & 1, status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int term = 0; term < 3; ++term) {
+          const uint32_t pa_ = (term == 2) ? 1 : 0, pb = (term == 1) ? 3 : 2;
+#pragma unroll
+          for (int ks = 0; ks < GK / 16; ++ks) {
+            const uint32_t so = (s * STAGE) >> 4;
+            const uint64_t da = (A_MN ? base_mn + ((pa_ * PLANE_TILE + ks * 2048) >> 4)
+                                      : base + ((pa_ * PLANE_TILE + ks * 32) >> 4)) + so;
+            const uint64_t db = (B_MN ? base_mn + ((pb * PLANE_TILE + ks * 2048) >> 4)
+                                      : base + ((pb * PLANE_TILE + ks * 32) >> 4)) + so;
+            umma_f16_ss(tmem, da, db, idesc, (kb > 0 || term > 0 || ks > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(empty(s));
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else if (warp >= 4) {
+    const int r = threadIdx.x - 128;
+    const int row = m0 + r;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    if (mbar_wait_warp(acc_full, 0, status)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < GB / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c * 32, v);
+        tmem_ld_wait();
+        if (row >= Mout) continue;
+        const int col0 = n0 + c * 32;
+        float* dst = C + static_cast<size_t>(row) * ldc + col0;
+        const bool vec = (col0 + 32 <= Nout) && ((ldc & 3) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+        if (vec) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                                   __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+            if (accumulate) {
+              const float4 p = d4[u];
+              f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
+            }
+            d4[u] = f;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (col0 + e < Nout) dst[e] = __uint_as_float(v[e]) + (accumulate ? dst[e] : 0.f);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+int round8(int x) { return (x + 7) & ~7; }
+
+// Bytes of the hi + lo planes of a [rows, cols] fp32 operand (rows padded to 8 columns).
+size_t planes_bytes(int rows, int cols) {
+  return 2 * up256(static_cast<size_t>(rows) * round8(cols) * 2);
+}
+
+// 2-D TMA map over a bf16 plane of `rows` x `cols` (row pitch round8(cols)).
+// K-major operand: box {64 cols, 128 rows}; MN-major operand: box {64, 64}.
+bool plane_map(CUtensorMap* m, const void* base, int rows, int cols, bool mn) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(round8(cols)) * 2};
+  const uint32_t box[2] = {64, mn ? 64u : 128u};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <bool A_MN, bool B_MN>
+int run_gemm(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred, int accumulate,
+             uint32_t* status, cudaStream_t s) {
+  static uint64_t attr = 0;
+  ensure_smem_attr(gemm_split_kernel<A_MN, B_MN>, GSMEM, attr);
+  dim3 grid((Nout + GB - 1) / GB, (Mout + GB - 1) / GB);
+  gemm_split_kernel<A_MN, B_MN><<<grid, 256, GSMEM, s>>>(m[0], m[1], m[2], m[3], C, ldc, Mout, Nout,
+                                                          Kred, accumulate, status);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+}  // namespace
+
+size_t gemm_workspace_bytes(int M, int N, int K) {
+  const size_t m0 = planes_bytes(M, K) + planes_bytes(K, N);   // A [M,K], B [K,N]
+  const size_t m1 = planes_bytes(M, K) + planes_bytes(N, K);   // dY [M,K], W [N,K]
+  const size_t m2 = planes_bytes(M, N) + planes_bytes(M, K);   // X [M,N], dY [M,K]
+  size_t mx = m0 > m1 ? m0 : m1;
+  return mx > m2 ? mx : m2;
+}
+
+int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, int N, int K,
+                    void* ws, uint32_t* status, cudaStream_t s) {
+  // (rows, cols) of the two stored operands, per mode
+  int ar, ac, br, bc;
+  if (mode == 0) { ar = M; ac = K; br = K; bc = N; }
+  else if (mode == 1) { ar = M; ac = K; br = N; bc = K; }
+  else { ar = M; ac = N; br = M; bc = K; }
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const size_t pa_ = up256(static_cast<size_t>(ar) * round8(ac) * 2);
+  const size_t pb = up256(static_cast<size_t>(br) * round8(bc) * 2);
+  uint8_t* ah = w;
+  uint8_t* al = w + pa_;
+  uint8_t* bh = w + 2 * pa_;
+  uint8_t* bl = w + 2 * pa_ + pb;
+  int st = launch_split_planes(A, ah, al, ar, ac, round8(ac), s);
+  if (st != PA_OK) return st;
+  st = launch_split_planes(B, bh, bl, br, bc, round8(bc), s);
+  if (st != PA_OK) return st;
+  const bool a_mn = (mode == 2), b_mn = (mode != 1);
+  CUtensorMap m[4];
+  if (!plane_map(&m[0], ah, ar, ac, a_mn) || !plane_map(&m[1], al, ar, ac, a_mn) ||
+      !plane_map(&m[2], bh, br, bc, b_mn) || !plane_map(&m[3], bl, br, bc, b_mn))
+    return PA_ERR_ALIGN;
+  if (mode == 0) return run_gemm<false, true>(m, C, N, M, N, K, 0, status, s);
+  if (mode == 1) return run_gemm<false, false>(m, C, N, M, N, K, 1, status, s);
+  return run_gemm<true, true>(m, C, K, N, K, M, 1, status, s);
 }
 
 }  // namespace pa

@@ -60,6 +60,7 @@ int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint3
 //   mode 1: C[M,N] += A[M,K] B[N,K]^T   (grad X: A = dY, B = W)
 //   mode 2: C[N,K] += A[M,N]^T B[M,K]   (grad W: A = X,  B = dY)
 int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, int N, int K,
-                    uint32_t* status, cudaStream_t s);
+                    void* ws, uint32_t* status, cudaStream_t s);
+size_t gemm_workspace_bytes(int M, int N, int K);
 
 }  // namespace pa

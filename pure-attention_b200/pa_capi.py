@@ -25,7 +25,7 @@ EXPORTS = [
     "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
-    "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
+    "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
 ]
@@ -62,9 +62,10 @@ _SIGS = {
     "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
     "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
     "pa_layer_norm_bwd": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
-    "pa_matmul": (_int, [_vp] * 3 + [_int] * 3 + [_vp]),
-    "pa_matmul_grad_x": (_int, [_vp] * 3 + [_int] * 3 + [_vp]),
-    "pa_matmul_grad_w": (_int, [_vp] * 3 + [_int] * 3 + [_vp]),
+    "pa_matmul_workspace_size": (_sz, [_int] * 3),
+    "pa_matmul": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
+    "pa_matmul_grad_x": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
+    "pa_matmul_grad_w": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_bias_add": (_int, [_vp] * 3 + [_int] * 2 + [_vp]),
     "pa_add": (_int, [_vp] * 3 + [_sz, _vp]),
     "pa_grad_accumulate": (_int, [_vp] * 2 + [_sz, _vp]),
@@ -211,18 +212,37 @@ def layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, workspace, strea
     _check("pa_layer_norm_bwd", st)
 
 
-def matmul(a, b, c, M, N, K, stream=None):
-    _check("pa_matmul", load().pa_matmul(_ptr(a), _ptr(b), _ptr(c), M, N, K,
+def matmul_workspace_size(M, N, K):
+    return load().pa_matmul_workspace_size(M, N, K)
+
+
+def _gemm_ws(M, N, K, workspace, device):
+    if workspace is None:
+        import torch
+        workspace = torch.empty(matmul_workspace_size(M, N, K), dtype=torch.uint8, device=device)
+    return workspace, workspace.numel() * workspace.element_size()
+
+
+def matmul(a, b, c, M, N, K, workspace=None, stream=None):
+    """c[M,N] = a[M,K] b[K,N] (fp32)."""
+    ws, nb = _gemm_ws(M, N, K, workspace, a.device)
+    _check("pa_matmul", load().pa_matmul(_ptr(a), _ptr(b), _ptr(c), M, N, K, _ptr(ws), nb,
                                          _stream() if stream is None else stream))
 
 
-def matmul_grad_x(dy, w, dx, M, N, K, stream=None):
+def matmul_grad_x(dy, w, dx, M, N, K, workspace=None, stream=None):
+    """dx[M,N] += dy[M,K] w[N,K]^T."""
+    ws, nb = _gemm_ws(M, N, K, workspace, dy.device)
     _check("pa_matmul_grad_x", load().pa_matmul_grad_x(_ptr(dy), _ptr(w), _ptr(dx), M, N, K,
+                                                       _ptr(ws), nb,
                                                        _stream() if stream is None else stream))
 
 
-def matmul_grad_w(x, dy, dw, M, N, K, stream=None):
+def matmul_grad_w(x, dy, dw, M, N, K, workspace=None, stream=None):
+    """dw[N,K] += x[M,N]^T dy[M,K]."""
+    ws, nb = _gemm_ws(M, N, K, workspace, x.device)
     _check("pa_matmul_grad_w", load().pa_matmul_grad_w(_ptr(x), _ptr(dy), _ptr(dw), M, N, K,
+                                                       _ptr(ws), nb,
                                                        _stream() if stream is None else stream))
 
 

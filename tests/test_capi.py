@@ -71,8 +71,10 @@ def test_layer_norm_and_matmul_validation_without_gpu():
     assert lib.pa_layer_norm_fwd(16, 16, 16, 16, 16, 16, 0, 8, 1e-5, None) == 1
     assert lib.pa_layer_norm_fwd(16, 16, 16, 16, 16, 16, 4, 6, 1e-5, None) == 4
     assert lib.pa_layer_norm_bwd(16, 16, 16, 16, 16, 16, 16, 16, 4, 8, None, 0, None) == 7
-    assert lib.pa_matmul(16, 16, 16, 0, 4, 4, None) == 1
-    assert lib.pa_matmul_grad_x(None, 16, 16, 4, 4, 4, None) == 8
+    assert lib.pa_matmul(16, 16, 16, 0, 4, 4, None, 0, None) == 1
+    assert lib.pa_matmul_grad_x(None, 16, 16, 4, 4, 4, None, 0, None) == 8
+    assert lib.pa_matmul_grad_w(16, 16, 16, 4, 4, 4, None, 0, None) == 7   # no workspace
+    assert lib.pa_matmul_workspace_size(8192, 1536, 512) >= 4 * 8192 * 1536
     assert lib.pa_split_last_dim(16, None, 3, 4, 4, None) == 8
     arr = (ctypes.c_void_p * 9)(*([16] * 9))
     assert lib.pa_split_last_dim(16, arr, 9, 4, 4, None) == 1          # more than 8 parts
