@@ -167,6 +167,31 @@ int pa_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint3
 int pa_concat_last_dim_grad(const float* const* part_grads, float* grad_in, uint32_t parts,
                             uint32_t rows, uint32_t width, pa_stream_t stream);
 
+/* ---------------------------------------------------------------- training utilities
+ * Kernels behind the rest of the operator surface (ReLU, MSE, Adam, init).
+ * They sit off the attention path; gradient outputs are accumulated (+=). */
+
+/* y = max(x, 0). Replaces launch_ReLU_tiled (Launchers.cuh:34-40). */
+int pa_relu_fwd(const float* x, float* y, size_t n, pa_stream_t stream);
+/* dx += dy * (x > 0). Replaces launch_relu_backward (Launchers.cuh:99-105). */
+int pa_relu_bwd(const float* dy, const float* x, float* dx, size_t n, pa_stream_t stream);
+/* loss[0] = mean((pred - target)^2), deterministic. Replaces launch_mse_forward (Launchers.cuh:116-122). */
+int pa_mse_fwd(const float* pred, const float* target, float* loss, size_t n, pa_stream_t stream);
+/* dpred += 2/n * (pred - target) * dloss[0]. Replaces launch_mse_backward (Launchers.cuh:107-114). */
+int pa_mse_bwd(const float* pred, const float* target, const float* dloss, float* dpred, size_t n,
+               pa_stream_t stream);
+/* Adam update with host-computed bias corrections c1 = 1 - beta1^t, c2 = 1 - beta2^t.
+ * Replaces launch_adam_step (Launchers.cuh:124-137). */
+int pa_adam_step(float* param, const float* grad, float* m, float* v, size_t n, float lr,
+                 float beta1, float beta2, float eps, float bias_corr1, float bias_corr2,
+                 pa_stream_t stream);
+/* x[i] ~ N(0, std_dev^2) from a counter-based generator keyed by seed
+ * (reproducible). Replaces launch_normal_population (Launchers.cuh:56-62),
+ * which seeded from the clock. */
+int pa_fill_normal(float* x, size_t n, float std_dev, uint64_t seed, pa_stream_t stream);
+/* x[i] = value. */
+int pa_fill(float* x, size_t n, float value, pa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,7 @@ KERNEL_SOURCES = [
     "layernorm.cu",
     "elementwise.cu",
     "gemm.cu",
+    "training.cu",
     "capi.cu",
     "attn_bwd_noalloc.cu",
 ]
@@ -76,8 +77,46 @@ def build_kernels(force=False):
     return LIB
 
 
+HOST = os.path.join(HERE, "host")
+HOST_SOURCES = ["src/Tensor.cpp", "src/Autograd.cpp", "src/Functional.cpp", "src/Adam.cpp",
+                "src/layers.cpp", "bindings.cpp"]
+
+
+def build_host(force=False):
+    """Compile the C++ host layer + pybind11 bindings into PureAttention<ext>.so,
+    linked against libpa_kernels.so (found next to it at run time)."""
+    import pybind11
+    ext = sysconfig.get_config_var("EXT_SUFFIX")
+    out = os.path.join(HERE, "PureAttention" + ext)
+    srcs = [os.path.join(HOST, f) for f in HOST_SOURCES]
+    hdrs = []
+    for root, _, files in os.walk(HOST):
+        hdrs += [os.path.join(root, f) for f in files if f.endswith(".h")]
+    hdrs.append(os.path.join(REPO, "include", "pa_kernels.h"))
+    if not force and _newer(out, srcs + hdrs + [LIB]):
+        return out
+    os.makedirs(OBJ, exist_ok=True)
+    inc = ["-I" + os.path.join(HOST, "include"), "-I" + os.path.join(HOST, "src"),
+           "-I" + os.path.join(REPO, "include"), "-I/usr/local/cuda/include",
+           "-I" + pybind11.get_include(), "-I" + sysconfig.get_paths()["include"]]
+    flags = ["-O2", "-std=c++20", "-fPIC", "-Wall", "-fvisibility=hidden"]
+    objs = []
+    jobs = []
+    for src in srcs:
+        o = os.path.join(OBJ, "host_" + os.path.basename(src).replace(".cpp", ".o"))
+        objs.append(o)
+        jobs.append(["g++"] + flags + inc + ["-c", src, "-o", o])
+    with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
+        list(ex.map(_run, jobs))
+    _run(["g++", "-shared", "-o", out] + objs +
+         ["-L" + HERE, "-lpa_kernels", "-Wl,-rpath,$ORIGIN",
+          "-L/usr/local/cuda/lib64", "-lcudart_static", "-ldl", "-lrt", "-lpthread"])
+    return out
+
+
 def build_all(force=False):
     build_kernels(force)
+    build_host(force)
 
 
 if __name__ == "__main__":

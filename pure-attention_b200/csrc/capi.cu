@@ -256,3 +256,45 @@ int pa_concat_last_dim_grad(const float* const* part_grads, float* grad_in, uint
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ training utilities
+extern "C" {
+
+int pa_relu_fwd(const float* x, float* y, size_t n, pa_stream_t stream) {
+  if (!x || !y) return PA_ERR_NULL;
+  return n ? pa::launch_relu_fwd(x, y, n, static_cast<cudaStream_t>(stream)) : PA_OK;
+}
+int pa_relu_bwd(const float* dy, const float* x, float* dx, size_t n, pa_stream_t stream) {
+  if (!dy || !x || !dx) return PA_ERR_NULL;
+  return n ? pa::launch_relu_bwd(dy, x, dx, n, static_cast<cudaStream_t>(stream)) : PA_OK;
+}
+int pa_mse_fwd(const float* pred, const float* target, float* loss, size_t n, pa_stream_t stream) {
+  if (!pred || !target || !loss) return PA_ERR_NULL;
+  if (n == 0) return PA_ERR_SHAPE;
+  return pa::launch_mse_fwd(pred, target, loss, n, static_cast<cudaStream_t>(stream));
+}
+int pa_mse_bwd(const float* pred, const float* target, const float* dloss, float* dpred, size_t n,
+               pa_stream_t stream) {
+  if (!pred || !target || !dloss || !dpred) return PA_ERR_NULL;
+  if (n == 0) return PA_ERR_SHAPE;
+  return pa::launch_mse_bwd(pred, target, dloss, dpred, n, static_cast<cudaStream_t>(stream));
+}
+int pa_adam_step(float* param, const float* grad, float* m, float* v, size_t n, float lr,
+                 float beta1, float beta2, float eps, float bias_corr1, float bias_corr2,
+                 pa_stream_t stream) {
+  if (!param || !grad || !m || !v) return PA_ERR_NULL;
+  if (bias_corr1 <= 0.f || bias_corr2 <= 0.f) return PA_ERR_SHAPE;
+  return n ? pa::launch_adam(param, grad, m, v, n, lr, beta1, beta2, eps, bias_corr1, bias_corr2,
+                             static_cast<cudaStream_t>(stream))
+           : PA_OK;
+}
+int pa_fill_normal(float* x, size_t n, float std_dev, uint64_t seed, pa_stream_t stream) {
+  if (!x) return PA_ERR_NULL;
+  return n ? pa::launch_fill_normal(x, n, std_dev, seed, static_cast<cudaStream_t>(stream)) : PA_OK;
+}
+int pa_fill(float* x, size_t n, float value, pa_stream_t stream) {
+  if (!x) return PA_ERR_NULL;
+  return n ? pa::launch_fill(x, n, value, static_cast<cudaStream_t>(stream)) : PA_OK;
+}
+
+}  // extern "C"

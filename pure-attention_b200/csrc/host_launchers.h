@@ -63,4 +63,15 @@ int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, i
                     void* ws, uint32_t* status, cudaStream_t s);
 size_t gemm_workspace_bytes(int M, int N, int K);
 
+// training.cu
+int launch_relu_fwd(const float* x, float* y, size_t n, cudaStream_t s);
+int launch_relu_bwd(const float* dy, const float* x, float* dx, size_t n, cudaStream_t s);
+int launch_mse_fwd(const float* p, const float* t, float* loss, size_t n, cudaStream_t s);
+int launch_mse_bwd(const float* p, const float* t, const float* dl, float* dp, size_t n,
+                   cudaStream_t s);
+int launch_adam(float* w, const float* g, float* m, float* v, size_t n, float lr, float b1, float b2,
+                float eps, float c1, float c2, cudaStream_t s);
+int launch_fill_normal(float* x, size_t n, float std_dev, uint64_t seed, cudaStream_t s);
+int launch_fill(float* x, size_t n, float value, cudaStream_t s);
+
 }  // namespace pa

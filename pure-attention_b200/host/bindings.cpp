@@ -1,0 +1,129 @@
+// PureAttention Python module: the reference's surface (bindings.cpp:37-125)
+// over the B200 host layer. Names, signatures and defaults match; additions
+// are set_seed, device_status and Tensor.zero_grad.
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <numeric>
+
+#include "core/Adam.h"
+#include "core/Context.h"
+#include "core/Functional.h"
+#include "core/Tensor.h"
+#include "layers/LayerNorm.h"
+#include "layers/Linear.h"
+#include "layers/MHA.h"
+#include "layers/Module.h"
+#include "layers/ReLU.h"
+#include "loss/MSE.h"
+#include "pa_kernels.h"
+
+namespace py = pybind11;
+using core::Tensor;
+
+class PyModule : public layers::Module {
+ public:
+  using layers::Module::Module;
+  std::shared_ptr<Tensor> forward(const std::shared_ptr<Tensor>& input) override {
+    PYBIND11_OVERRIDE_PURE(std::shared_ptr<Tensor>, layers::Module, forward, input);
+  }
+  std::vector<std::shared_ptr<Tensor>> parameters() override {
+    PYBIND11_OVERRIDE(std::vector<std::shared_ptr<Tensor>>, layers::Module, parameters, );
+  }
+};
+
+PYBIND11_MODULE(PureAttention, m) {
+  m.doc() = "Pure-Attention operator surface over sm_100a kernels";
+
+  py::class_<Tensor, std::shared_ptr<Tensor>>(m, "Tensor")
+      .def(py::init([](std::vector<uint32_t> shape, bool requires_grad) {
+             return std::make_shared<Tensor>(shape, requires_grad);
+           }),
+           py::arg("shape"), py::arg("requires_grad") = false)
+      .def("backward", &Tensor::backward, py::arg("seed_with_ones") = true)
+      .def("to_host", &Tensor::to_host)
+      .def("to_device", &Tensor::to_device)
+      .def("grad_to_host", &Tensor::grad_to_host)
+      .def("shape", &Tensor::get_shape)
+      .def("zero_grad", &Tensor::zero_grad)
+      .def("get_grad_stats", [](const Tensor& t) {
+        const std::vector<float> g = t.grad_to_host();
+        py::dict d;
+        if (g.empty()) return d;
+        double s = 0.0, s2 = 0.0;
+        for (float v : g) {
+          s += v;
+          s2 += static_cast<double>(v) * v;
+        }
+        const double mean = s / g.size();
+        d["mean"] = mean;
+        d["std"] = std::sqrt(std::max(0.0, s2 / g.size() - mean * mean));
+        d["min"] = *std::min_element(g.begin(), g.end());
+        d["max"] = *std::max_element(g.begin(), g.end());
+        return d;
+      }, "Gradient stats");
+
+  py::class_<layers::Module, PyModule, std::shared_ptr<layers::Module>>(m, "Module")
+      .def(py::init<>())
+      .def("forward", &layers::Module::forward)
+      .def("parameters", &layers::Module::parameters);
+
+  py::class_<layers::Linear, layers::Module, std::shared_ptr<layers::Linear>>(m, "Linear")
+      .def(py::init<uint32_t, uint32_t>())
+      .def("forward", &layers::Linear::forward)
+      .def("parameters", &layers::Linear::parameters)
+      .def_readwrite("weight", &layers::Linear::weight)
+      .def_readwrite("bias", &layers::Linear::bias);
+
+  py::class_<layers::ReLU, layers::Module, std::shared_ptr<layers::ReLU>>(m, "ReLU")
+      .def(py::init<>())
+      .def("forward", &layers::ReLU::forward)
+      .def("parameters", &layers::ReLU::parameters);
+
+  py::class_<layers::MultiheadAttention, layers::Module, std::shared_ptr<layers::MultiheadAttention>>(
+      m, "MultiheadAttention")
+      .def(py::init<uint32_t, uint32_t>())
+      .def("forward", py::overload_cast<const std::shared_ptr<Tensor>&>(
+                          &layers::MultiheadAttention::forward))
+      .def("forward",
+           py::overload_cast<const std::shared_ptr<Tensor>&, const std::shared_ptr<Tensor>&,
+                             const std::shared_ptr<Tensor>&>(&layers::MultiheadAttention::forward))
+      .def("parameters", &layers::MultiheadAttention::parameters);
+
+  py::class_<layers::LayerNorm, layers::Module, std::shared_ptr<layers::LayerNorm>>(m, "LayerNorm")
+      .def(py::init<uint32_t, float>(), py::arg("normalized_shape"), py::arg("epsilon") = 1e-5f)
+      .def("forward", &layers::LayerNorm::forward)
+      .def("parameters", &layers::LayerNorm::parameters)
+      .def_property_readonly("gamma", &layers::LayerNorm::get_gamma)
+      .def_property_readonly("beta", &layers::LayerNorm::get_beta);
+
+  py::class_<loss::MSE, std::shared_ptr<loss::MSE>>(m, "MSE")
+      .def(py::init<>())
+      .def("forward", &loss::MSE::forward)
+      .def("__call__", &loss::MSE::forward);
+
+  py::class_<optim::Adam, std::shared_ptr<optim::Adam>>(m, "Adam")
+      .def(py::init<std::vector<std::shared_ptr<Tensor>>, float, float, float, float>(),
+           py::arg("params"), py::arg("lr") = 0.001f, py::arg("beta1") = 0.9f,
+           py::arg("beta2") = 0.999f, py::arg("eps") = 1e-8f)
+      .def("step", &optim::Adam::step)
+      .def("zero_grad", &optim::Adam::zero_grad);
+
+  m.def("fill_normal", [](const std::shared_ptr<Tensor>& t, float std_dev) {
+    core::pop_data_normal(t, std_dev, CudaContext::getStream());
+  }, "Fill tensor with normal distribution", py::arg("tensor"), py::arg("std_dev") = 1.0f);
+
+  m.def("add", [](const std::shared_ptr<Tensor>& a, const std::shared_ptr<Tensor>& b) {
+    std::shared_ptr<Tensor> c;
+    core::matadd(a, b, c, CudaContext::getStream());
+    return c;
+  }, "Element-wise addition (a [1, N] second operand is broadcast over rows)", py::arg("a"),
+        py::arg("b"));
+
+  m.def("set_seed", &CudaContext::setSeed, "Seed of fill_normal and layer initialisation",
+        py::arg("seed"));
+  m.def("device_status", []() { return pa_device_status(CudaContext::getStream(), 1); },
+        "Synchronise and return the kernels' status word (0 = ok)");
+}

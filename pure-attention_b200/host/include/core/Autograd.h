@@ -1,0 +1,97 @@
+// Graph nodes. Each node keeps the reference's public members
+// (include/core/Autograd.h:6-105) and computes the gradients of its inputs
+// from its output's gradient, accumulating into them. Unlike the reference,
+// apply_backward does not recurse into its inputs: Tensor::backward visits
+// the nodes in reverse topological order using inputs().
+#pragma once
+#include <memory>
+#include <vector>
+#include "core/Tensor.h"
+
+namespace core {
+
+struct Function {
+  virtual void apply_backward() = 0;
+  virtual std::vector<std::shared_ptr<Tensor>> inputs() const = 0;
+  virtual ~Function() = default;
+};
+
+struct MatMulFunction : public Function {
+  std::shared_ptr<Tensor> X_input;
+  std::shared_ptr<Tensor> W_input;
+  std::weak_ptr<Tensor> Y_output;
+  MatMulFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w, std::shared_ptr<Tensor> y);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {X_input, W_input}; }
+};
+
+// Bias add (bias of shape [1, N] broadcast over rows) or same-shape add.
+struct AddFunction : public Function {
+  std::shared_ptr<Tensor> X_input;
+  std::shared_ptr<Tensor> bias_input;
+  std::weak_ptr<Tensor> Y_output;
+  AddFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> bias, std::shared_ptr<Tensor> y);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {X_input, bias_input}; }
+};
+
+struct ReLUFunction : public Function {
+  std::shared_ptr<Tensor> Input;
+  std::weak_ptr<Tensor> Output;
+  ReLUFunction(std::shared_ptr<Tensor> in, std::shared_ptr<Tensor> out);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {Input}; }
+};
+
+struct MSEFunction : public Function {
+  std::shared_ptr<Tensor> predictions;
+  std::shared_ptr<Tensor> targets;
+  std::weak_ptr<Tensor> output_loss;
+  MSEFunction(const std::shared_ptr<Tensor>& preds, const std::shared_ptr<Tensor>& targs,
+              const std::shared_ptr<Tensor>& out);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {predictions}; }
+};
+
+struct SplitFunction : public Function {
+  std::shared_ptr<Tensor> Input;
+  std::vector<std::weak_ptr<Tensor>> Outputs;
+  SplitFunction(std::shared_ptr<Tensor> in, std::vector<std::shared_ptr<Tensor>> outs);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {Input}; }
+};
+
+struct FlashAttentionFunction : public Function {
+  std::shared_ptr<Tensor> Q_input;
+  std::shared_ptr<Tensor> K_input;
+  std::shared_ptr<Tensor> V_input;
+  std::weak_ptr<Tensor> O_output;
+  std::shared_ptr<Tensor> L_cache;
+  int num_heads;
+  FlashAttentionFunction(const std::shared_ptr<Tensor>& q, const std::shared_ptr<Tensor>& k,
+                         const std::shared_ptr<Tensor>& v, const std::shared_ptr<Tensor>& o,
+                         const std::shared_ptr<Tensor>& lcache, int heads);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override {
+    return {Q_input, K_input, V_input};
+  }
+};
+
+struct LayerNormFunction : public Function {
+  std::shared_ptr<Tensor> input;
+  std::shared_ptr<Tensor> gamma;
+  std::shared_ptr<Tensor> beta;
+  std::weak_ptr<Tensor> output;
+  std::shared_ptr<Tensor> mean;
+  std::shared_ptr<Tensor> rstd;
+  uint32_t M;
+  uint32_t N;
+  LayerNormFunction(const std::shared_ptr<Tensor>& inp, const std::shared_ptr<Tensor>& g,
+                    const std::shared_ptr<Tensor>& b, const std::shared_ptr<Tensor>& out,
+                    const std::shared_ptr<Tensor>& m, const std::shared_ptr<Tensor>& r,
+                    uint32_t m_size, uint32_t n_size);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {input, gamma, beta}; }
+};
+
+}  // namespace core

@@ -1,0 +1,56 @@
+// core::Tensor - fp32 device tensor with an optional gradient and a link to the
+// graph node that produced it. Same interface as the reference's
+// include/core/Tensor.h:22-53; storage is stream-ordered (cudaMallocAsync on
+// the context stream) and gradients start at zero.
+#pragma once
+#include <cstdint>
+#include <memory>
+#include <vector>
+
+namespace core {
+using float32_t = float;
+
+struct Function;
+
+class Tensor : public std::enable_shared_from_this<Tensor> {
+ public:
+  explicit Tensor(const std::vector<uint32_t>& shape, bool requires_gradient = false,
+                  bool is_leaf = true);
+  ~Tensor();
+  Tensor(const Tensor&) = delete;
+  Tensor& operator=(const Tensor&) = delete;
+
+  void to_device(const std::vector<float32_t>& host_data) const;
+  std::vector<float32_t> to_host() const;
+  std::vector<float32_t> grad_to_host() const;
+
+  std::vector<uint32_t> get_shape() const { return shape; }
+  float32_t* get_data_ptr() const { return data_ptr; }
+  size_t numel() const { return size; }
+
+  bool requires_grad() const { return requires_gradient; }
+  bool leaf() const { return is_leaf; }
+  float32_t* get_gradient_ptr() const { return gradient_ptr; }
+  void set_grad_fn(std::shared_ptr<Function> fn);
+  std::shared_ptr<Function> grad_fn() const { return grad_function; }
+  void zero_grad() const;
+
+  // Seeds this tensor's gradient with ones (or keeps the gradient already
+  // written there) and runs every graph node reachable from it once, in
+  // reverse topological order, so shared inputs receive the sum of all
+  // contributions before their own node runs.
+  void backward(bool seed_with_ones = true) const;
+
+ private:
+  float32_t* data_ptr = nullptr;
+  float32_t* gradient_ptr = nullptr;
+  std::vector<uint32_t> shape;
+  size_t size = 0;
+  bool requires_gradient = false;
+  bool is_leaf = true;
+  std::shared_ptr<Function> grad_function;
+};
+
+// Throws std::runtime_error("<what>: <status string>") for a non-zero pa_status.
+void check_status(int status, const char* what);
+}  // namespace core

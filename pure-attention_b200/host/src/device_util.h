@@ -1,0 +1,44 @@
+// Internal helpers of the host layer: status checks and stream-ordered scratch.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <stdexcept>
+#include <string>
+#include "core/Context.h"
+#include "core/Tensor.h"
+#include "pa_kernels.h"
+
+namespace core {
+
+// Stream-ordered device scratch (cudaMallocAsync / cudaFreeAsync on `s`).
+class Scratch {
+ public:
+  Scratch(size_t bytes, cudaStream_t s) : s_(s), n_(bytes) {
+    if (bytes) {
+      const cudaError_t e = cudaMallocAsync(&p_, bytes, s);
+      if (e != cudaSuccess)
+        throw std::runtime_error(std::string("CUDA Error: ") + cudaGetErrorString(e));
+    }
+  }
+  ~Scratch() {
+    if (p_) cudaFreeAsync(p_, s_);
+  }
+  Scratch(const Scratch&) = delete;
+  Scratch& operator=(const Scratch&) = delete;
+  void* get() const { return p_; }
+  size_t size() const { return n_; }
+
+ private:
+  void* p_ = nullptr;
+  cudaStream_t s_;
+  size_t n_;
+};
+
+inline pa_stream_t ps(cudaStream_t s) { return static_cast<pa_stream_t>(s); }
+
+inline size_t last_dim(const Tensor& t) {
+  const auto sh = t.get_shape();
+  return sh.empty() ? 1 : sh.back();
+}
+
+}  // namespace core

@@ -1,0 +1,109 @@
+// Layers and loss over core::Functional (reference: source/layers/*.cpp, source/loss/MSE.cpp).
+#include <cmath>
+
+#include "core/Functional.h"
+#include "device_util.h"
+#include "layers/LayerNorm.h"
+#include "layers/Linear.h"
+#include "layers/MHA.h"
+#include "layers/ReLU.h"
+#include "loss/MSE.h"
+
+namespace layers {
+
+namespace {
+cudaStream_t stream() { return CudaContext::getStream(); }
+std::shared_ptr<core::Tensor> param(std::vector<uint32_t> shape) {
+  return std::make_shared<core::Tensor>(shape, true);
+}
+}  // namespace
+
+// He-normal weights (std = sqrt(2 / fan_in)) and zero bias, as Linear.cpp:8-22.
+Linear::Linear(uint32_t in_channels, uint32_t out_channels)
+    : weight(param({in_channels, out_channels})), bias(param({1, out_channels})) {
+  core::pop_data_normal(weight, std::sqrt(2.0f / static_cast<float>(in_channels)), stream());
+  core::pop_data_zeros(bias, stream());
+}
+
+std::shared_ptr<core::Tensor> Linear::forward(const std::shared_ptr<core::Tensor>& input) {
+  std::shared_ptr<core::Tensor> xw, y;
+  core::matmul(input, weight, xw, stream());
+  core::matadd(xw, bias, y, stream());
+  return y;
+}
+
+std::vector<std::shared_ptr<core::Tensor>> Linear::parameters() { return {weight, bias}; }
+
+std::shared_ptr<core::Tensor> ReLU::forward(const std::shared_ptr<core::Tensor>& In) {
+  return core::relu(In, stream());
+}
+
+LayerNorm::LayerNorm(uint32_t n, float eps)
+    : gamma(param({1, n})), beta(param({1, n})), normalized_shape(n), epsilon(eps) {
+  core::check_status(pa_fill(gamma->get_data_ptr(), n, 1.0f, core::ps(stream())), "LayerNorm init");
+  core::pop_data_zeros(beta, stream());
+}
+
+std::shared_ptr<core::Tensor> LayerNorm::forward(const std::shared_ptr<core::Tensor>& input) {
+  return core::layer_norm(input, gamma, beta, epsilon, stream());
+}
+
+std::vector<std::shared_ptr<core::Tensor>> LayerNorm::parameters() { return {gamma, beta}; }
+
+// Same parameter shapes and He-normal init as MHA.cpp:10-28.
+MultiheadAttention::MultiheadAttention(uint32_t e, uint32_t h)
+    : in_proj_weight(param({e, 3 * e})),
+      in_proj_bias(param({1, 3 * e})),
+      out_proj_weight(param({e, e})),
+      out_proj_bias(param({1, e})),
+      embed_dim(e),
+      num_heads(h) {
+  const float std_dev = std::sqrt(2.0f / static_cast<float>(e));
+  core::pop_data_normal(in_proj_weight, std_dev, stream());
+  core::pop_data_zeros(in_proj_bias, stream());
+  core::pop_data_normal(out_proj_weight, std_dev, stream());
+  core::pop_data_zeros(out_proj_bias, stream());
+}
+
+std::shared_ptr<core::Tensor> MultiheadAttention::forward(const std::shared_ptr<core::Tensor>& x) {
+  std::shared_ptr<core::Tensor> xw, proj, attn, o1, out;
+  core::matmul(x, in_proj_weight, xw, stream());
+  core::matadd(xw, in_proj_bias, proj, stream());
+  std::vector<std::shared_ptr<core::Tensor>> qkv;
+  core::split(proj, 3, -1, qkv, stream());
+  core::flash_attention(qkv[0], qkv[1], qkv[2], attn, static_cast<int>(num_heads), stream());
+  core::matmul(attn, out_proj_weight, o1, stream());
+  core::matadd(o1, out_proj_bias, out, stream());
+  return out;
+}
+
+std::shared_ptr<core::Tensor> MultiheadAttention::forward(const std::shared_ptr<core::Tensor>& q,
+                                                          const std::shared_ptr<core::Tensor>& k,
+                                                          const std::shared_ptr<core::Tensor>& v) {
+  std::vector<std::shared_ptr<core::Tensor>> w, b;
+  core::split(in_proj_weight, 3, 1, w, stream());
+  core::split(in_proj_bias, 3, 1, b, stream());
+  std::shared_ptr<core::Tensor> t[3], p[3], attn, o1, out;
+  const std::shared_ptr<core::Tensor>* in[3] = {&q, &k, &v};
+  for (int i = 0; i < 3; ++i) {
+    core::matmul(*in[i], w[i], t[i], stream());
+    core::matadd(t[i], b[i], p[i], stream());
+  }
+  core::flash_attention(p[0], p[1], p[2], attn, static_cast<int>(num_heads), stream());
+  core::matmul(attn, out_proj_weight, o1, stream());
+  core::matadd(o1, out_proj_bias, out, stream());
+  return out;
+}
+
+std::vector<std::shared_ptr<core::Tensor>> MultiheadAttention::parameters() {
+  return {in_proj_weight, in_proj_bias, out_proj_weight, out_proj_bias};
+}
+
+}  // namespace layers
+
+namespace loss {
+std::shared_ptr<core::Tensor> MSE::forward(const std::shared_ptr<core::Tensor>& predictions,
+                                           const std::shared_ptr<core::Tensor>& targets) {
+  return core::mse_loss(predictions, targets, CudaContext::getStream());
+}
+}  // namespace loss

@@ -28,6 +28,8 @@ EXPORTS = [
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
+    "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_bwd", "pa_adam_step",
+    "pa_fill_normal", "pa_fill",
 ]
 
 
@@ -72,6 +74,13 @@ _SIGS = {
     "pa_bias_grad": (_int, [_vp] * 2 + [_int] * 2 + [_vp]),
     "pa_split_last_dim": (_int, [_vp, ctypes.POINTER(_vp), _u32, _u32, _u32, _vp]),
     "pa_concat_last_dim_grad": (_int, [ctypes.POINTER(_vp), _vp, _u32, _u32, _u32, _vp]),
+    "pa_relu_fwd": (_int, [_vp, _vp, _sz, _vp]),
+    "pa_relu_bwd": (_int, [_vp, _vp, _vp, _sz, _vp]),
+    "pa_mse_fwd": (_int, [_vp, _vp, _vp, _sz, _vp]),
+    "pa_mse_bwd": (_int, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "pa_adam_step": (_int, [_vp, _vp, _vp, _vp, _sz] + [_flt] * 6 + [_vp]),
+    "pa_fill_normal": (_int, [_vp, _sz, _flt, ctypes.c_uint64, _vp]),
+    "pa_fill": (_int, [_vp, _sz, _flt, _vp]),
 }
 
 _lib = None

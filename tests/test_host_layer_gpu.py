@@ -1,0 +1,168 @@
+"""The host operator layer (PureAttention module over the C ABI) against
+float64 references: Tensor round trips, the reverse-topological backward on
+a graph with fan-out, Linear / ReLU / MSE / Adam against torch float64, and
+the pre-LayerNorm multi-head-attention block (B=8, L=1024, E=512, H=8, fp32)
+forward + backward against the float64 oracle, every gradient within 1e-3."""
+import numpy as np
+import pytest
+
+from conftest import rel_err, seeded_normal
+
+torch = pytest.importorskip("torch")
+F32_TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def pa():
+    import PureAttention
+    PureAttention.set_seed(1234)
+    return PureAttention
+
+
+def _t(pa, x, requires_grad=False):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    t = pa.Tensor(list(x.shape), requires_grad)
+    t.to_device(x.ravel().tolist())
+    return t
+
+
+def _h(t):
+    return np.asarray(t.to_host(), dtype=np.float64).reshape(t.shape())
+
+
+def _g(t):
+    return np.asarray(t.grad_to_host(), dtype=np.float64).reshape(t.shape())
+
+
+@pytest.mark.gpu
+def test_tensor_round_trip_and_zero_grads(pa):
+    x = seeded_normal(1, (3, 5))
+    t = _t(pa, x, True)
+    np.testing.assert_array_equal(_h(t), x)
+    np.testing.assert_array_equal(_g(t), np.zeros((3, 5)))
+    with pytest.raises(Exception):
+        t.to_device([1.0])
+    with pytest.raises(RuntimeError):
+        pa.Tensor([2], False).backward()
+
+
+@pytest.mark.gpu
+def test_fan_out_gradients_accumulate_once(pa):
+    """y = x W;  z = y + y (same-shape add);  loss = mse(z, t). The shared y
+    must receive both contributions before its matmul node runs."""
+    x = seeded_normal(2, (64, 32))
+    t = seeded_normal(3, (64, 16))
+    lin = pa.Linear(32, 16)
+    w = _h(lin.weight)
+    X = _t(pa, x, True)
+    y = lin.forward(X)
+    z = pa.add(y, y)
+    loss = pa.MSE()(z, _t(pa, t))
+    loss.backward()
+    tx = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    tw = torch.tensor(w, dtype=torch.float64, requires_grad=True)
+    tb = torch.zeros(16, dtype=torch.float64, requires_grad=True)
+    ty = tx @ tw + tb
+    tl = torch.mean((ty + ty - torch.tensor(t, dtype=torch.float64)) ** 2)
+    tl.backward()
+    assert abs(_h(loss)[0] - tl.item()) < 1e-5 * abs(tl.item())
+    assert rel_err(_g(X), tx.grad.numpy()) < 1e-4
+    assert rel_err(_g(lin.weight), tw.grad.numpy()) < 1e-4
+    assert rel_err(_g(lin.bias).ravel(), tb.grad.numpy()) < 1e-4
+
+
+@pytest.mark.gpu
+def test_mlp_relu_mse_adam_matches_torch(pa):
+    x = seeded_normal(4, (128, 24))
+    t = seeded_normal(5, (128, 8))
+    l1, act, l2 = pa.Linear(24, 32), pa.ReLU(), pa.Linear(32, 8)
+    params = l1.parameters() + l2.parameters()
+    init = [_h(p) for p in params]
+    tp = [torch.tensor(v, dtype=torch.float64, requires_grad=True) for v in init]
+    opt = pa.Adam(params, lr=1e-2)
+    topt = torch.optim.Adam(tp, lr=1e-2, betas=(0.9, 0.999), eps=1e-8)
+    X, T = _t(pa, x), _t(pa, t)
+    tx, tt = torch.tensor(x, dtype=torch.float64), torch.tensor(t, dtype=torch.float64)
+    for _ in range(3):
+        opt.zero_grad()
+        loss = pa.MSE()(l2.forward(act.forward(l1.forward(X))), T)
+        loss.backward()
+        opt.step()
+        topt.zero_grad()
+        tl = torch.mean(((torch.relu(tx @ tp[0] + tp[1]) @ tp[2] + tp[3]) - tt) ** 2)
+        tl.backward()
+        topt.step()
+        assert abs(_h(loss)[0] - tl.item()) < 1e-4 * abs(tl.item())
+    for p, q in zip(params, tp):
+        assert rel_err(_h(p), q.detach().numpy()) < 1e-4
+
+
+def _xavier(seed, fan_in, fan_out, shape):
+    rng = np.random.default_rng(seed)
+    a = np.sqrt(6.0 / (fan_in + fan_out))
+    return rng.uniform(-a, a, size=shape).astype(np.float32)
+
+
+@pytest.mark.gpu
+def test_pre_ln_mha_block_matches_oracle(pa):
+    """One pre-LN multi-head-attention block (LN -> MHA(q=k=v) -> residual add
+    -> MSE), B=8, L=1024, E=512, H=8, fp32; gradients for X and all weights."""
+    import oracle
+    B, L, E, H = 8, 1024, 512, 8
+    D = E // H
+    M = B * L
+    x = seeded_normal(2, (B, L, E))
+    tgt = seeded_normal(3, (B, L, E))
+    w_in = _xavier(10, E, 3 * E, (E, 3 * E))
+    w_out = _xavier(11, E, E, (E, E))
+    ln = pa.LayerNorm(E)
+    mha = pa.MultiheadAttention(E, H)
+    in_w, in_b, out_w, out_b = mha.parameters()
+    in_w.to_device(w_in.ravel().tolist())
+    out_w.to_device(w_out.ravel().tolist())
+    X = _t(pa, x, True)
+    xn = ln.forward(X)
+    attn = mha.forward(xn, xn, xn)
+    out = pa.add(X, attn)
+    loss = pa.MSE()(out, _t(pa, tgt))
+    loss.backward()
+    assert pa.device_status() == 0
+
+    # float64 oracle of the same block
+    x2 = x.reshape(M, E).astype(np.float64)
+    g1, b1 = np.ones(E), np.zeros(E)
+    y1, mu, rs = oracle.layer_norm_fwd(x2, g1, b1)
+    qkv = y1 @ w_in.astype(np.float64)
+    q, k, v = (qkv[:, i * E:(i + 1) * E].reshape(B, L, H, D) for i in range(3))
+    o, lse = oracle.attn_fwd(q, k, v)
+    o2 = o.reshape(M, E)
+    a = o2 @ w_out.astype(np.float64)
+    res = x2 + a
+    n = res.size
+    ref_loss = np.mean((res - tgt.reshape(M, E)) ** 2)
+    dres = 2.0 / n * (res - tgt.reshape(M, E))
+    dw_out = o2.T @ dres
+    db_out = dres.sum(0)
+    do = (dres @ w_out.T.astype(np.float64)).reshape(B, L, H, D)
+    dq, dk, dv, _ = oracle.attn_bwd(q, k, v, o, do, lse)
+    dqkv = np.concatenate([g.reshape(M, E) for g in (dq, dk, dv)], axis=1)
+    dw_in = y1.T @ dqkv
+    db_in = dqkv.sum(0)
+    dy1 = dqkv @ w_in.T.astype(np.float64)
+    dx_ln, dg1, db1 = oracle.layer_norm_bwd(dy1, x2, mu, rs, g1)
+    dx = dres + dx_ln
+
+    assert abs(_h(loss)[0] - ref_loss) < 1e-4 * ref_loss
+    assert rel_err(_h(out).reshape(M, E), res) < 1e-5
+    errs = {
+        "dX": rel_err(_g(X).reshape(M, E), dx),
+        "d in_proj_weight": rel_err(_g(in_w), dw_in),
+        "d in_proj_bias": rel_err(_g(in_b).ravel(), db_in),
+        "d out_proj_weight": rel_err(_g(out_w), dw_out),
+        "d out_proj_bias": rel_err(_g(out_b).ravel(), db_out),
+        "d gamma": rel_err(_g(ln.gamma).ravel(), dg1),
+        "d beta": rel_err(_g(ln.beta).ravel(), db1),
+    }
+    print("pre-LN block relative errors:", errs)
+    for name, e in errs.items():
+        assert e < F32_TOL, (name, e)
