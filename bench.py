@@ -4,8 +4,11 @@ Workload: flash-attention forward + backward, bf16 inputs with fp32
 accumulation, non-causal, B=8 H=16 L=4096 d=64 per GPU (the headline shape).
 One step = pa_attn_fwd + pa_attn_bwd over one batch of seeded synthetic
 inputs. Multi-GPU runs shard along batch x heads with no collective on the data
-path: every rank owns its own B=8 x H=16 units (weak scaling), and `value` is
-the FLOPs of all ranks over the slowest rank's device time.
+path: by default every rank owns its own B=8 x H=16 units (weak scaling);
+--scaling strong splits the B=8 batches across ranks. `value` is the FLOPs of
+all ranks over the slowest rank's device time. `e2e` runs the same step
+through the C ABI from pinned host buffers (H2D of Q, K, V, dO and D2H of dQ,
+dK, dV every step), pipelined over three streams; the serial figure is kept.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -39,6 +42,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: B=8 x H=16 per GPU; strong: the B=8 batches split across GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -50,13 +55,6 @@ def peaks():
         return p["bf16_tflops"], p.get("bf16_tflops_sustained"), p["hbm_gbs"], "measured"
     except Exception:
         return 1590.0, 1400.0, 6650.0, "fallback"
-
-
-def dist_env():
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
 
 
 class ClockSampler:
@@ -125,10 +123,11 @@ def traffic_from_profile():
     return None
 
 
-def make_inputs(torch, seed, device):
+def make_host_inputs(torch, seed, b0, b1):
+    """Q, K, V, dO for batches [b0, b1): seeded N(0,1)*0.5, bf16, on the host."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     ts = [(torch.randn(B, L, H, D, generator=g) * 0.5).to(torch.bfloat16) for _ in range(4)]
-    return [t.to(device) for t in ts], ts
+    return [t[b0:b1].contiguous() for t in ts]
 
 
 def cpu_baseline(budget_s=12.0):
@@ -163,7 +162,8 @@ def cpu_baseline(budget_s=12.0):
 def run_reference_arm(args):
     """--impl reference: the multithreaded CPU implementation of the same
     fwd+bwd on the host cores (the reference's own path is CUDA-only)."""
-    rank, world, _ = dist_env()
+    import sharding
+    rank, world, _ = sharding.dist_env()
     if rank != 0:
         return 0
     import numpy as np
@@ -210,35 +210,51 @@ def main():
         return run_reference_arm(args)
     import torch
     import pa_capi
-    rank, world, local = dist_env()
+    import sharding
+    rank, world, local = sharding.dist_env()
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    pg = None
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-        pg = dist
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
     pa_capi.load()
     peak, peak_sus, hbm, peak_src = peaks()
     stream = torch.cuda.current_stream()
+    # Weak scaling: every rank owns B x H units. Strong: the B batches are split.
+    b0, b1 = (0, B) if args.scaling == "weak" else sharding.shard_batches(B, world, rank)
+    Bl = b1 - b0
+    flops_rank = 14 * Bl * H * L * L * D
+    flops_bwd = 10 * Bl * H * L * L * D
+    host = make_host_inputs(torch, sharding.rank_seed(1234, rank) if args.scaling == "weak" else 1234,
+                            b0, b1)
 
-    (q, k, v, g), host = make_inputs(torch, 1234 + rank, dev)
-    o = torch.empty_like(q)
-    lse = torch.empty(B * H, L, dtype=torch.float32, device=dev)
+    def alloc():
+        ins = [t.to(dev) for t in host]
+        o = torch.empty_like(ins[0])
+        lse = torch.empty(Bl * H, L, dtype=torch.float32, device=dev)
+        grads = [torch.empty_like(ins[0]) for _ in range(3)]
+        return ins, o, lse, grads
+
+    (q, k, v, g), o, lse, (dq, dk, dv) = alloc()
     desc = pa_capi.attn_desc(q)
     ws = torch.empty(pa_capi.attn_bwd_workspace_size(desc), dtype=torch.uint8, device=dev)
-    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
 
-    def step():
-        pa_capi.attn_fwd(q, k, v, o, lse, desc)
-        pa_capi.attn_bwd(q, k, v, o, g, lse, dq, dk, dv, ws, desc=desc)
+    def step(ins, o, lse, grads, s=None):
+        pa_capi.attn_fwd(ins[0], ins[1], ins[2], o, lse, desc, stream=s)
+        pa_capi.attn_bwd(ins[0], ins[1], ins[2], o, ins[3], lse, *grads, ws, desc=desc, stream=s)
 
     for _ in range(max(3, args.warmup)):
-        step()
+        step((q, k, v, g), o, lse, (dq, dk, dv))
     torch.cuda.synchronize()
     if pa_capi.device_status() != 0:
         raise SystemExit("device status reports a timed-out wait during warm-up")
@@ -246,8 +262,7 @@ def main():
     # ---------------- device-timed region: K steps, per-kernel events on the launch stream
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     clocks = ClockSampler(local)
-    if pg:
-        pg.barrier()
+    barrier()
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.25)
@@ -262,64 +277,96 @@ def main():
         ev[i][2].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
-    if pg:
-        pg.barrier()
-    elapsed_ms = t_begin.elapsed_time(t_end)
+    barrier()
+    elapsed_ms = sharding.max_over_ranks(t_begin.elapsed_time(t_end), dev)
     fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
     bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
-    if pg:
-        t = torch.tensor([elapsed_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
     status = pa_capi.device_status()
 
-    # ---------------- end to end through the C ABI with host buffers
+    # ---------------- end to end through the C ABI from pinned host buffers
     pinned = [t.pin_memory() for t in host]
-    outs_h = [torch.empty(B, L, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
-    e2e_steps = max(3, args.steps // 2)
+    outs_h = [[torch.empty(Bl, L, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+              for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in pinned)
+    d2h = sum(t.numel() * t.element_size() for t in outs_h[0])
+    e2e_steps = max(4, args.steps // 4)
 
-    def e2e_step():
+    # serial: copy in, compute, copy out, all on the compute stream
+    def serial_step():
         for src, dst in zip(pinned, (q, k, v, g)):
             dst.copy_(src, non_blocking=True)
-        step()
-        for src, dst in zip((dq, dk, dv), outs_h):
+        step((q, k, v, g), o, lse, (dq, dk, dv))
+        for src, dst in zip((dq, dk, dv), outs_h[0]):
             dst.copy_(src, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
+    serial_step()
     torch.cuda.synchronize()
-    if pg:
-        pg.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        serial_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    clk = clocks.stop()  # sampled across both timed regions
-    if pg:
-        t = torch.tensor([e2e_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    h2d = sum(t.numel() * t.element_size() for t in pinned)
-    d2h = sum(t.numel() * t.element_size() for t in outs_h)
+    serial_ms = sharding.max_over_ranks(e0.elapsed_time(e1), dev) / e2e_steps
+
+    # pipelined: H2D of step i+1 and D2H of step i-1 overlap step i's kernels
+    # (separate copy streams, two device buffer sets; PCIe copies both ways at once)
+    bufs = [((q, k, v, g), o, lse, (dq, dk, dv)), alloc()]
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
+
+    def pipelined(n, first_event=None, last_event=None):
+        for i in range(n):
+            bi = i % 2
+            ins, ob, lb, grads = bufs[bi]
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(comp_done[bi])
+                if i == 0 and first_event is not None:
+                    first_event.record(s_in)
+                for src, dst in zip(pinned, ins):
+                    dst.copy_(src, non_blocking=True)
+                h2d_done[bi].record(s_in)
+            stream.wait_event(h2d_done[bi])
+            if i >= 2:
+                stream.wait_event(d2h_done[bi])
+            step(ins, ob, lb, grads)
+            comp_done[bi].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done[bi])
+                for src, dst in zip(grads, outs_h[bi]):
+                    dst.copy_(src, non_blocking=True)
+                d2h_done[bi].record(s_out)
+        if last_event is not None:
+            last_event.record(s_out)
+
+    pipelined(2)
+    torch.cuda.synchronize()
+    barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pipelined(e2e_steps, p0, p1)
+    torch.cuda.synchronize()
+    e2e_ms = sharding.max_over_ranks(p0.elapsed_time(p1), dev)
+    clk = clocks.stop()  # sampled across the timed regions
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
 
-    if pg:
-        pg.barrier()
-        pg.destroy_process_group()
+    barrier()
+    if world > 1:
+        torch.distributed.destroy_process_group()
     if rank != 0:
         return 0
     ms_step = elapsed_ms / args.steps
-    value = world * FLOPS_STEP / (ms_step * 1e-3) / 1e12
+    total_flops = world * flops_rank if args.scaling == "weak" else FLOPS_STEP
+    value = total_flops / (ms_step * 1e-3) / 1e12
     per_gpu = value / world
-    e2e_val = world * FLOPS_STEP * e2e_steps / (e2e_ms * 1e-3) / 1e12
-    bwd_tflops = FLOPS_BWD / (bwd_ms * 1e-3) / 1e12
+    e2e_val = total_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    bwd_tflops = flops_bwd / (bwd_ms * 1e-3) / 1e12
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -329,13 +376,14 @@ def main():
         "warmup": max(3, args.warmup),
         "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1)*0.5 per rank)",
-        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": L, "heads": H,
-                   "head_dim": D, "parallelism": f"dp{world} (batch x head shards, no collective)",
-                   "l2": "inputs (4 x 64 MiB bf16) exceed the 126 MB L2; no flush"},
+        "data": "synthetic (seeded N(0,1)*0.5)",
+        "config": {"workload": WORKLOAD, "global_batch": B * world if args.scaling == "weak" else B,
+                   "seq_len": L, "heads": H, "head_dim": D,
+                   "parallelism": f"dp{world} (batch x head shards, no collective)",
+                   "l2": "inputs (4 x 64 MiB bf16 per 8 batches) exceed the 126 MB L2; no flush"},
         "per_gpu_tflops": round(per_gpu, 2),
         "frac_of_dense_peak": {"measured_bf16": round(per_gpu / peak, 4),
                                "datasheet_2250": round(per_gpu / 2250.0, 4)},
@@ -345,10 +393,12 @@ def main():
                      "achieved": round(bwd_tflops, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(bwd_tflops / peak, 4), "traffic": traffic_from_profile(),
                      "peak_source": f"{peak_src} burst bf16 (cuBLAS)",
-                     "algorithmic_flops_per_launch": FLOPS_BWD},
+                     "algorithmic_flops_per_launch": flops_bwd},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 4)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 4),
+                "mode": "pipelined: H2D / kernels / D2H on three streams, two buffer sets",
+                "serial_ms_per_step": round(serial_ms, 4)},
         "gpu_launches": 4 * args.steps,
         "clocks": clk,
         "device_status": status,
