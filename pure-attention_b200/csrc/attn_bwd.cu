@@ -63,13 +63,45 @@ struct BwdCfg {
 };
 
 // ---------------------------------------------------------------- prep
+// v ~= hi + mid + lo in bf16 (about 24 significant bits); packed (hi, mid), (lo, 0).
+__device__ __forceinline__ uint2 split3_bf16(float v) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+  const float r1 = v - __bfloat162float(hi);
+  const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+  return make_uint2(static_cast<uint32_t>(__bfloat16_as_ushort(hi)) |
+                        (static_cast<uint32_t>(__bfloat16_as_ushort(mid)) << 16),
+                    static_cast<uint32_t>(__bfloat16_as_ushort(lo)));
+}
+
+// Extension tile of the head-dim-64 backward: per (b*H + h, 128-query tile)
+// 4 KB = 128 query rows x 16 bf16 columns in the K-major no-swizzle
+// core-matrix layout (row r, column k at byte (r/8)*256 + (k/8)*128 +
+// (r%8)*16 + 2*(k%8)). Columns 0-2 hold -LSE/scale split in three bf16
+// parts, columns 8-10 -Delta likewise; the rest are zero. Against a tile of
+// ones in columns 0-2 (resp. 8-10) they add -LSE/scale to S (resp. -Delta to
+// dP) inside the S and dP MMAs. Padded query rows get -1e30 so their P is
+// exactly 0.
+constexpr int kExtTileBytes = 4096;
+__device__ __forceinline__ void write_ext_rows(uint8_t* ext, size_t bh, int Lp, int l, float q_val,
+                                               float do_val, bool pad) {
+  uint8_t* t = ext + (bh * (Lp / 128) + l / 128) * kExtTileBytes;
+  const int r = l % 128;
+  const int off = (r / 8) * 256 + (r % 8) * 16;
+  const uint2 q = pad ? make_uint2(static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(-1e30f))), 0u)
+                      : split3_bf16(q_val);
+  const uint2 d = split3_bf16(do_val);
+  *reinterpret_cast<uint4*>(t + off) = make_uint4(q.x, q.y, 0u, 0u);
+  *reinterpret_cast<uint4*>(t + off + 128) = make_uint4(d.x, d.y, 0u, 0u);
+}
+
 // G = D/8 threads per (b, l, h) row, each reading 8 values of dO and O.
 template <int D, typename InT>
 __global__ void __launch_bounds__(256)
     attn_bwd_prep_kernel(const InT* __restrict__ dO, const InT* __restrict__ O,
                          const float* __restrict__ lse, float* __restrict__ lse2_t,
-                         float* __restrict__ delta_t, float* __restrict__ delta_ref, int B, int L,
-                         int Lp, int H) {
+                         float* __restrict__ delta_t, float* __restrict__ delta_ref,
+                         uint8_t* __restrict__ ext, float inv_scale, int B, int L, int Lp, int H) {
   constexpr int G = D / 8;
   const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t rowi = gt / G;  // over B * Lp * H, ordered (b, l, h)
@@ -111,6 +143,9 @@ __global__ void __launch_bounds__(256)
     if (lse2_t) lse2_t[bh * Lp + l] = real ? lse[bh * L + l] * kLog2e : INFINITY;
     if (delta_t) delta_t[bh * Lp + l] = real ? acc : 0.f;
     if (delta_ref && real) delta_ref[(static_cast<size_t>(b) * L + l) * H + h] = acc;
+    if (ext)
+      write_ext_rows(ext, bh, Lp, l, real ? -lse[bh * L + l] * inv_scale : 0.f, real ? -acc : 0.f,
+                     !real);
   }
 }
 
@@ -532,6 +567,416 @@ __global__ void __launch_bounds__(512, 1)
   }
 }
 
+// ---------------------------------------------------------------- head dim 64 (bf16)
+// Schedule for d = 64 that keeps the tensor pipe fed from one TMEM budget:
+//   S [0,128) | dP [128,256) | P^T packed bf16 [256,320) | dV [320,384) | dK [384,448) | dQ [448,512)
+// -LSE/scale and -Delta enter the S and dP MMAs as one extra K-step
+// (an extension tile written by the prep kernel, against tiles of ones), so
+// S' = S - LSE/scale and dP' = dP - Delta come out of the tensor core and the
+// elementwise step needs no per-query loads: P = exp2(S' * scale * log2 e),
+// dS = P * dP'.
+// Each tile's elementwise work runs in two phases, each of which frees TMEM
+// for the next tile's MMAs as early as possible:
+//   P phase:  load S (s_free) -> P in registers -> P^T to TMEM (pt_full)
+//   dS phase: load dP (dp_free) -> dS = P * dP' to shared memory (p_full)
+// and the MMA issuer interleaves the two tiles on the tensor pipe:
+//   s_free(j)  -> S(j+1)      pt_full(j) -> dV(j)       dp_free(j) -> dP(j+1)
+//   p_full(j)  -> dK(j), dQ(j)
+// dS goes to shared memory only (dK reads it K-major, dQ MN-major, from a
+// double-buffered tile). Q and the extension tile are triple-buffered because
+// Q(j) is released only by dK(j); dO is double-buffered (released by dV(j)).
+// The dQ readout frees dQ's TMEM right after its tcgen05.ld and adds the tile
+// into the fp32 accumulator with 8-byte vector reductions straight from
+// registers (no shared memory: the MMAs already use all of its bandwidth).
+// It loads with the 16x256b shape, so four neighbouring lanes cover a whole
+// 32-byte sector of a dQ row and each warp-wide reduction writes 8 full
+// sectors.
+struct Bwd64Cfg {
+  static constexpr int EWG = 4;                        // elementwise warpgroups
+  static constexpr int QPG = 32;                       // queries per warpgroup
+  static constexpr int NEW = 128 * EWG;                // elementwise threads
+  static constexpr int THREADS = 32 * (8 + 4 * EWG);   // + producer, MMA, 2 idle, 4 readout warps
+  static constexpr int READOUT_WARP = 4 + 4 * EWG;
+  static constexpr int QSTAGES = 3;                    // Q + extension buffers
+  static constexpr int OSTAGES = 2;                    // dO buffers
+  static constexpr int CHUNK = 128 * 128;              // one SW128 tile: 128 rows x 128 B
+  static constexpr int KV_BYTES = 128 * 64 * 2;
+  static constexpr int QT_BYTES = 128 * 64 * 2;
+  static constexpr int EXT_BYTES = kExtTileBytes;      // 128 rows x 16 bf16
+  static constexpr int QSTAGE_BYTES = QT_BYTES + EXT_BYTES;
+  static constexpr int DS_BYTES = 2 * CHUNK;           // queries [0,64) and [64,128)
+  static constexpr int SMEM = 2 * KV_BYTES + 2 * EXT_BYTES + QSTAGES * QSTAGE_BYTES +
+                              OSTAGES * QT_BYTES + 2 * DS_BYTES + 1024;
+  static constexpr uint32_t T_S = 0, T_DP = 128, T_PT = 256, T_DV = 320, T_DK = 384, T_DQ = 448;
+};
+
+__global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
+    attn_bwd_d64_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                        const __grid_constant__ CUtensorMap mapV,
+                        const __grid_constant__ CUtensorMap mapdO, float* __restrict__ dq_acc,
+                        __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                        const uint8_t* __restrict__ ext, int L, int Lp, int H, float scale,
+                        float scale_log2, int accumulate, uint32_t* status) {
+  using C = Bwd64Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bars[24];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  if (cta_aborted(status, &abort_flag)) return;
+
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::KV_BYTES;
+  // tiles of ones in the extension layout: columns 0-2 (picks -LSE/scale) and
+  // columns 8-10 (picks -Delta)
+  uint8_t* sOnesS = sV + C::KV_BYTES;
+  uint8_t* sOnesP = sOnesS + C::EXT_BYTES;
+  uint8_t* sQ = sOnesP + C::EXT_BYTES;  // stage s: Q tile, then its extension tile
+  uint8_t* sO = sQ + C::QSTAGES * C::QSTAGE_BYTES;
+  uint8_t* sdS = sO + C::OSTAGES * C::QT_BYTES;
+  if (threadIdx.x < 256) {
+    const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const uint4 one3 = make_uint4(0x3f803f80u, 0x00003f80u, 0u, 0u);
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    const int off = (r / 8) * 256 + (r % 8) * 16 + half * 128;
+    *reinterpret_cast<uint4*>(sOnesS + off) = half ? zero : one3;
+    *reinterpret_cast<uint4*>(sOnesP + off) = half ? one3 : zero;
+    fence_proxy_async_smem();
+  }
+
+  const uint32_t kv_full = smem_u32(&bars[0]);
+  auto q_full = [&](int s) { return smem_u32(&bars[1 + s]); };
+  auto q_empty = [&](int s) { return smem_u32(&bars[4 + s]); };
+  auto o_full = [&](int s) { return smem_u32(&bars[18 + s]); };
+  auto o_empty = [&](int s) { return smem_u32(&bars[20 + s]); };
+  const uint32_t s_full = smem_u32(&bars[7]);    // S' of the tile is in TMEM
+  const uint32_t s_free = smem_u32(&bars[8]);    // elementwise warps have read S'
+  const uint32_t pt_full = smem_u32(&bars[9]);   // P^T is in TMEM
+  const uint32_t pt_free = smem_u32(&bars[10]);  // the dV MMA has read P^T
+  const uint32_t dp_full = smem_u32(&bars[11]);  // dP' of the tile is in TMEM
+  const uint32_t dp_free = smem_u32(&bars[12]);  // elementwise warps have read dP'
+  // dS of tile j is in shared memory. Two barriers, by tile parity: the
+  // elementwise warps can finish tile j+1 before the issuer has polled tile j.
+  auto p_full = [&](int j) { return smem_u32(&bars[(j & 1) ? 17 : 13]); };
+  const uint32_t dq_full = smem_u32(&bars[14]);
+  const uint32_t dq_empty = smem_u32(&bars[15]);
+  const uint32_t kv_done = smem_u32(&bars[16]);
+
+  const int warp = warp_id();
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int k0 = blockIdx.x * 128;
+  const int n_q = Lp / 128;
+  // Query tiles are visited from tile blockIdx.x onwards (mod n_q): the CTAs of
+  // one (batch, head) then reduce into different dQ rows at any moment instead
+  // of all into the same tile. jq(j) = query tile of iteration j.
+  const int q_first = blockIdx.x % n_q;
+  auto jq = [&](int j) { const int t = j + q_first; return t < n_q ? t : t - n_q; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::QSTAGES; ++s) {
+      mbar_init(q_full(s), 1);
+      mbar_init(q_empty(s), 1);
+    }
+    for (int s = 0; s < C::OSTAGES; ++s) {
+      mbar_init(o_full(s), 1);
+      mbar_init(o_empty(s), 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, C::NEW);
+    mbar_init(pt_full, C::NEW);
+    mbar_init(pt_free, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(dp_free, C::NEW);
+    mbar_init(p_full(0), C::NEW);
+    mbar_init(p_full(1), C::NEW);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(kv_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      tma_prefetch_desc(&mapQ);
+      tma_prefetch_desc(&mapdO);
+      mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
+      tma_load_4d(smem_u32(sK), &mapK, kv_full, 0, h, k0, b);
+      tma_load_4d(smem_u32(sV), &mapV, kv_full, 0, h, k0, b);
+      // buffers free up in the order dK(j-3) < dV(j-2) < dK(j-2) < ..., so the
+      // loads below are requested in the order they can be granted
+      for (int j = 0; j < n_q; ++j) {
+        const int s = j % C::QSTAGES, t = j % C::OSTAGES;
+        if (j >= C::QSTAGES && !mbar_wait(q_empty(s), ((j / C::QSTAGES) - 1) & 1, status)) break;
+        uint8_t* sq = sQ + s * C::QSTAGE_BYTES;
+        mbar_arrive_expect_tx(q_full(s), C::QT_BYTES + C::EXT_BYTES);
+        tma_load_4d(smem_u32(sq), &mapQ, q_full(s), 0, h, jq(j) * 128, b);
+        bulk_load(smem_u32(sq + C::QT_BYTES),
+                  ext + (static_cast<size_t>(bh) * n_q + jq(j)) * C::EXT_BYTES, C::EXT_BYTES,
+                  q_full(s));
+        if (j >= C::OSTAGES && !mbar_wait(o_empty(t), ((j / C::OSTAGES) - 1) & 1, status)) break;
+        mbar_arrive_expect_tx(o_full(t), C::QT_BYTES);
+        tma_load_4d(smem_u32(sO + t * C::QT_BYTES), &mapdO, o_full(t), 0, h, jq(j) * 128, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idSP = make_idesc(128, 128, 1, false, false);
+      constexpr uint32_t idKV = make_idesc(128, 64, 1, false, true);  // A K-major, B MN-major
+      constexpr uint32_t idQ = make_idesc(128, 64, 1, true, true);    // A and B MN-major
+      const uint64_t dK_K = make_sdesc(smem_u32(sK), 16, 1024);
+      const uint64_t dV_K = make_sdesc(smem_u32(sV), 16, 1024);
+      const uint64_t dK_MN = make_sdesc(smem_u32(sK), C::CHUNK, 1024);
+      const uint64_t dQ_K = make_sdesc(smem_u32(sQ), 16, 1024);
+      const uint64_t dQ_MN = make_sdesc(smem_u32(sQ), C::CHUNK, 1024);
+      const uint64_t dO_K = make_sdesc(smem_u32(sO), 16, 1024);
+      const uint64_t dO_MN = make_sdesc(smem_u32(sO), C::CHUNK, 1024);
+      const uint64_t dDS_K = make_sdesc(smem_u32(sdS), 16, 1024);         // dS^T, K-major
+      const uint64_t dDS_MN = make_sdesc(smem_u32(sdS), C::CHUNK, 1024);  // dS, MN-major
+      // extension tiles: K-major, no swizzle; K-halves 128 B apart, 8-row groups 256 B apart
+      const uint64_t dOnesS = make_sdesc(smem_u32(sOnesS), 128, 256, 0);
+      const uint64_t dOnesP = make_sdesc(smem_u32(sOnesP), 128, 256, 0);
+      const uint64_t dExt = make_sdesc(smem_u32(sQ + C::QT_BYTES), 128, 256, 0);
+      auto q_off = [&](int j) { return static_cast<uint32_t>(((j % C::QSTAGES) * C::QSTAGE_BYTES) >> 4); };
+      auto o_off = [&](int j) { return static_cast<uint32_t>(((j % C::OSTAGES) * C::QT_BYTES) >> 4); };
+      auto issue_S = [&](int j) {  // S'^T = K Q^T - LSE/scale
+        const uint32_t so = q_off(j);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16_ss(tmem + C::T_S, dK_K + ((k * 32) >> 4), dQ_K + so + ((k * 32) >> 4), idSP,
+                      k > 0 ? 1u : 0u);
+        umma_f16_ss(tmem + C::T_S, dOnesS, dExt + so, idSP, 1u);
+      };
+      auto issue_dP = [&](int j) {  // dP'^T = V dO^T - Delta
+        const uint32_t so = o_off(j);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16_ss(tmem + C::T_DP, dV_K + ((k * 32) >> 4), dO_K + so + ((k * 32) >> 4), idSP,
+                      k > 0 ? 1u : 0u);
+        umma_f16_ss(tmem + C::T_DP, dOnesP, dExt + q_off(j), idSP, 1u);
+      };
+      auto issue_dV = [&](int j) {  // dV += P^T dO  (P^T from TMEM)
+        const uint32_t so = o_off(j);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(tmem + C::T_DV, tmem + C::T_PT + 8 * k, dO_MN + so + ((k * 2048) >> 4), idKV,
+                      (j > 0 || k > 0) ? 1u : 0u);
+      };
+      auto issue_dK = [&](int j) {  // dK += dS^T Q
+        const uint32_t so = q_off(j);
+        const uint32_t bo = ((j & 1) * C::DS_BYTES) >> 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ss(tmem + C::T_DK, dDS_K + bo + (((k / 4) * C::CHUNK + (k % 4) * 32) >> 4),
+                      dQ_MN + so + ((k * 2048) >> 4), idKV, (j > 0 || k > 0) ? 1u : 0u);
+      };
+      auto issue_dQ = [&](int j) {  // dQ = dS K
+        const uint32_t bo = ((j & 1) * C::DS_BYTES) >> 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ss(tmem + C::T_DQ, dDS_MN + bo + ((k * 2048) >> 4), dK_MN + ((k * 2048) >> 4), idQ,
+                      k > 0 ? 1u : 0u);
+      };
+      bool ok = mbar_wait(kv_full, 0, status) && mbar_wait(q_full(0), 0, status) &&
+                mbar_wait(o_full(0), 0, status);
+      if (ok) {
+        tc_fence_after();
+        issue_S(0);
+        umma_commit(s_full);
+        issue_dP(0);
+        umma_commit(dp_full);
+      }
+      for (int j = 0; ok && j < n_q; ++j) {
+        const bool more = j + 1 < n_q;
+        if (!(ok = mbar_wait(s_free, j & 1, status))) break;
+        if (more) {
+          if (!(ok = mbar_wait(q_full((j + 1) % C::QSTAGES), ((j + 1) / C::QSTAGES) & 1, status)))
+            break;
+          tc_fence_after();
+          issue_S(j + 1);
+          umma_commit(s_full);
+        }
+        if (!(ok = mbar_wait(pt_full, j & 1, status))) break;
+        tc_fence_after();
+        issue_dV(j);
+        umma_commit(pt_free);
+        umma_commit(o_empty(j % C::OSTAGES));
+        if (!(ok = mbar_wait(dp_free, j & 1, status))) break;
+        if (more) {
+          if (!(ok = mbar_wait(o_full((j + 1) % C::OSTAGES), ((j + 1) / C::OSTAGES) & 1, status)))
+            break;
+          tc_fence_after();
+          issue_dP(j + 1);
+          umma_commit(dp_full);
+        }
+        if (!(ok = mbar_wait(p_full(j), (j >> 1) & 1, status))) break;
+        tc_fence_after();
+        issue_dK(j);
+        umma_commit(q_empty(j % C::QSTAGES));
+        if (j > 0) {
+          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
+          tc_fence_after();
+        }
+        issue_dQ(j);
+        umma_commit(dq_full);
+      }
+      if (ok) umma_commit(kv_done);
+    }
+  } else if (warp >= 4 && warp < C::READOUT_WARP) {
+    // ------------------------------------------------------------ P / dS
+    // Warpgroup grp: queries [32 grp, 32 grp + 32) of each tile; thread = key row.
+    const int grp = (warp - 4) >> 2;
+    const int kr = ((warp & 3) << 5) + static_cast<int>(lane_id());  // key row == TMEM lane
+    const int key = k0 + kr;
+    const bool valid = key < L;
+    const bool full_tile = k0 + 128 <= L;  // CTA-uniform: no key masking needed
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + C::T_S + lane_base + grp * C::QPG;
+    const uint32_t tdP = tmem + C::T_DP + lane_base + grp * C::QPG;
+    const uint32_t tPT = tmem + C::T_PT + lane_base + grp * C::QPG / 2;
+    // this group's 32 queries: 64 bytes of a key row in dS chunk grp / 2, from byte 64 (grp % 2)
+    const int dsb0 = 64 * (grp & 1);
+    bool ok = true;
+    for (int j = 0; j < n_q; ++j) {
+      // P phase
+      if (!(ok = mbar_wait_warp(s_full, j & 1, status))) break;
+      tc_fence_after();
+      uint32_t va[16], vb[16];
+      tmem_ld16(tS, va);
+      tmem_ld16(tS + 16, vb);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(s_free);
+      float p[32];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        p[e] = ex2(__uint_as_float(va[e]) * scale_log2);
+        p[16 + e] = ex2(__uint_as_float(vb[e]) * scale_log2);
+      }
+      if (!full_tile && !valid) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) p[e] = 0.f;
+      }
+      uint32_t pk0[8], pk1[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        pk0[i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
+        pk1[i] = pack_bf16x2(p[16 + 2 * i], p[16 + 2 * i + 1]);
+      }
+      if (j > 0) {  // P^T columns are free once the previous tile's dV MMA has read them
+        if (!(ok = mbar_wait_warp(pt_free, (j - 1) & 1, status))) break;
+        tc_fence_after();
+      }
+      PA_TMEM_ST_X8(tPT, pk0);
+      PA_TMEM_ST_X8(tPT + 8, pk1);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(pt_full);
+      // dS phase
+      if (!(ok = mbar_wait_warp(dp_full, j & 1, status))) break;
+      tc_fence_after();
+      tmem_ld16(tdP, va);
+      tmem_ld16(tdP + 16, vb);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dp_free);
+      uint32_t ds[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ds[i] = pack_bf16x2(p[2 * i] * __uint_as_float(va[2 * i]),
+                            p[2 * i + 1] * __uint_as_float(va[2 * i + 1]));
+        ds[8 + i] = pack_bf16x2(p[16 + 2 * i] * __uint_as_float(vb[2 * i]),
+                                p[16 + 2 * i + 1] * __uint_as_float(vb[2 * i + 1]));
+      }
+      uint8_t* dsrow = sdS + (j & 1) * C::DS_BYTES + (grp >> 1) * C::CHUNK;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, dsb0 + 16 * u)) =
+            make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full(j));
+    }
+    // dV and dK (x scale) epilogue: groups 0, 1 write dV columns [0,32), [32,64);
+    // groups 2, 3 the same columns of dK.
+    if (ok && mbar_wait_warp(kv_done, 0, status)) {
+      tc_fence_after();
+      const bool is_dv = grp < 2;
+      const int c = grp & 1;
+      uint32_t o[32];
+      tmem_ld32(tmem + (is_dv ? C::T_DV : C::T_DK) + lane_base + c * 32, o);
+      tmem_ld_wait();
+      if (valid) {
+        const float mul = is_dv ? 1.f : scale;
+        __nv_bfloat16* dst =
+            (is_dv ? dv : dk) + ((static_cast<size_t>(b) * L + key) * H + h) * 64 + c * 32;
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * u + e]) * mul;
+          if (accumulate) {
+            const uint4 prev = d4[u];
+            const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&prev);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 pf = __bfloat1622float2(p2[e]);
+              f[2 * e] += pf.x;
+              f[2 * e + 1] += pf.y;
+            }
+          }
+          d4[u] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                             pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+        }
+      }
+    }
+  } else if (warp >= C::READOUT_WARP) {
+    // ------------------------------------------------------------ dQ readout
+    const int lane = static_cast<int>(lane_id());
+    const int wl = (warp & 3) * 32;  // this warp's TMEM lanes (query rows) wl .. wl+31
+    const uint32_t tdQ = tmem + C::T_DQ + (static_cast<uint32_t>(wl) << 16);
+    for (int j = 0; j < n_q; ++j) {
+      if (!mbar_wait_warp(dq_full, j & 1, status)) break;
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      tmem_ld_16x256b_x8(tdQ, r0);                  // rows wl .. wl+15
+      tmem_ld_16x256b_x8(tdQ + (16u << 16), r1);    // rows wl+16 .. wl+31
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dq_empty);  // dQ's TMEM columns are free for the next tile
+      float* base = dq_acc + (static_cast<size_t>(bh) * Lp + jq(j) * 128 + wl + (lane >> 2)) * 64 +
+                    2 * (lane & 3);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          red_add_v2_f32(base + (8 * a) * 64 + 8 * i, __uint_as_float(r0[4 * i + 2 * a]),
+                         __uint_as_float(r0[4 * i + 2 * a + 1]));
+          red_add_v2_f32(base + (16 + 8 * a) * 64 + 8 * i, __uint_as_float(r1[4 * i + 2 * a]),
+                         __uint_as_float(r1[4 * i + 2 * a + 1]));
+        }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------- dQ convert
 // dq[b, l, h, :] (=|+=) scale * dq_acc[b*H + h, l, :]; 8 values per thread.
 // D = row width of dq_acc; d_out (<= D, multiple of 8) = head dim of dq.
@@ -584,33 +1029,36 @@ __global__ void __launch_bounds__(256)
 namespace {
 size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// LSE2 [B*H, Lp], Delta [B*H, Lp], fp32 dQ accumulator [B*H*Lp, Dacc].
-size_t stats_bytes(const AttnShape& sh, int Dacc) {
+// LSE2 [B*H, Lp], Delta [B*H, Lp], fp32 dQ accumulator [B*H*Lp, Dacc], and
+// with `ext` the extension tiles [B*H, Lp/128, 8 KB] of the head-dim-64 kernel.
+size_t stats_bytes(const AttnShape& sh, int Dacc, bool ext = false) {
   const size_t Lp = static_cast<size_t>((sh.L + 127) / 128) * 128;
   const size_t bh = static_cast<size_t>(sh.B) * sh.H;
-  return up256(bh * Lp * 4) * 2 + up256(bh * Lp * Dacc * 4);
+  return up256(bh * Lp * 4) * 2 + up256(bh * Lp * Dacc * 4) +
+         (ext ? bh * (Lp / 128) * kExtTileBytes : 0);
 }
 
 // Delta (and LSE2) prep over rows of `Dreal` values of type InT.
 template <int Dreal, typename InT>
 int launch_prep(const AttnShape& sh, const void* dO, const void* o, const float* lse, float* lse2,
-                float* delta_t, float* delta_ref, int Lp, cudaStream_t stream) {
+                float* delta_t, float* delta_ref, uint8_t* ext, int Lp, cudaStream_t stream) {
   const size_t rows = static_cast<size_t>(sh.B) * Lp * sh.H;
   const size_t threads = rows * (Dreal / 8);
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
   attn_bwd_prep_kernel<Dreal, InT><<<blocks, 256, 0, stream>>>(
-      static_cast<const InT*>(dO), static_cast<const InT*>(o), lse, lse2, delta_t, delta_ref, sh.B,
-      sh.L, Lp, sh.H);
+      static_cast<const InT*>(dO), static_cast<const InT*>(o), lse, lse2, delta_t, delta_ref, ext,
+      1.f / sh.scale, sh.B, sh.L, Lp, sh.H);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
 template <typename InT>
 int prep_any(int Dreal, const AttnShape& sh, const void* dO, const void* o, const float* lse,
-             float* lse2, float* delta_t, float* delta_ref, int Lp, cudaStream_t stream) {
+             float* lse2, float* delta_t, float* delta_ref, int Lp, cudaStream_t stream,
+             uint8_t* ext = nullptr) {
   switch (Dreal) {
-    case 32: return launch_prep<32, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, Lp, stream);
-    case 64: return launch_prep<64, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, Lp, stream);
-    case 128: return launch_prep<128, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, Lp, stream);
+    case 32: return launch_prep<32, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, Lp, stream);
+    case 64: return launch_prep<64, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, Lp, stream);
+    case 128: return launch_prep<128, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, Lp, stream);
     default: return PA_ERR_UNSUPPORTED;
   }
 }
@@ -637,16 +1085,29 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
     return PA_ERR_ALIGN;
   if (cudaMemsetAsync(dq_acc, 0, bh * Lp * D * sizeof(float), stream) != cudaSuccess)
     return PA_ERR_LAUNCH;
-  int st = prep_any<T>(sh.D, sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream);
+  constexpr bool kD64 = D == 64 && !SPLIT;
+  uint8_t* ext = kD64 ? stats + 2 * up256(bh * Lp * 4) + up256(bh * Lp * D * 4) : nullptr;
+  int st = kD64 ? prep_any<T>(sh.D, sh, dO, o, lse, nullptr, nullptr, nullptr, Lp, stream, ext)
+                : prep_any<T>(sh.D, sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream);
   if (st != PA_OK) return st;
 
-  static uint64_t attr = 0;
-  ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr);
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
-  attn_bwd_kernel<D, SPLIT, T><<<grid, 512, C::SMEM, stream>>>(
-      m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], mdq, static_cast<T*>(dk),
-      static_cast<T*>(dv), lse2, delta_t, sh.L, Lp, sh.H, sh.D, sh.scale, sh.scale * kLog2e,
-      accumulate, status);
+  if constexpr (D == 64 && !SPLIT) {
+    using C64 = Bwd64Cfg;
+    static uint64_t attr64 = 0;
+    ensure_smem_attr(attn_bwd_d64_kernel, C64::SMEM, attr64);
+    attn_bwd_d64_kernel<<<grid, C64::THREADS, C64::SMEM, stream>>>(
+        m[0], m[1], m[2], m[3], dq_acc, static_cast<__nv_bfloat16*>(dk),
+        static_cast<__nv_bfloat16*>(dv), ext, sh.L, Lp, sh.H, sh.scale, sh.scale * kLog2e,
+        accumulate, status);
+  } else {
+    static uint64_t attr = 0;
+    ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr);
+    attn_bwd_kernel<D, SPLIT, T><<<grid, 512, C::SMEM, stream>>>(
+        m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], mdq, static_cast<T*>(dk),
+        static_cast<T*>(dv), lse2, delta_t, sh.L, Lp, sh.H, sh.D, sh.scale, sh.scale * kLog2e,
+        accumulate, status);
+  }
   if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
 
   const size_t threads = static_cast<size_t>(sh.B) * sh.L * sh.H * (sh.D / 8);
@@ -656,7 +1117,7 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
 }
 }  // namespace
 
-size_t attn_bwd_workspace_bytes(const AttnShape& sh) { return stats_bytes(sh, sh.D); }
+size_t attn_bwd_workspace_bytes(const AttnShape& sh) { return stats_bytes(sh, sh.D, sh.D == 64); }
 
 int launch_attn_delta_bf16(const AttnShape& sh, const void* dO, const void* o, float* delta,
                            cudaStream_t stream) {
