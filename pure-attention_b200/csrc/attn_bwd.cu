@@ -585,18 +585,22 @@ __global__ void __launch_bounds__(512, 1)
 // dS goes to shared memory only (dK reads it K-major, dQ MN-major, from a
 // double-buffered tile). Q and the extension tile are triple-buffered because
 // Q(j) is released only by dK(j); dO is double-buffered (released by dV(j)).
-// The dQ readout frees dQ's TMEM right after its tcgen05.ld and adds the tile
-// into the fp32 accumulator with 8-byte vector reductions straight from
-// registers (no shared memory: the MMAs already use all of its bandwidth).
-// It loads with the 16x256b shape, so four neighbouring lanes cover a whole
-// 32-byte sector of a dQ row and each warp-wide reduction writes 8 full
-// sectors.
+// The dQ readout frees dQ's TMEM right after its tcgen05.ld (16x256b shape:
+// four neighbouring lanes hold a whole 32-byte sector of a dQ row). The two
+// CTAs of a cluster (neighbouring key tiles, same query order) then swap
+// halves of their dQ tiles through distributed shared memory: each sends the
+// 32 columns its partner owns into the partner's 16 KB receive buffer, adds
+// the partner's contribution to its own 32 columns, and reduces only those
+// into the fp32 accumulator (8-byte vector reductions straight from
+// registers). Global reduction traffic is halved; the L2 reduction rate,
+// not the tensor pipe, bounds this kernel without it.
 struct Bwd64Cfg {
   static constexpr int EWG = 4;                        // elementwise warpgroups
   static constexpr int QPG = 32;                       // queries per warpgroup
   static constexpr int NEW = 128 * EWG;                // elementwise threads
-  static constexpr int THREADS = 32 * (8 + 4 * EWG);   // + producer, MMA, 2 idle, 4 readout warps
-  static constexpr int READOUT_WARP = 4 + 4 * EWG;
+  static constexpr int EW_WARP = 2;                    // warps 0, 1: producer, MMA issuer
+  static constexpr int READOUT_WARP = EW_WARP + 4 * EWG;
+  static constexpr int THREADS = 32 * (READOUT_WARP + 4);  // + 4 dQ readout warps
   static constexpr int QSTAGES = 3;                    // Q + extension buffers
   static constexpr int OSTAGES = 2;                    // dO buffers
   static constexpr int CHUNK = 128 * 128;              // one SW128 tile: 128 rows x 128 B
@@ -605,12 +609,52 @@ struct Bwd64Cfg {
   static constexpr int EXT_BYTES = kExtTileBytes;      // 128 rows x 16 bf16
   static constexpr int QSTAGE_BYTES = QT_BYTES + EXT_BYTES;
   static constexpr int DS_BYTES = 2 * CHUNK;           // queries [0,64) and [64,128)
+  static constexpr int RX_BYTES = 128 * 32 * 4;        // partner's half of a dQ tile
   static constexpr int SMEM = 2 * KV_BYTES + 2 * EXT_BYTES + QSTAGES * QSTAGE_BYTES +
-                              OSTAGES * QT_BYTES + 2 * DS_BYTES + 1024;
+                              OSTAGES * QT_BYTES + 2 * DS_BYTES + RX_BYTES + 1024;
   static constexpr uint32_t T_S = 0, T_DP = 128, T_PT = 256, T_DV = 320, T_DK = 384, T_DQ = 448;
 };
 
-__global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
+// dQ half exchange of the readout. A 16x256b load of 16 rows gives thread t
+// r[4i + 2a + q] = (row t/4 + 8a, column 8i + 2(t%4) + q). CTA rank OWN
+// reduces column blocks i in [4 OWN, 4 OWN + 4): dq_split sends the other
+// four blocks to the partner's receive buffer (slots v0 .. v0+3; slot v of
+// thread t at byte v * 2048 + t * 16) with st.async, which completes bytes of
+// the partner's rx_full barrier, and keeps its own four in `own`.
+template <int OWN>
+__device__ __forceinline__ void dq_split(const uint32_t (&r)[32], uint32_t (&own)[16],
+                                         uint32_t peer_slot, uint32_t peer_bar, int v0) {
+  constexpr int OTHER = 1 - OWN;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const int i = 4 * OTHER + v;
+    st_async_v4(peer_slot + (v0 + v) * 2048, make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]),
+                peer_bar);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) own[4 * v + e] = r[4 * (4 * OWN + v) + e];
+  }
+}
+__device__ __forceinline__ void dq_add_slots(uint32_t (&own)[16], const uint8_t* rx_slot, int v0) {
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const uint4 p = *reinterpret_cast<const uint4*>(rx_slot + (v0 + v) * 2048);
+    own[4 * v] = __float_as_uint(__uint_as_float(own[4 * v]) + __uint_as_float(p.x));
+    own[4 * v + 1] = __float_as_uint(__uint_as_float(own[4 * v + 1]) + __uint_as_float(p.y));
+    own[4 * v + 2] = __float_as_uint(__uint_as_float(own[4 * v + 2]) + __uint_as_float(p.z));
+    own[4 * v + 3] = __float_as_uint(__uint_as_float(own[4 * v + 3]) + __uint_as_float(p.w));
+  }
+}
+// row = accumulator element (row t/4 of a 16-row group, column 8 * 4 OWN + 2(t%4))
+__device__ __forceinline__ void dq_reduce_own(const uint32_t (&own)[16], float* row) {
+#pragma unroll
+  for (int v = 0; v < 4; ++v)
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+      red_add_v2_f32(row + (8 * a) * 64 + 8 * v, __uint_as_float(own[4 * v + 2 * a]),
+                     __uint_as_float(own[4 * v + 2 * a + 1]));
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1)
     attn_bwd_d64_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                         const __grid_constant__ CUtensorMap mapV,
                         const __grid_constant__ CUtensorMap mapdO, float* __restrict__ dq_acc,
@@ -622,7 +666,8 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
   __shared__ uint64_t bars[24];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
-  if (cta_aborted(status, &abort_flag)) return;
+  // No early return: both CTAs of the cluster must reach the cluster barriers.
+  const bool skip = cta_aborted(status, &abort_flag);
 
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sK = smem;
@@ -634,6 +679,7 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
   uint8_t* sQ = sOnesP + C::EXT_BYTES;  // stage s: Q tile, then its extension tile
   uint8_t* sO = sQ + C::QSTAGES * C::QSTAGE_BYTES;
   uint8_t* sdS = sO + C::OSTAGES * C::QT_BYTES;
+  uint8_t* sRX = sdS + 2 * C::DS_BYTES;  // partner's half of the current dQ tile
   if (threadIdx.x < 256) {
     const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
     const uint4 one3 = make_uint4(0x3f803f80u, 0x00003f80u, 0u, 0u);
@@ -661,6 +707,8 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
   const uint32_t dq_full = smem_u32(&bars[14]);
   const uint32_t dq_empty = smem_u32(&bars[15]);
   const uint32_t kv_done = smem_u32(&bars[16]);
+  const uint32_t rx_full = smem_u32(&bars[22]);  // partner's dQ half is in sRX (16 KB of st.async)
+  const uint32_t tx_free = smem_u32(&bars[23]);  // partner has read what this CTA sent
 
   const int warp = warp_id();
   const int bh = blockIdx.y;
@@ -670,7 +718,7 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
   // Query tiles are visited from tile blockIdx.x onwards (mod n_q): the CTAs of
   // one (batch, head) then reduce into different dQ rows at any moment instead
   // of all into the same tile. jq(j) = query tile of iteration j.
-  const int q_first = blockIdx.x % n_q;
+  const int q_first = (blockIdx.x >> 1) % n_q;  // same order in both CTAs of a cluster
   auto jq = [&](int j) { const int t = j + q_first; return t < n_q ? t : t - n_q; };
 
   if (threadIdx.x == 0) {
@@ -694,6 +742,8 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(kv_done, 1);
+    mbar_init(rx_full, 1);
+    mbar_init(tx_free, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -703,9 +753,11 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  cluster_sync();  // the partner's barriers are initialised before any remote arrive
   const uint32_t tmem = tmem_slot;
 
-  if (warp == 0) {
+  if (skip) {
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
       tma_prefetch_desc(&mapQ);
@@ -833,10 +885,11 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
       }
       if (ok) umma_commit(kv_done);
     }
-  } else if (warp >= 4 && warp < C::READOUT_WARP) {
+  } else if (warp >= C::EW_WARP && warp < C::READOUT_WARP) {
     // ------------------------------------------------------------ P / dS
-    // Warpgroup grp: queries [32 grp, 32 grp + 32) of each tile; thread = key row.
-    const int grp = (warp - 4) >> 2;
+    // Warpgroup grp (four consecutive warps, one per TMEM lane quarter warp & 3):
+    // queries [32 grp, 32 grp + 32) of each tile; thread = key row.
+    const int grp = (warp - C::EW_WARP) >> 2;
     const int kr = ((warp & 3) << 5) + static_cast<int>(lane_id());  // key row == TMEM lane
     const int key = k0 + kr;
     const bool valid = key < L;
@@ -944,33 +997,52 @@ __global__ void __launch_bounds__(Bwd64Cfg::THREADS, 1)
   } else if (warp >= C::READOUT_WARP) {
     // ------------------------------------------------------------ dQ readout
     const int lane = static_cast<int>(lane_id());
+    const int tid = threadIdx.x - 32 * C::READOUT_WARP;
     const int wl = (warp & 3) * 32;  // this warp's TMEM lanes (query rows) wl .. wl+31
     const uint32_t tdQ = tmem + C::T_DQ + (static_cast<uint32_t>(wl) << 16);
+    const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+    const uint32_t peer_slot = mapa_shared(smem_u32(sRX), peer) + tid * 16;
+    const uint8_t* rx_slot = sRX + tid * 16;
+    const uint32_t rx_full_peer = mapa_shared(rx_full, peer);
+    const uint32_t tx_free_peer = mapa_shared(tx_free, peer);
     for (int j = 0; j < n_q; ++j) {
       if (!mbar_wait_warp(dq_full, j & 1, status)) break;
+      // the partner has read what this CTA sent for the previous tile
+      if (j > 0 && !mbar_wait_cluster_warp(tx_free, (j - 1) & 1, status)) break;
+      if (tid == 0) mbar_arrive_expect_tx(rx_full, C::RX_BYTES);  // this tile's incoming bytes
       tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld_16x256b_x8(tdQ, r0);                  // rows wl .. wl+15
-      tmem_ld_16x256b_x8(tdQ + (16u << 16), r1);    // rows wl+16 .. wl+31
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(dq_empty);  // dQ's TMEM columns are free for the next tile
-      float* base = dq_acc + (static_cast<size_t>(bh) * Lp + jq(j) * 128 + wl + (lane >> 2)) * 64 +
-                    2 * (lane & 3);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          red_add_v2_f32(base + (8 * a) * 64 + 8 * i, __uint_as_float(r0[4 * i + 2 * a]),
-                         __uint_as_float(r0[4 * i + 2 * a + 1]));
-          red_add_v2_f32(base + (16 + 8 * a) * 64 + 8 * i, __uint_as_float(r1[4 * i + 2 * a]),
-                         __uint_as_float(r1[4 * i + 2 * a + 1]));
-        }
+      uint32_t own0[16], own1[16];
+      {
+        uint32_t r[32];
+        tmem_ld_16x256b_x8(tdQ, r);  // rows wl .. wl+15
+        tmem_ld_wait();
+        if (rank == 0) dq_split<0>(r, own0, peer_slot, rx_full_peer, 0);
+        else dq_split<1>(r, own0, peer_slot, rx_full_peer, 0);
+      }
+      {
+        uint32_t r[32];
+        tmem_ld_16x256b_x8(tdQ + (16u << 16), r);  // rows wl+16 .. wl+31
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(dq_empty);  // dQ's TMEM columns are free for the next tile
+        if (rank == 0) dq_split<0>(r, own1, peer_slot, rx_full_peer, 4);
+        else dq_split<1>(r, own1, peer_slot, rx_full_peer, 4);
+      }
+      // add the partner's contribution to this CTA's columns, then reduce them
+      if (!mbar_wait_cluster_warp(rx_full, j & 1, status)) break;
+      dq_add_slots(own0, rx_slot, 0);
+      dq_add_slots(own1, rx_slot, 4);
+      mbar_arrive_cluster_relaxed(tx_free_peer);  // the values read above are consumed
+      float* row = dq_acc + (static_cast<size_t>(bh) * Lp + jq(j) * 128 + wl + (lane >> 2)) * 64 +
+                   32 * rank + 2 * (lane & 3);
+      dq_reduce_own(own0, row);
+      dq_reduce_own(own1, row + 16 * 64);
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no remote access into this CTA's shared memory after this point
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -1094,6 +1166,7 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
   if constexpr (D == 64 && !SPLIT) {
     using C64 = Bwd64Cfg;
+    grid.x = (grid.x + 1) & ~1u;  // clusters of two key tiles (a tile past L has no keys)
     static uint64_t attr64 = 0;
     ensure_smem_attr(attn_bwd_d64_kernel, C64::SMEM, attr64);
     attn_bwd_d64_kernel<<<grid, C64::THREADS, C64::SMEM, stream>>>(

@@ -111,6 +111,79 @@ __device__ __forceinline__ bool cta_aborted(const uint32_t* status, int* flag_sm
   return *flag_smem != 0;
 }
 
+// ---------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// All threads of all CTAs of the cluster (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// 16-byte store into another CTA's shared memory that completes 16 bytes of
+// the transaction count of that CTA's mbarrier `remote_bar` (no fence).
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint4 v, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          remote_addr),
+      "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(remote_bar)
+      : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster without ordering this
+// thread's other memory operations (use once the values it read are consumed).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
+               : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster, releasing this
+// thread's earlier shared::cluster stores and shared-memory reads.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (as mbar_wait) acquiring at cluster scope, warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint32_t bar, uint32_t parity,
+                                                       uint32_t* status) {
+  bool ok = mbar_try_wait_cluster(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+#pragma unroll 1
+      for (int i = 0; i < 32 && !ok; ++i) ok = mbar_try_wait_cluster(bar, parity);
+      if (ok) break;
+      if (globaltimer() - t0 > PA_WAIT_NS) {
+        record_error(status, PA_DEV_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Order generic-proxy shared-memory writes before async-proxy (TMA/UMMA) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
