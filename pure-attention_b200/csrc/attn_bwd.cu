@@ -579,9 +579,9 @@ __global__ void __launch_bounds__(512, 1)
 // for the next tile's MMAs as early as possible:
 //   P phase:  load S (s_free) -> P in registers -> P^T to TMEM (pt_full)
 //   dS phase: load dP (dp_free) -> dS = P * dP' to shared memory (p_full)
-// and the MMA issuer interleaves the two tiles on the tensor pipe:
-//   s_free(j)  -> S(j+1)      pt_full(j) -> dV(j)       dp_free(j) -> dP(j+1)
-//   p_full(j)  -> dK(j), dQ(j)
+// and the MMA issuer interleaves the tiles on the tensor pipe, per tile j:
+//   s_free(j) -> S(j+1);  p_full(j-1) -> dK(j-1), dQ(j-1);
+//   pt_full(j) -> dV(j);  dp_free(j) -> dP(j+1)
 // dS goes to shared memory only (dK reads it K-major, dQ MN-major, from a
 // double-buffered tile). Q and the extension tile are triple-buffered because
 // Q(j) is released only by dK(j); dO is double-buffered (released by dV(j)).
@@ -849,6 +849,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
         issue_dP(0);
         umma_commit(dp_full);
       }
+      // dK / dQ of tile j-1 are issued after S of tile j+1, so the next tile's
+      // elementwise work never waits behind them.
+      auto issue_dKdQ = [&](int j) {
+        if (!(ok = mbar_wait(p_full(j), (j >> 1) & 1, status))) return;
+        tc_fence_after();
+        issue_dK(j);
+        umma_commit(q_empty(j % C::QSTAGES));
+        if (j > 0) {
+          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) return;
+          tc_fence_after();
+        }
+        issue_dQ(j);
+        umma_commit(dq_full);
+      };
       for (int j = 0; ok && j < n_q; ++j) {
         const bool more = j + 1 < n_q;
         if (!(ok = mbar_wait(s_free, j & 1, status))) break;
@@ -858,6 +872,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
           tc_fence_after();
           issue_S(j + 1);
           umma_commit(s_full);
+        }
+        if (j > 0) {
+          issue_dKdQ(j - 1);
+          if (!ok) break;
         }
         if (!(ok = mbar_wait(pt_full, j & 1, status))) break;
         tc_fence_after();
@@ -872,17 +890,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
           issue_dP(j + 1);
           umma_commit(dp_full);
         }
-        if (!(ok = mbar_wait(p_full(j), (j >> 1) & 1, status))) break;
-        tc_fence_after();
-        issue_dK(j);
-        umma_commit(q_empty(j % C::QSTAGES));
-        if (j > 0) {
-          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
-          tc_fence_after();
-        }
-        issue_dQ(j);
-        umma_commit(dq_full);
       }
+      if (ok) issue_dKdQ(n_q - 1);
       if (ok) umma_commit(kv_done);
     }
   } else if (warp >= C::EW_WARP && warp < C::READOUT_WARP) {
