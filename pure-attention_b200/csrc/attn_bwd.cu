@@ -610,7 +610,8 @@ struct Bwd64Cfg {
   static constexpr int QSTAGE_BYTES = QT_BYTES + EXT_BYTES;
   static constexpr int DS_BYTES = 2 * CHUNK;           // queries [0,64) and [64,128)
   static constexpr int RX_BYTES = 128 * 32 * 4;        // partner's half of a dQ tile
-  static constexpr int SMEM = 2 * KV_BYTES + 2 * EXT_BYTES + QSTAGES * QSTAGE_BYTES +
+  static constexpr int ONES_BYTES = 1024;  // two 256-byte tiles of ones, padded to 1 KB
+  static constexpr int SMEM = 2 * KV_BYTES + ONES_BYTES + QSTAGES * QSTAGE_BYTES +
                               OSTAGES * QT_BYTES + 2 * DS_BYTES + RX_BYTES + 1024;
   static constexpr uint32_t T_S = 0, T_DP = 128, T_PT = 256, T_DV = 320, T_DK = 384, T_DQ = 448;
 };
@@ -673,18 +674,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
   uint8_t* sK = smem;
   uint8_t* sV = sK + C::KV_BYTES;
   // tiles of ones in the extension layout: columns 0-2 (picks -LSE/scale) and
-  // columns 8-10 (picks -Delta)
+  // columns 8-10 (picks -Delta). Every 8-row group of the 128-row operand is
+  // the same, so each tile is one group (256 B) read with a zero group stride.
   uint8_t* sOnesS = sV + C::KV_BYTES;
-  uint8_t* sOnesP = sOnesS + C::EXT_BYTES;
-  uint8_t* sQ = sOnesP + C::EXT_BYTES;  // stage s: Q tile, then its extension tile
+  uint8_t* sOnesP = sOnesS + 256;
+  uint8_t* sQ = sOnesS + C::ONES_BYTES;  // stage s: Q tile, then its extension tile
   uint8_t* sO = sQ + C::QSTAGES * C::QSTAGE_BYTES;
   uint8_t* sdS = sO + C::OSTAGES * C::QT_BYTES;
   uint8_t* sRX = sdS + 2 * C::DS_BYTES;  // partner's half of the current dQ tile
-  if (threadIdx.x < 256) {
+  if (threadIdx.x < 16) {
     const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
     const uint4 one3 = make_uint4(0x3f803f80u, 0x00003f80u, 0u, 0u);
     const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-    const int off = (r / 8) * 256 + (r % 8) * 16 + half * 128;
+    const int off = r * 16 + half * 128;
     *reinterpret_cast<uint4*>(sOnesS + off) = half ? zero : one3;
     *reinterpret_cast<uint4*>(sOnesP + off) = half ? one3 : zero;
     fence_proxy_async_smem();
@@ -797,8 +799,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       const uint64_t dDS_K = make_sdesc(smem_u32(sdS), 16, 1024);         // dS^T, K-major
       const uint64_t dDS_MN = make_sdesc(smem_u32(sdS), C::CHUNK, 1024);  // dS, MN-major
       // extension tiles: K-major, no swizzle; K-halves 128 B apart, 8-row groups 256 B apart
-      const uint64_t dOnesS = make_sdesc(smem_u32(sOnesS), 128, 256, 0);
-      const uint64_t dOnesP = make_sdesc(smem_u32(sOnesP), 128, 256, 0);
+      const uint64_t dOnesS = make_sdesc(smem_u32(sOnesS), 128, 0, 0);
+      const uint64_t dOnesP = make_sdesc(smem_u32(sOnesP), 128, 0, 0);
       const uint64_t dExt = make_sdesc(smem_u32(sQ + C::QT_BYTES), 128, 256, 0);
       auto q_off = [&](int j) { return static_cast<uint32_t>(((j % C::QSTAGES) * C::QSTAGE_BYTES) >> 4); };
       auto o_off = [&](int j) { return static_cast<uint32_t>(((j % C::OSTAGES) * C::QT_BYTES) >> 4); };
