@@ -113,7 +113,7 @@ class ClockSampler:
 
 def traffic_from_profile():
     """DRAM bytes per backward launch from the committed ncu summary, or None."""
-    path = os.path.join(REPO, "profiles", "attn_bwd_kernel_B8H16L4096d64.md")
+    path = os.path.join(REPO, "profiles", "attn_bwd_d64_kernel_B8H16L4096d64.md")
     try:
         for ln in open(path):
             if ln.startswith("traffic_bytes_per_launch:"):
