@@ -575,15 +575,15 @@ __global__ void __launch_bounds__(512, 1)
 // S' = S - LSE/scale and dP' = dP - Delta come out of the tensor core and the
 // elementwise step needs no per-query loads: P = exp2(S' * scale * log2 e),
 // dS = P * dP'.
-// Each tile's elementwise work runs in two phases, each of which frees TMEM
-// for the next tile's MMAs as early as possible:
-//   P phase:  load S (s_free) -> P in registers -> P^T to TMEM (pt_full)
-//   dS phase: load dP (dp_free) -> dS = P * dP' to shared memory (p_full)
+// Each tile's elementwise work runs in two phases:
+//   P phase:  load S (s_free: the next S may start) -> P in registers ->
+//             P^T to its own TMEM columns (pt_full: dV may start)
+//   dS phase: load dP -> dS = P * dP' -> dS^T packed over the dP columns just
+//             read (the A operand of the TS dK MMA) and dS to a double-buffered
+//             shared tile (the A operand of dQ) (p_full)
 // and the MMA issuer interleaves the tiles on the tensor pipe, per tile j:
-//   s_free(j) -> S(j+1);  p_full(j-1) -> dK(j-1), dQ(j-1);
-//   pt_full(j) -> dV(j);  dp_free(j) -> dP(j+1)
-// dS goes to shared memory only (dK reads it K-major, dQ MN-major, from a
-// double-buffered tile). Q and the extension tile are triple-buffered because
+//   s_free(j) -> S(j+1);  pt_full(j) -> dV(j);
+//   p_full(j) -> dK(j), then dP(j+1) over dS^T(j), then dQ(j). Q and the extension tile are triple-buffered because
 // Q(j) is released only by dK(j); dO is double-buffered (released by dV(j)).
 // The dQ readout frees dQ's TMEM right after its tcgen05.ld (16x256b shape:
 // four neighbouring lanes hold a whole 32-byte sector of a dQ row). The two
@@ -702,7 +702,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
   const uint32_t pt_full = smem_u32(&bars[9]);   // P^T is in TMEM
   const uint32_t pt_free = smem_u32(&bars[10]);  // the dV MMA has read P^T
   const uint32_t dp_full = smem_u32(&bars[11]);  // dP' of the tile is in TMEM
-  const uint32_t dp_free = smem_u32(&bars[12]);  // elementwise warps have read dP'
   // dS of tile j is in shared memory. Two barriers, by tile parity: the
   // elementwise warps can finish tile j+1 before the issuer has polled tile j.
   auto p_full = [&](int j) { return smem_u32(&bars[(j & 1) ? 17 : 13]); };
@@ -738,7 +737,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
     mbar_init(pt_full, C::NEW);
     mbar_init(pt_free, 1);
     mbar_init(dp_full, 1);
-    mbar_init(dp_free, C::NEW);
     mbar_init(p_full(0), C::NEW);
     mbar_init(p_full(1), C::NEW);
     mbar_init(dq_full, 1);
@@ -796,7 +794,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       const uint64_t dQ_MN = make_sdesc(smem_u32(sQ), C::CHUNK, 1024);
       const uint64_t dO_K = make_sdesc(smem_u32(sO), 16, 1024);
       const uint64_t dO_MN = make_sdesc(smem_u32(sO), C::CHUNK, 1024);
-      const uint64_t dDS_K = make_sdesc(smem_u32(sdS), 16, 1024);         // dS^T, K-major
       const uint64_t dDS_MN = make_sdesc(smem_u32(sdS), C::CHUNK, 1024);  // dS, MN-major
       // extension tiles: K-major, no swizzle; K-halves 128 B apart, 8-row groups 256 B apart
       const uint64_t dOnesS = make_sdesc(smem_u32(sOnesS), 128, 0, 0);
@@ -827,12 +824,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
           umma_f16_ts(tmem + C::T_DV, tmem + C::T_PT + 8 * k, dO_MN + so + ((k * 2048) >> 4), idKV,
                       (j > 0 || k > 0) ? 1u : 0u);
       };
-      auto issue_dK = [&](int j) {  // dK += dS^T Q
+      auto issue_dK = [&](int j) {  // dK += dS^T Q  (dS^T packed over the dP columns)
         const uint32_t so = q_off(j);
-        const uint32_t bo = ((j & 1) * C::DS_BYTES) >> 4;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          umma_f16_ss(tmem + C::T_DK, dDS_K + bo + (((k / 4) * C::CHUNK + (k % 4) * 32) >> 4),
+          umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + 32 * (k / 2) + 8 * (k % 2),
                       dQ_MN + so + ((k * 2048) >> 4), idKV, (j > 0 || k > 0) ? 1u : 0u);
       };
       auto issue_dQ = [&](int j) {  // dQ = dS K
@@ -851,20 +847,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
         issue_dP(0);
         umma_commit(dp_full);
       }
-      // dK / dQ of tile j-1 are issued after S of tile j+1, so the next tile's
-      // elementwise work never waits behind them.
-      auto issue_dKdQ = [&](int j) {
-        if (!(ok = mbar_wait(p_full(j), (j >> 1) & 1, status))) return;
-        tc_fence_after();
-        issue_dK(j);
-        umma_commit(q_empty(j % C::QSTAGES));
-        if (j > 0) {
-          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) return;
-          tc_fence_after();
-        }
-        issue_dQ(j);
-        umma_commit(dq_full);
-      };
       for (int j = 0; ok && j < n_q; ++j) {
         const bool more = j + 1 < n_q;
         if (!(ok = mbar_wait(s_free, j & 1, status))) break;
@@ -875,16 +857,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
           issue_S(j + 1);
           umma_commit(s_full);
         }
-        if (j > 0) {
-          issue_dKdQ(j - 1);
-          if (!ok) break;
-        }
         if (!(ok = mbar_wait(pt_full, j & 1, status))) break;
         tc_fence_after();
         issue_dV(j);
         umma_commit(pt_free);
         umma_commit(o_empty(j % C::OSTAGES));
-        if (!(ok = mbar_wait(dp_free, j & 1, status))) break;
+        if (!(ok = mbar_wait(p_full(j), (j >> 1) & 1, status))) break;
+        tc_fence_after();
+        issue_dK(j);  // reads dS^T(j) from the dP columns before dP(j+1) overwrites them
+        umma_commit(q_empty(j % C::QSTAGES));
         if (more) {
           if (!(ok = mbar_wait(o_full((j + 1) % C::OSTAGES), ((j + 1) / C::OSTAGES) & 1, status)))
             break;
@@ -892,8 +873,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
           issue_dP(j + 1);
           umma_commit(dp_full);
         }
+        if (j > 0) {
+          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
+          tc_fence_after();
+        }
+        issue_dQ(j);
+        umma_commit(dq_full);
       }
-      if (ok) issue_dKdQ(n_q - 1);
       if (ok) umma_commit(kv_done);
     }
   } else if (warp >= C::EW_WARP && warp < C::READOUT_WARP) {
@@ -953,8 +939,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       tmem_ld16(tdP, va);
       tmem_ld16(tdP + 16, vb);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(dp_free);
       uint32_t ds[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -963,12 +947,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
         ds[8 + i] = pack_bf16x2(p[16 + 2 * i] * __uint_as_float(vb[2 * i]),
                                 p[16 + 2 * i + 1] * __uint_as_float(vb[2 * i + 1]));
       }
+      // dS^T packed over the first 16 of this group's 32 dP columns (read above)
+      PA_TMEM_ST_X8(tdP, ds);
+      PA_TMEM_ST_X8(tdP + 8, (ds + 8));
       uint8_t* dsrow = sdS + (j & 1) * C::DS_BYTES + (grp >> 1) * C::CHUNK;
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, dsb0 + 16 * u)) =
             make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+      tmem_st_wait();
       fence_proxy_async_smem();
+      tc_fence_before();
       mbar_arrive(p_full(j));
     }
     // dV and dK (x scale) epilogue: groups 0, 1 write dV columns [0,32), [32,64);
