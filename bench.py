@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: B=8 x H=16 per GPU; strong: the B=8 batches split across GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--linear", action="store_true",
+                    help="instead of the attention step: time the fused projection calls of the "
+                         "MHA block (B8 L1024 E512 fp32) against the unfused call sequence")
     return ap.parse_args()
 
 
@@ -204,10 +207,73 @@ def run_reference_arm(args):
     return 0
 
 
+def run_linear(args):
+    """Projections of the pre-LN MHA block (B8 L1024 E512, fp32), forward + backward:
+    pa_linear_fwd / pa_linear_bwd against pa_matmul + pa_bias_add + pa_split_last_dim and
+    pa_concat_last_dim_grad + pa_bias_grad + pa_matmul_grad_x + pa_matmul_grad_w."""
+    import torch
+    import pa_capi
+    torch.cuda.set_device(0)
+    M, E = 8 * 1024, 512
+    g = torch.Generator(device="cuda").manual_seed(7)
+    rnd = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    x, wi, bi, wo, bo = rnd(M, E), rnd(E, 3 * E) * 0.04, rnd(3 * E), rnd(E, E) * 0.04, rnd(E)
+    qkv = [torch.empty(M, E, device="cuda") for _ in range(3)]
+    attn, out = rnd(M, E), torch.empty(M, E, device="cuda")
+    d_qkv, d_out = [rnd(M, E) for _ in range(3)], rnd(M, E)
+    dx, dwi, dbi = torch.zeros(M, E, device="cuda"), torch.zeros(E, 3 * E, device="cuda"), torch.zeros(3 * E, device="cuda")
+    dat, dwo, dbo = torch.zeros(M, E, device="cuda"), torch.zeros(E, E, device="cuda"), torch.zeros(E, device="cuda")
+    ws = torch.empty(max(pa_capi.linear_workspace_size(M, E, 3 * E),
+                         pa_capi.matmul_workspace_size(M, 3 * E, E),
+                         pa_capi.matmul_workspace_size(M, E, 3 * E)), dtype=torch.uint8, device="cuda")
+    proj, dproj, tmp = torch.empty(M, 3 * E, device="cuda"), torch.zeros(M, 3 * E, device="cuda"), torch.empty(M, E, device="cuda")
+
+    def fused():
+        pa_capi.linear_fwd(x, wi, bi, qkv, M, E, 3 * E, ws)
+        pa_capi.linear_fwd(attn, wo, bo, [out], M, E, E, ws)
+        pa_capi.linear_bwd(attn, wo, [d_out], dat, dwo, dbo, M, E, E, ws)
+        pa_capi.linear_bwd(x, wi, d_qkv, dx, dwi, dbi, M, E, 3 * E, ws)
+
+    def unfused():
+        pa_capi.matmul(x, wi, proj, M, 3 * E, E, ws)
+        pa_capi.bias_add(proj, bi, proj, M, 3 * E)
+        pa_capi.split_last_dim(proj, qkv, M, E)
+        pa_capi.matmul(attn, wo, tmp, M, E, E, ws)
+        pa_capi.bias_add(tmp, bo, out, M, E)
+        pa_capi.bias_grad(d_out, dbo, M, E)
+        pa_capi.matmul_grad_x(d_out, wo, dat, M, E, E, ws)
+        pa_capi.matmul_grad_w(attn, d_out, dwo, M, E, E, ws)
+        pa_capi.concat_last_dim_grad(d_qkv, dproj, M, E)
+        pa_capi.bias_grad(dproj, dbi, M, 3 * E)
+        pa_capi.matmul_grad_x(dproj, wi, dx, M, E, 3 * E, ws)
+        pa_capi.matmul_grad_w(x, dproj, dwi, M, E, 3 * E, ws)
+
+    res = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / args.steps
+    flops = 2 * M * E * (3 * E + E) * 3  # fwd + dX + dW of both projections
+    print(json.dumps({"metric": "MHA block projections fwd+bwd (B8 L1024 E512 fp32)", "unit": "ms",
+                      "fused_ms": round(res["fused"], 4), "unfused_ms": round(res["unfused"], 4),
+                      "speedup": round(res["unfused"] / res["fused"], 3),
+                      "fused_tflops": round(flops / (res["fused"] * 1e-3) / 1e12, 1),
+                      "steps": args.steps, "device_status": pa_capi.device_status()}))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.linear:
+        return run_linear(args)
     import torch
     import pa_capi
     import sharding

@@ -142,6 +142,31 @@ int pa_matmul_grad_x(const float* dY, const float* W, float* dX, int M, int N, i
 int pa_matmul_grad_w(const float* X, const float* dY, float* dW, int M, int N, int K,
                      void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
+/* ---------------------------------------------------------------- fused projection
+ * No single reference counterpart: one call does what the reference does in
+ * separate passes around a projection - core::matmul + core::matadd + core::split
+ * forward (Functional.cpp:12-52, Functional.cpp:205-252, matadd_kernel.cu:4-12,
+ * split_forward_kernel.cu:4-21), and MatMulFunction + AddFunction +
+ * SplitFunction backward (Autograd.cpp:9-59, 113-177; sum_rows_grad_kernel.cu,
+ * split_backward_kernel.cu). fp32 in/out, same arithmetic as pa_matmul.
+ * out_features must be a multiple of n_outs (n_outs, n_parts in 1..3). */
+size_t pa_linear_workspace_size(int M, int in_features, int out_features);
+
+/* Y = X[M,in] W[in,out] (+ bias[out] if bias is not NULL), written as n_outs
+ * column blocks: outs (a HOST array of n_outs device pointers) receives
+ * outs[c][M, out/n_outs] = Y[:, c*out/n_outs : (c+1)*out/n_outs]. */
+int pa_linear_fwd(const float* X, const float* W, const float* bias, float* const* outs, int n_outs,
+                  int M, int in_features, int out_features, void* workspace, size_t workspace_bytes,
+                  pa_stream_t stream);
+
+/* With dY the concatenation of the n_parts column blocks dy_parts (a HOST array
+ * of device pointers, [M, out/n_parts] each): dX[M,in] += dY W^T,
+ * dW[in,out] += X^T dY, dbias[out] += column sums of dY. dX, dW and dbias may
+ * each be NULL (that gradient is skipped). */
+int pa_linear_bwd(const float* X, const float* W, const float* const* dy_parts, int n_parts,
+                  float* dX, float* dW, float* dbias, int M, int in_features, int out_features,
+                  void* workspace, size_t workspace_bytes, pa_stream_t stream);
+
 /* ---------------------------------------------------------------- elementwise */
 
 /* out[M,N] = A[M,N] + bias[N]. Replaces launch_matadd_tiled (Launchers.cuh:25-32). */

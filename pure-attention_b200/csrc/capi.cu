@@ -213,6 +213,46 @@ int pa_matmul_grad_w(const float* X, const float* dY, float* dW, int M, int N, i
   return gemm_call(2, X, dY, dW, M, N, K, workspace, workspace_bytes, stream);
 }
 
+size_t pa_linear_workspace_size(int M, int in_features, int out_features) {
+  if (M <= 0 || in_features <= 0 || out_features <= 0) return 0;
+  return pa::linear_workspace_bytes(M, in_features, out_features);
+}
+
+static int linear_check(int M, int in, int out, int n, void* ws, size_t ws_bytes) {
+  if (M <= 0 || in <= 0 || out <= 0 || n < 1 || n > 3 || out % n != 0) return PA_ERR_SHAPE;
+  if (!ws || ws_bytes < pa::linear_workspace_bytes(M, in, out)) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return PA_ERR_ALIGN;
+  return PA_OK;
+}
+
+int pa_linear_fwd(const float* X, const float* W, const float* bias, float* const* outs, int n_outs,
+                  int M, int in_features, int out_features, void* workspace, size_t workspace_bytes,
+                  pa_stream_t stream) {
+  if (!X || !W || !outs) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, n_outs, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i]) return PA_ERR_NULL;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  return pa::launch_linear_fwd(X, W, bias, outs, n_outs, M, in_features, out_features, workspace,
+                               status, static_cast<cudaStream_t>(stream));
+}
+
+int pa_linear_bwd(const float* X, const float* W, const float* const* dy_parts, int n_parts,
+                  float* dX, float* dW, float* dbias, int M, int in_features, int out_features,
+                  void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  if (!X || !W || !dy_parts) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, n_parts, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  for (int i = 0; i < n_parts; ++i)
+    if (!dy_parts[i]) return PA_ERR_NULL;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  return pa::launch_linear_bwd(X, W, dy_parts, n_parts, dX, dW, dbias, M, in_features,
+                               out_features, workspace, status, static_cast<cudaStream_t>(stream));
+}
+
 int pa_bias_add(const float* A, const float* bias, float* out, int M, int N, pa_stream_t stream) {
   if (!A || !bias || !out) return PA_ERR_NULL;
   if (M <= 0 || N <= 0) return PA_ERR_SHAPE;

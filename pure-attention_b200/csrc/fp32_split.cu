@@ -6,7 +6,9 @@
 // a_lo*b_lo term is below 2^-16 relative), which keeps the fp32 path within
 // 1e-3 of float64 where a single tf32 or bf16 pass would not. Rows of D
 // values are written as rows of Dp >= D values, zero-padded, so the head
-// dimension of the planes is a multiple of 64 (one 128-byte TMA box).
+// dimension of the planes is a multiple of 64 (one 128-byte TMA box). The
+// planes may also be a column block [c0, c0 + Dp) of wider planes with row
+// pitch ldp, which gathers several [rows, D] operands into one.
 #include <cuda_bf16.h>
 #include "host_launchers.h"
 
@@ -16,7 +18,8 @@ namespace {
 
 // One thread per 4 output columns of one row (D % 4 == 0, 16-byte aligned x).
 __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
-                                    __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp) {
+                                    __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp,
+                                    size_t ldp, int c0) {
   const int groups = Dp / 4;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
        i < rows * groups; i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -35,22 +38,23 @@ __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* 
       h2[e] = ph;
       l2[e] = pack_bf16x2(v[2 * e] - h0, v[2 * e + 1] - h1);
     }
-    *reinterpret_cast<uint2*>(hi + r * Dp + c) = make_uint2(h2[0], h2[1]);
-    *reinterpret_cast<uint2*>(lo + r * Dp + c) = make_uint2(l2[0], l2[1]);
+    *reinterpret_cast<uint2*>(hi + r * ldp + c0 + c) = make_uint2(h2[0], h2[1]);
+    *reinterpret_cast<uint2*>(lo + r * ldp + c0 + c) = make_uint2(l2[0], l2[1]);
   }
 }
 
 // Any D: one thread per output element.
 __global__ void split_planes_scalar_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
-                                           __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp) {
+                                           __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp,
+                                           size_t ldp, int c0) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < rows * Dp;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const size_t r = i / Dp;
     const int c = static_cast<int>(i % Dp);
     const float v = c < D ? x[r * D + c] : 0.f;
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    hi[i] = h;
-    lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    hi[r * ldp + c0 + c] = h;
+    lo[r * ldp + c0 + c] = __float2bfloat16_rn(v - __bfloat162float(h));
   }
 }
 
@@ -58,17 +62,23 @@ __global__ void split_planes_scalar_kernel(const float* __restrict__ x, __nv_bfl
 
 int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
                         cudaStream_t s) {
-  if (D > Dp || D <= 0) return PA_ERR_SHAPE;
+  return launch_split_planes_into(x, hi, lo, rows, D, Dp, static_cast<size_t>(Dp), 0, s);
+}
+
+int launch_split_planes_into(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
+                             size_t ldp, int c0, cudaStream_t s) {
+  if (D > Dp || D <= 0 || c0 < 0 || static_cast<size_t>(c0) + Dp > ldp) return PA_ERR_SHAPE;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (D % 4 != 0 || Dp % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
+  if (D % 4 != 0 || Dp % 4 != 0 || c0 % 4 != 0 || ldp % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
     const size_t n = rows * Dp;
     size_t blocks = (n + 255) / 256;
     if (blocks > static_cast<size_t>(sms) * 16) blocks = static_cast<size_t>(sms) * 16;
     if (blocks == 0) blocks = 1;
     split_planes_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp);
+        x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp, ldp, c0);
     return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
   }
   const size_t work = rows * (Dp / 4);
@@ -76,7 +86,7 @@ int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, 
   if (blocks > static_cast<size_t>(sms) * 16) blocks = static_cast<size_t>(sms) * 16;
   if (blocks == 0) blocks = 1;
   split_planes_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-      x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp);
+      x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp, ldp, c0);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

@@ -12,6 +12,15 @@
 // reduction index is the row index is simply fed as an MN-major tcgen05
 // operand, so each mode reads its inputs in place.
 //
+// The projection layer built on it (launch_linear_fwd / _bwd) fuses what the
+// reference does in separate passes around each projection
+// (Functional.cpp:12-52 matmul, matadd_kernel.cu bias add, split_forward_kernel.cu
+// and its adjoint, sum_rows_grad_kernel.cu): the forward epilogue adds the
+// bias and writes the output as up to three column blocks (Q, K, V of the
+// attention in-projection) to separate tensors; the backward gathers the
+// column-block gradients straight into one pair of bf16 planes, shared by
+// the dX and dW GEMMs.
+//
 // One CTA = one 128 x 128 output tile; K in blocks of 64 through a 3-stage
 // TMA ring (hi and lo planes of both operands per stage).
 //   warp 0     TMA producer
@@ -38,7 +47,8 @@ __global__ void __launch_bounds__(256, 1)
     gemm_split_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                       const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
                       float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
-                      uint32_t* status) {
+                      const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
+                      int nsplit, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[2 * GSTAGES + 1];
   __shared__ uint32_t tmem_slot;
@@ -125,6 +135,14 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     if (mbar_wait_warp(acc_full, 0, status)) {
       tc_fence_after();
+      // Output column `col` goes to C[row * ldc + col], or with nsplit > 0 to
+      // part p = col / nsplit (C, C1, C2) at [row * nsplit + col - p * nsplit].
+      auto dst_of = [&](int col) -> float* {
+        if (nsplit <= 0) return C + static_cast<size_t>(row) * ldc + col;
+        const int p = col / nsplit;
+        float* base = p == 0 ? C : (p == 1 ? C1 : C2);
+        return base + static_cast<size_t>(row) * nsplit + (col - p * nsplit);
+      };
 #pragma unroll 1
       for (int c = 0; c < GB / 32; ++c) {
         uint32_t v[32];
@@ -132,15 +150,22 @@ __global__ void __launch_bounds__(256, 1)
         tmem_ld_wait();
         if (row >= Mout) continue;
         const int col0 = n0 + c * 32;
-        float* dst = C + static_cast<size_t>(row) * ldc + col0;
-        const bool vec = (col0 + 32 <= Nout) && ((ldc & 3) == 0) &&
-                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+        float* dst = dst_of(col0);
+        const bool one_part = nsplit <= 0 || (col0 % nsplit) + 32 <= nsplit;
+        const int ld = nsplit > 0 ? nsplit : ldc;
+        const bool vec = (col0 + 32 <= Nout) && one_part && ((ld & 3) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) &&
+                         (!bias || (reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0);
         if (vec) {
           float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
                                    __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+            if (bias) {
+              const float4 bb = *reinterpret_cast<const float4*>(bias + col0 + 4 * u);
+              f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
+            }
             if (accumulate) {
               const float4 p = d4[u];
               f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
@@ -149,8 +174,13 @@ __global__ void __launch_bounds__(256, 1)
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (col0 + e < Nout) dst[e] = __uint_as_float(v[e]) + (accumulate ? dst[e] : 0.f);
+          for (int e = 0; e < 32; ++e) {
+            const int col = col0 + e;
+            if (col < Nout) {
+              float* de = dst_of(col);
+              *de = __uint_as_float(v[e]) + (bias ? bias[col] : 0.f) + (accumulate ? *de : 0.f);
+            }
+          }
         }
       }
     }
@@ -181,15 +211,53 @@ bool plane_map(CUtensorMap* m, const void* base, int rows, int cols, bool mn) {
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+struct Epilogue {
+  const float* bias = nullptr;
+  float* c1 = nullptr;
+  float* c2 = nullptr;
+  int nsplit = 0;
+};
+
 template <bool A_MN, bool B_MN>
 int run_gemm(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred, int accumulate,
-             uint32_t* status, cudaStream_t s) {
+             const Epilogue& ep, uint32_t* status, cudaStream_t s) {
   static uint64_t attr = 0;
   ensure_smem_attr(gemm_split_kernel<A_MN, B_MN>, GSMEM, attr);
   dim3 grid((Nout + GB - 1) / GB, (Mout + GB - 1) / GB);
   gemm_split_kernel<A_MN, B_MN><<<grid, 256, GSMEM, s>>>(m[0], m[1], m[2], m[3], C, ldc, Mout, Nout,
-                                                          Kred, accumulate, status);
+                                                          Kred, accumulate, ep.bias, ep.c1, ep.c2,
+                                                          ep.nsplit, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+// bf16 hi/lo planes of one [rows, cols] operand in the workspace (row pitch round8(cols)).
+struct Planes {
+  uint8_t* hi;
+  uint8_t* lo;
+  int rows, cols;
+};
+size_t plane_size(int rows, int cols) { return up256(static_cast<size_t>(rows) * round8(cols) * 2); }
+Planes carve(uint8_t*& w, int rows, int cols) {
+  const size_t b = plane_size(rows, cols);
+  Planes p{w, w + b, rows, cols};
+  w += 2 * b;
+  return p;
+}
+int split_into(const float* x, const Planes& p, cudaStream_t s) {
+  return launch_split_planes(x, p.hi, p.lo, static_cast<size_t>(p.rows), p.cols, round8(p.cols), s);
+}
+
+// GEMM of `mode` (see launch_gemm_f32) on operands already split into planes.
+int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int N, int K,
+                const Epilogue& ep, uint32_t* status, cudaStream_t s) {
+  const bool a_mn = (mode == 2), b_mn = (mode != 1);
+  CUtensorMap m[4];
+  if (!plane_map(&m[0], a.hi, a.rows, a.cols, a_mn) || !plane_map(&m[1], a.lo, a.rows, a.cols, a_mn) ||
+      !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn) || !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn))
+    return PA_ERR_ALIGN;
+  if (mode == 0) return run_gemm<false, true>(m, C, N, M, N, K, 0, ep, status, s);
+  if (mode == 1) return run_gemm<false, false>(m, C, N, M, N, K, 1, ep, status, s);
+  return run_gemm<true, true>(m, C, K, N, K, M, 1, ep, status, s);
 }
 
 }  // namespace
@@ -210,24 +278,72 @@ int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, i
   else if (mode == 1) { ar = M; ac = K; br = N; bc = K; }
   else { ar = M; ac = N; br = M; bc = K; }
   uint8_t* w = static_cast<uint8_t*>(ws);
-  const size_t pa_ = up256(static_cast<size_t>(ar) * round8(ac) * 2);
-  const size_t pb = up256(static_cast<size_t>(br) * round8(bc) * 2);
-  uint8_t* ah = w;
-  uint8_t* al = w + pa_;
-  uint8_t* bh = w + 2 * pa_;
-  uint8_t* bl = w + 2 * pa_ + pb;
-  int st = launch_split_planes(A, ah, al, ar, ac, round8(ac), s);
+  const Planes a = carve(w, ar, ac), b = carve(w, br, bc);
+  int st = split_into(A, a, s);
   if (st != PA_OK) return st;
-  st = launch_split_planes(B, bh, bl, br, bc, round8(bc), s);
+  st = split_into(B, b, s);
   if (st != PA_OK) return st;
-  const bool a_mn = (mode == 2), b_mn = (mode != 1);
-  CUtensorMap m[4];
-  if (!plane_map(&m[0], ah, ar, ac, a_mn) || !plane_map(&m[1], al, ar, ac, a_mn) ||
-      !plane_map(&m[2], bh, br, bc, b_mn) || !plane_map(&m[3], bl, br, bc, b_mn))
-    return PA_ERR_ALIGN;
-  if (mode == 0) return run_gemm<false, true>(m, C, N, M, N, K, 0, status, s);
-  if (mode == 1) return run_gemm<false, false>(m, C, N, M, N, K, 1, status, s);
-  return run_gemm<true, true>(m, C, K, N, K, M, 1, status, s);
+  return gemm_planes(mode, a, b, C, M, N, K, Epilogue{}, status, s);
+}
+
+// Projection Y[M, OUT] = X[M, IN] W[IN, OUT] (+ bias), as column blocks.
+size_t linear_workspace_bytes(int M, int IN, int OUT) {
+  const size_t fwd = planes_bytes(M, IN) + planes_bytes(IN, OUT);
+  const size_t bwd = planes_bytes(M, OUT) + planes_bytes(IN, OUT) + planes_bytes(M, IN);
+  return fwd > bwd ? fwd : bwd;
+}
+
+int launch_linear_fwd(const float* x, const float* wt, const float* bias, float* const* outs,
+                      int n_outs, int M, int IN, int OUT, void* ws, uint32_t* status,
+                      cudaStream_t s) {
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const Planes a = carve(w, M, IN), b = carve(w, IN, OUT);
+  int st = split_into(x, a, s);
+  if (st != PA_OK) return st;
+  st = split_into(wt, b, s);
+  if (st != PA_OK) return st;
+  Epilogue ep;
+  ep.bias = bias;
+  if (n_outs > 1) {
+    ep.nsplit = OUT / n_outs;
+    ep.c1 = outs[1];
+    ep.c2 = n_outs > 2 ? outs[2] : nullptr;
+  }
+  return gemm_planes(0, a, b, outs[0], M, OUT, IN, ep, status, s);
+}
+
+int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_parts, int n_parts,
+                      float* dx, float* dw, float* dbias, int M, int IN, int OUT, void* ws,
+                      uint32_t* status, cudaStream_t s) {
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const Planes dy = carve(w, M, OUT), wp = carve(w, IN, OUT), xp = carve(w, M, IN);
+  // gather the column-block gradients into one pair of planes (row pitch round8(OUT))
+  const int part = OUT / n_parts;
+  for (int p = 0; p < n_parts; ++p) {
+    const int width = p + 1 < n_parts ? part : round8(OUT) - p * part;  // last block takes the pad
+    const int st = launch_split_planes_into(dy_parts[p], dy.hi, dy.lo, static_cast<size_t>(M), part,
+                                            width, static_cast<size_t>(round8(OUT)), p * part, s);
+    if (st != PA_OK) return st;
+  }
+  if (dx) {
+    int st = split_into(wt, wp, s);
+    if (st != PA_OK) return st;
+    st = gemm_planes(1, dy, wp, dx, M, IN, OUT, Epilogue{}, status, s);
+    if (st != PA_OK) return st;
+  }
+  if (dw) {
+    int st = split_into(x, xp, s);
+    if (st != PA_OK) return st;
+    st = gemm_planes(2, xp, dy, dw, M, IN, OUT, Epilogue{}, status, s);
+    if (st != PA_OK) return st;
+  }
+  if (dbias)
+    for (int p = 0; p < n_parts; ++p) {
+      const int st = launch_bias_grad(dy_parts[p], dbias + p * part, static_cast<uint32_t>(M),
+                                      static_cast<uint32_t>(part), s);
+      if (st != PA_OK) return st;
+    }
+  return PA_OK;
 }
 
 }  // namespace pa

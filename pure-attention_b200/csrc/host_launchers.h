@@ -18,6 +18,9 @@ int f32_plane_dim(int D);  // padded head dim of the fp32 path's bf16 planes (-1
 // fp32_split.cu: x [rows, D] fp32 -> hi, lo [rows, Dp] bf16 (zero-padded).
 int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
                         cudaStream_t s);
+// Same, into columns [c0, c0 + Dp) of planes with row pitch ldp (elements).
+int launch_split_planes_into(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
+                             size_t ldp, int c0, cudaStream_t s);
 
 // attn_bwd.cu
 size_t attn_bwd_workspace_bytes(const AttnShape& sh);
@@ -62,6 +65,16 @@ int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint3
 int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, int N, int K,
                     void* ws, uint32_t* status, cudaStream_t s);
 size_t gemm_workspace_bytes(int M, int N, int K);
+// Projection Y[M, OUT] = X[M, IN] W[IN, OUT] (+ bias) written as n_outs column
+// blocks of OUT / n_outs (n_outs <= 3); backward from n_parts column-block
+// gradients, accumulating into dx, dw, dbias (each may be null).
+size_t linear_workspace_bytes(int M, int IN, int OUT);
+int launch_linear_fwd(const float* x, const float* w, const float* bias, float* const* outs,
+                      int n_outs, int M, int IN, int OUT, void* ws, uint32_t* status,
+                      cudaStream_t s);
+int launch_linear_bwd(const float* x, const float* w, const float* const* dy_parts, int n_parts,
+                      float* dx, float* dw, float* dbias, int M, int IN, int OUT, void* ws,
+                      uint32_t* status, cudaStream_t s);
 
 // training.cu
 int launch_relu_fwd(const float* x, float* y, size_t n, cudaStream_t s);

@@ -53,6 +53,21 @@ struct MSEFunction : public Function {
   std::vector<std::shared_ptr<Tensor>> inputs() const override { return {predictions}; }
 };
 
+// Fused projection X W + bias, output as column blocks (core::linear): one
+// node for what MatMulFunction + AddFunction + SplitFunction do in three.
+struct LinearFunction : public Function {
+  std::shared_ptr<Tensor> X_input;
+  std::shared_ptr<Tensor> W_input;
+  std::shared_ptr<Tensor> bias_input;
+  std::vector<std::weak_ptr<Tensor>> Outputs;
+  LinearFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w, std::shared_ptr<Tensor> b,
+                 std::vector<std::shared_ptr<Tensor>> outs);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override {
+    return {X_input, W_input, bias_input};
+  }
+};
+
 struct SplitFunction : public Function {
   std::shared_ptr<Tensor> Input;
   std::vector<std::weak_ptr<Tensor>> Outputs;

@@ -25,6 +25,13 @@ void pop_data_normal(const std::shared_ptr<Tensor>& A, float std_dev, const cuda
 std::shared_ptr<Tensor> mse_loss(const std::shared_ptr<Tensor>& preds,
                                  const std::shared_ptr<Tensor>& targets,
                                  const cudaStream_t& stream);
+// Fused projection (no single reference counterpart: core::matmul + core::matadd
+// + core::split in one pass, Functional.cpp:12-52, 205-252): parts receive the
+// num_parts column blocks of A W + bias, with one LinearFunction node.
+void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
+            const std::shared_ptr<Tensor>& bias, uint32_t num_parts,
+            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream);
+
 void split(const std::shared_ptr<Tensor>& A, uint32_t num_parts, int dim,
            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream);
 // Q, K, V [N, L, E] with E = num_heads * head_dim (head_dim 32 or 64, fp32).

@@ -85,6 +85,43 @@ void MSEFunction::apply_backward() {
                "mse backward");
 }
 
+LinearFunction::LinearFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w,
+                               std::shared_ptr<Tensor> b, std::vector<std::shared_ptr<Tensor>> outs)
+    : X_input(std::move(x)), W_input(std::move(w)), bias_input(std::move(b)),
+      Outputs(outs.begin(), outs.end()) {}
+
+// dX += dY W^T, dW += X^T dY, dbias += column sums of dY, with dY the column
+// blocks' gradients (a block whose tensor has expired contributes zero).
+void LinearFunction::apply_backward() {
+  const int K = static_cast<int>(W_input->get_shape()[0]);
+  const int N = static_cast<int>(W_input->get_shape()[1]);
+  const int M = static_cast<int>(rows_of(*X_input));
+  const int parts = static_cast<int>(Outputs.size());
+  const size_t part_bytes = static_cast<size_t>(M) * (N / parts) * sizeof(float);
+  std::vector<const float*> grads;
+  std::vector<std::unique_ptr<Scratch>> zeros;
+  bool any = false;
+  for (auto& w : Outputs) {
+    auto t = w.lock();
+    if (t && t->get_gradient_ptr()) {
+      grads.push_back(t->get_gradient_ptr());
+      any = true;
+    } else {
+      zeros.push_back(std::make_unique<Scratch>(part_bytes, stream()));
+      cudaMemsetAsync(zeros.back()->get(), 0, part_bytes, stream());
+      grads.push_back(static_cast<const float*>(zeros.back()->get()));
+    }
+  }
+  if (!any) return;
+  Scratch ws(pa_linear_workspace_size(M, K, N), stream());
+  check_status(pa_linear_bwd(X_input->get_data_ptr(), W_input->get_data_ptr(), grads.data(), parts,
+                             X_input->requires_grad() ? X_input->get_gradient_ptr() : nullptr,
+                             W_input->requires_grad() ? W_input->get_gradient_ptr() : nullptr,
+                             bias_input->requires_grad() ? bias_input->get_gradient_ptr() : nullptr,
+                             M, K, N, ws.get(), ws.size(), ps(stream())),
+               "linear backward");
+}
+
 SplitFunction::SplitFunction(std::shared_ptr<Tensor> in, std::vector<std::shared_ptr<Tensor>> outs)
     : Input(std::move(in)), Outputs(outs.begin(), outs.end()) {}
 

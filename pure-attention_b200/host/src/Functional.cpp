@@ -88,6 +88,39 @@ std::shared_ptr<Tensor> mse_loss(const std::shared_ptr<Tensor>& preds,
   return loss;
 }
 
+void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
+            const std::shared_ptr<Tensor>& bias, uint32_t num_parts,
+            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream) {
+  const auto a = A->get_shape(), w = W->get_shape();
+  if (w.size() != 2) throw std::runtime_error("Linear: W (weights) must be 2D");
+  if (a.empty() || a.back() != w[0])
+    throw std::runtime_error("Linear: Dimension mismatch A[..., K] and W[K, N]");
+  const int K = static_cast<int>(w[0]), N = static_cast<int>(w[1]);
+  if (bias->numel() != static_cast<size_t>(N))
+    throw std::runtime_error("Linear: bias must have W's output dimension");
+  if (num_parts < 1 || num_parts > 3 || N % num_parts)
+    throw std::runtime_error("Linear: 1 to 3 parts, dividing the output dimension");
+  const int M = static_cast<int>(A->numel() / K);
+  const bool g = A->requires_grad() || W->requires_grad() || bias->requires_grad();
+  auto ps_ = a;
+  ps_.back() = static_cast<uint32_t>(N / num_parts);
+  std::vector<std::shared_ptr<Tensor>> mine;
+  std::vector<float*> outs;
+  for (uint32_t i = 0; i < num_parts; ++i) {
+    mine.push_back(std::make_shared<Tensor>(ps_, g, false));
+    outs.push_back(mine.back()->get_data_ptr());
+  }
+  Scratch ws(pa_linear_workspace_size(M, K, N), stream);
+  check_status(pa_linear_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(), outs.data(),
+                             static_cast<int>(num_parts), M, K, N, ws.get(), ws.size(), ps(stream)),
+               "Linear");
+  if (g) {
+    auto node = std::make_shared<LinearFunction>(A, W, bias, mine);
+    for (auto& p : mine) p->set_grad_fn(node);
+  }
+  parts.insert(parts.end(), mine.begin(), mine.end());
+}
+
 void split(const std::shared_ptr<Tensor>& A, uint32_t num_parts, int dim,
            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream) {
   auto shape = A->get_shape();

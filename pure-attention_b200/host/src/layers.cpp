@@ -25,11 +25,11 @@ Linear::Linear(uint32_t in_channels, uint32_t out_channels)
   core::pop_data_zeros(bias, stream());
 }
 
+// X W + bias in one fused projection (matmul and bias add of Linear.cpp:24-35).
 std::shared_ptr<core::Tensor> Linear::forward(const std::shared_ptr<core::Tensor>& input) {
-  std::shared_ptr<core::Tensor> xw, y;
-  core::matmul(input, weight, xw, stream());
-  core::matadd(xw, bias, y, stream());
-  return y;
+  std::vector<std::shared_ptr<core::Tensor>> out;
+  core::linear(input, weight, bias, 1, out, stream());
+  return out[0];
 }
 
 std::vector<std::shared_ptr<core::Tensor>> Linear::parameters() { return {weight, bias}; }
@@ -65,16 +65,16 @@ MultiheadAttention::MultiheadAttention(uint32_t e, uint32_t h)
   core::pop_data_zeros(out_proj_bias, stream());
 }
 
+// Self-attention: the in-projection writes Q, K, V directly (bias added in the
+// GEMM epilogue) and the out-projection adds its bias the same way - the
+// reference's matmul / bias add / split passes (MHA.cpp:50-77) fused.
 std::shared_ptr<core::Tensor> MultiheadAttention::forward(const std::shared_ptr<core::Tensor>& x) {
-  std::shared_ptr<core::Tensor> xw, proj, attn, o1, out;
-  core::matmul(x, in_proj_weight, xw, stream());
-  core::matadd(xw, in_proj_bias, proj, stream());
-  std::vector<std::shared_ptr<core::Tensor>> qkv;
-  core::split(proj, 3, -1, qkv, stream());
+  std::vector<std::shared_ptr<core::Tensor>> qkv, out;
+  std::shared_ptr<core::Tensor> attn;
+  core::linear(x, in_proj_weight, in_proj_bias, 3, qkv, stream());
   core::flash_attention(qkv[0], qkv[1], qkv[2], attn, static_cast<int>(num_heads), stream());
-  core::matmul(attn, out_proj_weight, o1, stream());
-  core::matadd(o1, out_proj_bias, out, stream());
-  return out;
+  core::linear(attn, out_proj_weight, out_proj_bias, 1, out, stream());
+  return out[0];
 }
 
 std::shared_ptr<core::Tensor> MultiheadAttention::forward(const std::shared_ptr<core::Tensor>& q,

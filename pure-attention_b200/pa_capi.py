@@ -26,6 +26,7 @@ EXPORTS = [
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
+    "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
     "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_bwd", "pa_adam_step",
@@ -68,6 +69,10 @@ _SIGS = {
     "pa_matmul": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_matmul_grad_x": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_matmul_grad_w": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
+    "pa_linear_workspace_size": (_sz, [_int] * 3),
+    "pa_linear_fwd": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp), _int, _int, _int, _int, _vp, _sz, _vp]),
+    "pa_linear_bwd": (_int, [_vp, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp, _int, _int, _int,
+                             _vp, _sz, _vp]),
     "pa_bias_add": (_int, [_vp] * 3 + [_int] * 2 + [_vp]),
     "pa_add": (_int, [_vp] * 3 + [_sz, _vp]),
     "pa_grad_accumulate": (_int, [_vp] * 2 + [_sz, _vp]),
@@ -273,6 +278,37 @@ def grad_accumulate(src, dst, n, stream=None):
 def bias_grad(dy, db, M, N, stream=None):
     _check("pa_bias_grad", load().pa_bias_grad(_ptr(dy), _ptr(db), M, N,
                                                _stream() if stream is None else stream))
+
+
+def linear_workspace_size(M, in_features, out_features):
+    return load().pa_linear_workspace_size(M, in_features, out_features)
+
+
+def _linear_ws(M, i, o, workspace, device):
+    if workspace is None:
+        import torch
+        workspace = torch.empty(linear_workspace_size(M, i, o), dtype=torch.uint8, device=device)
+    return workspace, workspace.numel() * workspace.element_size()
+
+
+def linear_fwd(x, w, bias, outs, M, in_features, out_features, workspace=None, stream=None):
+    """outs[c] = (x[M,in] w[in,out] + bias)[:, c*out/n : (c+1)*out/n] (bias may be None)."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    arr = (_vp * len(outs))(*[_ptr(o) for o in outs])
+    _check("pa_linear_fwd", load().pa_linear_fwd(_ptr(x), _ptr(w), _ptr(bias) if bias is not None else None,
+                                                 arr, len(outs), M, in_features, out_features,
+                                                 _ptr(ws), nb, _stream() if stream is None else stream))
+
+
+def linear_bwd(x, w, dy_parts, dx, dw, dbias, M, in_features, out_features, workspace=None,
+               stream=None):
+    """dx += dY w^T, dw += x^T dY, dbias += colsum(dY), dY = concat(dy_parts); any output may be None."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    arr = (_vp * len(dy_parts))(*[_ptr(t) for t in dy_parts])
+    opt = lambda t: _ptr(t) if t is not None else None
+    _check("pa_linear_bwd", load().pa_linear_bwd(_ptr(x), _ptr(w), arr, len(dy_parts), opt(dx), opt(dw),
+                                                 opt(dbias), M, in_features, out_features, _ptr(ws),
+                                                 nb, _stream() if stream is None else stream))
 
 
 def split_last_dim(inp, outs, rows, width, stream=None):

@@ -151,3 +151,46 @@ def test_split_and_concat_grad_match_oracle():
     gin = _cu(g0)
     pa_capi.concat_last_dim_grad(outs, gin, rows, w)
     np.testing.assert_allclose(_np(gin), oracle.concat_last_dim_grad(ref, g0), rtol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,IN,OUT,n", [
+    (8192, 512, 1536, 3),   # pre-LN block in-projection: Q, K, V written directly
+    (8192, 512, 512, 1),    # out-projection with bias
+    (100, 70, 48, 3),       # ragged: partial tiles, 16-column blocks
+    (300, 64, 96, 2),
+])
+def test_linear_fwd_matches_oracle(M, IN, OUT, n):
+    import oracle
+    import pa_capi
+    x = seeded_normal(M + 31, (M, IN))
+    w = seeded_normal(IN + 32, (IN, OUT))
+    bias = seeded_normal(OUT + 33, (OUT,))
+    outs = [torch.full((M, OUT // n), float("nan"), device="cuda") for _ in range(n)]
+    pa_capi.linear_fwd(_cu(x), _cu(w), _cu(bias), outs, M, IN, OUT)
+    assert pa_capi.device_status() == 0
+    ref = oracle.bias_add(oracle.matmul(x, w), bias)
+    for c in range(n):
+        assert rel_err(_np(outs[c]), ref[:, c * (OUT // n):(c + 1) * (OUT // n)]) < GEMM_TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,IN,OUT,n", [(8192, 512, 1536, 3), (100, 70, 48, 3), (256, 192, 320, 1)])
+def test_linear_bwd_accumulates_like_oracle(M, IN, OUT, n):
+    import oracle
+    import pa_capi
+    x = seeded_normal(M + 41, (M, IN))
+    w = seeded_normal(IN + 42, (IN, OUT))
+    parts = [seeded_normal(M + 43 + c, (M, OUT // n)) for c in range(n)]
+    dy = np.concatenate(parts, axis=1)
+    dx0, dw0, db0 = seeded_normal(1, (M, IN)), seeded_normal(2, (IN, OUT)), seeded_normal(3, (OUT,))
+    dx, dw, db = _cu(dx0), _cu(dw0), _cu(db0)
+    pa_capi.linear_bwd(_cu(x), _cu(w), [_cu(p) for p in parts], dx, dw, db, M, IN, OUT)
+    assert pa_capi.device_status() == 0
+    assert rel_err(_np(dx), oracle.matmul_grad_x(dy, w, dx0)) < GEMM_TOL
+    assert rel_err(_np(dw), oracle.matmul_grad_w(x, dy, dw0)) < GEMM_TOL
+    assert rel_err(_np(db), oracle.bias_grad(dy, db0)) < 1e-5  # fp32 column sums over M rows
+    # skipped outputs are left alone
+    dw2 = _cu(dw0)
+    pa_capi.linear_bwd(_cu(x), _cu(w), [_cu(p) for p in parts], None, dw2, None, M, IN, OUT)
+    assert rel_err(_np(dw2), oracle.matmul_grad_w(x, dy, dw0)) < GEMM_TOL
