@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--linear", action="store_true",
                     help="instead of the attention step: time the fused projection calls of the "
                          "MHA block (B8 L1024 E512 fp32) against the unfused call sequence")
+    ap.add_argument("--train", action="store_true",
+                    help="instead of the attention step: the data-parallel denoise training step "
+                         "(6 layers, E1024 H16 FFN4096, N2048, 8 sequences per GPU, fp32 weights), "
+                         "gradients averaged over the ranks with NCCL")
     return ap.parse_args()
 
 
@@ -268,12 +272,120 @@ def run_linear(args):
                       "steps": args.steps, "device_status": pa_capi.device_status()}))
 
 
+TRAIN = dict(layers=6, embed=1024, heads=16, ffn=4096, seq=2048, batch=8)
+
+
+def train_flops_per_gpu(layers, embed, heads, ffn, seq, batch):
+    """Model FLOPs of one training step on one GPU: projections and FFN
+    (fwd + dX + dW) plus attention fwd+bwd in the flash convention."""
+    tokens = batch * seq
+    gemm = 3 * 2 * tokens * (4 * embed * embed + 2 * embed * ffn)
+    attn = 14 * batch * heads * seq * seq * (embed // heads)
+    return layers * (gemm + attn)
+
+
+def run_train(args):
+    """Denoise training step (tests/main_denoise.py model, stacked) on N GPUs,
+    one process each; weak scaling (8 sequences per GPU)."""
+    import datetime
+    import numpy as np
+    import torch
+    import sharding
+    rank, world, local = sharding.dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import denoise
+    peak, peak_sus, _, peak_src = peaks()
+    tr = denoise.DenoiseTrainer(lr=1e-4, **TRAIN)
+    lift = denoise.embedding(TRAIN["embed"], 5)
+    rng = np.random.default_rng(5 + rank)
+    data = [tuple(torch.from_numpy(a).pin_memory()
+                  for a in denoise.denoise_batch(rng, TRAIN["batch"], TRAIN["seq"], lift))
+            for _ in range(2)]
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    warm = max(3, args.warmup)
+    for i in range(warm):
+        tr.step(*data[i % 2])
+    tr.load(*data[0])
+    torch.cuda.synchronize()
+    import PureAttention as pa
+    if pa.device_status() != 0:
+        raise SystemExit("device status reports a timed-out wait during warm-up")
+
+    def timed(fn):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return sharding.max_over_ranks(e0.elapsed_time(e1), dev)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms_res = timed(lambda i: tr.step_resident())
+    losses = []
+    ms_e2e = timed(lambda i: losses.append(tr.step(*data[i % 2])))
+    clk = clocks.stop()
+    ms_ar = None
+    if tr.reducer is not None:
+        ms_ar = timed(lambda i: tr.reducer())
+    status = pa.device_status()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    tokens = world * TRAIN["batch"] * TRAIN["seq"]
+    step_ms = ms_res / args.steps
+    flops = train_flops_per_gpu(**TRAIN)
+    tflops = flops / (step_ms * 1e-3) / 1e12
+    e2e_step = ms_e2e / args.steps
+    h2d = 2 * TRAIN["batch"] * TRAIN["seq"] * TRAIN["embed"] * 4
+    print(json.dumps({
+        "metric": "denoise training tokens/s (6 layers E1024 H16 FFN4096 N2048, 8 seq/GPU)",
+        "value": round(tokens / (step_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": warm, "ms_per_step": round(step_ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 weights and activations; GEMMs and attention on bf16 split planes",
+        "data": "synthetic denoise sequences (4 sinusoids lifted by a fixed Linear(1->1024) + noise)",
+        "config": {"workload": "denoise transformer training step", **TRAIN,
+                   "global_batch": TRAIN["batch"] * world, "parallelism": "dp%d" % world,
+                   "params": tr.num_parameters},
+        "model_tflops_per_gpu": round(tflops, 1),
+        "model_flops_per_gpu_step": flops,
+        "frac_of_sustained_peak": round(tflops / (peak_sus or peak), 4),
+        "peak_source": "%s sustained bf16 (cuBLAS)" % peak_src,
+        "allreduce_ms": None if ms_ar is None else round(ms_ar / args.steps, 3),
+        "allreduce_bytes": None if tr.reducer is None else tr.reducer.nbytes,
+        "e2e": {"value": round(tokens / (e2e_step * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                "ms_per_step": round(e2e_step, 3)},
+        "loss_first_last": [round(losses[0], 5), round(losses[-1], 5)],
+        "clocks": clk, "device_status": status}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference_arm(args)
     if args.linear:
         return run_linear(args)
+    if args.train:
+        return run_train(args)
     import torch
     import pa_capi
     import sharding

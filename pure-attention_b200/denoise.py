@@ -1,0 +1,249 @@
+"""Denoising-transformer training, data-parallel with one process per GPU.
+
+Model: the reference's denoise layer (tests/main_denoise.py:11-54) - pre-LN
+self-attention with a residual add, pre-LN feed-forward (Linear, ReLU, Linear)
+with a residual add, then a final LayerNorm - stacked `layers` deep and built
+from the PureAttention operators; MSE loss against the clean signal and Adam
+(src/core/Adam.cpp:28-59), as the reference's training loop does
+(tests/main_denoise.py:79-110).
+
+Data: each sequence is a sum of four sinusoids a*sin(f*t + phi), f ~ U(0.5, 8),
+phi ~ U(0, 2pi), a ~ U(0.2, 1), sampled at `seq` points of t in [0, 1); a fixed
+Linear(1 -> embed) map (weights and bias U(-1, 1), the same on every rank)
+lifts it to [batch, seq, embed]. The input adds N(0, noise^2) to that lift and
+the target is the clean lift, so output and target have the reference's
+[batch, seq, embed] shape (tests/main_denoise.py:69-77).
+
+Data parallelism: every rank builds the model from the same seed and rank 0's
+parameters are broadcast once, so all replicas start identical. Each rank runs
+forward and backward on its own sequences; `GradAllReduce` then averages the
+weight gradients over ranks with NCCL all-reduce on zero-copy views of the
+host tensors' gradient buffers, in buckets (per bucket: one gather into a flat
+buffer, one all-reduce, one scatter back), and every rank takes the same Adam
+step.
+
+Stream order: the operators run on the CUDA legacy default stream, which is
+also torch's default stream, so the torch copies and process-group collectives
+issued from the same thread are ordered with them without host syncs.
+"""
+import math
+
+import numpy as np
+
+import PureAttention as pa
+
+
+class FeedForward(pa.Module):
+    """Linear(embed, hidden) -> ReLU -> Linear(hidden, embed)
+    (tests/main_denoise.py:11-25)."""
+
+    def __init__(self, embed_dim, hidden_dim):
+        super().__init__()
+        self.fc1 = pa.Linear(embed_dim, hidden_dim)
+        self.relu = pa.ReLU()
+        self.fc2 = pa.Linear(hidden_dim, embed_dim)
+
+    def forward(self, x):
+        return self.fc2.forward(self.relu.forward(self.fc1.forward(x)))
+
+    def parameters(self):
+        return self.fc1.parameters() + self.fc2.parameters()
+
+
+class TransformerLayer(pa.Module):
+    """Pre-LN attention and feed-forward sublayers with residual adds and a
+    final LayerNorm (tests/main_denoise.py:27-54)."""
+
+    def __init__(self, embed_dim, num_heads, ffn_dim):
+        super().__init__()
+        self.mha = pa.MultiheadAttention(embed_dim, num_heads)
+        self.ln1 = pa.LayerNorm(embed_dim)
+        self.ffn = FeedForward(embed_dim, ffn_dim)
+        self.ln2 = pa.LayerNorm(embed_dim)
+        self.ln_final = pa.LayerNorm(embed_dim)
+
+    def forward(self, x):
+        x_norm = self.ln1.forward(x)
+        x = pa.add(x, self.mha.forward(x_norm, x_norm, x_norm))
+        x = pa.add(x, self.ffn.forward(self.ln2.forward(x)))
+        return self.ln_final.forward(x)
+
+    def parameters(self):
+        return (self.mha.parameters() + self.ln1.parameters() + self.ffn.parameters()
+                + self.ln2.parameters() + self.ln_final.parameters())
+
+
+class DenoiseTransformer(pa.Module):
+    def __init__(self, layers, embed_dim, num_heads, ffn_dim):
+        super().__init__()
+        self.layers = [TransformerLayer(embed_dim, num_heads, ffn_dim) for _ in range(layers)]
+
+    def forward(self, x):
+        for layer in self.layers:
+            x = layer.forward(x)
+        return x
+
+    def parameters(self):
+        return [p for layer in self.layers for p in layer.parameters()]
+
+
+def embedding(embed, seed):
+    """The fixed Linear(1 -> embed) lift: (weight, bias), U(-1, 1) each."""
+    rng = np.random.default_rng(seed)
+    return (rng.uniform(-1.0, 1.0, embed).astype(np.float32),
+            rng.uniform(-1.0, 1.0, embed).astype(np.float32))
+
+
+def denoise_batch(rng, batch, seq, lift, noise=0.1):
+    """(noisy input, clean target), float32 [batch, seq, embed] each."""
+    t = np.arange(seq, dtype=np.float64) / seq
+    f = rng.uniform(0.5, 8.0, (batch, 4, 1))
+    phi = rng.uniform(0.0, 2.0 * math.pi, (batch, 4, 1))
+    a = rng.uniform(0.2, 1.0, (batch, 4, 1))
+    signal = (a * np.sin(f * t + phi)).sum(axis=1)                  # [batch, seq]
+    w, b = lift
+    clean = (signal[..., None] * w + b).astype(np.float32)          # [batch, seq, embed]
+    noisy = clean + rng.normal(0.0, noise, clean.shape).astype(np.float32)
+    return noisy, clean
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def device_view(t):
+    """torch view (no copy) of a PureAttention tensor's data."""
+    return _torch().as_tensor(t, device="cuda")
+
+
+def grad_view(t):
+    """torch view (no copy) of a PureAttention tensor's gradient."""
+    return _torch().as_tensor(t.grad_view(), device="cuda")
+
+
+class GradAllReduce:
+    """Average gradients over the ranks of a process group, in buckets.
+
+    `grads` are flat-viewable torch tensors (views of the gradient buffers).
+    They are packed into buckets of at most `bucket_bytes` (a tensor larger
+    than that gets a bucket of its own) in reverse order, the order in which
+    backward finishes them. Each bucket owns a flat buffer; a call gathers the
+    bucket into it, all-reduces it and scatters the averaged values back.
+    NCCL averages in the collective (ReduceOp.AVG); other backends sum and the
+    scatter divides by the world size.
+    """
+
+    def __init__(self, grads, bucket_bytes=25 << 20, group=None):
+        torch = _torch()
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.world = dist.get_world_size(group)
+        self.avg_in_collective = dist.get_backend(group) == "nccl"
+        self.buckets = []
+        cur, cur_bytes = [], 0
+        for g in reversed(list(grads)):
+            nb = g.numel() * g.element_size()
+            if cur and cur_bytes + nb > bucket_bytes:
+                self.buckets.append(cur)
+                cur, cur_bytes = [], 0
+            cur.append(g.view(-1))
+            cur_bytes += nb
+        if cur:
+            self.buckets.append(cur)
+        self.flat = [torch.empty(sum(v.numel() for v in b), dtype=b[0].dtype, device=b[0].device)
+                     for b in self.buckets]
+        self.sizes = [[v.numel() for v in b] for b in self.buckets]
+
+    def __call__(self):
+        torch = _torch()
+        op = self.dist.ReduceOp.AVG if self.avg_in_collective else self.dist.ReduceOp.SUM
+        for views, flat, sizes in zip(self.buckets, self.flat, self.sizes):
+            torch.cat(views, out=flat)
+            self.dist.all_reduce(flat, op=op, group=self.group)
+            if not self.avg_in_collective:
+                flat.div_(self.world)
+            torch._foreach_copy_(views, list(torch.split(flat, sizes)))
+
+    @property
+    def nbytes(self):
+        return sum(f.numel() * f.element_size() for f in self.flat)
+
+
+class DenoiseTrainer:
+    """One replica of the data-parallel denoise training loop.
+
+    step(x, t) takes one batch from (pinned) host memory: copies it to the
+    device, runs forward, MSE, backward, the gradient all-reduce (when a
+    process group with more than one rank is up) and Adam, and returns the
+    loss as a float. step_resident() runs the same step on the batch already
+    on the device and returns the loss tensor without a host read.
+    """
+
+    def __init__(self, layers=6, embed=1024, heads=16, ffn=4096, seq=2048, batch=8, lr=1e-4,
+                 seed=5, bucket_bytes=25 << 20, group=None):
+        import torch.distributed as dist
+        self.shape = (batch, seq, embed)
+        pa.set_seed(seed)  # same initial weights on every rank
+        self.model = DenoiseTransformer(layers, embed, heads, ffn)
+        self.params = self.model.parameters()
+        self.opt = pa.Adam(self.params, lr=lr)
+        self.criterion = pa.MSE()
+        self.x = pa.Tensor(list(self.shape), False)
+        self.t = pa.Tensor(list(self.shape), False)
+        self.x_dev, self.t_dev = device_view(self.x), device_view(self.t)
+        self.reducer = None
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+            src = dist.get_global_rank(group, 0) if group is not None else 0
+            for p in self.params:
+                dist.broadcast(device_view(p), src=src, group=group)
+            self.reducer = GradAllReduce([grad_view(p) for p in self.params], bucket_bytes, group)
+
+    @property
+    def num_parameters(self):
+        return sum(int(np.prod(p.shape())) for p in self.params)
+
+    def load(self, x_host, t_host):
+        """Queue the copies of one batch (torch CPU tensors, pinned for
+        asynchronous copies) into the input tensors."""
+        self.x_dev.view(x_host.shape).copy_(x_host, non_blocking=True)
+        self.t_dev.view(t_host.shape).copy_(t_host, non_blocking=True)
+
+    def step_resident(self):
+        self.opt.zero_grad()
+        out = self.model.forward(self.x)
+        loss = self.criterion(out, self.t)
+        loss.backward()
+        del out
+        if self.reducer is not None:
+            self.reducer()
+        self.opt.step()
+        return loss  # holds this step's graph until the caller drops it
+
+    def step(self, x_host, t_host):
+        self.load(x_host, t_host)
+        return float(device_view(self.step_resident()).item())
+
+    def save(self, path):
+        """Parameters, Adam moments and step count to an .npz file."""
+        m, v = self.opt.state()
+        arrays = {}
+        for i, p in enumerate(self.params):
+            arrays["p%d" % i] = device_view(p).cpu().numpy()
+            arrays["m%d" % i] = device_view(m[i]).cpu().numpy()
+            arrays["v%d" % i] = device_view(v[i]).cpu().numpy()
+        np.savez(path, step=np.int64(self.opt.step_count), **arrays)
+
+    def restore(self, path):
+        torch = _torch()
+        m, v = self.opt.state()
+        with np.load(path) as z:
+            if sum(1 for k in z.files if k.startswith("p")) != len(self.params):
+                raise ValueError("checkpoint holds a different number of parameters")
+            for i, p in enumerate(self.params):
+                for name, t in (("p", p), ("m", m[i]), ("v", v[i])):
+                    a = z["%s%d" % (name, i)]
+                    if list(a.shape) != list(t.shape()):
+                        raise ValueError("checkpoint shape mismatch at %s%d" % (name, i))
+                    device_view(t).copy_(torch.from_numpy(a))
+            self.opt.step_count = int(z["step"])

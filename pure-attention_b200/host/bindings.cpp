@@ -37,6 +37,28 @@ class PyModule : public layers::Module {
 PYBIND11_MODULE(PureAttention, m) {
   m.doc() = "Pure-Attention operator surface over sm_100a kernels";
 
+  // Zero-copy views for other CUDA libraries (torch.as_tensor, cupy): the
+  // gradient of a tensor, kept alive by the view. Not in the reference's surface.
+  struct GradView {
+    std::shared_ptr<Tensor> owner;
+  };
+  auto cai = [](float* ptr, const std::vector<uint32_t>& shape) {
+    py::dict d;
+    py::tuple sh(shape.size());
+    for (size_t i = 0; i < shape.size(); ++i) sh[i] = shape[i];
+    d["shape"] = sh;
+    d["typestr"] = "<f4";
+    d["data"] = py::make_tuple(reinterpret_cast<uintptr_t>(ptr), false);
+    d["version"] = 3;
+    d["strides"] = py::none();
+    return d;
+  };
+  py::class_<GradView>(m, "GradView")
+      .def_property_readonly("__cuda_array_interface__", [cai](const GradView& g) {
+        if (!g.owner->get_gradient_ptr()) throw std::runtime_error("tensor has no gradient");
+        return cai(g.owner->get_gradient_ptr(), g.owner->get_shape());
+      });
+
   py::class_<Tensor, std::shared_ptr<Tensor>>(m, "Tensor")
       .def(py::init([](std::vector<uint32_t> shape, bool requires_grad) {
              return std::make_shared<Tensor>(shape, requires_grad);
@@ -48,6 +70,10 @@ PYBIND11_MODULE(PureAttention, m) {
       .def("grad_to_host", &Tensor::grad_to_host)
       .def("shape", &Tensor::get_shape)
       .def("zero_grad", &Tensor::zero_grad)
+      .def_property_readonly("__cuda_array_interface__",
+                             [cai](const Tensor& t) { return cai(t.get_data_ptr(), t.get_shape()); })
+      .def("grad_view", [](const std::shared_ptr<Tensor>& t) { return GradView{t}; },
+           "Zero-copy view of the gradient (has __cuda_array_interface__)")
       .def("get_grad_stats", [](const Tensor& t) {
         const std::vector<float> g = t.grad_to_host();
         py::dict d;
@@ -109,7 +135,12 @@ PYBIND11_MODULE(PureAttention, m) {
            py::arg("params"), py::arg("lr") = 0.001f, py::arg("beta1") = 0.9f,
            py::arg("beta2") = 0.999f, py::arg("eps") = 1e-8f)
       .def("step", &optim::Adam::step)
-      .def("zero_grad", &optim::Adam::zero_grad);
+      .def("zero_grad", &optim::Adam::zero_grad)
+      .def_property("step_count", &optim::Adam::steps, &optim::Adam::set_steps,
+                    "Steps taken (drives the bias corrections); for checkpoints")
+      .def("state", [](const optim::Adam& a) {
+        return py::make_tuple(a.first_moments(), a.second_moments());
+      }, "(first moments, second moments): one Tensor per parameter, for checkpoints");
 
   m.def("fill_normal", [](const std::shared_ptr<Tensor>& t, float std_dev) {
     core::pop_data_normal(t, std_dev, CudaContext::getStream());

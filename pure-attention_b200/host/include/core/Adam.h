@@ -11,6 +11,11 @@ class Adam {
        float beta2 = 0.999f, float eps = 1e-8f);
   void step();
   void zero_grad();
+  // Optimizer state for checkpoints (not in the reference's interface).
+  int steps() const { return step_count; }
+  void set_steps(int n) { step_count = n; }
+  const std::vector<std::shared_ptr<core::Tensor>>& first_moments() const { return m_states; }
+  const std::vector<std::shared_ptr<core::Tensor>>& second_moments() const { return v_states; }
 
  private:
   std::vector<std::shared_ptr<core::Tensor>> parameters;

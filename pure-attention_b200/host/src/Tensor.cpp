@@ -17,6 +17,7 @@ void check_status(int status, const char* what) {
 
 static float32_t* device_alloc(size_t n, cudaStream_t s) {
   void* p = nullptr;
+  retain_pool_memory();
   const cudaError_t e = cudaMallocAsync(&p, std::max<size_t>(n, 1) * sizeof(float32_t), s);
   if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA Error: ") + cudaGetErrorString(e));
   return static_cast<float32_t*>(p);

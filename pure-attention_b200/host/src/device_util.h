@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <cstddef>
+#include <cstdint>
 #include <stdexcept>
 #include <string>
 #include "core/Context.h"
@@ -10,11 +11,29 @@
 
 namespace core {
 
+// The device's default memory pool hands freed memory back to the driver at
+// every synchronisation unless its release threshold is raised, and the next
+// cudaMallocAsync then maps it again. A training step frees and re-allocates
+// its activations every step, so the pool keeps what it has (this process's
+// pool only; nothing outlives the process).
+inline void retain_pool_memory() {
+  static thread_local int set_for = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev == set_for) return;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  set_for = dev;
+}
+
 // Stream-ordered device scratch (cudaMallocAsync / cudaFreeAsync on `s`).
 class Scratch {
  public:
   Scratch(size_t bytes, cudaStream_t s) : s_(s), n_(bytes) {
     if (bytes) {
+      retain_pool_memory();
       const cudaError_t e = cudaMallocAsync(&p_, bytes, s);
       if (e != cudaSuccess)
         throw std::runtime_error(std::string("CUDA Error: ") + cudaGetErrorString(e));

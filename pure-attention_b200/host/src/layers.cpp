@@ -80,6 +80,8 @@ std::shared_ptr<core::Tensor> MultiheadAttention::forward(const std::shared_ptr<
 std::shared_ptr<core::Tensor> MultiheadAttention::forward(const std::shared_ptr<core::Tensor>& q,
                                                           const std::shared_ptr<core::Tensor>& k,
                                                           const std::shared_ptr<core::Tensor>& v) {
+  // forward(x, x, x) (how the reference's denoise layer calls it) is self-attention
+  if (q == k && k == v) return forward(q);
   std::vector<std::shared_ptr<core::Tensor>> w, b;
   core::split(in_proj_weight, 3, 1, w, stream());
   core::split(in_proj_bias, 3, 1, b, stream());

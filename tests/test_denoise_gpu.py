@@ -1,0 +1,205 @@
+"""The denoise training step on one GPU: a two-layer denoise transformer
+(tests/main_denoise.py:27-54 stacked) forward + MSE + backward against torch
+float64 with the same weights (loss within 1e-4, every parameter gradient and
+the input gradient within 1e-3 norm-wise); the trainer reduces the loss on the
+synthetic denoise data; a checkpoint restores parameters, Adam moments and
+step count exactly; two NCCL ranks with half the batch each take the same
+steps as one rank with the whole batch (needs two GPUs)."""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import PKG, REPO, rel_err
+
+torch = pytest.importorskip("torch")
+F32_TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def dn():
+    import denoise
+    return denoise
+
+
+def _h(t):
+    return np.asarray(t.to_host(), dtype=np.float64).reshape(t.shape())
+
+
+def _g(t):
+    return np.asarray(t.grad_to_host(), dtype=np.float64).reshape(t.shape())
+
+
+def _ref_layer(x, P, H):
+    """float64 torch restatement of one denoise layer; P = its 14 parameters
+    in TransformerLayer.parameters() order."""
+    wi, bi, wo, bo, g1, c1, w1, b1, w2, b2, g2, c2, g3, c3 = P
+    B, L, E = x.shape
+    D = E // H
+
+    def ln(v, g, c):
+        mu = v.mean(-1, keepdim=True)
+        var = ((v - mu) ** 2).mean(-1, keepdim=True)
+        return (v - mu) / torch.sqrt(var + 1e-5) * g + c
+
+    xn = ln(x, g1, c1)
+    qkv = xn @ wi + bi
+    q, k, v = (qkv[..., i * E:(i + 1) * E].reshape(B, L, H, D).transpose(1, 2) for i in range(3))
+    s = q @ k.transpose(-1, -2) / math.sqrt(D)
+    o = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B, L, E)
+    x = x + (o @ wo + bo)
+    h = torch.relu(ln(x, g2, c2) @ w1 + b1) @ w2 + b2
+    return ln(x + h, g3, c3)
+
+
+@pytest.mark.gpu
+def test_two_layer_denoise_model_matches_float64(dn):
+    import PureAttention as pa
+    B, L, E, H, F = 2, 160, 128, 4, 256
+    pa.set_seed(77)
+    model = dn.DenoiseTransformer(2, E, H, F)
+    params = model.parameters()
+    assert len(params) == 28
+    # non-trivial LayerNorm affine parameters and biases
+    rng = np.random.default_rng(8)
+    for p in params:
+        if p.shape()[0] == 1:
+            n = p.shape()[1]
+            base = 1.0 if np.allclose(_h(p), 1.0) else 0.0
+            p.to_device((base + 0.1 * rng.standard_normal(n)).astype(np.float32).tolist())
+    lift = dn.embedding(E, 5)
+    xn, tn = dn.denoise_batch(np.random.default_rng(5), B, L, lift)
+    X = pa.Tensor([B, L, E], True)
+    X.to_device(xn.ravel().tolist())
+    T = pa.Tensor([B, L, E], False)
+    T.to_device(tn.ravel().tolist())
+    loss = pa.MSE()(model.forward(X), T)
+    loss.backward()
+    assert pa.device_status() == 0
+
+    tp = [torch.tensor(_h(p), dtype=torch.float64, requires_grad=True) for p in params]
+    tx = torch.tensor(xn, dtype=torch.float64, requires_grad=True)
+    y = tx
+    for i in range(2):
+        y = _ref_layer(y, tp[14 * i:14 * (i + 1)], H)
+    tl = torch.mean((y - torch.tensor(tn, dtype=torch.float64)) ** 2)
+    tl.backward()
+    assert abs(_h(loss)[0] - tl.item()) < 1e-4 * tl.item()
+    errs = {"dX": rel_err(_g(X), tx.grad.numpy())}
+    for i, (p, q) in enumerate(zip(params, tp)):
+        errs["p%d%s" % (i, p.shape())] = rel_err(_g(p), q.grad.numpy())
+    print("denoise model relative errors:", errs)
+    for name, e in errs.items():
+        assert e < F32_TOL, (name, e)
+
+
+def _pinned(a):
+    return torch.from_numpy(a).pin_memory()
+
+
+SMALL = dict(layers=2, embed=128, heads=4, ffn=256, seq=256, batch=4)
+
+
+@pytest.mark.gpu
+def test_trainer_reduces_denoise_loss(dn):
+    tr = dn.DenoiseTrainer(lr=1e-3, **SMALL)
+    lift = dn.embedding(SMALL["embed"], 5)
+    rng = np.random.default_rng(5)
+    data = [tuple(_pinned(a) for a in dn.denoise_batch(rng, SMALL["batch"], SMALL["seq"], lift))
+            for _ in range(4)]
+    losses = [tr.step(*data[i % 4]) for i in range(60)]
+    import PureAttention as pa
+    assert pa.device_status() == 0
+    assert all(np.isfinite(losses))
+    first, last = np.mean(losses[:4]), np.mean(losses[-4:])
+    print("denoise loss: first %.4f last %.4f" % (first, last))
+    assert last < 0.5 * first
+
+
+@pytest.mark.gpu
+def test_checkpoint_restores_training_state(dn, tmp_path):
+    lift = dn.embedding(SMALL["embed"], 5)
+    rng = np.random.default_rng(9)
+    data = [tuple(_pinned(a) for a in dn.denoise_batch(rng, SMALL["batch"], SMALL["seq"], lift))
+            for _ in range(3)]
+    a = dn.DenoiseTrainer(lr=1e-3, seed=5, **SMALL)
+    for i in range(3):
+        a.step(*data[i])
+    path = os.path.join(tmp_path, "ckpt.npz")
+    a.save(path)
+    la = [a.step(*data[i]) for i in range(3)]
+    b = dn.DenoiseTrainer(lr=1e-3, seed=6, **SMALL)  # different initial weights
+    b.restore(path)
+    assert b.opt.step_count == 3
+    lb = [b.step(*data[i]) for i in range(3)]
+    assert la[0] == lb[0]  # the forward pass of restored weights is bit-identical
+    np.testing.assert_allclose(lb, la, rtol=1e-4)
+    with pytest.raises(ValueError):
+        dn.DenoiseTrainer(lr=1e-3, **dict(SMALL, layers=1)).restore(path)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _dp_worker(rank, world, port, out_dir):
+    import sys
+    for p in (REPO, PKG):
+        sys.path.insert(0, p)
+    import datetime
+    import torch as th
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_DEBUG="WARN")
+    th.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=th.device("cuda", rank))
+    try:
+        import denoise as d
+        cfg = dict(SMALL, batch=SMALL["batch"] // world)
+        tr = d.DenoiseTrainer(lr=1e-3, **cfg)
+        x, t = d.denoise_batch(np.random.default_rng(11), SMALL["batch"], SMALL["seq"],
+                               d.embedding(SMALL["embed"], 5))
+        n = cfg["batch"]
+        xs, ts = (th.from_numpy(np.ascontiguousarray(a[rank * n:(rank + 1) * n])).pin_memory()
+                  for a in (x, t))
+        for _ in range(3):
+            tr.step(xs, ts)
+        th.cuda.synchronize()
+        np.savez(os.path.join(out_dir, "dp%d.npz" % rank),
+                 *[d.device_view(p).cpu().numpy() for p in tr.params])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_rank_data_parallel_matches_one_rank(dn, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, world, port, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    tr = dn.DenoiseTrainer(lr=1e-3, **SMALL)
+    x, t = dn.denoise_batch(np.random.default_rng(11), SMALL["batch"], SMALL["seq"],
+                            dn.embedding(SMALL["embed"], 5))
+    for _ in range(3):
+        tr.step(_pinned(x), _pinned(t))
+    ref = [dn.device_view(p).cpu().numpy() for p in tr.params]
+    outs = [np.load(os.path.join(tmp_path, "dp%d.npz" % r)) for r in range(world)]
+    for i, want in enumerate(ref):
+        np.testing.assert_array_equal(outs[0]["arr_%d" % i], outs[1]["arr_%d" % i])
+        assert rel_err(outs[0]["arr_%d" % i], want) < 1e-3, i
