@@ -55,6 +55,20 @@ typedef struct pa_attn_desc {
   float softmax_scale; /* <= 0 selects 1/sqrt(head_dim) */
 } pa_attn_desc;
 
+/* Arithmetic of the fp32 entry points (pa_matmul*, pa_linear_*, and
+ * pa_attn_fwd / pa_attn_bwd with dtype PA_F32 and head_dim 64), set per
+ * calling thread:
+ *   PA_F32_MATH_SPLIT3 (default): operands split into bf16 hi/lo planes and
+ *     every product taken as hi*hi + hi*lo + lo*hi (fp32-level accuracy,
+ *     within 1e-3 of float64 where the reference computes in fp32);
+ *   PA_F32_MATH_BF16: operands rounded to bf16, one product, fp32 accumulation
+ *     and fp32 storage (mixed-precision training; about 3x fewer tensor-core
+ *     cycles and half the operand traffic).
+ * Not in the reference, which computes every product in fp32 SIMT code. */
+typedef enum pa_f32_math { PA_F32_MATH_SPLIT3 = 0, PA_F32_MATH_BF16 = 1 } pa_f32_math;
+int pa_set_f32_math(int mode); /* PA_OK, or PA_ERR_UNSUPPORTED for an unknown mode */
+int pa_get_f32_math(void);
+
 /* Library information and status. */
 int pa_abi_version(void);
 const char* pa_status_string(int status);
@@ -122,6 +136,16 @@ int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const 
                       const float* gamma, float* dx, float* dgamma, float* dbeta, uint32_t M,
                       uint32_t N, void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
+/* As pa_layer_norm_bwd, but dx is accumulated (dx += dL/dx), for an input that
+ * also feeds a residual branch whose gradient is already in dx: no temporary
+ * and no extra add pass. (The reference's LayerNorm node hands the input's
+ * gradient buffer to the overwriting kernel, source/core/Autograd.cpp:257-280,
+ * which drops the other consumers' contributions.) */
+int pa_layer_norm_bwd_accumulate(const float* dy, const float* x, const float* mean,
+                                 const float* rstd, const float* gamma, float* dx, float* dgamma,
+                                 float* dbeta, uint32_t M, uint32_t N, void* workspace,
+                                 size_t workspace_bytes, pa_stream_t stream);
+
 /* ---------------------------------------------------------------- matmul */
 
 /* fp32 GEMMs on the tensor cores: operands are split into bf16 hi/lo planes
@@ -167,6 +191,20 @@ int pa_linear_bwd(const float* X, const float* W, const float* const* dy_parts, 
                   float* dX, float* dW, float* dbias, int M, int in_features, int out_features,
                   void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
+/* Projection followed by a ReLU, Y = max(0, X W + bias) [M, out], the clamp in
+ * the GEMM epilogue (the reference runs Linear then ReLU: matmul, matadd and
+ * ReLU_kernel.cu:4-12 passes, tests/main_denoise.py:18-22). Its backward takes
+ * that Y and the gradient dY of Y: dY is masked by Y > 0 while it is gathered
+ * into the GEMM operands (ReLU_backward_kernel.cu:4-10 folded in), then
+ * dX += dZ W^T, dW += X^T dZ, dbias += colsum(dZ) with dZ = dY * (Y > 0).
+ * Same workspace as pa_linear_fwd / pa_linear_bwd. */
+int pa_linear_relu_fwd(const float* X, const float* W, const float* bias, float* Y, int M,
+                       int in_features, int out_features, void* workspace, size_t workspace_bytes,
+                       pa_stream_t stream);
+int pa_linear_relu_bwd(const float* X, const float* W, const float* Y, const float* dY, float* dX,
+                       float* dW, float* dbias, int M, int in_features, int out_features,
+                       void* workspace, size_t workspace_bytes, pa_stream_t stream);
+
 /* ---------------------------------------------------------------- elementwise */
 
 /* out[M,N] = A[M,N] + bias[N]. Replaces launch_matadd_tiled (Launchers.cuh:25-32). */
@@ -210,6 +248,13 @@ int pa_mse_bwd(const float* pred, const float* target, const float* dloss, float
 int pa_adam_step(float* param, const float* grad, float* m, float* v, size_t n, float lr,
                  float beta1, float beta2, float eps, float bias_corr1, float bias_corr2,
                  pa_stream_t stream);
+/* The same update for `count` tensors (host arrays of device pointers and
+ * sizes) in one launch per 48 tensors, instead of the reference's launch per
+ * parameter (Adam.cpp:28-59). Elementwise results equal pa_adam_step's. */
+int pa_adam_step_multi(float* const* params, const float* const* grads, float* const* m,
+                       float* const* v, const size_t* sizes, int count, float lr, float beta1,
+                       float beta2, float eps, float bias_corr1, float bias_corr2,
+                       pa_stream_t stream);
 /* x[i] ~ N(0, std_dev^2) from a counter-based generator keyed by seed
  * (reproducible). Replaces launch_normal_population (Launchers.cuh:56-62),
  * which seeded from the clock. */

@@ -35,6 +35,7 @@
 // head dim padded to 64) and every product is hi*hi + hi*lo + lo*hi, three
 // chained MMAs; P and dS are split the same way. In TMEM the hi and lo halves
 // of each 16-query K-step sit in adjacent 8-column groups (16k, 16k + 8).
+#include <type_traits>
 #include "host_launchers.h"
 
 namespace pa {
@@ -655,11 +656,14 @@ __device__ __forceinline__ void dq_reduce_own(const uint32_t (&own)[16], float* 
                      __uint_as_float(own[4 * v + 2 * a + 1]));
 }
 
+// OutT: dK / dV storage, __nv_bfloat16 (bf16 tensors) or float (fp32 tensors
+// computed in the bf16 math mode).
+template <typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1)
     attn_bwd_d64_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                         const __grid_constant__ CUtensorMap mapV,
                         const __grid_constant__ CUtensorMap mapdO, float* __restrict__ dq_acc,
-                        __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                        OutT* __restrict__ dk, OutT* __restrict__ dv,
                         const uint8_t* __restrict__ ext, int L, int Lp, int H, float scale,
                         float scale_log2, int accumulate, uint32_t* status) {
   using C = Bwd64Cfg;
@@ -969,9 +973,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       uint32_t o[32];
       tmem_ld32(tmem + (is_dv ? C::T_DV : C::T_DK) + lane_base + c * 32, o);
       tmem_ld_wait();
-      if (valid) {
+      if (valid && std::is_same<OutT, float>::value) {
         const float mul = is_dv ? 1.f : scale;
-        __nv_bfloat16* dst =
+        float4* d4 = reinterpret_cast<float4*>((is_dv ? dv : dk) +
+                                               ((static_cast<size_t>(b) * L + key) * H + h) * 64 +
+                                               c * 32);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float4 f = make_float4(__uint_as_float(o[4 * u]) * mul, __uint_as_float(o[4 * u + 1]) * mul,
+                                 __uint_as_float(o[4 * u + 2]) * mul,
+                                 __uint_as_float(o[4 * u + 3]) * mul);
+          if (accumulate) {
+            const float4 prev = d4[u];
+            f.x += prev.x; f.y += prev.y; f.z += prev.z; f.w += prev.w;
+          }
+          d4[u] = f;
+        }
+      } else if (valid) {
+        const float mul = is_dv ? 1.f : scale;
+        OutT* dst =
             (is_dv ? dv : dk) + ((static_cast<size_t>(b) * L + key) * H + h) * 64 + c * 32;
         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -1168,11 +1188,10 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
     using C64 = Bwd64Cfg;
     grid.x = (grid.x + 1) & ~1u;  // clusters of two key tiles (a tile past L has no keys)
     static uint64_t attr64 = 0;
-    ensure_smem_attr(attn_bwd_d64_kernel, C64::SMEM, attr64);
-    attn_bwd_d64_kernel<<<grid, C64::THREADS, C64::SMEM, stream>>>(
-        m[0], m[1], m[2], m[3], dq_acc, static_cast<__nv_bfloat16*>(dk),
-        static_cast<__nv_bfloat16*>(dv), ext, sh.L, Lp, sh.H, sh.scale, sh.scale * kLog2e,
-        accumulate, status);
+    ensure_smem_attr(attn_bwd_d64_kernel<T>, C64::SMEM, attr64);
+    attn_bwd_d64_kernel<T><<<grid, C64::THREADS, C64::SMEM, stream>>>(
+        m[0], m[1], m[2], m[3], dq_acc, static_cast<T*>(dk), static_cast<T*>(dv), ext, sh.L, Lp,
+        sh.H, sh.scale, sh.scale * kLog2e, accumulate, status);
   } else {
     static uint64_t attr = 0;
     ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr);
@@ -1218,11 +1237,13 @@ int launch_attn_bwd_bf16(const AttnShape& sh, const void* q, const void* k, cons
 
 // fp32 path: bf16 hi/lo planes of q, k, v, dO (head dim padded to 64), then
 // the statistics block.
+// (The bf16 math mode uses the hi planes only, plus the key-extension tiles
+// of the d64 kernel; the size covers both modes.)
 size_t attn_bwd_workspace_bytes_f32(const AttnShape& sh) {
   const int Dp = f32_plane_dim(sh.D);
   if (Dp < 0) return 0;
   const size_t plane = up256(static_cast<size_t>(sh.B) * sh.L * sh.H * Dp * 2);
-  return 8 * plane + stats_bytes(sh, Dp);
+  return 8 * plane + stats_bytes(sh, Dp, sh.D == 64);
 }
 
 int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v,
@@ -1238,6 +1259,18 @@ int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const
   AttnShape ps = sh;
   ps.D = Dp;
   CUtensorMap m[8];
+  if (sh.D == 64 && f32_math() == PA_F32_MATH_BF16) {
+    // one bf16 plane per operand, the bf16 d64 kernel with fp32 dK / dV
+    for (int i = 0; i < 4; ++i) {
+      uint8_t* hi = w + (2 * i) * plane;
+      const int st = launch_split_planes(src[i], hi, nullptr, rows, sh.D, Dp, stream);
+      if (st != PA_OK) return st;
+      if (!make_qkv_map(&m[i], hi, ps, 128)) return PA_ERR_ALIGN;
+      m[4 + i] = m[i];
+    }
+    return run_bwd<64, false, float>(sh, m, o, dO, lse, dq, dk, dv, accumulate, w + 8 * plane,
+                                     status, stream);
+  }
   for (int i = 0; i < 4; ++i) {
     uint8_t* hi = w + (2 * i) * plane;
     uint8_t* lo = w + (2 * i + 1) * plane;

@@ -30,6 +30,7 @@
 // The row max is kept in the log2 domain and only raised when a new tile's max
 // exceeds it by more than 8 (a factor 256): O and the row sum are rescaled
 // then, and otherwise P entries may reach 2^8, which fp32/bf16 hold exactly.
+#include <type_traits>
 #include "host_launchers.h"
 
 namespace pa {
@@ -305,7 +306,7 @@ __global__ void __launch_bounds__(384, 1)
         uint32_t o[32];
         tmem_ld32(tO + c * 32, o);
         tmem_ld_wait();
-        if constexpr (SPLIT) {
+        if constexpr (std::is_same<OutT, float>::value) {
           if (row < L && c * 32 < d_out) {
             float4* dst = reinterpret_cast<float4*>(orow + c * 32);
 #pragma unroll
@@ -389,14 +390,24 @@ int launch_attn_fwd_f32(const AttnShape& sh, const void* q, const void* k, const
   uint8_t* w = static_cast<uint8_t*>(ws);
   const float* src[3] = {static_cast<const float*>(q), static_cast<const float*>(k),
                          static_cast<const float*>(v)};
+  const bool bf16_math = sh.D == 64 && f32_math() == PA_F32_MATH_BF16;
   for (int i = 0; i < 3; ++i) {
-    const int st = launch_split_planes(src[i], w + (2 * i) * up, w + (2 * i + 1) * up, rows, sh.D,
-                                       Dp, stream);
+    const int st = launch_split_planes(src[i], w + (2 * i) * up,
+                                       bf16_math ? nullptr : w + (2 * i + 1) * up, rows, sh.D, Dp,
+                                       stream);
     if (st != PA_OK) return st;
   }
   AttnShape ps = sh;
   ps.D = Dp;
   CUtensorMap m[6];
+  if (sh.D == 64 && f32_math() == PA_F32_MATH_BF16) {
+    // bf16 math: the hi planes alone (bf16 roundings of q, k, v), bf16 kernel, fp32 O
+    for (int i = 0; i < 3; ++i) {
+      if (!make_qkv_map(&m[i], w + (2 * i) * up, ps, 128)) return PA_ERR_ALIGN;
+      m[3 + i] = m[i];
+    }
+    return launch_fwd<64, false, float>(ps, m, o, lse, 64, status, stream);
+  }
   // m[0..2] = hi planes of q, k, v; m[3..5] = lo planes
   for (int i = 0; i < 3; ++i)
     if (!make_qkv_map(&m[i], w + (2 * i) * up, ps, 128) ||

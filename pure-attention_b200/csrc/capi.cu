@@ -48,6 +48,13 @@ int check_attn(const pa_attn_desc* d, pa::AttnShape* sh) {
 
 extern "C" {
 
+int pa_set_f32_math(int mode) {
+  if (mode != PA_F32_MATH_SPLIT3 && mode != PA_F32_MATH_BF16) return PA_ERR_UNSUPPORTED;
+  pa::set_f32_math(mode);
+  return PA_OK;
+}
+int pa_get_f32_math(void) { return pa::f32_math(); }
+
 int pa_abi_version(void) { return PA_ABI_VERSION; }
 
 const char* pa_status_string(int s) {
@@ -167,9 +174,10 @@ size_t pa_layer_norm_bwd_workspace_size(uint32_t M, uint32_t N) {
   return pa::layer_norm_bwd_workspace_bytes(M, N);
 }
 
-int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
-                      const float* gamma, float* dx, float* dgamma, float* dbeta, uint32_t M,
-                      uint32_t N, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+static int layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                          const float* gamma, float* dx, float* dgamma, float* dbeta, uint32_t M,
+                          uint32_t N, void* workspace, size_t workspace_bytes, int accumulate,
+                          pa_stream_t stream) {
   if (!dy || !x || !mean || !rstd || !gamma) return PA_ERR_NULL;
   if (M == 0 || N == 0) return PA_ERR_SHAPE;
   if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
@@ -178,8 +186,23 @@ int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const 
       (!workspace || workspace_bytes < pa::layer_norm_bwd_workspace_bytes(M, N)))
     return PA_ERR_WORKSPACE;
   return pa::launch_layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, M, N,
-                                   static_cast<float*>(workspace),
+                                   static_cast<float*>(workspace), accumulate,
                                    static_cast<cudaStream_t>(stream));
+}
+
+int pa_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                      const float* gamma, float* dx, float* dgamma, float* dbeta, uint32_t M,
+                      uint32_t N, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  return layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, M, N, workspace,
+                        workspace_bytes, 0, stream);
+}
+
+int pa_layer_norm_bwd_accumulate(const float* dy, const float* x, const float* mean,
+                                 const float* rstd, const float* gamma, float* dx, float* dgamma,
+                                 float* dbeta, uint32_t M, uint32_t N, void* workspace,
+                                 size_t workspace_bytes, pa_stream_t stream) {
+  return layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, M, N, workspace,
+                        workspace_bytes, 1, stream);
 }
 
 size_t pa_matmul_workspace_size(int M, int N, int K) {
@@ -235,7 +258,20 @@ int pa_linear_fwd(const float* X, const float* W, const float* bias, float* cons
     if (!outs[i]) return PA_ERR_NULL;
   uint32_t* status = status_word();
   if (!status) return PA_ERR_DEVICE;
-  return pa::launch_linear_fwd(X, W, bias, outs, n_outs, M, in_features, out_features, workspace,
+  return pa::launch_linear_fwd(X, W, bias, outs, n_outs, M, in_features, out_features, 0,
+                               workspace, status, static_cast<cudaStream_t>(stream));
+}
+
+int pa_linear_relu_fwd(const float* X, const float* W, const float* bias, float* Y, int M,
+                       int in_features, int out_features, void* workspace, size_t workspace_bytes,
+                       pa_stream_t stream) {
+  if (!X || !W || !Y) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, 1, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  float* outs[1] = {Y};
+  return pa::launch_linear_fwd(X, W, bias, outs, 1, M, in_features, out_features, 1, workspace,
                                status, static_cast<cudaStream_t>(stream));
 }
 
@@ -249,8 +285,21 @@ int pa_linear_bwd(const float* X, const float* W, const float* const* dy_parts, 
     if (!dy_parts[i]) return PA_ERR_NULL;
   uint32_t* status = status_word();
   if (!status) return PA_ERR_DEVICE;
-  return pa::launch_linear_bwd(X, W, dy_parts, n_parts, dX, dW, dbias, M, in_features,
+  return pa::launch_linear_bwd(X, W, dy_parts, n_parts, nullptr, dX, dW, dbias, M, in_features,
                                out_features, workspace, status, static_cast<cudaStream_t>(stream));
+}
+
+int pa_linear_relu_bwd(const float* X, const float* W, const float* Y, const float* dY, float* dX,
+                       float* dW, float* dbias, int M, int in_features, int out_features,
+                       void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  if (!X || !W || !Y || !dY) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, 1, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  const float* parts[1] = {dY};
+  return pa::launch_linear_bwd(X, W, parts, 1, Y, dX, dW, dbias, M, in_features, out_features,
+                               workspace, status, static_cast<cudaStream_t>(stream));
 }
 
 int pa_bias_add(const float* A, const float* bias, float* out, int M, int N, pa_stream_t stream) {
@@ -327,6 +376,19 @@ int pa_adam_step(float* param, const float* grad, float* m, float* v, size_t n, 
   return n ? pa::launch_adam(param, grad, m, v, n, lr, beta1, beta2, eps, bias_corr1, bias_corr2,
                              static_cast<cudaStream_t>(stream))
            : PA_OK;
+}
+int pa_adam_step_multi(float* const* params, const float* const* grads, float* const* m,
+                       float* const* v, const size_t* sizes, int count, float lr, float beta1,
+                       float beta2, float eps, float bias_corr1, float bias_corr2,
+                       pa_stream_t stream) {
+  if (count < 0) return PA_ERR_SHAPE;
+  if (count == 0) return PA_OK;
+  if (!params || !grads || !m || !v || !sizes) return PA_ERR_NULL;
+  for (int i = 0; i < count; ++i)
+    if (sizes[i] && (!params[i] || !grads[i] || !m[i] || !v[i])) return PA_ERR_NULL;
+  if (bias_corr1 <= 0.f || bias_corr2 <= 0.f) return PA_ERR_SHAPE;
+  return pa::launch_adam_multi(params, grads, m, v, sizes, count, lr, beta1, beta2, eps, bias_corr1,
+                               bias_corr2, static_cast<cudaStream_t>(stream));
 }
 int pa_fill_normal(float* x, size_t n, float std_dev, uint64_t seed, pa_stream_t stream) {
   if (!x) return PA_ERR_NULL;

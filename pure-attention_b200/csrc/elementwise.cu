@@ -63,14 +63,19 @@ __global__ void add_kernel(const float* __restrict__ a, const float* b, float* o
 }
 
 // Column sums: CTA = 32 columns x 32 row lanes; fixed-order reduction, then db += .
+// (With a mask, rows of dy count only where mask > 0.)
 __global__ void __launch_bounds__(1024)
-    bias_grad_kernel(const float* __restrict__ dy, float* __restrict__ db, uint32_t M, uint32_t N) {
+    bias_grad_kernel(const float* __restrict__ dy, const float* __restrict__ mask,
+                     float* __restrict__ db, uint32_t M, uint32_t N) {
   __shared__ float part[32][33];
   const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const uint32_t col = blockIdx.x * 32 + tx;
   float acc = 0.f;
   if (col < N)
-    for (uint32_t r = ty; r < M; r += 32) acc += dy[static_cast<size_t>(r) * N + col];
+    for (uint32_t r = ty; r < M; r += 32) {
+      const size_t i = static_cast<size_t>(r) * N + col;
+      if (!mask || mask[i] > 0.f) acc += dy[i];
+    }
   part[ty][tx] = acc;
   __syncthreads();
   if (ty == 0 && col < N) {
@@ -78,6 +83,44 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll 8
     for (int k = 0; k < 32; ++k) s += part[k][tx];
     db[col] += s;
+  }
+}
+
+// Column sums over many CTAs, stage 1: CTA (x, y) sums rows [y*rows_per,
+// (y+1)*rows_per) of the 128 columns x*128.. (one float4 per lane, a warp per
+// row, 8 rows in flight per CTA) into part[y][cols].
+__global__ void __launch_bounds__(256)
+    colsum_partial_kernel(const float* __restrict__ dy, const float* __restrict__ mask,
+                          float* __restrict__ part, uint32_t M, uint32_t N, uint32_t rows_per) {
+  __shared__ float4 red[8][32];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t c4 = blockIdx.x * 32 + lane, n4 = N / 4;
+  const uint32_t r0 = blockIdx.y * rows_per, r1 = min(M, r0 + rows_per);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c4 < n4) {
+#pragma unroll 4
+    for (uint32_t r = r0 + warp; r < r1; r += 8) {
+      float4 v = reinterpret_cast<const float4*>(dy + static_cast<size_t>(r) * N)[c4];
+      if (mask) {
+        const float4 m = reinterpret_cast<const float4*>(mask + static_cast<size_t>(r) * N)[c4];
+        v.x = m.x > 0.f ? v.x : 0.f;
+        v.y = m.y > 0.f ? v.y : 0.f;
+        v.z = m.z > 0.f ? v.z : 0.f;
+        v.w = m.w > 0.f ? v.w : 0.f;
+      }
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c4 < n4) {
+    float4 t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 v = red[w][lane];
+      t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+    }
+    reinterpret_cast<float4*>(part + static_cast<size_t>(blockIdx.y) * N)[c4] = t;
   }
 }
 
@@ -139,9 +182,32 @@ int launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_
   return done();
 }
 
+// db += column sums of dy. Rows are split over enough CTAs to fill the GPU
+// (stage 1 into a stream-ordered scratch), then bias_grad_kernel sums the
+// partial rows in fixed order: deterministic for a given shape and device.
 int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStream_t s) {
-  bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(dy, db, M, N);
-  return done();
+  return launch_bias_grad_masked(dy, nullptr, db, M, N, s);
+}
+
+int launch_bias_grad_masked(const float* dy, const float* mask, float* db, uint32_t M, uint32_t N,
+                            cudaStream_t s) {
+  const uint32_t col_blocks = (N + 127) / 128;
+  uint32_t R = (4u * static_cast<uint32_t>(sm_count()) + col_blocks - 1) / col_blocks;
+  if (R > (M + 63) / 64) R = (M + 63) / 64;  // at least 64 rows per CTA
+  float* part = nullptr;
+  if (N % 4 != 0 || !al16(dy) || (mask && !al16(mask)) || R < 2 ||
+      cudaMallocAsync(reinterpret_cast<void**>(&part), static_cast<size_t>(R) * N * sizeof(float),
+                      s) != cudaSuccess) {
+    bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(dy, mask, db, M, N);
+    return done();
+  }
+  const uint32_t rows_per = (M + R - 1) / R;
+  R = (M + rows_per - 1) / rows_per;
+  colsum_partial_kernel<<<dim3(col_blocks, R), 256, 0, s>>>(dy, mask, part, M, N, rows_per);
+  bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(part, nullptr, db, R, N);
+  const int st = done();
+  cudaFreeAsync(part, s);
+  return st;
 }
 
 int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,

@@ -8,7 +8,10 @@
 // values are written as rows of Dp >= D values, zero-padded, so the head
 // dimension of the planes is a multiple of 64 (one 128-byte TMA box). The
 // planes may also be a column block [c0, c0 + Dp) of wider planes with row
-// pitch ldp, which gathers several [rows, D] operands into one.
+// pitch ldp, which gathers several [rows, D] operands into one. With a null lo
+// pointer only the hi plane (the bf16 rounding of x) is written. With a mask
+// (same layout as x), x is taken as zero where mask <= 0: the gradient of a
+// ReLU whose output is the mask, folded into the gather.
 #include <cuda_bf16.h>
 #include "host_launchers.h"
 
@@ -19,7 +22,7 @@ namespace {
 // One thread per 4 output columns of one row (D % 4 == 0, 16-byte aligned x).
 __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
                                     __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp,
-                                    size_t ldp, int c0) {
+                                    size_t ldp, int c0, const float* __restrict__ mask) {
   const int groups = Dp / 4;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
        i < rows * groups; i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -29,6 +32,13 @@ __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* 
     if (c < D) {
       const float4 f = *reinterpret_cast<const float4*>(x + r * D + c);
       v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+      if (mask) {
+        const float4 m = *reinterpret_cast<const float4*>(mask + r * D + c);
+        v[0] = m.x > 0.f ? v[0] : 0.f;
+        v[1] = m.y > 0.f ? v[1] : 0.f;
+        v[2] = m.z > 0.f ? v[2] : 0.f;
+        v[3] = m.w > 0.f ? v[3] : 0.f;
+      }
     }
     uint32_t h2[2], l2[2];
 #pragma unroll
@@ -39,26 +49,31 @@ __global__ void split_planes_kernel(const float* __restrict__ x, __nv_bfloat16* 
       l2[e] = pack_bf16x2(v[2 * e] - h0, v[2 * e + 1] - h1);
     }
     *reinterpret_cast<uint2*>(hi + r * ldp + c0 + c) = make_uint2(h2[0], h2[1]);
-    *reinterpret_cast<uint2*>(lo + r * ldp + c0 + c) = make_uint2(l2[0], l2[1]);
+    if (lo) *reinterpret_cast<uint2*>(lo + r * ldp + c0 + c) = make_uint2(l2[0], l2[1]);
   }
 }
 
 // Any D: one thread per output element.
 __global__ void split_planes_scalar_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
                                            __nv_bfloat16* __restrict__ lo, size_t rows, int D, int Dp,
-                                           size_t ldp, int c0) {
+                                           size_t ldp, int c0, const float* __restrict__ mask) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < rows * Dp;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const size_t r = i / Dp;
     const int c = static_cast<int>(i % Dp);
-    const float v = c < D ? x[r * D + c] : 0.f;
+    const float v = c < D && (!mask || mask[r * D + c] > 0.f) ? x[r * D + c] : 0.f;
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
     hi[r * ldp + c0 + c] = h;
-    lo[r * ldp + c0 + c] = __float2bfloat16_rn(v - __bfloat162float(h));
+    if (lo) lo[r * ldp + c0 + c] = __float2bfloat16_rn(v - __bfloat162float(h));
   }
 }
 
+thread_local int t_f32_math = PA_F32_MATH_SPLIT3;
+
 }  // namespace
+
+int f32_math() { return t_f32_math; }
+void set_f32_math(int mode) { t_f32_math = mode; }
 
 int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
                         cudaStream_t s) {
@@ -67,18 +82,24 @@ int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, 
 
 int launch_split_planes_into(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
                              size_t ldp, int c0, cudaStream_t s) {
+  return launch_split_planes_masked(x, nullptr, hi, lo, rows, D, Dp, ldp, c0, s);
+}
+
+int launch_split_planes_masked(const float* x, const float* mask, void* hi, void* lo, size_t rows,
+                               int D, int Dp, size_t ldp, int c0, cudaStream_t s) {
   if (D > Dp || D <= 0 || c0 < 0 || static_cast<size_t>(c0) + Dp > ldp) return PA_ERR_SHAPE;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (D % 4 != 0 || Dp % 4 != 0 || c0 % 4 != 0 || ldp % 4 != 0 ||
-      (reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(mask)) & 15u) != 0) {
     const size_t n = rows * Dp;
     size_t blocks = (n + 255) / 256;
     if (blocks > static_cast<size_t>(sms) * 16) blocks = static_cast<size_t>(sms) * 16;
     if (blocks == 0) blocks = 1;
     split_planes_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp, ldp, c0);
+        x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp, ldp, c0,
+        mask);
     return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
   }
   const size_t work = rows * (Dp / 4);
@@ -86,7 +107,8 @@ int launch_split_planes_into(const float* x, void* hi, void* lo, size_t rows, in
   if (blocks > static_cast<size_t>(sms) * 16) blocks = static_cast<size_t>(sms) * 16;
   if (blocks == 0) blocks = 1;
   split_planes_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-      x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp, ldp, c0);
+      x, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), rows, D, Dp, ldp, c0,
+      mask);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

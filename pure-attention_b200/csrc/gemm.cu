@@ -19,7 +19,10 @@
 // bias and writes the output as up to three column blocks (Q, K, V of the
 // attention in-projection) to separate tensors; the backward gathers the
 // column-block gradients straight into one pair of bf16 planes, shared by
-// the dX and dW GEMMs.
+// the dX and dW GEMMs. A projection followed by a ReLU (the feed-forward's
+// first layer) clamps in the same epilogue, and its backward masks the
+// incoming gradient by the saved output while gathering it (no ReLU passes,
+// no pre-activation tensor).
 //
 // One CTA = one 128 x 128 output tile; K in blocks of 64 through a 3-stage
 // TMA ring (hi and lo planes of both operands per stage).
@@ -35,20 +38,31 @@ namespace {
 
 constexpr int GB = 128;          // output tile (rows and columns)
 constexpr int GK = 64;           // K block (one 128-byte swizzle row of bf16)
-constexpr int GSTAGES = 3;
 constexpr int PLANE_TILE = GB * GK * 2;       // 16 KB: one operand plane of one stage
-constexpr int STAGE = 4 * PLANE_TILE;         // A hi, A lo, B hi, B lo
-constexpr int GSMEM = GSTAGES * STAGE + 1024;
+
+// NT = product terms: 3 (hi/lo planes, fp32-level accuracy) or 1 (one bf16
+// plane per operand, the bf16 math mode). A stage holds the A planes, then
+// the B planes; with one plane per operand it is half the size and the ring
+// twice as deep.
+template <int NT>
+struct GemmCfg {
+  static constexpr int PLANES = NT == 3 ? 4 : 2;
+  static constexpr int STAGE = PLANES * PLANE_TILE;
+  static constexpr int STAGES = NT == 3 ? 3 : 6;
+  static constexpr int SMEM = STAGES * STAGE + 1024;
+};
 
 // A_MN / B_MN: the operand is stored with its reduction index as the row index
 // (MN-major for tcgen05); otherwise the reduction index is contiguous (K-major).
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int NT>
 __global__ void __launch_bounds__(256, 1)
     gemm_split_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                       const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
                       float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
                       const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
-                      int nsplit, uint32_t* status) {
+                      int nsplit, int relu, uint32_t* status) {
+  using G = GemmCfg<NT>;
+  constexpr int GSTAGES = G::STAGES, STAGE = G::STAGE, HALF = G::PLANES / 2;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[2 * GSTAGES + 1];
   __shared__ uint32_t tmem_slot;
@@ -81,16 +95,16 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      const CUtensorMap* maps[4] = {&mAh, &mAl, &mBh, &mBl};
+      const CUtensorMap* maps[4] = {&mAh, HALF == 2 ? &mAl : &mBh, &mBh, &mBl};
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % GSTAGES;
         if (kb >= GSTAGES && !mbar_wait(empty(s), ((kb / GSTAGES) - 1) & 1, status)) break;
         mbar_arrive_expect_tx(full(s), STAGE);
         uint8_t* st = smem + s * STAGE;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const bool mn = p < 2 ? A_MN : B_MN;
-          const int r0 = p < 2 ? m0 : n0;
+        for (int p = 0; p < G::PLANES; ++p) {
+          const bool mn = p < HALF ? A_MN : B_MN;
+          const int r0 = p < HALF ? m0 : n0;
           const uint32_t dst = smem_u32(st + p * PLANE_TILE);
           if (mn) {
             // two 64-wide groups along M/N, 64 K rows each
@@ -113,8 +127,9 @@ __global__ void __launch_bounds__(256, 1)
         if (!(ok = mbar_wait(full(s), (kb / GSTAGES) & 1, status))) break;
         tc_fence_after();
 #pragma unroll
-        for (int term = 0; term < 3; ++term) {
-          const uint32_t pa_ = (term == 2) ? 1 : 0, pb = (term == 1) ? 3 : 2;
+        for (int term = 0; term < NT; ++term) {
+          // planes (A, B) of each term: (hi, hi), (hi, lo), (lo, hi)
+          const uint32_t pa_ = (term == 2) ? 1 : 0, pb = HALF + ((term == 1) ? 1 : 0);
 #pragma unroll
           for (int ks = 0; ks < GK / 16; ++ks) {
             const uint32_t so = (s * STAGE) >> 4;
@@ -166,6 +181,10 @@ __global__ void __launch_bounds__(256, 1)
               const float4 bb = *reinterpret_cast<const float4*>(bias + col0 + 4 * u);
               f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
             }
+            if (relu) {
+              f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
+              f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
+            }
             if (accumulate) {
               const float4 p = d4[u];
               f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
@@ -178,7 +197,9 @@ __global__ void __launch_bounds__(256, 1)
             const int col = col0 + e;
             if (col < Nout) {
               float* de = dst_of(col);
-              *de = __uint_as_float(v[e]) + (bias ? bias[col] : 0.f) + (accumulate ? *de : 0.f);
+              float f = __uint_as_float(v[e]) + (bias ? bias[col] : 0.f);
+              if (relu) f = fmaxf(f, 0.f);
+              *de = f + (accumulate ? *de : 0.f);
             }
           }
         }
@@ -216,18 +237,27 @@ struct Epilogue {
   float* c1 = nullptr;
   float* c2 = nullptr;
   int nsplit = 0;
+  int relu = 0;  // max(0, .) after the bias (forward projections only)
 };
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int NT>
 int run_gemm(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred, int accumulate,
              const Epilogue& ep, uint32_t* status, cudaStream_t s) {
   static uint64_t attr = 0;
-  ensure_smem_attr(gemm_split_kernel<A_MN, B_MN>, GSMEM, attr);
+  ensure_smem_attr(gemm_split_kernel<A_MN, B_MN, NT>, GemmCfg<NT>::SMEM, attr);
   dim3 grid((Nout + GB - 1) / GB, (Mout + GB - 1) / GB);
-  gemm_split_kernel<A_MN, B_MN><<<grid, 256, GSMEM, s>>>(m[0], m[1], m[2], m[3], C, ldc, Mout, Nout,
-                                                          Kred, accumulate, ep.bias, ep.c1, ep.c2,
-                                                          ep.nsplit, status);
+  gemm_split_kernel<A_MN, B_MN, NT><<<grid, 256, GemmCfg<NT>::SMEM, s>>>(
+      m[0], m[1], m[2], m[3], C, ldc, Mout, Nout, Kred, accumulate, ep.bias, ep.c1, ep.c2,
+      ep.nsplit, ep.relu, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+template <bool A_MN, bool B_MN>
+int run_gemm_math(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred,
+                  int accumulate, const Epilogue& ep, uint32_t* status, cudaStream_t s) {
+  if (f32_math() == PA_F32_MATH_BF16)
+    return run_gemm<A_MN, B_MN, 1>(m, C, ldc, Mout, Nout, Kred, accumulate, ep, status, s);
+  return run_gemm<A_MN, B_MN, 3>(m, C, ldc, Mout, Nout, Kred, accumulate, ep, status, s);
 }
 
 // bf16 hi/lo planes of one [rows, cols] operand in the workspace (row pitch round8(cols)).
@@ -243,8 +273,10 @@ Planes carve(uint8_t*& w, int rows, int cols) {
   w += 2 * b;
   return p;
 }
+// hi and lo planes, or the hi plane alone in the bf16 math mode
 int split_into(const float* x, const Planes& p, cudaStream_t s) {
-  return launch_split_planes(x, p.hi, p.lo, static_cast<size_t>(p.rows), p.cols, round8(p.cols), s);
+  return launch_split_planes(x, p.hi, f32_math() == PA_F32_MATH_BF16 ? nullptr : p.lo,
+                             static_cast<size_t>(p.rows), p.cols, round8(p.cols), s);
 }
 
 // GEMM of `mode` (see launch_gemm_f32) on operands already split into planes.
@@ -255,9 +287,9 @@ int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int
   if (!plane_map(&m[0], a.hi, a.rows, a.cols, a_mn) || !plane_map(&m[1], a.lo, a.rows, a.cols, a_mn) ||
       !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn) || !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn))
     return PA_ERR_ALIGN;
-  if (mode == 0) return run_gemm<false, true>(m, C, N, M, N, K, 0, ep, status, s);
-  if (mode == 1) return run_gemm<false, false>(m, C, N, M, N, K, 1, ep, status, s);
-  return run_gemm<true, true>(m, C, K, N, K, M, 1, ep, status, s);
+  if (mode == 0) return run_gemm_math<false, true>(m, C, N, M, N, K, 0, ep, status, s);
+  if (mode == 1) return run_gemm_math<false, false>(m, C, N, M, N, K, 1, ep, status, s);
+  return run_gemm_math<true, true>(m, C, K, N, K, M, 1, ep, status, s);
 }
 
 }  // namespace
@@ -294,7 +326,7 @@ size_t linear_workspace_bytes(int M, int IN, int OUT) {
 }
 
 int launch_linear_fwd(const float* x, const float* wt, const float* bias, float* const* outs,
-                      int n_outs, int M, int IN, int OUT, void* ws, uint32_t* status,
+                      int n_outs, int M, int IN, int OUT, int relu, void* ws, uint32_t* status,
                       cudaStream_t s) {
   uint8_t* w = static_cast<uint8_t*>(ws);
   const Planes a = carve(w, M, IN), b = carve(w, IN, OUT);
@@ -304,6 +336,7 @@ int launch_linear_fwd(const float* x, const float* wt, const float* bias, float*
   if (st != PA_OK) return st;
   Epilogue ep;
   ep.bias = bias;
+  ep.relu = relu;
   if (n_outs > 1) {
     ep.nsplit = OUT / n_outs;
     ep.c1 = outs[1];
@@ -313,16 +346,18 @@ int launch_linear_fwd(const float* x, const float* wt, const float* bias, float*
 }
 
 int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_parts, int n_parts,
-                      float* dx, float* dw, float* dbias, int M, int IN, int OUT, void* ws,
-                      uint32_t* status, cudaStream_t s) {
+                      const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
+                      int OUT, void* ws, uint32_t* status, cudaStream_t s) {
   uint8_t* w = static_cast<uint8_t*>(ws);
   const Planes dy = carve(w, M, OUT), wp = carve(w, IN, OUT), xp = carve(w, M, IN);
   // gather the column-block gradients into one pair of planes (row pitch round8(OUT))
   const int part = OUT / n_parts;
   for (int p = 0; p < n_parts; ++p) {
     const int width = p + 1 < n_parts ? part : round8(OUT) - p * part;  // last block takes the pad
-    const int st = launch_split_planes_into(dy_parts[p], dy.hi, dy.lo, static_cast<size_t>(M), part,
-                                            width, static_cast<size_t>(round8(OUT)), p * part, s);
+    const int st = launch_split_planes_masked(
+        dy_parts[p], relu_out, dy.hi,  // relu_out: single-part projections only
+        f32_math() == PA_F32_MATH_BF16 ? nullptr : dy.lo, static_cast<size_t>(M), part, width,
+        static_cast<size_t>(round8(OUT)), p * part, s);
     if (st != PA_OK) return st;
   }
   if (dx) {
@@ -339,8 +374,8 @@ int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_pa
   }
   if (dbias)
     for (int p = 0; p < n_parts; ++p) {
-      const int st = launch_bias_grad(dy_parts[p], dbias + p * part, static_cast<uint32_t>(M),
-                                      static_cast<uint32_t>(part), s);
+      const int st = launch_bias_grad_masked(dy_parts[p], relu_out, dbias + p * part,
+                                             static_cast<uint32_t>(M), static_cast<uint32_t>(part), s);
       if (st != PA_OK) return st;
     }
   return PA_OK;

@@ -7,6 +7,10 @@
 
 namespace pa {
 
+// fp32_split.cu: the calling thread's pa_f32_math mode
+int f32_math();
+void set_f32_math(int mode);
+
 // attn_fwd.cu
 int launch_attn_fwd_bf16(const AttnShape& sh, const void* q, const void* k, const void* v, void* o,
                          float* lse, uint32_t* status, cudaStream_t stream);
@@ -21,6 +25,9 @@ int launch_split_planes(const float* x, void* hi, void* lo, size_t rows, int D, 
 // Same, into columns [c0, c0 + Dp) of planes with row pitch ldp (elements).
 int launch_split_planes_into(const float* x, void* hi, void* lo, size_t rows, int D, int Dp,
                              size_t ldp, int c0, cudaStream_t s);
+// Same, x taken as zero where mask (same layout as x) <= 0.
+int launch_split_planes_masked(const float* x, const float* mask, void* hi, void* lo, size_t rows,
+                               int D, int Dp, size_t ldp, int c0, cudaStream_t s);
 
 // attn_bwd.cu
 size_t attn_bwd_workspace_bytes(const AttnShape& sh);
@@ -46,13 +53,15 @@ int launch_layer_norm_fwd(const float* x, const float* g, const float* b, float*
 size_t layer_norm_bwd_workspace_bytes(uint32_t M, uint32_t N);
 int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, const float* rs,
                           const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,
-                          float* part, cudaStream_t s);
+                          float* part, int accumulate_dx, cudaStream_t s);
 
 // elementwise.cu
 int launch_bias_add(const float* a, const float* bias, float* out, uint32_t M, uint32_t N,
                     cudaStream_t s);
 int launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
 int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStream_t s);
+int launch_bias_grad_masked(const float* dy, const float* mask, float* db, uint32_t M, uint32_t N,
+                            cudaStream_t s);
 int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
                           uint32_t width, cudaStream_t s);
 int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint32_t parts,
@@ -69,15 +78,20 @@ size_t gemm_workspace_bytes(int M, int N, int K);
 // blocks of OUT / n_outs (n_outs <= 3); backward from n_parts column-block
 // gradients, accumulating into dx, dw, dbias (each may be null).
 size_t linear_workspace_bytes(int M, int IN, int OUT);
+// relu: Y = max(0, X W + bias). relu_out (backward, n_parts = 1): that Y,
+// whose sign masks dy.
 int launch_linear_fwd(const float* x, const float* w, const float* bias, float* const* outs,
-                      int n_outs, int M, int IN, int OUT, void* ws, uint32_t* status,
+                      int n_outs, int M, int IN, int OUT, int relu, void* ws, uint32_t* status,
                       cudaStream_t s);
 int launch_linear_bwd(const float* x, const float* w, const float* const* dy_parts, int n_parts,
-                      float* dx, float* dw, float* dbias, int M, int IN, int OUT, void* ws,
-                      uint32_t* status, cudaStream_t s);
+                      const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
+                      int OUT, void* ws, uint32_t* status, cudaStream_t s);
 
 // training.cu
 int launch_relu_fwd(const float* x, float* y, size_t n, cudaStream_t s);
+int launch_adam_multi(float* const* w, const float* const* g, float* const* m, float* const* v,
+                      const size_t* n, int count, float lr, float b1, float b2, float eps, float c1,
+                      float c2, cudaStream_t s);
 int launch_relu_bwd(const float* dy, const float* x, float* dx, size_t n, cudaStream_t s);
 int launch_mse_fwd(const float* p, const float* t, float* loss, size_t n, cudaStream_t s);
 int launch_mse_bwd(const float* p, const float* t, const float* dl, float* dp, size_t n,

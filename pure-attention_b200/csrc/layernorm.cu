@@ -77,68 +77,83 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
   }
 }
 
-// Backward: dX per row; per-CTA partial dgamma/dbeta written to part[blockIdx][2][N].
-template <int VPL>
+// Backward: dX per row (one warp per row, x and dY held in registers, with
+// ACC the old dX too); dgamma / dbeta partials accumulated per warp in shared
+// memory (each warp owns its [2][N] slice, so the order is fixed), summed over
+// the warps in index order and written to part[blockIdx][2][N]. Holding only
+// the loaded rows keeps the kernel near 100 registers, so several CTAs share
+// an SM and enough loads are in flight to stream HBM.
+template <int VPL, bool ACC>
 __global__ void __launch_bounds__(LN_WARPS * 32)
     ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                   const float* __restrict__ mean, const float* __restrict__ rstd,
                   const float* __restrict__ gamma, float* __restrict__ dx,
                   float* __restrict__ part, uint32_t M, uint32_t N) {
-  extern __shared__ float red[];  // [LN_WARPS][2][N]
+  extern __shared__ float red[];  // [LN_WARPS][2][N] when part != nullptr
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x / 32;
   const uint32_t nvec = N / 4;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
-  float4 pg[VPL], pb[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) pg[i] = pb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4* rg = reinterpret_cast<float4*>(red + static_cast<size_t>(warp) * 2 * N);
+  float4* rb = reinterpret_cast<float4*>(red + static_cast<size_t>(warp) * 2 * N + N);
+  if (part)
+    for (uint32_t c = lane; c < nvec; c += 32) rg[c] = rb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float inv_n = 1.f / N;
+  const float fn = static_cast<float>(N);
   for (uint32_t row = blockIdx.x * LN_WARPS + warp; row < M; row += gridDim.x * LN_WARPS) {
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * N);
     const float4* dr = reinterpret_cast<const float4*>(dy + static_cast<size_t>(row) * N);
+    float4* xo = dx ? reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * N) : nullptr;
+    float4 xv[VPL], dv[VPL], ov[ACC ? VPL : 1];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const uint32_t c = lane + 32 * i;
+      const bool in = c < nvec;
+      xv[i] = in ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      dv[i] = in ? dr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (ACC) ov[i] = in && xo ? xo[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const float mu = mean[row], rs = rstd[row];
-    float4 xh[VPL], t[VPL];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const uint32_t c = lane + 32 * i;
       if (c < nvec) {
-        const float4 xv = xr[c], dv = dr[c], g = g4[c];
-        xh[i] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
-        t[i] = make_float4(dv.x * g.x, dv.y * g.y, dv.z * g.z, dv.w * g.w);
-        s1 += (t[i].x + t[i].y) + (t[i].z + t[i].w);
-        s2 += (t[i].x * xh[i].x + t[i].y * xh[i].y) + (t[i].z * xh[i].z + t[i].w * xh[i].w);
-        pg[i].x += dv.x * xh[i].x; pg[i].y += dv.y * xh[i].y;
-        pg[i].z += dv.z * xh[i].z; pg[i].w += dv.w * xh[i].w;
-        pb[i].x += dv.x; pb[i].y += dv.y; pb[i].z += dv.z; pb[i].w += dv.w;
+        const float4 g = g4[c];
+        const float t0 = dv[i].x * g.x, t1 = dv[i].y * g.y, t2 = dv[i].z * g.z, t3 = dv[i].w * g.w;
+        s1 += (t0 + t1) + (t2 + t3);
+        s2 += (t0 * (xv[i].x - mu) + t1 * (xv[i].y - mu)) + (t2 * (xv[i].z - mu) + t3 * (xv[i].w - mu));
       }
     }
-    if (dx) {
-      s1 = warp_sum(s1);
-      s2 = warp_sum(s2);
-      const float inv_n = 1.f / N;
-      const float fn = static_cast<float>(N);
-      float4* xo = reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * N);
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2) * rs;
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const uint32_t c = lane + 32 * i;
-        if (c < nvec)
-          xo[c] = make_float4((fn * t[i].x - s1 - xh[i].x * s2) * rs * inv_n,
-                              (fn * t[i].y - s1 - xh[i].y * s2) * rs * inv_n,
-                              (fn * t[i].z - s1 - xh[i].z * s2) * rs * inv_n,
-                              (fn * t[i].w - s1 - xh[i].w * s2) * rs * inv_n);
+    for (int i = 0; i < VPL; ++i) {
+      const uint32_t c = lane + 32 * i;
+      if (c < nvec) {
+        const float4 g = g4[c];
+        const float h0 = (xv[i].x - mu) * rs, h1 = (xv[i].y - mu) * rs;
+        const float h2 = (xv[i].z - mu) * rs, h3 = (xv[i].w - mu) * rs;
+        if (xo) {
+          float4 o = make_float4((fn * dv[i].x * g.x - s1 - h0 * s2) * rs * inv_n,
+                                 (fn * dv[i].y * g.y - s1 - h1 * s2) * rs * inv_n,
+                                 (fn * dv[i].z * g.z - s1 - h2 * s2) * rs * inv_n,
+                                 (fn * dv[i].w * g.w - s1 - h3 * s2) * rs * inv_n);
+          if constexpr (ACC) {
+            o.x += ov[i].x; o.y += ov[i].y; o.z += ov[i].z; o.w += ov[i].w;
+          }
+          xo[c] = o;
+        }
+        if (part) {
+          float4 a = rg[c], b = rb[c];
+          a.x += dv[i].x * h0; a.y += dv[i].y * h1; a.z += dv[i].z * h2; a.w += dv[i].w * h3;
+          b.x += dv[i].x; b.y += dv[i].y; b.z += dv[i].z; b.w += dv[i].w;
+          rg[c] = a;
+          rb[c] = b;
+        }
       }
     }
   }
   if (!part) return;
-  float4* rg = reinterpret_cast<float4*>(red + static_cast<size_t>(warp) * 2 * N);
-  float4* rb = reinterpret_cast<float4*>(red + static_cast<size_t>(warp) * 2 * N + N);
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const uint32_t c = lane + 32 * i;
-    if (c < nvec) {
-      rg[c] = pg[i];
-      rb[c] = pb[i];
-    }
-  }
   __syncthreads();
   float* out = part + static_cast<size_t>(blockIdx.x) * 2 * N;
   for (uint32_t c = threadIdx.x; c < 2 * N; c += blockDim.x) {
@@ -149,18 +164,26 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
   }
 }
 
-// dgamma[c] += sum_b part[b][0][c]; dbeta[c] += sum_b part[b][1][c] (fixed order).
-__global__ void ln_param_reduce_kernel(const float* __restrict__ part, float* __restrict__ dgamma,
-                                       float* __restrict__ dbeta, uint32_t nblk, uint32_t N) {
-  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= N) return;
-  float g = 0.f, b = 0.f;
-  for (uint32_t k = 0; k < nblk; ++k) {
-    g += part[static_cast<size_t>(k) * 2 * N + c];
-    b += part[static_cast<size_t>(k) * 2 * N + N + c];
+// dgamma[c] += sum_b part[b][0][c]; dbeta[c] += sum_b part[b][1][c] (fixed
+// order). CTA = 32 of the 2N columns x 32 lanes over the partial rows.
+__global__ void __launch_bounds__(1024)
+    ln_param_reduce_kernel(const float* __restrict__ part, float* __restrict__ dgamma,
+                           float* __restrict__ dbeta, uint32_t nblk, uint32_t N) {
+  __shared__ float red[32][33];
+  const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const uint32_t c = blockIdx.x * 32 + tx;
+  float acc = 0.f;
+  if (c < 2 * N)
+    for (uint32_t k = ty; k < nblk; k += 32) acc += part[static_cast<size_t>(k) * 2 * N + c];
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < 2 * N) {
+    float t = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) t += red[k][tx];
+    float* out = c < N ? dgamma : dbeta;
+    if (out) out[c < N ? c : c - N] += t;
   }
-  if (dgamma) dgamma[c] += g;
-  if (dbeta) dbeta[c] += b;
 }
 
 int num_sms() {
@@ -172,9 +195,11 @@ int num_sms() {
   return sms[dev] > 0 ? sms[dev] : 148;
 }
 
-uint32_t ln_bwd_blocks(uint32_t M) {
+// One wave of CTAs: two per SM for rows of up to 1024 values (about 100-130
+// registers per thread, 64 KB of partials), three for shorter rows.
+uint32_t ln_bwd_blocks(uint32_t M, uint32_t N) {
   const uint32_t want = (M + LN_WARPS - 1) / LN_WARPS;
-  const uint32_t cap = static_cast<uint32_t>(num_sms()) * 4;
+  const uint32_t cap = static_cast<uint32_t>(num_sms()) * (N > 512 ? 2 : 3);
   return want < cap ? want : cap;
 }
 
@@ -189,16 +214,25 @@ int ln_fwd_launch(const float* x, const float* g, const float* b, float* y, floa
 template <int VPL>
 int ln_bwd_launch(const float* dy, const float* x, const float* mu, const float* rs,
                   const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,
-                  float* part, cudaStream_t s) {
-  const uint32_t blocks = ln_bwd_blocks(M);
+                  float* part, int accumulate, cudaStream_t s) {
+  const uint32_t blocks = ln_bwd_blocks(M, N);
   const size_t smem = static_cast<size_t>(LN_WARPS) * 2 * N * sizeof(float);
-  static uint64_t attr = 0;
-  ensure_smem_attr(ln_bwd_kernel<VPL>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4), attr);
-  ln_bwd_kernel<VPL><<<blocks, LN_WARPS * 32, (dg || db) ? smem : 0, s>>>(
-      dy, x, mu, rs, g, dx, (dg || db) ? part : nullptr, M, N);
+  float* p = (dg || db) ? part : nullptr;
+  if (accumulate && dx) {
+    static uint64_t attr = 0;
+    ensure_smem_attr(ln_bwd_kernel<VPL, true>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4), attr);
+    ln_bwd_kernel<VPL, true><<<blocks, LN_WARPS * 32, p ? smem : 0, s>>>(dy, x, mu, rs, g, dx, p,
+                                                                          M, N);
+  } else {
+    static uint64_t attr = 0;
+    ensure_smem_attr(ln_bwd_kernel<VPL, false>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4),
+                     attr);
+    ln_bwd_kernel<VPL, false><<<blocks, LN_WARPS * 32, p ? smem : 0, s>>>(dy, x, mu, rs, g, dx, p,
+                                                                           M, N);
+  }
   if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
   if (dg || db) {
-    ln_param_reduce_kernel<<<(N + 255) / 256, 256, 0, s>>>(part, dg, db, blocks, N);
+    ln_param_reduce_kernel<<<(2 * N + 31) / 32, 1024, 0, s>>>(part, dg, db, blocks, N);
     if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
   }
   return PA_OK;
@@ -218,16 +252,16 @@ int launch_layer_norm_fwd(const float* x, const float* g, const float* b, float*
 }
 
 size_t layer_norm_bwd_workspace_bytes(uint32_t M, uint32_t N) {
-  return static_cast<size_t>(ln_bwd_blocks(M)) * 2 * N * sizeof(float);
+  return static_cast<size_t>(ln_bwd_blocks(M, N)) * 2 * N * sizeof(float);
 }
 
 int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, const float* rs,
                           const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,
-                          float* part, cudaStream_t s) {
-  if (N <= 128) return ln_bwd_launch<1>(dy, x, mu, rs, g, dx, dg, db, M, N, part, s);
-  if (N <= 256) return ln_bwd_launch<2>(dy, x, mu, rs, g, dx, dg, db, M, N, part, s);
-  if (N <= 512) return ln_bwd_launch<4>(dy, x, mu, rs, g, dx, dg, db, M, N, part, s);
-  if (N <= 1024) return ln_bwd_launch<8>(dy, x, mu, rs, g, dx, dg, db, M, N, part, s);
+                          float* part, int acc, cudaStream_t s) {
+  if (N <= 128) return ln_bwd_launch<1>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
+  if (N <= 256) return ln_bwd_launch<2>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
+  if (N <= 512) return ln_bwd_launch<4>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
+  if (N <= 1024) return ln_bwd_launch<8>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
   return PA_ERR_UNSUPPORTED;
 }
 

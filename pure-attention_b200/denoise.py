@@ -22,6 +22,12 @@ host tensors' gradient buffers, in buckets (per bucket: one gather into a flat
 buffer, one all-reduce, one scatter back), and every rank takes the same Adam
 step.
 
+Precision: weights, activations and gradients are fp32 tensors. math="split3"
+computes every product at fp32-level accuracy (bf16 hi/lo planes, three
+products); math="bf16" rounds the operands of each matmul and attention to
+bf16 (one product, fp32 accumulation) - mixed-precision training with fp32
+master weights and fp32 Adam.
+
 Stream order: the operators run on the CUDA legacy default stream, which is
 also torch's default stream, so the torch copies and process-group collectives
 issued from the same thread are ordered with them without host syncs.
@@ -35,16 +41,21 @@ import PureAttention as pa
 
 class FeedForward(pa.Module):
     """Linear(embed, hidden) -> ReLU -> Linear(hidden, embed)
-    (tests/main_denoise.py:11-25)."""
+    (tests/main_denoise.py:11-25). fused=True runs the first Linear and the
+    ReLU as one op (the clamp in the GEMM epilogue, the mask folded into its
+    backward); the parameters are the same either way."""
 
-    def __init__(self, embed_dim, hidden_dim):
+    def __init__(self, embed_dim, hidden_dim, fused=True):
         super().__init__()
-        self.fc1 = pa.Linear(embed_dim, hidden_dim)
-        self.relu = pa.ReLU()
+        self.fc1 = pa.Linear(embed_dim, hidden_dim, relu=fused)
+        self.relu = None if fused else pa.ReLU()
         self.fc2 = pa.Linear(hidden_dim, embed_dim)
 
     def forward(self, x):
-        return self.fc2.forward(self.relu.forward(self.fc1.forward(x)))
+        h = self.fc1.forward(x)
+        if self.relu is not None:
+            h = self.relu.forward(h)
+        return self.fc2.forward(h)
 
     def parameters(self):
         return self.fc1.parameters() + self.fc2.parameters()
@@ -181,9 +192,11 @@ class DenoiseTrainer:
     """
 
     def __init__(self, layers=6, embed=1024, heads=16, ffn=4096, seq=2048, batch=8, lr=1e-4,
-                 seed=5, bucket_bytes=25 << 20, group=None):
+                 seed=5, bucket_bytes=25 << 20, group=None, math="split3"):
         import torch.distributed as dist
         self.shape = (batch, seq, embed)
+        self.math = math
+        pa.set_float32_math(math)  # fp32 master weights; "bf16": bf16 products
         pa.set_seed(seed)  # same initial weights on every rank
         self.model = DenoiseTransformer(layers, embed, heads, ffn)
         self.params = self.model.parameters()
@@ -210,6 +223,7 @@ class DenoiseTrainer:
         self.t_dev.view(t_host.shape).copy_(t_host, non_blocking=True)
 
     def step_resident(self):
+        pa.set_float32_math(self.math)
         self.opt.zero_grad()
         out = self.model.forward(self.x)
         loss = self.criterion(out, self.t)

@@ -2,6 +2,7 @@
 // over the B200 host layer. Names, signatures and defaults match; additions
 // are set_seed, device_status and Tensor.zero_grad.
 #include <pybind11/pybind11.h>
+#include <string>
 #include <pybind11/stl.h>
 
 #include <algorithm>
@@ -97,7 +98,9 @@ PYBIND11_MODULE(PureAttention, m) {
       .def("parameters", &layers::Module::parameters);
 
   py::class_<layers::Linear, layers::Module, std::shared_ptr<layers::Linear>>(m, "Linear")
-      .def(py::init<uint32_t, uint32_t>())
+      .def(py::init<uint32_t, uint32_t, bool>(), py::arg("in_channels"), py::arg("out_channels"),
+           py::arg("relu") = false,
+           "relu=True (not in the reference): y = max(0, x W + b) as one fused op")
       .def("forward", &layers::Linear::forward)
       .def("parameters", &layers::Linear::parameters)
       .def_readwrite("weight", &layers::Linear::weight)
@@ -153,6 +156,18 @@ PYBIND11_MODULE(PureAttention, m) {
   }, "Element-wise addition (a [1, N] second operand is broadcast over rows)", py::arg("a"),
         py::arg("b"));
 
+  m.def("set_float32_math", [](const std::string& mode) {
+    int m_ = -1;
+    if (mode == "split3") m_ = PA_F32_MATH_SPLIT3;
+    if (mode == "bf16") m_ = PA_F32_MATH_BF16;
+    if (m_ < 0 || pa_set_f32_math(m_) != PA_OK)
+      throw std::invalid_argument("float32 math mode must be 'split3' or 'bf16'");
+  }, "Products of the calling thread's matmuls and attention: 'split3' (default; bf16 hi/lo "
+     "planes, fp32-level accuracy) or 'bf16' (one bf16 product, fp32 accumulation and storage). "
+     "Not in the reference.", py::arg("mode"));
+  m.def("get_float32_math", []() {
+    return std::string(pa_get_f32_math() == PA_F32_MATH_BF16 ? "bf16" : "split3");
+  });
   m.def("set_seed", &CudaContext::setSeed, "Seed of fill_normal and layer initialisation",
         py::arg("seed"));
   m.def("device_status", []() { return pa_device_status(CudaContext::getStream(), 1); },

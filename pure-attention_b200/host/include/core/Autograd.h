@@ -55,13 +55,15 @@ struct MSEFunction : public Function {
 
 // Fused projection X W + bias, output as column blocks (core::linear): one
 // node for what MatMulFunction + AddFunction + SplitFunction do in three.
+// With relu (one output), Y = max(0, X W + bias): one node for Linear + ReLU.
 struct LinearFunction : public Function {
   std::shared_ptr<Tensor> X_input;
   std::shared_ptr<Tensor> W_input;
   std::shared_ptr<Tensor> bias_input;
   std::vector<std::weak_ptr<Tensor>> Outputs;
+  bool relu;
   LinearFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w, std::shared_ptr<Tensor> b,
-                 std::vector<std::shared_ptr<Tensor>> outs);
+                 std::vector<std::shared_ptr<Tensor>> outs, bool relu_ = false);
   void apply_backward() override;
   std::vector<std::shared_ptr<Tensor>> inputs() const override {
     return {X_input, W_input, bias_input};

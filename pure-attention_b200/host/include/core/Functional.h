@@ -27,10 +27,12 @@ std::shared_ptr<Tensor> mse_loss(const std::shared_ptr<Tensor>& preds,
                                  const cudaStream_t& stream);
 // Fused projection (no single reference counterpart: core::matmul + core::matadd
 // + core::split in one pass, Functional.cpp:12-52, 205-252): parts receive the
-// num_parts column blocks of A W + bias, with one LinearFunction node.
+// num_parts column blocks of A W + bias, with one LinearFunction node; with
+// relu (num_parts = 1) the block is max(0, A W + bias).
 void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
             const std::shared_ptr<Tensor>& bias, uint32_t num_parts,
-            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream);
+            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream,
+            bool relu = false);
 
 void split(const std::shared_ptr<Tensor>& A, uint32_t num_parts, int dim,
            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream);

@@ -24,15 +24,23 @@ void Adam::step() {
   ++step_count;
   const float c1 = 1.0f - std::pow(beta1, static_cast<float>(step_count));
   const float c2 = 1.0f - std::pow(beta2, static_cast<float>(step_count));
+  // every parameter in one multi-tensor launch (per 48 tensors)
+  std::vector<float*> w, m, v;
+  std::vector<const float*> g;
+  std::vector<size_t> n;
   for (size_t i = 0; i < parameters.size(); ++i) {
     auto& p = parameters[i];
     if (!p->requires_grad() || !p->get_gradient_ptr()) continue;
-    core::check_status(
-        pa_adam_step(p->get_data_ptr(), p->get_gradient_ptr(), m_states[i]->get_data_ptr(),
-                     v_states[i]->get_data_ptr(), p->numel(), lr, beta1, beta2, epsilon, c1, c2,
-                     core::ps(CudaContext::getStream())),
-        "Adam");
+    w.push_back(p->get_data_ptr());
+    g.push_back(p->get_gradient_ptr());
+    m.push_back(m_states[i]->get_data_ptr());
+    v.push_back(v_states[i]->get_data_ptr());
+    n.push_back(p->numel());
   }
+  core::check_status(pa_adam_step_multi(w.data(), g.data(), m.data(), v.data(), n.data(),
+                                        static_cast<int>(w.size()), lr, beta1, beta2, epsilon, c1,
+                                        c2, core::ps(CudaContext::getStream())),
+                     "Adam");
 }
 
 void Adam::zero_grad() {

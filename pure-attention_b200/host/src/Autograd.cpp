@@ -86,9 +86,10 @@ void MSEFunction::apply_backward() {
 }
 
 LinearFunction::LinearFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w,
-                               std::shared_ptr<Tensor> b, std::vector<std::shared_ptr<Tensor>> outs)
+                               std::shared_ptr<Tensor> b, std::vector<std::shared_ptr<Tensor>> outs,
+                               bool relu_)
     : X_input(std::move(x)), W_input(std::move(w)), bias_input(std::move(b)),
-      Outputs(outs.begin(), outs.end()) {}
+      Outputs(outs.begin(), outs.end()), relu(relu_) {}
 
 // dX += dY W^T, dW += X^T dY, dbias += column sums of dY, with dY the column
 // blocks' gradients (a block whose tensor has expired contributes zero).
@@ -98,6 +99,19 @@ void LinearFunction::apply_backward() {
   const int M = static_cast<int>(rows_of(*X_input));
   const int parts = static_cast<int>(Outputs.size());
   const size_t part_bytes = static_cast<size_t>(M) * (N / parts) * sizeof(float);
+  float* dX = X_input->requires_grad() ? X_input->get_gradient_ptr() : nullptr;
+  float* dW = W_input->requires_grad() ? W_input->get_gradient_ptr() : nullptr;
+  float* db = bias_input->requires_grad() ? bias_input->get_gradient_ptr() : nullptr;
+  if (relu) {  // the saved output's sign masks its gradient inside the call
+    auto Y = Outputs[0].lock();
+    if (!Y || !Y->get_gradient_ptr()) return;
+    Scratch ws(pa_linear_workspace_size(M, K, N), stream());
+    check_status(pa_linear_relu_bwd(X_input->get_data_ptr(), W_input->get_data_ptr(),
+                                    Y->get_data_ptr(), Y->get_gradient_ptr(), dX, dW, db, M, K, N,
+                                    ws.get(), ws.size(), ps(stream())),
+                 "linear + ReLU backward");
+    return;
+  }
   std::vector<const float*> grads;
   std::vector<std::unique_ptr<Scratch>> zeros;
   bool any = false;
@@ -115,10 +129,7 @@ void LinearFunction::apply_backward() {
   if (!any) return;
   Scratch ws(pa_linear_workspace_size(M, K, N), stream());
   check_status(pa_linear_bwd(X_input->get_data_ptr(), W_input->get_data_ptr(), grads.data(), parts,
-                             X_input->requires_grad() ? X_input->get_gradient_ptr() : nullptr,
-                             W_input->requires_grad() ? W_input->get_gradient_ptr() : nullptr,
-                             bias_input->requires_grad() ? bias_input->get_gradient_ptr() : nullptr,
-                             M, K, N, ws.get(), ws.size(), ps(stream())),
+                             dX, dW, db, M, K, N, ws.get(), ws.size(), ps(stream())),
                "linear backward");
 }
 
@@ -183,24 +194,21 @@ LayerNormFunction::LayerNormFunction(const std::shared_ptr<Tensor>& inp,
                                      uint32_t n_size)
     : input(inp), gamma(g), beta(b), output(out), mean(m), rstd(r), M(m_size), N(n_size) {}
 
-// dX is written by the kernel (the reference's overwrite), so it goes through
-// a temporary and is then added into the input's gradient.
+// dX is accumulated by the kernel into the input's gradient, which may
+// already hold a residual branch's contribution (the reference's node
+// overwrites it, source/core/Autograd.cpp:257-280).
 void LayerNormFunction::apply_backward() {
   auto Y = output.lock();
   if (!Y || !Y->get_gradient_ptr()) return;
   Scratch ws(pa_layer_norm_bwd_workspace_size(M, N), stream());
-  Scratch dx(input->requires_grad() ? static_cast<size_t>(M) * N * sizeof(float) : 0, stream());
-  check_status(pa_layer_norm_bwd(Y->get_gradient_ptr(), input->get_data_ptr(), mean->get_data_ptr(),
-                                 rstd->get_data_ptr(), gamma->get_data_ptr(),
-                                 static_cast<float*>(dx.get()),
-                                 gamma->requires_grad() ? gamma->get_gradient_ptr() : nullptr,
-                                 beta->requires_grad() ? beta->get_gradient_ptr() : nullptr, M, N,
-                                 ws.get(), ws.size(), ps(stream())),
+  check_status(pa_layer_norm_bwd_accumulate(
+                   Y->get_gradient_ptr(), input->get_data_ptr(), mean->get_data_ptr(),
+                   rstd->get_data_ptr(), gamma->get_data_ptr(),
+                   input->requires_grad() ? input->get_gradient_ptr() : nullptr,
+                   gamma->requires_grad() ? gamma->get_gradient_ptr() : nullptr,
+                   beta->requires_grad() ? beta->get_gradient_ptr() : nullptr, M, N, ws.get(),
+                   ws.size(), ps(stream())),
                "LayerNorm backward");
-  if (input->requires_grad())
-    check_status(pa_grad_accumulate(static_cast<const float*>(dx.get()), input->get_gradient_ptr(),
-                                    static_cast<size_t>(M) * N, ps(stream())),
-                 "LayerNorm backward");
 }
 
 }  // namespace core

@@ -90,7 +90,7 @@ std::shared_ptr<Tensor> mse_loss(const std::shared_ptr<Tensor>& preds,
 
 void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
             const std::shared_ptr<Tensor>& bias, uint32_t num_parts,
-            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream) {
+            std::vector<std::shared_ptr<Tensor>>& parts, const cudaStream_t& stream, bool relu) {
   const auto a = A->get_shape(), w = W->get_shape();
   if (w.size() != 2) throw std::runtime_error("Linear: W (weights) must be 2D");
   if (a.empty() || a.back() != w[0])
@@ -98,7 +98,7 @@ void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
   const int K = static_cast<int>(w[0]), N = static_cast<int>(w[1]);
   if (bias->numel() != static_cast<size_t>(N))
     throw std::runtime_error("Linear: bias must have W's output dimension");
-  if (num_parts < 1 || num_parts > 3 || N % num_parts)
+  if (num_parts < 1 || num_parts > 3 || N % num_parts || (relu && num_parts != 1))
     throw std::runtime_error("Linear: 1 to 3 parts, dividing the output dimension");
   const int M = static_cast<int>(A->numel() / K);
   const bool g = A->requires_grad() || W->requires_grad() || bias->requires_grad();
@@ -111,11 +111,17 @@ void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
     outs.push_back(mine.back()->get_data_ptr());
   }
   Scratch ws(pa_linear_workspace_size(M, K, N), stream);
-  check_status(pa_linear_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(), outs.data(),
-                             static_cast<int>(num_parts), M, K, N, ws.get(), ws.size(), ps(stream)),
-               "Linear");
+  if (relu)
+    check_status(pa_linear_relu_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
+                                    outs[0], M, K, N, ws.get(), ws.size(), ps(stream)),
+                 "Linear + ReLU");
+  else
+    check_status(pa_linear_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
+                               outs.data(), static_cast<int>(num_parts), M, K, N, ws.get(),
+                               ws.size(), ps(stream)),
+                 "Linear");
   if (g) {
-    auto node = std::make_shared<LinearFunction>(A, W, bias, mine);
+    auto node = std::make_shared<LinearFunction>(A, W, bias, mine, relu);
     for (auto& p : mine) p->set_grad_fn(node);
   }
   parts.insert(parts.end(), mine.begin(), mine.end());

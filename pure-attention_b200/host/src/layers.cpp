@@ -19,8 +19,8 @@ std::shared_ptr<core::Tensor> param(std::vector<uint32_t> shape) {
 }  // namespace
 
 // He-normal weights (std = sqrt(2 / fan_in)) and zero bias, as Linear.cpp:8-22.
-Linear::Linear(uint32_t in_channels, uint32_t out_channels)
-    : weight(param({in_channels, out_channels})), bias(param({1, out_channels})) {
+Linear::Linear(uint32_t in_channels, uint32_t out_channels, bool relu_)
+    : weight(param({in_channels, out_channels})), bias(param({1, out_channels})), relu(relu_) {
   core::pop_data_normal(weight, std::sqrt(2.0f / static_cast<float>(in_channels)), stream());
   core::pop_data_zeros(bias, stream());
 }
@@ -28,7 +28,7 @@ Linear::Linear(uint32_t in_channels, uint32_t out_channels)
 // X W + bias in one fused projection (matmul and bias add of Linear.cpp:24-35).
 std::shared_ptr<core::Tensor> Linear::forward(const std::shared_ptr<core::Tensor>& input) {
   std::vector<std::shared_ptr<core::Tensor>> out;
-  core::linear(input, weight, bias, 1, out, stream());
+  core::linear(input, weight, bias, 1, out, stream(), relu);
   return out[0];
 }
 

@@ -21,15 +21,17 @@ STATUS = {
 
 # Every symbol include/pa_kernels.h declares.
 EXPORTS = [
-    "pa_abi_version", "pa_status_string", "pa_device_status",
+    "pa_abi_version", "pa_status_string", "pa_device_status", "pa_set_f32_math", "pa_get_f32_math",
     "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
+    "pa_layer_norm_bwd_accumulate",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
-    "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd",
+    "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
+    "pa_linear_relu_bwd",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
-    "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_bwd", "pa_adam_step",
+    "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_bwd", "pa_adam_step", "pa_adam_step_multi",
     "pa_fill_normal", "pa_fill",
 ]
 
@@ -54,6 +56,8 @@ _flt = ctypes.c_float
 
 _SIGS = {
     "pa_abi_version": (_int, []),
+    "pa_set_f32_math": (_int, [_int]),
+    "pa_get_f32_math": (_int, []),
     "pa_status_string": (ctypes.c_char_p, [_int]),
     "pa_device_status": (_int, [_vp, _int]),
     "pa_attn_fwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
@@ -65,11 +69,14 @@ _SIGS = {
     "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
     "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
     "pa_layer_norm_bwd": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
+    "pa_layer_norm_bwd_accumulate": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
     "pa_matmul_workspace_size": (_sz, [_int] * 3),
     "pa_matmul": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_matmul_grad_x": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_matmul_grad_w": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_linear_workspace_size": (_sz, [_int] * 3),
+    "pa_linear_relu_fwd": (_int, [_vp] * 4 + [_int] * 3 + [_vp, _sz, _vp]),
+    "pa_linear_relu_bwd": (_int, [_vp] * 7 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_linear_fwd": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp), _int, _int, _int, _int, _vp, _sz, _vp]),
     "pa_linear_bwd": (_int, [_vp, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp, _int, _int, _int,
                              _vp, _sz, _vp]),
@@ -84,6 +91,7 @@ _SIGS = {
     "pa_mse_fwd": (_int, [_vp, _vp, _vp, _sz, _vp]),
     "pa_mse_bwd": (_int, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "pa_adam_step": (_int, [_vp, _vp, _vp, _vp, _sz] + [_flt] * 6 + [_vp]),
+    "pa_adam_step_multi": (_int, [_vp] * 5 + [_int] + [_flt] * 6 + [_vp]),
     "pa_fill_normal": (_int, [_vp, _sz, _flt, ctypes.c_uint64, _vp]),
     "pa_fill": (_int, [_vp, _sz, _flt, _vp]),
 }
@@ -117,6 +125,19 @@ def _ptr(t):
 def _stream():
     import torch
     return torch.cuda.current_stream().cuda_stream
+
+
+F32_MATH = {"split3": 0, "bf16": 1}
+
+
+def set_f32_math(mode):
+    """Arithmetic of the fp32 entry points for this thread: "split3" (default,
+    fp32-level accuracy) or "bf16" (one bf16 product, fp32 accumulation)."""
+    _check("pa_set_f32_math", load().pa_set_f32_math(F32_MATH[mode]))
+
+
+def get_f32_math():
+    return {v: k for k, v in F32_MATH.items()}[load().pa_get_f32_math()]
 
 
 def _check(fn, st):
@@ -216,14 +237,17 @@ def layer_norm_bwd_workspace_size(M, N):
     return load().pa_layer_norm_bwd_workspace_size(M, N)
 
 
-def layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, workspace, stream=None):
+def layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, workspace, stream=None,
+                   accumulate=False):
+    """dx is overwritten, or accumulated into with accumulate=True."""
     M = x.numel() // x.shape[-1]
     N = x.shape[-1]
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    st = load().pa_layer_norm_bwd(_ptr(dy), _ptr(x), _ptr(mean), _ptr(rstd), _ptr(gamma),
-                                  _ptr(dx), _ptr(dgamma), _ptr(dbeta), M, N, _ptr(workspace),
-                                  ws_bytes, _stream() if stream is None else stream)
-    _check("pa_layer_norm_bwd", st)
+    name = "pa_layer_norm_bwd_accumulate" if accumulate else "pa_layer_norm_bwd"
+    st = getattr(load(), name)(_ptr(dy), _ptr(x), _ptr(mean), _ptr(rstd), _ptr(gamma),
+                               _ptr(dx), _ptr(dgamma), _ptr(dbeta), M, N, _ptr(workspace),
+                               ws_bytes, _stream() if stream is None else stream)
+    _check(name, st)
 
 
 def matmul_workspace_size(M, N, K):
@@ -309,6 +333,24 @@ def linear_bwd(x, w, dy_parts, dx, dw, dbias, M, in_features, out_features, work
     _check("pa_linear_bwd", load().pa_linear_bwd(_ptr(x), _ptr(w), arr, len(dy_parts), opt(dx), opt(dw),
                                                  opt(dbias), M, in_features, out_features, _ptr(ws),
                                                  nb, _stream() if stream is None else stream))
+
+
+def linear_relu_fwd(x, w, bias, y, M, in_features, out_features, workspace=None, stream=None):
+    """y = max(0, x w + bias) (bias may be None)."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    _check("pa_linear_relu_fwd", load().pa_linear_relu_fwd(
+        _ptr(x), _ptr(w), _ptr(bias) if bias is not None else None, _ptr(y), M, in_features,
+        out_features, _ptr(ws), nb, _stream() if stream is None else stream))
+
+
+def linear_relu_bwd(x, w, y, dy, dx, dw, dbias, M, in_features, out_features, workspace=None,
+                    stream=None):
+    """With dZ = dy * (y > 0): dx += dZ w^T, dw += x^T dZ, dbias += colsum(dZ)."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    opt = lambda t: _ptr(t) if t is not None else None
+    _check("pa_linear_relu_bwd", load().pa_linear_relu_bwd(
+        _ptr(x), _ptr(w), _ptr(y), _ptr(dy), opt(dx), opt(dw), opt(dbias), M, in_features,
+        out_features, _ptr(ws), nb, _stream() if stream is None else stream))
 
 
 def split_last_dim(inp, outs, rows, width, stream=None):

@@ -250,3 +250,36 @@ def test_attention_f32_matches_reference_golden_c1():
     assert np.max(np.abs(lse - z["lse"])) < 1e-4
     assert rel_err(dk, z["dk"]) < F32_TOL
     assert rel_err(dv, z["dv"]) < F32_TOL
+
+
+# ---------------------------------------------------------------- fp32 tensors, bf16 math
+@pytest.fixture
+def bf16_math():
+    import pa_capi
+    pa_capi.set_f32_math("bf16")
+    yield
+    pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,H,D", [(2, 256, 2, 64), (1, 300, 3, 64)])
+def test_attention_f32_tensors_bf16_math(B, L, H, D, bf16_math):
+    """fp32 q, k, v, dO computed in the bf16 math mode (the bf16 d=64 kernels
+    on bf16 roundings, fp32 O / dQ / dK / dV): the bf16 path's accuracy
+    against the oracle on the rounded inputs, and accumulate adds into the
+    fp32 gradients."""
+    import pa_capi
+    shape = (B, L, H, D)
+    raw = [seeded_normal(s, shape, 0.5) for s in (B + L + 7, B + L + 8, B + L + 9, B + L + 10)]
+    rounded = [torch.from_numpy(x).to(torch.bfloat16).float().numpy().astype(np.float64) for x in raw]
+    tq, tk, tv, tg = (torch.from_numpy(x).cuda() for x in raw)
+    o = torch.empty_like(tq)
+    lse = torch.empty(B * H, L, device="cuda")
+    pa_capi.attn_fwd(tq, tk, tv, o, lse)
+    d = pa_capi.attn_desc(tq)
+    ws = torch.empty(pa_capi.attn_bwd_workspace_size(d), dtype=torch.uint8, device="cuda")
+    dq, dk, dv = (torch.ones_like(tq) for _ in range(3))
+    pa_capi.attn_bwd(tq, tk, tv, o, tg, lse, dq, dk, dv, ws, accumulate=True)
+    assert pa_capi.device_status() == 0
+    f = lambda t: t.cpu().numpy().astype(np.float64)
+    _check(tuple(rounded), (f(o), f(lse), f(dq), f(dk), f(dv)), accumulate=True)

@@ -4,7 +4,9 @@ forward and backward, bias add / bias grad / grad accumulate / residual add,
 and the last-dimension split and its adjoint.
 
 Tolerances (fp32 path): GEMMs 1e-4 norm-wise (bf16 hi/lo split products),
-LayerNorm 1e-5 (y, dgamma, dbeta) and 1e-4 (dX), elementwise 1e-6."""
+LayerNorm 1e-5 (y, dgamma, dbeta) and 1e-4 (dX), elementwise 1e-6. In the
+bf16 math mode the GEMMs are checked against the oracle on bf16-rounded
+operands (exact products, fp32 accumulation): 1e-5."""
 import numpy as np
 import pytest
 
@@ -94,6 +96,12 @@ def test_layer_norm_matches_oracle(M, N):
     assert rel_err(_np(dx), odx) < 1e-4
     assert rel_err(_np(dg), dg0 + odg) < 1e-5
     assert rel_err(_np(db), db0 + odb) < 1e-5
+    # accumulating form: dx += dL/dx (the residual branch's gradient kept)
+    dx0 = seeded_normal(5, (M, N))
+    dxa = _cu(dx0)
+    pa_capi.layer_norm_bwd(_cu(dy), _cu(x), mean, rstd, _cu(gamma), dxa, None, None, None,
+                           accumulate=True)
+    assert rel_err(_np(dxa), dx0 + odx) < 1e-4
 
 
 @pytest.mark.gpu
@@ -134,6 +142,47 @@ def test_elementwise_kernels_match_oracle():
     db = _cu(db0)
     pa_capi.bias_grad(_cu(a), db, M, N)
     assert rel_err(_np(db), oracle.bias_grad(a, db0)) < 1e-6
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N", [(16384, 1024), (16384, 4096), (8192, 1536), (300, 12), (77, 130)])
+def test_bias_grad_large_and_ragged(M, N):
+    """Column sums split over many CTAs (two stages) or one stage for small or
+    unaligned shapes; accumulated into db; deterministic."""
+    import oracle
+    import pa_capi
+    a = seeded_normal(M + N, (M, N))
+    db0 = seeded_normal(15, (N,))
+    outs = []
+    for _ in range(2):
+        db = _cu(db0)
+        pa_capi.bias_grad(_cu(a), db, M, N)
+        outs.append(_np(db))
+    assert rel_err(outs[0], oracle.bias_grad(a, db0)) < 1e-6
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,offset", [(16384 * 1024, 0), (16384 * 1024 + 3, 1), (5, 0), (1000, 0)])
+def test_mse_forward_matches_float64(n, offset):
+    """loss = mean((p - t)^2): two-stage deterministic reduction; an odd
+    length and a 4-byte offset take the scalar path."""
+    import ctypes
+    import pa_capi
+    p = seeded_normal(21, (n + offset,))
+    t = seeded_normal(22, (n + offset,))
+    pd, td = _cu(p), _cu(t)
+    want = np.mean((p[offset:].astype(np.float64) - t[offset:]) ** 2)
+    got = []
+    for _ in range(2):
+        loss = torch.full((1,), float("nan"), device="cuda")
+        st = pa_capi.load().pa_mse_fwd(ctypes.c_void_p(pd.data_ptr() + 4 * offset),
+                                       ctypes.c_void_p(td.data_ptr() + 4 * offset),
+                                       ctypes.c_void_p(loss.data_ptr()), n, None)
+        assert st == 0
+        got.append(float(loss.item()))
+    assert abs(got[0] - want) < 1e-6 * want
+    assert got[0] == got[1]
 
 
 @pytest.mark.gpu
@@ -194,3 +243,125 @@ def test_linear_bwd_accumulates_like_oracle(M, IN, OUT, n):
     dw2 = _cu(dw0)
     pa_capi.linear_bwd(_cu(x), _cu(w), [_cu(p) for p in parts], None, dw2, None, M, IN, OUT)
     assert rel_err(_np(dw2), oracle.matmul_grad_w(x, dy, dw0)) < GEMM_TOL
+
+
+# ---------------------------------------------------------------- bf16 math mode
+BF16_MATH_TOL = 1e-5
+
+
+def _rb(x):
+    """x rounded to bf16 (round to nearest even), back as float32."""
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(torch.bfloat16).float().numpy()
+
+
+@pytest.fixture
+def bf16_math():
+    import pa_capi
+    pa_capi.set_f32_math("bf16")
+    assert pa_capi.get_f32_math() == "bf16"
+    yield
+    pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(256, 192, 320), (100, 70, 50), (8192, 1536, 512)])
+def test_matmul_bf16_math_matches_rounded_oracle(M, N, K, bf16_math):
+    import oracle
+    import pa_capi
+    a, b = seeded_normal(M, (M, K)), seeded_normal(N, (K, N))
+    c = torch.empty(M, N, device="cuda")
+    pa_capi.matmul(_cu(a), _cu(b), c, M, N, K)
+    assert rel_err(_np(c), oracle.matmul(_rb(a), _rb(b))) < BF16_MATH_TOL
+    dy, w = seeded_normal(K + 1, (M, K)), seeded_normal(K + 2, (N, K))
+    dx0 = seeded_normal(3, (M, N))
+    dx = _cu(dx0)
+    pa_capi.matmul_grad_x(_cu(dy), _cu(w), dx, M, N, K)
+    assert rel_err(_np(dx), oracle.matmul_grad_x(_rb(dy), _rb(w), dx0)) < BF16_MATH_TOL
+    x = seeded_normal(K + 3, (M, N))
+    dw0 = seeded_normal(4, (N, K))
+    dw = _cu(dw0)
+    pa_capi.matmul_grad_w(_cu(x), _cu(dy), dw, M, N, K)
+    assert rel_err(_np(dw), oracle.matmul_grad_w(_rb(x), _rb(dy), dw0)) < BF16_MATH_TOL
+
+
+@pytest.mark.gpu
+def test_linear_bf16_math_matches_rounded_oracle(bf16_math):
+    """Fused projection (three column blocks, bias) forward and backward in
+    the bf16 math mode; the bias and its gradient stay fp32."""
+    import oracle
+    import pa_capi
+    M, IN, OUT, n = 4096, 256, 768, 3
+    x, w, bias = seeded_normal(1, (M, IN)), seeded_normal(2, (IN, OUT)), seeded_normal(3, (OUT,))
+    outs = [torch.empty(M, OUT // n, device="cuda") for _ in range(n)]
+    ws = torch.empty(pa_capi.linear_workspace_size(M, IN, OUT), dtype=torch.uint8, device="cuda")
+    pa_capi.linear_fwd(_cu(x), _cu(w), _cu(bias), outs, M, IN, OUT, ws)
+    ref = oracle.matmul(_rb(x), _rb(w)) + bias
+    got = np.concatenate([_np(o) for o in outs], axis=1)
+    assert rel_err(got, ref) < BF16_MATH_TOL
+    dys = [seeded_normal(10 + i, (M, OUT // n)) for i in range(n)]
+    dy = np.concatenate(dys, axis=1)
+    dx0, dw0, db0 = seeded_normal(4, (M, IN)), seeded_normal(5, (IN, OUT)), seeded_normal(6, (OUT,))
+    dx, dw, db = _cu(dx0), _cu(dw0), _cu(db0)
+    pa_capi.linear_bwd(_cu(x), _cu(w), [_cu(d) for d in dys], dx, dw, db, M, IN, OUT, ws)
+    assert rel_err(_np(dx), oracle.matmul_grad_x(_rb(dy), _rb(w), dx0)) < BF16_MATH_TOL
+    assert rel_err(_np(dw), oracle.matmul_grad_w(_rb(x), _rb(dy), dw0)) < BF16_MATH_TOL
+    assert rel_err(_np(db), oracle.bias_grad(dy, db0)) < 1e-6
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("math_mode", ["split3", "bf16"])
+def test_linear_relu_matches_oracle(math_mode):
+    """Y = max(0, X W + b) with the clamp in the GEMM epilogue; backward masks
+    dY by Y > 0 in the operand gather and in the bias column sums."""
+    import oracle
+    import pa_capi
+    M, IN, OUT = 2048, 256, 1024
+    x, w, bias = seeded_normal(31, (M, IN)), seeded_normal(32, (IN, OUT), 0.1), seeded_normal(33, (OUT,))
+    dy = seeded_normal(34, (M, OUT))
+    rb = _rb if math_mode == "bf16" else (lambda a: a)
+    tol = BF16_MATH_TOL if math_mode == "bf16" else GEMM_TOL
+    pa_capi.set_f32_math(math_mode)
+    try:
+        y = torch.full((M, OUT), float("nan"), device="cuda")
+        ws = torch.empty(pa_capi.linear_workspace_size(M, IN, OUT), dtype=torch.uint8, device="cuda")
+        pa_capi.linear_relu_fwd(_cu(x), _cu(w), _cu(bias), y, M, IN, OUT, ws)
+        z = oracle.matmul(rb(x), rb(w)) + bias
+        yn = _np(y)
+        assert rel_err(yn, np.maximum(z, 0.0)) < tol
+        assert (yn >= 0).all() and 0.2 < (yn > 0).mean() < 0.8
+        dx0, dw0, db0 = seeded_normal(35, (M, IN)), seeded_normal(36, (IN, OUT)), seeded_normal(37, (OUT,))
+        dx, dw, db = _cu(dx0), _cu(dw0), _cu(db0)
+        pa_capi.linear_relu_bwd(_cu(x), _cu(w), y, _cu(dy), dx, dw, db, M, IN, OUT, ws)
+        dz = np.where(yn > 0, dy, 0.0)
+        assert rel_err(_np(dx), oracle.matmul_grad_x(rb(dz), rb(w), dx0)) < tol
+        assert rel_err(_np(dw), oracle.matmul_grad_w(rb(x), rb(dz), dw0)) < tol
+        assert rel_err(_np(db), oracle.bias_grad(dz, db0)) < 1e-6
+    finally:
+        pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
+def test_adam_multi_tensor_matches_single_tensor_updates():
+    """pa_adam_step_multi over 100 tensors (three launches of up to 48; sizes
+    ragged, empty, one element and several chunks) equals pa_adam_step per
+    tensor."""
+    import ctypes
+    import pa_capi
+    lib = pa_capi.load()
+    rng = np.random.default_rng(40)
+    sizes = [int(s) for s in rng.integers(1, 20000, size=96)] + [0, 1, 3, 70001]
+    def make(seed):
+        g = np.random.default_rng(seed)
+        return [torch.from_numpy(g.standard_normal(max(n, 1)).astype(np.float32)).cuda() for n in sizes]
+    w1, g1, m1, v1 = make(1), make(2), make(3), [t.abs() for t in make(4)]
+    w2, m2, v2 = [t.clone() for t in w1], [t.clone() for t in m1], [t.clone() for t in v1]
+    args = (1e-3, 0.9, 0.999, 1e-8, 0.19, 0.002)
+    for i, n in enumerate(sizes):
+        assert lib.pa_adam_step(w1[i].data_ptr(), g1[i].data_ptr(), m1[i].data_ptr(), v1[i].data_ptr(),
+                                n, *args, None) == 0
+    arr = lambda ts: (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+    szs = (ctypes.c_size_t * len(sizes))(*sizes)
+    assert lib.pa_adam_step_multi(arr(w2), arr(g1), arr(m2), arr(v2), szs, len(sizes), *args, None) == 0
+    assert pa_capi.device_status() == 0
+    for a, b in zip(w1 + m1 + v1, w2 + m2 + v2):
+        np.testing.assert_allclose(_np(b), _np(a), rtol=2e-6, atol=1e-7)
