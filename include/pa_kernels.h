@@ -218,6 +218,11 @@ int pa_grad_accumulate(const float* src, float* dst, size_t n, pa_stream_t strea
 
 /* db[N] += column sums of dY[M,N]. Replaces launch_sum_rows_grad (Launchers.cuh:91-97). */
 int pa_bias_grad(const float* dY, float* db, int M, int N, pa_stream_t stream);
+/* The same sums split over the whole GPU in two deterministic stages, with a
+ * workspace of pa_bias_grad_workspace_size(M, N) bytes (16-byte aligned). */
+size_t pa_bias_grad_workspace_size(int M, int N);
+int pa_bias_grad_ws(const float* dY, float* db, int M, int N, void* workspace,
+                    size_t workspace_bytes, pa_stream_t stream);
 
 /* Split [rows, parts*width] along the last dimension into `parts` arrays of
  * [rows, width]; outs is a HOST array of `parts` device pointers (parts <= 8).
@@ -240,6 +245,12 @@ int pa_relu_fwd(const float* x, float* y, size_t n, pa_stream_t stream);
 int pa_relu_bwd(const float* dy, const float* x, float* dx, size_t n, pa_stream_t stream);
 /* loss[0] = mean((pred - target)^2), deterministic. Replaces launch_mse_forward (Launchers.cuh:116-122). */
 int pa_mse_fwd(const float* pred, const float* target, float* loss, size_t n, pa_stream_t stream);
+/* pa_mse_fwd computes the sum in one CTA (deterministic, slow for large n);
+ * pa_mse_fwd_ws spreads it over the GPU in two deterministic stages using
+ * pa_mse_fwd_workspace_size(n) bytes (16-byte aligned). */
+size_t pa_mse_fwd_workspace_size(size_t n);
+int pa_mse_fwd_ws(const float* pred, const float* target, float* loss, size_t n, void* workspace,
+                  size_t workspace_bytes, pa_stream_t stream);
 /* dpred += 2/n * (pred - target) * dloss[0]. Replaces launch_mse_backward (Launchers.cuh:107-114). */
 int pa_mse_bwd(const float* pred, const float* target, const float* dloss, float* dpred, size_t n,
                pa_stream_t stream);

@@ -326,6 +326,21 @@ int pa_bias_grad(const float* dY, float* db, int M, int N, pa_stream_t stream) {
   return pa::launch_bias_grad(dY, db, M, N, static_cast<cudaStream_t>(stream));
 }
 
+size_t pa_bias_grad_workspace_size(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  return pa::bias_grad_workspace_bytes(static_cast<uint32_t>(M), static_cast<uint32_t>(N));
+}
+
+int pa_bias_grad_ws(const float* dY, float* db, int M, int N, void* workspace,
+                    size_t workspace_bytes, pa_stream_t stream) {
+  if (!dY || !db) return PA_ERR_NULL;
+  if (M <= 0 || N <= 0) return PA_ERR_SHAPE;
+  if (!workspace || workspace_bytes < pa::bias_grad_workspace_bytes(M, N)) return PA_ERR_WORKSPACE;
+  if (!al16(workspace)) return PA_ERR_ALIGN;
+  return pa::launch_bias_grad_masked(dY, nullptr, db, M, N, static_cast<float*>(workspace),
+                                     static_cast<cudaStream_t>(stream));
+}
+
 int pa_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
                       uint32_t width, pa_stream_t stream) {
   if (!in || !outs) return PA_ERR_NULL;
@@ -360,7 +375,19 @@ int pa_relu_bwd(const float* dy, const float* x, float* dx, size_t n, pa_stream_
 int pa_mse_fwd(const float* pred, const float* target, float* loss, size_t n, pa_stream_t stream) {
   if (!pred || !target || !loss) return PA_ERR_NULL;
   if (n == 0) return PA_ERR_SHAPE;
-  return pa::launch_mse_fwd(pred, target, loss, n, static_cast<cudaStream_t>(stream));
+  return pa::launch_mse_fwd(pred, target, loss, n, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+size_t pa_mse_fwd_workspace_size(size_t n) { return n ? pa::mse_workspace_bytes(n) : 0; }
+
+int pa_mse_fwd_ws(const float* pred, const float* target, float* loss, size_t n, void* workspace,
+                  size_t workspace_bytes, pa_stream_t stream) {
+  if (!pred || !target || !loss) return PA_ERR_NULL;
+  if (n == 0) return PA_ERR_SHAPE;
+  if (!workspace || workspace_bytes < pa::mse_workspace_bytes(n)) return PA_ERR_WORKSPACE;
+  if (!al16(workspace)) return PA_ERR_ALIGN;
+  return pa::launch_mse_fwd(pred, target, loss, n, static_cast<float*>(workspace),
+                            static_cast<cudaStream_t>(stream));
 }
 int pa_mse_bwd(const float* pred, const float* target, const float* dloss, float* dpred, size_t n,
                pa_stream_t stream) {

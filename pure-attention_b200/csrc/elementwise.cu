@@ -182,32 +182,48 @@ int launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_
   return done();
 }
 
-// db += column sums of dy. Rows are split over enough CTAs to fill the GPU
-// (stage 1 into a stream-ordered scratch), then bias_grad_kernel sums the
-// partial rows in fixed order: deterministic for a given shape and device.
+namespace {
+
+// Row chunks of the two-stage column sum: about four CTAs per SM, at least
+// 64 rows each; returns the rows per chunk and sets R, the chunk count.
+uint32_t colsum_chunks(uint32_t M, uint32_t N, uint32_t* R) {
+  const uint32_t col_blocks = (N + 127) / 128;
+  uint32_t r = (4u * static_cast<uint32_t>(sm_count()) + col_blocks - 1) / col_blocks;
+  if (r > (M + 63) / 64) r = (M + 63) / 64;
+  if (r < 1) r = 1;
+  const uint32_t rows_per = (M + r - 1) / r;
+  *R = (M + rows_per - 1) / rows_per;
+  return rows_per;
+}
+
+}  // namespace
+
+size_t bias_grad_workspace_bytes(uint32_t M, uint32_t N) {
+  uint32_t R = 1;
+  colsum_chunks(M, N, &R);
+  return static_cast<size_t>(R) * N * sizeof(float);
+}
+
+// db += column sums of dy (rows counted only where mask > 0, if given). With a
+// workspace of bias_grad_workspace_bytes: rows split over enough CTAs to fill
+// the GPU, partial rows to the workspace, then bias_grad_kernel sums them in
+// fixed order. Without one (or for unaligned rows): one pass of 32-column CTAs.
+// Deterministic for a given shape and device either way.
 int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStream_t s) {
-  return launch_bias_grad_masked(dy, nullptr, db, M, N, s);
+  return launch_bias_grad_masked(dy, nullptr, db, M, N, nullptr, s);
 }
 
 int launch_bias_grad_masked(const float* dy, const float* mask, float* db, uint32_t M, uint32_t N,
-                            cudaStream_t s) {
-  const uint32_t col_blocks = (N + 127) / 128;
-  uint32_t R = (4u * static_cast<uint32_t>(sm_count()) + col_blocks - 1) / col_blocks;
-  if (R > (M + 63) / 64) R = (M + 63) / 64;  // at least 64 rows per CTA
-  float* part = nullptr;
-  if (N % 4 != 0 || !al16(dy) || (mask && !al16(mask)) || R < 2 ||
-      cudaMallocAsync(reinterpret_cast<void**>(&part), static_cast<size_t>(R) * N * sizeof(float),
-                      s) != cudaSuccess) {
+                            float* ws, cudaStream_t s) {
+  uint32_t R = 1;
+  const uint32_t rows_per = colsum_chunks(M, N, &R);
+  if (!ws || N % 4 != 0 || !al16(dy) || (mask && !al16(mask)) || !al16(ws) || R < 2) {
     bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(dy, mask, db, M, N);
     return done();
   }
-  const uint32_t rows_per = (M + R - 1) / R;
-  R = (M + rows_per - 1) / rows_per;
-  colsum_partial_kernel<<<dim3(col_blocks, R), 256, 0, s>>>(dy, mask, part, M, N, rows_per);
-  bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(part, nullptr, db, R, N);
-  const int st = done();
-  cudaFreeAsync(part, s);
-  return st;
+  colsum_partial_kernel<<<dim3((N + 127) / 128, R), 256, 0, s>>>(dy, mask, ws, M, N, rows_per);
+  bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(ws, nullptr, db, R, N);
+  return done();
 }
 
 int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,

@@ -319,9 +319,22 @@ int launch_gemm_f32(int mode, const float* A, const float* B, float* C, int M, i
 }
 
 // Projection Y[M, OUT] = X[M, IN] W[IN, OUT] (+ bias), as column blocks.
+// Bias-gradient partials of the widest column block (1, 2 or 3 blocks).
+size_t bias_partials_bytes(int M, int OUT) {
+  size_t b = 0;
+  for (int n = 1; n <= 3; ++n)
+    if (OUT % n == 0) {
+      const size_t x = up256(bias_grad_workspace_bytes(static_cast<uint32_t>(M),
+                                                       static_cast<uint32_t>(OUT / n)));
+      b = x > b ? x : b;
+    }
+  return b;
+}
+
 size_t linear_workspace_bytes(int M, int IN, int OUT) {
   const size_t fwd = planes_bytes(M, IN) + planes_bytes(IN, OUT);
-  const size_t bwd = planes_bytes(M, OUT) + planes_bytes(IN, OUT) + planes_bytes(M, IN);
+  const size_t bwd = planes_bytes(M, OUT) + planes_bytes(IN, OUT) + planes_bytes(M, IN) +
+                     bias_partials_bytes(M, OUT);
   return fwd > bwd ? fwd : bwd;
 }
 
@@ -350,6 +363,7 @@ int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_pa
                       int OUT, void* ws, uint32_t* status, cudaStream_t s) {
   uint8_t* w = static_cast<uint8_t*>(ws);
   const Planes dy = carve(w, M, OUT), wp = carve(w, IN, OUT), xp = carve(w, M, IN);
+  float* bias_ws = reinterpret_cast<float*>(w);  // bias_partials_bytes(M, OUT)
   // gather the column-block gradients into one pair of planes (row pitch round8(OUT))
   const int part = OUT / n_parts;
   for (int p = 0; p < n_parts; ++p) {
@@ -375,7 +389,8 @@ int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_pa
   if (dbias)
     for (int p = 0; p < n_parts; ++p) {
       const int st = launch_bias_grad_masked(dy_parts[p], relu_out, dbias + p * part,
-                                             static_cast<uint32_t>(M), static_cast<uint32_t>(part), s);
+                                             static_cast<uint32_t>(M), static_cast<uint32_t>(part),
+                                             bias_ws, s);
       if (st != PA_OK) return st;
     }
   return PA_OK;

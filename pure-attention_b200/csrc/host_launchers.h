@@ -60,8 +60,10 @@ int launch_bias_add(const float* a, const float* bias, float* out, uint32_t M, u
                     cudaStream_t s);
 int launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
 int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStream_t s);
+// With ws (bias_grad_workspace_bytes): two stages over the whole GPU; without: one pass.
+size_t bias_grad_workspace_bytes(uint32_t M, uint32_t N);
 int launch_bias_grad_masked(const float* dy, const float* mask, float* db, uint32_t M, uint32_t N,
-                            cudaStream_t s);
+                            float* ws, cudaStream_t s);
 int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
                           uint32_t width, cudaStream_t s);
 int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint32_t parts,
@@ -93,7 +95,8 @@ int launch_adam_multi(float* const* w, const float* const* g, float* const* m, f
                       const size_t* n, int count, float lr, float b1, float b2, float eps, float c1,
                       float c2, cudaStream_t s);
 int launch_relu_bwd(const float* dy, const float* x, float* dx, size_t n, cudaStream_t s);
-int launch_mse_fwd(const float* p, const float* t, float* loss, size_t n, cudaStream_t s);
+size_t mse_workspace_bytes(size_t n);
+int launch_mse_fwd(const float* p, const float* t, float* loss, size_t n, float* ws, cudaStream_t s);
 int launch_mse_bwd(const float* p, const float* t, const float* dl, float* dp, size_t n,
                    cudaStream_t s);
 int launch_adam(float* w, const float* g, float* m, float* v, size_t n, float lr, float b1, float b2,

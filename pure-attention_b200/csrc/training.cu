@@ -55,6 +55,19 @@ __device__ __forceinline__ float block_sum(float v) {
   return v;
 }
 
+// MSE without workspace: one CTA (fixed order, deterministic, slow on large n).
+__global__ void __launch_bounds__(1024)
+    mse_fwd_kernel(const float* __restrict__ p, const float* __restrict__ t, float* __restrict__ loss,
+                   size_t n) {
+  float acc = 0.f;
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float d = p[i] - t[i];
+    acc = fmaf(d, d, acc);
+  }
+  acc = block_sum(acc);
+  if (threadIdx.x == 0) loss[0] = acc / static_cast<float>(n);
+}
+
 // MSE, stage 1: CTA b sums (p - t)^2 over its grid-stride share into part[b].
 // The grid depends only on n, so the summation order (and the loss) is
 // deterministic.
@@ -206,18 +219,23 @@ int launch_relu_bwd(const float* dy, const float* x, float* dx, size_t n, cudaSt
   relu_bwd_kernel<<<grid(n), 256, 0, s>>>(dy, x, dx, n);
   return ok();
 }
-// Two launches over a stream-ordered scratch of one float per stage-1 CTA.
-int launch_mse_fwd(const float* p, const float* t, float* loss, size_t n, cudaStream_t s) {
+int mse_parts(size_t n) {
   const size_t want = (n + 4 * 256 - 1) / (4 * 256), cap = static_cast<size_t>(sms()) * 4;
-  const int parts = static_cast<int>(want < cap ? (want ? want : 1) : cap);
-  float* part = nullptr;
-  if (cudaMallocAsync(reinterpret_cast<void**>(&part), parts * sizeof(float), s) != cudaSuccess)
-    return PA_ERR_LAUNCH;
-  mse_partial_kernel<<<parts, 256, 0, s>>>(p, t, part, n);
-  mse_final_kernel<<<1, 1024, 0, s>>>(part, parts, loss, n);
-  const int st = ok();
-  cudaFreeAsync(part, s);
-  return st;
+  return static_cast<int>(want < cap ? (want ? want : 1) : cap);
+}
+size_t mse_workspace_bytes(size_t n) { return static_cast<size_t>(mse_parts(n)) * sizeof(float); }
+
+// With a workspace (one float per stage-1 CTA): two launches over the whole GPU.
+int launch_mse_fwd(const float* p, const float* t, float* loss, size_t n, float* ws,
+                   cudaStream_t s) {
+  if (!ws) {
+    mse_fwd_kernel<<<1, 1024, 0, s>>>(p, t, loss, n);
+    return ok();
+  }
+  const int parts = mse_parts(n);
+  mse_partial_kernel<<<parts, 256, 0, s>>>(p, t, ws, n);
+  mse_final_kernel<<<1, 1024, 0, s>>>(ws, parts, loss, n);
+  return ok();
 }
 int launch_mse_bwd(const float* p, const float* t, const float* dl, float* dp, size_t n,
                    cudaStream_t s) {

@@ -238,6 +238,59 @@ class DenoiseTrainer:
         self.load(x_host, t_host)
         return float(device_view(self.step_resident()).item())
 
+    def train(self, batches):
+        """Pipelined loop over (x, t) batches in pinned host memory; returns
+        the losses. Batch i+1 is copied on a side stream into the second
+        input buffer while step i computes, and each step's loss is copied to
+        pinned host memory without blocking and read one step later, so the
+        host keeps the GPU fed (what step() cannot do: it copies, then waits
+        for the loss)."""
+        torch = _torch()
+        batches = list(batches)
+        if not batches:
+            return []
+        if not hasattr(self, "_bufs"):
+            self._bufs = [(self.x, self.t)] + [
+                (pa.Tensor(list(self.shape), False), pa.Tensor(list(self.shape), False))]
+            self._copy_stream = torch.cuda.Stream()
+            self._loss_host = torch.empty(2, dtype=torch.float32).pin_memory()
+        main = torch.cuda.default_stream()  # the operators' stream
+        cs = self._copy_stream
+        copied = [torch.cuda.Event() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]
+        read = [torch.cuda.Event() for _ in range(2)]
+
+        def copy_in(i):
+            x, t = batches[i]
+            bx, bt = self._bufs[i % 2]
+            with torch.cuda.stream(cs):
+                if i >= 2:
+                    cs.wait_event(freed[i % 2])  # step i-2 is done with this buffer
+                device_view(bx).view(x.shape).copy_(x, non_blocking=True)
+                device_view(bt).view(t.shape).copy_(t, non_blocking=True)
+                copied[i % 2].record(cs)
+
+        losses = []
+        copy_in(0)
+        for i in range(len(batches)):
+            if i + 1 < len(batches):
+                copy_in(i + 1)
+            main.wait_event(copied[i % 2])
+            self.x, self.t = self._bufs[i % 2]
+            loss = self.step_resident()
+            freed[i % 2].record(main)
+            if i >= 2:
+                read[i % 2].synchronize()  # loss of step i-2 (its slot is reused now)
+                losses.append(float(self._loss_host[i % 2]))
+            self._loss_host[i % 2].copy_(device_view(loss).view(()), non_blocking=True)
+            read[i % 2].record(main)
+            del loss
+        for i in range(max(0, len(batches) - 2), len(batches)):
+            read[i % 2].synchronize()
+            losses.append(float(self._loss_host[i % 2]))
+        self.x, self.t = self._bufs[0]
+        return losses
+
     def save(self, path):
         """Parameters, Adam moments and step count to an .npz file."""
         m, v = self.opt.state()

@@ -54,8 +54,10 @@ void AddFunction::apply_backward() {
                    "add grad");
     } else {
       const int N = static_cast<int>(bias_input->numel());
-      check_status(pa_bias_grad(Y->get_gradient_ptr(), bias_input->get_gradient_ptr(),
-                                static_cast<int>(n / N), N, ps(stream())),
+      const int M = static_cast<int>(n / N);
+      Scratch ws(pa_bias_grad_workspace_size(M, N), stream());
+      check_status(pa_bias_grad_ws(Y->get_gradient_ptr(), bias_input->get_gradient_ptr(), M, N,
+                                   ws.get(), ws.size(), ps(stream())),
                    "bias grad");
     }
   }

@@ -81,8 +81,9 @@ std::shared_ptr<Tensor> mse_loss(const std::shared_ptr<Tensor>& preds,
   if (preds->numel() != targets->numel())
     throw std::runtime_error("MSE: predictions and targets differ in size");
   auto loss = std::make_shared<Tensor>(std::vector<uint32_t>{1}, preds->requires_grad(), false);
-  check_status(pa_mse_fwd(preds->get_data_ptr(), targets->get_data_ptr(), loss->get_data_ptr(),
-                          preds->numel(), ps(stream)),
+  Scratch ws(pa_mse_fwd_workspace_size(preds->numel()), stream);
+  check_status(pa_mse_fwd_ws(preds->get_data_ptr(), targets->get_data_ptr(), loss->get_data_ptr(),
+                             preds->numel(), ws.get(), ws.size(), ps(stream)),
                "MSE");
   if (preds->requires_grad()) loss->set_grad_fn(std::make_shared<MSEFunction>(preds, targets, loss));
   return loss;

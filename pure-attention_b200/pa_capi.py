@@ -29,9 +29,9 @@ EXPORTS = [
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
     "pa_linear_relu_bwd",
-    "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad",
+    "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad", "pa_bias_grad_workspace_size", "pa_bias_grad_ws",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
-    "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_bwd", "pa_adam_step", "pa_adam_step_multi",
+    "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_fwd_workspace_size", "pa_mse_fwd_ws", "pa_mse_bwd", "pa_adam_step", "pa_adam_step_multi",
     "pa_fill_normal", "pa_fill",
 ]
 
@@ -84,11 +84,15 @@ _SIGS = {
     "pa_add": (_int, [_vp] * 3 + [_sz, _vp]),
     "pa_grad_accumulate": (_int, [_vp] * 2 + [_sz, _vp]),
     "pa_bias_grad": (_int, [_vp] * 2 + [_int] * 2 + [_vp]),
+    "pa_bias_grad_workspace_size": (_sz, [_int, _int]),
+    "pa_bias_grad_ws": (_int, [_vp, _vp, _int, _int, _vp, _sz, _vp]),
     "pa_split_last_dim": (_int, [_vp, ctypes.POINTER(_vp), _u32, _u32, _u32, _vp]),
     "pa_concat_last_dim_grad": (_int, [ctypes.POINTER(_vp), _vp, _u32, _u32, _u32, _vp]),
     "pa_relu_fwd": (_int, [_vp, _vp, _sz, _vp]),
     "pa_relu_bwd": (_int, [_vp, _vp, _vp, _sz, _vp]),
     "pa_mse_fwd": (_int, [_vp, _vp, _vp, _sz, _vp]),
+    "pa_mse_fwd_workspace_size": (_sz, [_sz]),
+    "pa_mse_fwd_ws": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _vp]),
     "pa_mse_bwd": (_int, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "pa_adam_step": (_int, [_vp, _vp, _vp, _vp, _sz] + [_flt] * 6 + [_vp]),
     "pa_adam_step_multi": (_int, [_vp] * 5 + [_int] + [_flt] * 6 + [_vp]),
@@ -299,9 +303,18 @@ def grad_accumulate(src, dst, n, stream=None):
                                                            _stream() if stream is None else stream))
 
 
-def bias_grad(dy, db, M, N, stream=None):
-    _check("pa_bias_grad", load().pa_bias_grad(_ptr(dy), _ptr(db), M, N,
-                                               _stream() if stream is None else stream))
+def bias_grad(dy, db, M, N, stream=None, workspace=None):
+    """db += column sums of dy; with a workspace (bias_grad_workspace_size bytes) over the whole GPU."""
+    st = _stream() if stream is None else stream
+    if workspace is None:
+        _check("pa_bias_grad", load().pa_bias_grad(_ptr(dy), _ptr(db), M, N, st))
+    else:
+        _check("pa_bias_grad_ws", load().pa_bias_grad_ws(
+            _ptr(dy), _ptr(db), M, N, _ptr(workspace), workspace.numel() * workspace.element_size(), st))
+
+
+def bias_grad_workspace_size(M, N):
+    return load().pa_bias_grad_workspace_size(M, N)
 
 
 def linear_workspace_size(M, in_features, out_features):

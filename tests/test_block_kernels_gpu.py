@@ -147,42 +147,54 @@ def test_elementwise_kernels_match_oracle():
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,N", [(16384, 1024), (16384, 4096), (8192, 1536), (300, 12), (77, 130)])
 def test_bias_grad_large_and_ragged(M, N):
-    """Column sums split over many CTAs (two stages) or one stage for small or
-    unaligned shapes; accumulated into db; deterministic."""
+    """Column sums in one pass, or with a workspace split over many CTAs (two
+    stages; one pass for small or unaligned shapes); accumulated into db;
+    deterministic."""
     import oracle
     import pa_capi
     a = seeded_normal(M + N, (M, N))
     db0 = seeded_normal(15, (N,))
-    outs = []
-    for _ in range(2):
-        db = _cu(db0)
-        pa_capi.bias_grad(_cu(a), db, M, N)
-        outs.append(_np(db))
-    assert rel_err(outs[0], oracle.bias_grad(a, db0)) < 1e-6
-    np.testing.assert_array_equal(outs[0], outs[1])
+    ws = torch.empty(pa_capi.bias_grad_workspace_size(M, N), dtype=torch.uint8, device="cuda")
+    for w in (None, ws):  # one pass / two stages over the GPU
+        outs = []
+        for _ in range(2):
+            db = _cu(db0)
+            pa_capi.bias_grad(_cu(a), db, M, N, workspace=w)
+            outs.append(_np(db))
+        assert rel_err(outs[0], oracle.bias_grad(a, db0)) < 1e-6
+        np.testing.assert_array_equal(outs[0], outs[1])
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,offset", [(16384 * 1024, 0), (16384 * 1024 + 3, 1), (5, 0), (1000, 0)])
 def test_mse_forward_matches_float64(n, offset):
-    """loss = mean((p - t)^2): two-stage deterministic reduction; an odd
-    length and a 4-byte offset take the scalar path."""
+    """loss = mean((p - t)^2): with a workspace a two-stage reduction over the
+    GPU, without one a single CTA; both deterministic. An odd length and a
+    4-byte offset take the scalar path."""
     import ctypes
     import pa_capi
     p = seeded_normal(21, (n + offset,))
     t = seeded_normal(22, (n + offset,))
     pd, td = _cu(p), _cu(t)
     want = np.mean((p[offset:].astype(np.float64) - t[offset:]) ** 2)
-    got = []
-    for _ in range(2):
-        loss = torch.full((1,), float("nan"), device="cuda")
-        st = pa_capi.load().pa_mse_fwd(ctypes.c_void_p(pd.data_ptr() + 4 * offset),
-                                       ctypes.c_void_p(td.data_ptr() + 4 * offset),
-                                       ctypes.c_void_p(loss.data_ptr()), n, None)
-        assert st == 0
-        got.append(float(loss.item()))
-    assert abs(got[0] - want) < 1e-6 * want
-    assert got[0] == got[1]
+    lib = pa_capi.load()
+    ws = torch.empty(lib.pa_mse_fwd_workspace_size(n), dtype=torch.uint8, device="cuda")
+    args = (ctypes.c_void_p(pd.data_ptr() + 4 * offset), ctypes.c_void_p(td.data_ptr() + 4 * offset))
+    for with_ws in (True, False):
+        if not with_ws and n > 4 * 1024 * 1024:
+            continue  # the one-CTA form is for small losses
+        got = []
+        for _ in range(2):
+            loss = torch.full((1,), float("nan"), device="cuda")
+            if with_ws:
+                st = lib.pa_mse_fwd_ws(*args, ctypes.c_void_p(loss.data_ptr()), n, ws.data_ptr(),
+                                       ws.numel(), None)
+            else:
+                st = lib.pa_mse_fwd(*args, ctypes.c_void_p(loss.data_ptr()), n, None)
+            assert st == 0
+            got.append(float(loss.item()))
+        assert abs(got[0] - want) < 1e-6 * want
+        assert got[0] == got[1]
 
 
 @pytest.mark.gpu
