@@ -214,6 +214,253 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+
+// ---------------------------------------------------------------- bf16 math: persistent GEMM
+// One CTA per SM walks the 128 x 256 output tiles (tile i, i + gridDim.x, ...;
+// M-tile index fastest). K in blocks of 64 through a 4-stage TMA ring (A
+// 128 x 64 and B 256 x 64 bf16 per stage, 48 KB). The fp32 accumulator is
+// double-buffered in TMEM (2 x 256 columns): the epilogue warps drain tile i
+// while the MMA warp accumulates tile i + 1, and every MMA is M=128 N=256 K=16
+// (full rate; the 128 x 128 kernel above leaves the tensor core idle during
+// each epilogue and pays twice the operand traffic per FLOP).
+// Epilogue with tma_out: each 128 x 32 chunk is staged in shared memory
+// (128-byte swizzled, two buffers) and written by one TMA store - or, when
+// accumulating, one TMA add-reduction - per chunk, so the stores are whole
+// 128-byte row segments instead of one row per thread. Without tma_out
+// (unaligned outputs, column blocks not multiples of 32) each thread stores
+// its own row.
+constexpr int PB_N = 256;
+constexpr int PB_STAGES = 4;
+constexpr int PB_A = GB * GK * 2;    // 16 KB
+constexpr int PB_B = PB_N * GK * 2;  // 32 KB
+constexpr int PB_STAGE = PB_A + PB_B;
+constexpr int PB_STG = 128 * 32 * 4;  // one 128-row x 32-column fp32 output chunk (16 KB)
+constexpr int PB_SMEM = PB_STAGES * PB_STAGE + 2 * PB_STG + 1024;
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(256, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
+                     const __grid_constant__ CUtensorMap mC0, const __grid_constant__ CUtensorMap mC1,
+                     const __grid_constant__ CUtensorMap mC2, int tma_out,
+                     float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
+                     const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
+                     int nsplit, int relu, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bars[2 * PB_STAGES + 4];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  if (cta_aborted(status, &abort_flag)) return;
+  uint8_t* smem = align1024(smem_raw);
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[PB_STAGES + s]); };
+  auto acc_full = [&](int b) { return smem_u32(&bars[2 * PB_STAGES + b]); };
+  auto acc_empty = [&](int b) { return smem_u32(&bars[2 * PB_STAGES + 2 + b]); };
+  const int warp = warp_id();
+  const int tiles_m = (Mout + GB - 1) / GB;
+  const int tiles = tiles_m * ((Nout + PB_N - 1) / PB_N);
+  const int nk = (Kred + GK - 1) / GK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PB_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int g = 0;  // k-blocks loaded so far: ring slot and phase
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile % tiles_m) * GB, n0 = (tile / tiles_m) * PB_N;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % PB_STAGES;
+          if (g >= PB_STAGES && !(ok = mbar_wait(empty(s), ((g / PB_STAGES) - 1) & 1, status)))
+            break;
+          mbar_arrive_expect_tx(full(s), PB_STAGE);
+          const uint32_t da = smem_u32(smem + s * PB_STAGE), db = da + PB_A;
+          if (A_MN) {  // two 64-wide M groups of 64 K rows
+            tma_load_2d(da, &mA, full(s), m0, kb * GK);
+            tma_load_2d(da + PB_A / 2, &mA, full(s), m0 + 64, kb * GK);
+          } else {
+            tma_load_2d(da, &mA, full(s), kb * GK, m0);
+          }
+          if (B_MN) {  // four 64-wide N groups of 64 K rows
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              tma_load_2d(db + q * (PB_B / 4), &mB, full(s), n0 + 64 * q, kb * GK);
+          } else {
+            tma_load_2d(db, &mB, full(s), kb * GK, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc(128, PB_N, 1, A_MN, B_MN);
+      const uint32_t s0 = smem_u32(smem);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++it) {
+        const int b = it & 1;
+        // the epilogue has drained this accumulator buffer (tile it - 2)
+        if (it >= 2 && !(ok = mbar_wait(acc_empty(b), ((it >> 1) - 1) & 1, status))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * PB_N;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % PB_STAGES;
+          if (!(ok = mbar_wait(full(s), (g / PB_STAGES) & 1, status))) break;
+          tc_fence_after();
+          const uint32_t sa = s0 + s * PB_STAGE, sb = sa + PB_A;
+#pragma unroll
+          for (int ks = 0; ks < GK / 16; ++ks) {
+            const uint64_t da = A_MN ? make_sdesc(sa + ks * 2048, PB_A / 2, 1024)
+                                     : make_sdesc(sa + ks * 32, 16, 1024);
+            const uint64_t db = B_MN ? make_sdesc(sb + ks * 2048, PB_B / 4, 1024)
+                                     : make_sdesc(sb + ks * 32, 16, 1024);
+            umma_f16_ss(d, da, db, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(empty(s));
+        }
+        if (ok) umma_commit(acc_full(b));
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int r = threadIdx.x - 128;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const bool leader = threadIdx.x == 128;
+    uint8_t* stg = smem + PB_STAGES * PB_STAGE;
+    int q = 0;  // staged chunks so far (buffer q & 1)
+    int it = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+      const int b = it & 1;
+      bool ok = mbar_wait_warp(acc_full(b), (it >> 1) & 1, status);
+      if (tma_out) ok = named_bar_and(1, 128, ok);  // the four warps leave together
+      if (!ok) break;
+      tc_fence_after();
+      const int row = (tile % tiles_m) * GB + r, n0 = (tile / tiles_m) * PB_N;
+      // Output column `col` goes to C[row * ldc + col], or with nsplit > 0 to
+      // part p = col / nsplit (C, C1, C2) at [row * nsplit + col - p * nsplit].
+      auto dst_of = [&](int col) -> float* {
+        if (nsplit <= 0) return C + static_cast<size_t>(row) * ldc + col;
+        const int p = col / nsplit;
+        float* base = p == 0 ? C : (p == 1 ? C1 : C2);
+        return base + static_cast<size_t>(row) * nsplit + (col - p * nsplit);
+      };
+#pragma unroll 1
+      for (int c = 0; c < PB_N / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + b * PB_N + c * 32 + lane_base, v);
+        tmem_ld_wait();
+        if (c == PB_N / 32 - 1) {  // the buffer is free for tile it + 2
+          tc_fence_before();
+          mbar_arrive(acc_empty(b));
+        }
+        const int col0 = n0 + c * 32;
+        if (tma_out) {
+          if (col0 >= Nout) continue;  // uniform over the epilogue warps
+          const int buf = q++ & 1;
+          if (leader) bulk_wait_read<1>();  // the store of two chunks ago has read this buffer
+          named_bar_sync(1, 128);
+          uint8_t* srow = stg + buf * PB_STG;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                                   __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+            if (bias) {
+              const int cb = col0 + 4 * u;
+              f.x += cb < Nout ? bias[cb] : 0.f;
+              f.y += cb + 1 < Nout ? bias[cb + 1] : 0.f;
+              f.z += cb + 2 < Nout ? bias[cb + 2] : 0.f;
+              f.w += cb + 3 < Nout ? bias[cb + 3] : 0.f;
+            }
+            if (relu) {
+              f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
+              f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
+            }
+            *reinterpret_cast<float4*>(srow + sw128_offset(r, 16 * u)) = f;
+          }
+          fence_proxy_async_smem();
+          named_bar_sync(1, 128);
+          if (leader) {
+            const int p = nsplit > 0 ? col0 / nsplit : 0;
+            const CUtensorMap* map = p == 0 ? &mC0 : (p == 1 ? &mC1 : &mC2);
+            const int x = col0 - p * (nsplit > 0 ? nsplit : 0), y = row - r;
+            if (accumulate)
+              tma_reduce_add_2d(map, smem_u32(srow), x, y);
+            else
+              tma_store_2d(map, smem_u32(srow), x, y);
+            tma_store_commit();
+          }
+          continue;
+        }
+        if (row >= Mout || col0 >= Nout) continue;
+        float* dst = dst_of(col0);
+        const bool one_part = nsplit <= 0 || (col0 % nsplit) + 32 <= nsplit;
+        const int ld = nsplit > 0 ? nsplit : ldc;
+        const bool vec = (col0 + 32 <= Nout) && one_part && ((ld & 3) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) &&
+                         (!bias || (reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0);
+        if (vec) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                                   __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+            if (bias) {
+              const float4 bb = *reinterpret_cast<const float4*>(bias + col0 + 4 * u);
+              f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
+            }
+            if (relu) {
+              f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
+              f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
+            }
+            if (accumulate) {
+              const float4 p = d4[u];
+              f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
+            }
+            d4[u] = f;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = col0 + e;
+            if (col < Nout) {
+              float* de = dst_of(col);
+              float f = __uint_as_float(v[e]) + (bias ? bias[col] : 0.f);
+              if (relu) f = fmaxf(f, 0.f);
+              *de = f + (accumulate ? *de : 0.f);
+            }
+          }
+        }
+      }
+    }
+    if (leader) bulk_wait_all();  // staged chunks fully written before the CTA ends
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 int round8(int x) { return (x + 7) & ~7; }
 
@@ -224,10 +471,11 @@ size_t planes_bytes(int rows, int cols) {
 
 // 2-D TMA map over a bf16 plane of `rows` x `cols` (row pitch round8(cols)).
 // K-major operand: box {64 cols, 128 rows}; MN-major operand: box {64, 64}.
-bool plane_map(CUtensorMap* m, const void* base, int rows, int cols, bool mn) {
+bool plane_map(CUtensorMap* m, const void* base, int rows, int cols, bool mn,
+               uint32_t kmajor_rows = 128) {
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
   const uint64_t strides[1] = {static_cast<uint64_t>(round8(cols)) * 2};
-  const uint32_t box[2] = {64, mn ? 64u : 128u};
+  const uint32_t box[2] = {64, mn ? 64u : kmajor_rows};
   return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -252,12 +500,57 @@ int run_gemm(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kr
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+// bf16 math: maps over the hi planes, A boxes of 128 rows and B boxes of 256.
+// fp32 [rows, cols] output with row pitch ld, as 128-row x 32-column TMA boxes.
+bool out_map(CUtensorMap* m, const float* base, int rows, int cols, int ld) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
+  const uint32_t box[2] = {32, 128};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <bool A_MN, bool B_MN>
-int run_gemm_math(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred,
-                  int accumulate, const Epilogue& ep, uint32_t* status, cudaStream_t s) {
-  if (f32_math() == PA_F32_MATH_BF16)
-    return run_gemm<A_MN, B_MN, 1>(m, C, ldc, Mout, Nout, Kred, accumulate, ep, status, s);
-  return run_gemm<A_MN, B_MN, 3>(m, C, ldc, Mout, Nout, Kred, accumulate, ep, status, s);
+int run_gemm_bf16(const CUtensorMap& mA, const CUtensorMap& mB, float* C, int ldc, int Mout,
+                  int Nout, int Kred, int accumulate, const Epilogue& ep, uint32_t* status,
+                  cudaStream_t s) {
+  static uint64_t attr = 0;
+  ensure_smem_attr(gemm_bf16_kernel<A_MN, B_MN>, PB_SMEM, attr);
+  // TMA-store epilogue when every output is 16-byte aligned with a 16-byte row
+  // pitch and column blocks hold whole 32-column chunks
+  CUtensorMap mc[3];
+  const bool al = [&] {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (ep.nsplit > 0) {
+      const int parts = Nout / ep.nsplit;
+      if (ep.nsplit % 32 != 0 || Nout % ep.nsplit != 0 || parts > 3) return false;
+      float* outs[3] = {C, ep.c1, ep.c2};
+      for (int p = 0; p < parts; ++p)
+        if (!outs[p] || !a16(outs[p]) || !out_map(&mc[p], outs[p], Mout, ep.nsplit, ep.nsplit))
+          return false;
+      for (int p = parts; p < 3; ++p) mc[p] = mc[0];
+      return true;
+    }
+    if (ldc % 4 != 0 || !a16(C) || !out_map(&mc[0], C, Mout, Nout, ldc)) return false;
+    mc[1] = mc[2] = mc[0];
+    return true;
+  }();
+  if (!al) mc[0] = mc[1] = mc[2] = mA;  // unused
+  const int tiles = ((Mout + GB - 1) / GB) * ((Nout + PB_N - 1) / PB_N);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  gemm_bf16_kernel<A_MN, B_MN><<<grid, 256, PB_SMEM, s>>>(
+      mA, mB, mc[0], mc[1], mc[2], al ? 1 : 0, C, ldc, Mout, Nout, Kred, accumulate, ep.bias,
+      ep.c1, ep.c2, ep.nsplit, ep.relu, status);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
 // bf16 hi/lo planes of one [rows, cols] operand in the workspace (row pitch round8(cols)).
@@ -283,13 +576,22 @@ int split_into(const float* x, const Planes& p, cudaStream_t s) {
 int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int N, int K,
                 const Epilogue& ep, uint32_t* status, cudaStream_t s) {
   const bool a_mn = (mode == 2), b_mn = (mode != 1);
+  if (f32_math() == PA_F32_MATH_BF16) {
+    CUtensorMap mA, mB;
+    if (!plane_map(&mA, a.hi, a.rows, a.cols, a_mn, 128) ||
+        !plane_map(&mB, b.hi, b.rows, b.cols, b_mn, 256))
+      return PA_ERR_ALIGN;
+    if (mode == 0) return run_gemm_bf16<false, true>(mA, mB, C, N, M, N, K, 0, ep, status, s);
+    if (mode == 1) return run_gemm_bf16<false, false>(mA, mB, C, N, M, N, K, 1, ep, status, s);
+    return run_gemm_bf16<true, true>(mA, mB, C, K, N, K, M, 1, ep, status, s);
+  }
   CUtensorMap m[4];
   if (!plane_map(&m[0], a.hi, a.rows, a.cols, a_mn) || !plane_map(&m[1], a.lo, a.rows, a.cols, a_mn) ||
       !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn) || !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn))
     return PA_ERR_ALIGN;
-  if (mode == 0) return run_gemm_math<false, true>(m, C, N, M, N, K, 0, ep, status, s);
-  if (mode == 1) return run_gemm_math<false, false>(m, C, N, M, N, K, 1, ep, status, s);
-  return run_gemm_math<true, true>(m, C, K, N, K, M, 1, ep, status, s);
+  if (mode == 0) return run_gemm<false, true, 3>(m, C, N, M, N, K, 0, ep, status, s);
+  if (mode == 1) return run_gemm<false, false, 3>(m, C, N, M, N, K, 1, ep, status, s);
+  return run_gemm<true, true, 3>(m, C, K, N, K, M, 1, ep, status, s);
 }
 
 }  // namespace
