@@ -6,7 +6,8 @@
 //   mode 2  dW[N,K] += X[M,N]^T dY[M,K]   matmul_backward_W_kernel.cu:5-55
 // on the bf16 tensor cores at fp32-level accuracy: each fp32 operand is split
 // into bf16 hi/lo planes in the caller's workspace (fp32_split.cu) and every
-// product is hi*hi + hi*lo + lo*hi, three MMAs into one fp32 TMEM accumulator.
+// product is hi*hi + hi*lo + lo*hi, three MMAs into one fp32 TMEM accumulator
+// (in the bf16 math mode, pa_set_f32_math, only the hi planes and one MMA).
 //
 // The transposes of the gradients cost nothing: a row-major operand whose
 // reduction index is the row index is simply fed as an MN-major tcgen05
@@ -24,11 +25,15 @@
 // incoming gradient by the saved output while gathering it (no ReLU passes,
 // no pre-activation tensor).
 //
-// One CTA = one 128 x 128 output tile; K in blocks of 64 through a 3-stage
-// TMA ring (hi and lo planes of both operands per stage).
+// One persistent CTA per SM walks 128 x 256 output tiles (work units: tiles,
+// or tiles x K slices for accumulating GEMMs that would fill the GPU badly);
+// K in blocks of 64 through a TMA ring of bf16 planes; the fp32 accumulator is
+// double-buffered in TMEM so the epilogue of one unit overlaps the MMAs of the
+// next; the epilogue stages 128 x 32 chunks in shared memory for TMA stores or
+// TMA add-reductions.
 //   warp 0     TMA producer
 //   warp 1     TMEM allocator + MMA issuer
-//   warps 4-7  epilogue: TMEM -> registers -> C (thread = one output row)
+//   warps 4-7  epilogue: TMEM -> registers (+ bias, ReLU) -> shared -> TMA
 #include <cuda_bf16.h>
 #include "host_launchers.h"
 
@@ -36,193 +41,19 @@ namespace pa {
 
 namespace {
 
-constexpr int GB = 128;          // output tile (rows and columns)
+constexpr int GB = 128;          // output tile rows (the tile is GB x PB_N)
 constexpr int GK = 64;           // K block (one 128-byte swizzle row of bf16)
-constexpr int PLANE_TILE = GB * GK * 2;       // 16 KB: one operand plane of one stage
 
-// NT = product terms: 3 (hi/lo planes, fp32-level accuracy) or 1 (one bf16
-// plane per operand, the bf16 math mode). A stage holds the A planes, then
-// the B planes; with one plane per operand it is half the size and the ring
-// twice as deep.
-template <int NT>
-struct GemmCfg {
-  static constexpr int PLANES = NT == 3 ? 4 : 2;
-  static constexpr int STAGE = PLANES * PLANE_TILE;
-  static constexpr int STAGES = NT == 3 ? 3 : 6;
-  static constexpr int SMEM = STAGES * STAGE + 1024;
-};
-
-// A_MN / B_MN: the operand is stored with its reduction index as the row index
-// (MN-major for tcgen05); otherwise the reduction index is contiguous (K-major).
-template <bool A_MN, bool B_MN, int NT>
-__global__ void __launch_bounds__(256, 1)
-    gemm_split_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
-                      const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
-                      float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
-                      const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
-                      int nsplit, int relu, uint32_t* status) {
-  using G = GemmCfg<NT>;
-  constexpr int GSTAGES = G::STAGES, STAGE = G::STAGE, HALF = G::PLANES / 2;
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bars[2 * GSTAGES + 1];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-  if (cta_aborted(status, &abort_flag)) return;
-  uint8_t* smem = align1024(smem_raw);
-  auto full = [&](int s) { return smem_u32(&bars[s]); };
-  auto empty = [&](int s) { return smem_u32(&bars[GSTAGES + s]); };
-  const uint32_t acc_full = smem_u32(&bars[2 * GSTAGES]);
-  const int warp = warp_id();
-  const int m0 = blockIdx.y * GB, n0 = blockIdx.x * GB;
-  const int nk = (Kred + GK - 1) / GK;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < GSTAGES; ++s) {
-      mbar_init(full(s), 1);
-      mbar_init(empty(s), 1);
-    }
-    mbar_init(acc_full, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(&tmem_slot), 128);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-
-  if (warp == 0) {
-    if (elect_one()) {
-      const CUtensorMap* maps[4] = {&mAh, HALF == 2 ? &mAl : &mBh, &mBh, &mBl};
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % GSTAGES;
-        if (kb >= GSTAGES && !mbar_wait(empty(s), ((kb / GSTAGES) - 1) & 1, status)) break;
-        mbar_arrive_expect_tx(full(s), STAGE);
-        uint8_t* st = smem + s * STAGE;
-#pragma unroll
-        for (int p = 0; p < G::PLANES; ++p) {
-          const bool mn = p < HALF ? A_MN : B_MN;
-          const int r0 = p < HALF ? m0 : n0;
-          const uint32_t dst = smem_u32(st + p * PLANE_TILE);
-          if (mn) {
-            // two 64-wide groups along M/N, 64 K rows each
-            tma_load_2d(dst, maps[p], full(s), r0, kb * GK);
-            tma_load_2d(dst + PLANE_TILE / 2, maps[p], full(s), r0 + 64, kb * GK);
-          } else {
-            tma_load_2d(dst, maps[p], full(s), kb * GK, r0);
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t idesc = make_idesc(128, 128, 1, A_MN, B_MN);
-      const uint64_t base = make_sdesc(smem_u32(smem), 16, 1024);
-      const uint64_t base_mn = make_sdesc(smem_u32(smem), PLANE_TILE / 2, 1024);
-      bool ok = true;
-      for (int kb = 0; ok && kb < nk; ++kb) {
-        const int s = kb % GSTAGES;
-        if (!(ok = mbar_wait(full(s), (kb / GSTAGES) & 1, status))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int term = 0; term < NT; ++term) {
-          // planes (A, B) of each term: (hi, hi), (hi, lo), (lo, hi)
-          const uint32_t pa_ = (term == 2) ? 1 : 0, pb = HALF + ((term == 1) ? 1 : 0);
-#pragma unroll
-          for (int ks = 0; ks < GK / 16; ++ks) {
-            const uint32_t so = (s * STAGE) >> 4;
-            const uint64_t da = (A_MN ? base_mn + ((pa_ * PLANE_TILE + ks * 2048) >> 4)
-                                      : base + ((pa_ * PLANE_TILE + ks * 32) >> 4)) + so;
-            const uint64_t db = (B_MN ? base_mn + ((pb * PLANE_TILE + ks * 2048) >> 4)
-                                      : base + ((pb * PLANE_TILE + ks * 32) >> 4)) + so;
-            umma_f16_ss(tmem, da, db, idesc, (kb > 0 || term > 0 || ks > 0) ? 1u : 0u);
-          }
-        }
-        umma_commit(empty(s));
-      }
-      if (ok) umma_commit(acc_full);
-    }
-  } else if (warp >= 4) {
-    const int r = threadIdx.x - 128;
-    const int row = m0 + r;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    if (mbar_wait_warp(acc_full, 0, status)) {
-      tc_fence_after();
-      // Output column `col` goes to C[row * ldc + col], or with nsplit > 0 to
-      // part p = col / nsplit (C, C1, C2) at [row * nsplit + col - p * nsplit].
-      auto dst_of = [&](int col) -> float* {
-        if (nsplit <= 0) return C + static_cast<size_t>(row) * ldc + col;
-        const int p = col / nsplit;
-        float* base = p == 0 ? C : (p == 1 ? C1 : C2);
-        return base + static_cast<size_t>(row) * nsplit + (col - p * nsplit);
-      };
-#pragma unroll 1
-      for (int c = 0; c < GB / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c * 32, v);
-        tmem_ld_wait();
-        if (row >= Mout) continue;
-        const int col0 = n0 + c * 32;
-        float* dst = dst_of(col0);
-        const bool one_part = nsplit <= 0 || (col0 % nsplit) + 32 <= nsplit;
-        const int ld = nsplit > 0 ? nsplit : ldc;
-        const bool vec = (col0 + 32 <= Nout) && one_part && ((ld & 3) == 0) &&
-                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) &&
-                         (!bias || (reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0);
-        if (vec) {
-          float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
-                                   __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
-            if (bias) {
-              const float4 bb = *reinterpret_cast<const float4*>(bias + col0 + 4 * u);
-              f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
-            }
-            if (relu) {
-              f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
-              f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
-            }
-            if (accumulate) {
-              const float4 p = d4[u];
-              f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
-            }
-            d4[u] = f;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = col0 + e;
-            if (col < Nout) {
-              float* de = dst_of(col);
-              float f = __uint_as_float(v[e]) + (bias ? bias[col] : 0.f);
-              if (relu) f = fmaxf(f, 0.f);
-              *de = f + (accumulate ? *de : 0.f);
-            }
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 128);
-  }
-}
-
-
-// ---------------------------------------------------------------- bf16 math: persistent GEMM
-// One CTA per SM walks the 128 x 256 output tiles (tile i, i + gridDim.x, ...;
-// M-tile index fastest). K in blocks of 64 through a 4-stage TMA ring (A
-// 128 x 64 and B 256 x 64 bf16 per stage, 48 KB). The fp32 accumulator is
-// double-buffered in TMEM (2 x 256 columns): the epilogue warps drain tile i
-// while the MMA warp accumulates tile i + 1, and every MMA is M=128 N=256 K=16
-// (full rate; the 128 x 128 kernel above leaves the tensor core idle during
-// each epilogue and pays twice the operand traffic per FLOP).
+// ---------------------------------------------------------------- persistent GEMM
+// One CTA per SM walks the work units (unit i, i + gridDim.x, ...; M-tile index
+// fastest). K in blocks of 64 through a TMA ring: per stage A 128 x 64 and
+// B 256 x 64 bf16 (48 KB) for one product (bf16 math, 4 stages), or the hi and
+// lo planes of both (96 KB) for three (split3, 2 stages). The fp32 accumulator
+// is double-buffered in TMEM (2 x 256 columns): the epilogue warps drain unit
+// i while the MMA warp accumulates unit i + 1. Every MMA is M=128 N=256 K=16,
+// the full-rate shape (a 128 x 128 tile leaves the tensor core idle during
+// each epilogue and reads twice the operand bytes per FLOP: 1.3-1.5x slower
+// at the training step's shapes).
 // Epilogue with tma_out: each 128 x 32 chunk is staged in shared memory
 // (128-byte swizzled, two buffers) and written by one TMA store - or, when
 // accumulating, one TMA add-reduction - per chunk, so the stores are whole
@@ -230,21 +61,29 @@ __global__ void __launch_bounds__(256, 1)
 // (unaligned outputs, column blocks not multiples of 32) each thread stores
 // its own row.
 constexpr int PB_N = 256;
-constexpr int PB_STAGES = 4;
-constexpr int PB_A = GB * GK * 2;    // 16 KB
-constexpr int PB_B = PB_N * GK * 2;  // 32 KB
-constexpr int PB_STAGE = PB_A + PB_B;
+constexpr int PB_A = GB * GK * 2;    // 16 KB: one A plane of one stage
+constexpr int PB_B = PB_N * GK * 2;  // 32 KB: one B plane
 constexpr int PB_STG = 128 * 32 * 4;  // one 128-row x 32-column fp32 output chunk (16 KB)
-constexpr int PB_SMEM = PB_STAGES * PB_STAGE + 2 * PB_STG + 1024;
+// NT = 1: planes A, B per stage, 4 stages; NT = 3 (hi/lo): A hi, A lo, B hi, B lo, 2 stages.
+template <int NT>
+struct PersistCfg {
+  static constexpr int NP = NT == 3 ? 2 : 1;
+  static constexpr int STAGE = NP * (PB_A + PB_B);
+  static constexpr int STAGES = NT == 3 ? 2 : 4;
+  static constexpr int SMEM = STAGES * STAGE + 2 * PB_STG + 1024;
+};
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int NT>
 __global__ void __launch_bounds__(256, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
+    gemm_persist_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAl,
+                     const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBl,
                      const __grid_constant__ CUtensorMap mC0, const __grid_constant__ CUtensorMap mC1,
-                     const __grid_constant__ CUtensorMap mC2, int tma_out,
+                     const __grid_constant__ CUtensorMap mC2, int tma_out, int ksplit,
                      float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
                      const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
                      int nsplit, int relu, uint32_t* status) {
+  using P = PersistCfg<NT>;
+  constexpr int PB_STAGES = P::STAGES, PB_STAGE = P::STAGE, NP = P::NP;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[2 * PB_STAGES + 4];
   __shared__ uint32_t tmem_slot;
@@ -257,8 +96,15 @@ __global__ void __launch_bounds__(256, 1)
   auto acc_empty = [&](int b) { return smem_u32(&bars[2 * PB_STAGES + 2 + b]); };
   const int warp = warp_id();
   const int tiles_m = (Mout + GB - 1) / GB;
-  const int tiles = tiles_m * ((Nout + PB_N - 1) / PB_N);
-  const int nk = (Kred + GK - 1) / GK;
+  // work unit u = (tile u / ksplit, K slice u % ksplit); slices > 1 only when
+  // accumulating through TMA add-reductions
+  const int units = tiles_m * ((Nout + PB_N - 1) / PB_N) * ksplit;
+  const int nk_all = (Kred + GK - 1) / GK;
+  auto kslice = [&](int u, int& kb0, int& kb1) {
+    const int sl = u % ksplit;
+    kb0 = static_cast<int>((static_cast<long long>(nk_all) * sl) / ksplit);
+    kb1 = static_cast<int>((static_cast<long long>(nk_all) * (sl + 1)) / ksplit);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PB_STAGES; ++s) {
@@ -285,26 +131,36 @@ __global__ void __launch_bounds__(256, 1)
     if (elect_one()) {
       int g = 0;  // k-blocks loaded so far: ring slot and phase
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const int tile = u / ksplit;
         const int m0 = (tile % tiles_m) * GB, n0 = (tile / tiles_m) * PB_N;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        int kb0, kb1;
+        kslice(u, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % PB_STAGES;
           if (g >= PB_STAGES && !(ok = mbar_wait(empty(s), ((g / PB_STAGES) - 1) & 1, status)))
             break;
           mbar_arrive_expect_tx(full(s), PB_STAGE);
-          const uint32_t da = smem_u32(smem + s * PB_STAGE), db = da + PB_A;
-          if (A_MN) {  // two 64-wide M groups of 64 K rows
-            tma_load_2d(da, &mA, full(s), m0, kb * GK);
-            tma_load_2d(da + PB_A / 2, &mA, full(s), m0 + 64, kb * GK);
-          } else {
-            tma_load_2d(da, &mA, full(s), kb * GK, m0);
-          }
-          if (B_MN) {  // four 64-wide N groups of 64 K rows
+          // stage: A planes (hi[, lo]) then B planes
+          const uint32_t st0 = smem_u32(smem + s * PB_STAGE);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              tma_load_2d(db + q * (PB_B / 4), &mB, full(s), n0 + 64 * q, kb * GK);
-          } else {
-            tma_load_2d(db, &mB, full(s), kb * GK, n0);
+          for (int pl = 0; pl < NP; ++pl) {
+            const uint32_t da = st0 + pl * PB_A, db = st0 + NP * PB_A + pl * PB_B;
+            const CUtensorMap* ma = pl ? &mAl : &mA;
+            const CUtensorMap* mb = pl ? &mBl : &mB;
+            if (A_MN) {  // two 64-wide M groups of 64 K rows
+              tma_load_2d(da, ma, full(s), m0, kb * GK);
+              tma_load_2d(da + PB_A / 2, ma, full(s), m0 + 64, kb * GK);
+            } else {
+              tma_load_2d(da, ma, full(s), kb * GK, m0);
+            }
+            if (B_MN) {  // four 64-wide N groups of 64 K rows
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                tma_load_2d(db + q * (PB_B / 4), mb, full(s), n0 + 64 * q, kb * GK);
+            } else {
+              tma_load_2d(db, mb, full(s), kb * GK, n0);
+            }
           }
         }
       }
@@ -316,24 +172,31 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t s0 = smem_u32(smem);
       int g = 0, it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++it) {
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++it) {
         const int b = it & 1;
-        // the epilogue has drained this accumulator buffer (tile it - 2)
+        int kb0, kb1;
+        kslice(u, kb0, kb1);
+        // the epilogue has drained this accumulator buffer (unit it - 2)
         if (it >= 2 && !(ok = mbar_wait(acc_empty(b), ((it >> 1) - 1) & 1, status))) break;
         tc_fence_after();
         const uint32_t d = tmem + b * PB_N;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % PB_STAGES;
           if (!(ok = mbar_wait(full(s), (g / PB_STAGES) & 1, status))) break;
           tc_fence_after();
-          const uint32_t sa = s0 + s * PB_STAGE, sb = sa + PB_A;
 #pragma unroll
-          for (int ks = 0; ks < GK / 16; ++ks) {
-            const uint64_t da = A_MN ? make_sdesc(sa + ks * 2048, PB_A / 2, 1024)
-                                     : make_sdesc(sa + ks * 32, 16, 1024);
-            const uint64_t db = B_MN ? make_sdesc(sb + ks * 2048, PB_B / 4, 1024)
-                                     : make_sdesc(sb + ks * 32, 16, 1024);
-            umma_f16_ss(d, da, db, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+          for (int term = 0; term < NT; ++term) {
+            // planes (A, B) of each term: (hi, hi), (hi, lo), (lo, hi)
+            const uint32_t sa = s0 + s * PB_STAGE + (term == 2 ? PB_A : 0);
+            const uint32_t sb = s0 + s * PB_STAGE + NP * PB_A + (term == 1 ? PB_B : 0);
+#pragma unroll
+            for (int ks = 0; ks < GK / 16; ++ks) {
+              const uint64_t da = A_MN ? make_sdesc(sa + ks * 2048, PB_A / 2, 1024)
+                                       : make_sdesc(sa + ks * 32, 16, 1024);
+              const uint64_t db = B_MN ? make_sdesc(sb + ks * 2048, PB_B / 4, 1024)
+                                       : make_sdesc(sb + ks * 32, 16, 1024);
+              umma_f16_ss(d, da, db, idesc, (kb > kb0 || term > 0 || ks > 0) ? 1u : 0u);
+            }
           }
           umma_commit(empty(s));
         }
@@ -348,7 +211,8 @@ __global__ void __launch_bounds__(256, 1)
     uint8_t* stg = smem + PB_STAGES * PB_STAGE;
     int q = 0;  // staged chunks so far (buffer q & 1)
     int it = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+      const int tile = u / ksplit;
       const int b = it & 1;
       bool ok = mbar_wait_warp(acc_full(b), (it >> 1) & 1, status);
       if (tma_out) ok = named_bar_and(1, 128, ok);  // the four warps leave together
@@ -488,17 +352,6 @@ struct Epilogue {
   int relu = 0;  // max(0, .) after the bias (forward projections only)
 };
 
-template <bool A_MN, bool B_MN, int NT>
-int run_gemm(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred, int accumulate,
-             const Epilogue& ep, uint32_t* status, cudaStream_t s) {
-  static uint64_t attr = 0;
-  ensure_smem_attr(gemm_split_kernel<A_MN, B_MN, NT>, GemmCfg<NT>::SMEM, attr);
-  dim3 grid((Nout + GB - 1) / GB, (Mout + GB - 1) / GB);
-  gemm_split_kernel<A_MN, B_MN, NT><<<grid, 256, GemmCfg<NT>::SMEM, s>>>(
-      m[0], m[1], m[2], m[3], C, ldc, Mout, Nout, Kred, accumulate, ep.bias, ep.c1, ep.c2,
-      ep.nsplit, ep.relu, status);
-  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
-}
 
 int sm_count() {
   static int n[64] = {0};
@@ -519,12 +372,12 @@ bool out_map(CUtensorMap* m, const float* base, int rows, int cols, int ld) {
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <bool A_MN, bool B_MN>
-int run_gemm_bf16(const CUtensorMap& mA, const CUtensorMap& mB, float* C, int ldc, int Mout,
-                  int Nout, int Kred, int accumulate, const Epilogue& ep, uint32_t* status,
-                  cudaStream_t s) {
+template <bool A_MN, bool B_MN, int NT>
+int run_gemm_persist(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred,
+                     int accumulate, const Epilogue& ep, uint32_t* status, cudaStream_t s) {
+  const CUtensorMap& mA = m[0];
   static uint64_t attr = 0;
-  ensure_smem_attr(gemm_bf16_kernel<A_MN, B_MN>, PB_SMEM, attr);
+  ensure_smem_attr(gemm_persist_kernel<A_MN, B_MN, NT>, PersistCfg<NT>::SMEM, attr);
   // TMA-store epilogue when every output is 16-byte aligned with a 16-byte row
   // pitch and column blocks hold whole 32-column chunks
   CUtensorMap mc[3];
@@ -546,10 +399,27 @@ int run_gemm_bf16(const CUtensorMap& mA, const CUtensorMap& mB, float* C, int ld
   }();
   if (!al) mc[0] = mc[1] = mc[2] = mA;  // unused
   const int tiles = ((Mout + GB - 1) / GB) * ((Nout + PB_N - 1) / PB_N);
-  const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_bf16_kernel<A_MN, B_MN><<<grid, 256, PB_SMEM, s>>>(
-      mA, mB, mc[0], mc[1], mc[2], al ? 1 : 0, C, ldc, Mout, Nout, Kred, accumulate, ep.bias,
-      ep.c1, ep.c2, ep.nsplit, ep.relu, status);
+  // Accumulating GEMMs (dX, dW) through the TMA path may split K so that the
+  // work units fill whole waves of CTAs: the slices add into C in any order,
+  // so their results can differ in the last bits from run to run.
+  int ksplit = 1;
+  if (accumulate && al && !ep.bias && !ep.relu) {
+    const int nk = (Kred + GK - 1) / GK, sms = sm_count();
+    double best = 0.0;
+    for (int sp = 1; sp <= 16 && nk / sp >= 4; ++sp) {
+      const int units = tiles * sp, waves = (units + sms - 1) / sms;
+      const double eff = static_cast<double>(units) / (static_cast<double>(waves) * sms);
+      if (eff > best + 0.02) {
+        best = eff;
+        ksplit = sp;
+      }
+    }
+  }
+  const int units = tiles * ksplit;
+  const int grid = units < sm_count() ? units : sm_count();
+  gemm_persist_kernel<A_MN, B_MN, NT><<<grid, 256, PersistCfg<NT>::SMEM, s>>>(
+      m[0], m[1], m[2], m[3], mc[0], mc[1], mc[2], al ? 1 : 0, ksplit, C, ldc, Mout, Nout, Kred,
+      accumulate, ep.bias, ep.c1, ep.c2, ep.nsplit, ep.relu, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
@@ -576,22 +446,29 @@ int split_into(const float* x, const Planes& p, cudaStream_t s) {
 int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int N, int K,
                 const Epilogue& ep, uint32_t* status, cudaStream_t s) {
   const bool a_mn = (mode == 2), b_mn = (mode != 1);
-  if (f32_math() == PA_F32_MATH_BF16) {
-    CUtensorMap mA, mB;
-    if (!plane_map(&mA, a.hi, a.rows, a.cols, a_mn, 128) ||
-        !plane_map(&mB, b.hi, b.rows, b.cols, b_mn, 256))
+  // persistent 128 x 256 kernel: maps A hi, A lo, B hi, B lo (A boxes of 128 rows, B of 256)
+  {
+    const bool one = f32_math() == PA_F32_MATH_BF16;
+    CUtensorMap m[4];
+    if (!plane_map(&m[0], a.hi, a.rows, a.cols, a_mn, 128) ||
+        !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn, 256))
       return PA_ERR_ALIGN;
-    if (mode == 0) return run_gemm_bf16<false, true>(mA, mB, C, N, M, N, K, 0, ep, status, s);
-    if (mode == 1) return run_gemm_bf16<false, false>(mA, mB, C, N, M, N, K, 1, ep, status, s);
-    return run_gemm_bf16<true, true>(mA, mB, C, K, N, K, M, 1, ep, status, s);
+    if (one) {
+      m[1] = m[0];
+      m[3] = m[2];
+    } else if (!plane_map(&m[1], a.lo, a.rows, a.cols, a_mn, 128) ||
+               !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn, 256)) {
+      return PA_ERR_ALIGN;
+    }
+    if (one) {
+      if (mode == 0) return run_gemm_persist<false, true, 1>(m, C, N, M, N, K, 0, ep, status, s);
+      if (mode == 1) return run_gemm_persist<false, false, 1>(m, C, N, M, N, K, 1, ep, status, s);
+      return run_gemm_persist<true, true, 1>(m, C, K, N, K, M, 1, ep, status, s);
+    }
+    if (mode == 0) return run_gemm_persist<false, true, 3>(m, C, N, M, N, K, 0, ep, status, s);
+    if (mode == 1) return run_gemm_persist<false, false, 3>(m, C, N, M, N, K, 1, ep, status, s);
+    return run_gemm_persist<true, true, 3>(m, C, K, N, K, M, 1, ep, status, s);
   }
-  CUtensorMap m[4];
-  if (!plane_map(&m[0], a.hi, a.rows, a.cols, a_mn) || !plane_map(&m[1], a.lo, a.rows, a.cols, a_mn) ||
-      !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn) || !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn))
-    return PA_ERR_ALIGN;
-  if (mode == 0) return run_gemm<false, true, 3>(m, C, N, M, N, K, 0, ep, status, s);
-  if (mode == 1) return run_gemm<false, false, 3>(m, C, N, M, N, K, 1, ep, status, s);
-  return run_gemm<true, true, 3>(m, C, K, N, K, M, 1, ep, status, s);
 }
 
 }  // namespace
