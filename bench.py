@@ -47,7 +47,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--linear", action="store_true",
                     help="instead of the attention step: time the fused projection calls of the "
-                         "MHA block (B8 L1024 E512 fp32) against the unfused call sequence")
+                         "MHA block (B8 L1024 E512 fp32) against the unfused call sequence, in both "
+                         "math modes, and the training step's projection shapes (bf16 math)")
     ap.add_argument("--train", action="store_true",
                     help="instead of the attention step: the data-parallel denoise training step "
                          "(6 layers, E1024 H16 FFN4096, N2048, 8 sequences per GPU, fp32 weights), "
@@ -252,23 +253,49 @@ def run_linear(args):
         pa_capi.matmul_grad_x(dproj, wi, dx, M, E, 3 * E, ws)
         pa_capi.matmul_grad_w(x, dproj, dwi, M, E, 3 * E, ws)
 
-    res = {}
-    for name, fn in (("fused", fused), ("unfused", unfused)):
+    def timed(fn, n):
         for _ in range(max(3, args.warmup)):
             fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(n):
             fn()
         e1.record()
         torch.cuda.synchronize()
-        res[name] = e0.elapsed_time(e1) / args.steps
+        return e0.elapsed_time(e1) / n
+
+    res = {}
+    for mode in ("split3", "bf16"):
+        pa_capi.set_f32_math(mode)
+        res[mode] = {name: round(timed(fn, args.steps), 4)
+                     for name, fn in (("fused_ms", fused), ("unfused_ms", unfused))}
     flops = 2 * M * E * (3 * E + E) * 3  # fwd + dX + dW of both projections
+    # the training step's projection shapes (M = 8 x 2048 tokens), bf16 math, against
+    # cuBLAS on bf16 operands (no conversion, bf16 output) for scale
+    pa_capi.set_f32_math("bf16")
+    M5 = 16384
+    c5 = []
+    for IN, OUT in ((1024, 3072), (1024, 1024), (1024, 4096), (4096, 1024)):
+        x5, w5, b5 = rnd(M5, IN), rnd(IN, OUT) * 0.03, rnd(OUT)
+        y5, dy5 = torch.empty(M5, OUT, device="cuda"), rnd(M5, OUT)
+        dx5, dw5 = torch.zeros(M5, IN, device="cuda"), torch.zeros(IN, OUT, device="cuda")
+        ws5 = torch.empty(pa_capi.linear_workspace_size(M5, IN, OUT), dtype=torch.uint8, device="cuda")
+        f5 = 2 * M5 * IN * OUT
+        tf = timed(lambda: pa_capi.linear_fwd(x5, w5, b5, [y5], M5, IN, OUT, ws5), args.steps)
+        tb = timed(lambda: pa_capi.linear_bwd(x5, w5, [dy5], dx5, dw5, None, M5, IN, OUT, ws5), args.steps)
+        xb, wb = x5.bfloat16(), w5.bfloat16()
+        tc = timed(lambda: torch.matmul(xb, wb), args.steps)
+        c5.append({"in": IN, "out": OUT, "fwd_us": round(tf * 1e3, 1),
+                   "fwd_tflops": round(f5 / (tf * 1e-3) / 1e12, 1), "bwd_us": round(tb * 1e3, 1),
+                   "bwd_tflops": round(2 * f5 / (tb * 1e-3) / 1e12, 1),
+                   "cublas_bf16_us": round(tc * 1e3, 1)})
+    pa_capi.set_f32_math("split3")
     print(json.dumps({"metric": "MHA block projections fwd+bwd (B8 L1024 E512 fp32)", "unit": "ms",
-                      "fused_ms": round(res["fused"], 4), "unfused_ms": round(res["unfused"], 4),
-                      "speedup": round(res["unfused"] / res["fused"], 3),
-                      "fused_tflops": round(flops / (res["fused"] * 1e-3) / 1e12, 1),
+                      "split3": res["split3"], "bf16": res["bf16"],
+                      "speedup_split3": round(res["split3"]["unfused_ms"] / res["split3"]["fused_ms"], 3),
+                      "fused_tflops_split3": round(flops / (res["split3"]["fused_ms"] * 1e-3) / 1e12, 1),
+                      "training_step_projections_bf16_math": c5,
                       "steps": args.steps, "device_status": pa_capi.device_status()}))
 
 
