@@ -601,6 +601,8 @@ def main():
                    "l2": "inputs (4 x 64 MiB bf16 per 8 batches) exceed the 126 MB L2; no flush"},
         "per_gpu_tflops": round(per_gpu, 2),
         "frac_of_dense_peak": {"measured_bf16": round(per_gpu / peak, 4),
+                               "measured_bf16_sustained": (round(per_gpu / peak_sus, 4)
+                                                           if peak_sus else None),
                                "datasheet_2250": round(per_gpu / 2250.0, 4)},
         "fwd_ms": round(fwd_ms, 4),
         "bwd_ms": round(bwd_ms, 4),
