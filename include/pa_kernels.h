@@ -205,6 +205,28 @@ int pa_linear_relu_bwd(const float* X, const float* W, const float* Y, const flo
                        float* dW, float* dbias, int M, int in_features, int out_features,
                        void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
+/* Keeping X's operand planes from a projection's forward for its backward, so
+ * the backward does not convert X again (a graph node holds them in between).
+ * Bytes under the calling thread's f32 math mode (one bf16 plane of X for
+ * bf16 math, hi and lo for split3): */
+size_t pa_linear_kept_size(int M, int in_features);
+/* pa_linear_fwd (relu = 0) or pa_linear_relu_fwd (relu = 1, n_outs = 1) that
+ * also leaves X's planes in `kept` (256-byte aligned, pa_linear_kept_size bytes). */
+int pa_linear_fwd_keep(const float* X, const float* W, const float* bias, float* const* outs,
+                       int n_outs, int relu, int M, int in_features, int out_features, void* kept,
+                       size_t kept_bytes, void* workspace, size_t workspace_bytes,
+                       pa_stream_t stream);
+/* pa_linear_bwd (Y = NULL) or pa_linear_relu_bwd (Y = the ReLU output,
+ * n_parts = 1) reading X's planes from `kept`, written by pa_linear_fwd_keep
+ * under f32 math mode `kept_mode`. Where they cannot serve the current mode
+ * (a bf16 forward keeps no lo plane for a split3 backward) X is converted
+ * again, as pa_linear_bwd does. */
+int pa_linear_bwd_kept(const float* X, const float* W, const void* kept, size_t kept_bytes,
+                       int kept_mode, const float* Y, const float* const* dy_parts, int n_parts,
+                       float* dX, float* dW, float* dbias, int M, int in_features,
+                       int out_features, void* workspace, size_t workspace_bytes,
+                       pa_stream_t stream);
+
 /* ---------------------------------------------------------------- elementwise */
 
 /* out[M,N] = A[M,N] + bias[N]. Replaces launch_matadd_tiled (Launchers.cuh:25-32). */

@@ -289,6 +289,52 @@ int pa_linear_bwd(const float* X, const float* W, const float* const* dy_parts, 
                                out_features, workspace, status, static_cast<cudaStream_t>(stream));
 }
 
+size_t pa_linear_kept_size(int M, int in_features) {
+  if (M <= 0 || in_features <= 0) return 0;
+  return pa::linear_kept_bytes(M, in_features, pa::f32_math());
+}
+
+int pa_linear_fwd_keep(const float* X, const float* W, const float* bias, float* const* outs,
+                       int n_outs, int relu, int M, int in_features, int out_features, void* kept,
+                       size_t kept_bytes, void* workspace, size_t workspace_bytes,
+                       pa_stream_t stream) {
+  if (!X || !W || !outs || !kept) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, n_outs, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  if (relu && n_outs != 1) return PA_ERR_SHAPE;
+  if (kept_bytes < pa::linear_kept_bytes(M, in_features, pa::f32_math())) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(kept) & 255u) != 0) return PA_ERR_ALIGN;
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i]) return PA_ERR_NULL;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  return pa::launch_linear_fwd(X, W, bias, outs, n_outs, M, in_features, out_features, relu ? 1 : 0,
+                               workspace, status, static_cast<cudaStream_t>(stream), kept);
+}
+
+int pa_linear_bwd_kept(const float* X, const float* W, const void* kept, size_t kept_bytes,
+                       int kept_mode, const float* Y, const float* const* dy_parts, int n_parts,
+                       float* dX, float* dW, float* dbias, int M, int in_features,
+                       int out_features, void* workspace, size_t workspace_bytes,
+                       pa_stream_t stream) {
+  if (!X || !W || !dy_parts) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, n_parts, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  if (Y && n_parts != 1) return PA_ERR_SHAPE;
+  for (int i = 0; i < n_parts; ++i)
+    if (!dy_parts[i]) return PA_ERR_NULL;
+  const int mode = pa::f32_math();
+  // a split3 forward kept hi and lo (enough for either mode), a bf16 one only hi
+  const bool usable = kept && (reinterpret_cast<uintptr_t>(kept) & 255u) == 0 &&
+                      (mode == PA_F32_MATH_BF16 || kept_mode == PA_F32_MATH_SPLIT3) &&
+                      kept_bytes >= pa::linear_kept_bytes(M, in_features, mode);
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  return pa::launch_linear_bwd(X, W, dy_parts, n_parts, Y, dX, dW, dbias, M, in_features,
+                               out_features, workspace, status, static_cast<cudaStream_t>(stream),
+                               usable ? kept : nullptr);
+}
+
 int pa_linear_relu_bwd(const float* X, const float* W, const float* Y, const float* dY, float* dX,
                        float* dW, float* dbias, int M, int in_features, int out_features,
                        void* workspace, size_t workspace_bytes, pa_stream_t stream) {

@@ -517,11 +517,19 @@ size_t linear_workspace_bytes(int M, int IN, int OUT) {
   return fwd > bwd ? fwd : bwd;
 }
 
+// Kept planes of X: the hi plane and, under split3 math, the lo plane, in the
+// layout of the GEMM operands, written by a forward for its backward.
+size_t linear_kept_bytes(int M, int IN, int mode) {
+  return static_cast<size_t>(mode == PA_F32_MATH_BF16 ? 1 : 2) * plane_size(M, IN);
+}
+
 int launch_linear_fwd(const float* x, const float* wt, const float* bias, float* const* outs,
                       int n_outs, int M, int IN, int OUT, int relu, void* ws, uint32_t* status,
-                      cudaStream_t s) {
+                      cudaStream_t s, void* kept) {
   uint8_t* w = static_cast<uint8_t*>(ws);
-  const Planes a = carve(w, M, IN), b = carve(w, IN, OUT);
+  uint8_t* kp = static_cast<uint8_t*>(kept);
+  const Planes a = kept ? Planes{kp, kp + plane_size(M, IN), M, IN} : carve(w, M, IN);
+  const Planes b = carve(w, IN, OUT);
   int st = split_into(x, a, s);
   if (st != PA_OK) return st;
   st = split_into(wt, b, s);
@@ -539,9 +547,14 @@ int launch_linear_fwd(const float* x, const float* wt, const float* bias, float*
 
 int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_parts, int n_parts,
                       const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
-                      int OUT, void* ws, uint32_t* status, cudaStream_t s) {
+                      int OUT, void* ws, uint32_t* status, cudaStream_t s, const void* kept) {
   uint8_t* w = static_cast<uint8_t*>(ws);
-  const Planes dy = carve(w, M, OUT), wp = carve(w, IN, OUT), xp = carve(w, M, IN);
+  const Planes dy = carve(w, M, OUT), wp = carve(w, IN, OUT);
+  Planes xp = carve(w, M, IN);
+  if (kept) {  // X's planes from the forward, valid for the current math mode
+    uint8_t* kp = const_cast<uint8_t*>(static_cast<const uint8_t*>(kept));
+    xp = Planes{kp, kp + plane_size(M, IN), M, IN};
+  }
   float* bias_ws = reinterpret_cast<float*>(w);  // bias_partials_bytes(M, OUT)
   // gather the column-block gradients into one pair of planes (row pitch round8(OUT))
   const int part = OUT / n_parts;
@@ -560,7 +573,7 @@ int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_pa
     if (st != PA_OK) return st;
   }
   if (dw) {
-    int st = split_into(x, xp, s);
+    int st = kept ? PA_OK : split_into(x, xp, s);
     if (st != PA_OK) return st;
     st = gemm_planes(2, xp, dy, dw, M, IN, OUT, Epilogue{}, status, s);
     if (st != PA_OK) return st;

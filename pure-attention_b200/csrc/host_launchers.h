@@ -82,12 +82,16 @@ size_t gemm_workspace_bytes(int M, int N, int K);
 size_t linear_workspace_bytes(int M, int IN, int OUT);
 // relu: Y = max(0, X W + bias). relu_out (backward, n_parts = 1): that Y,
 // whose sign masks dy.
+// kept (optional): X's operand planes, written by the forward (linear_kept_bytes
+// for the math mode) and read by the backward instead of converting X again.
 int launch_linear_fwd(const float* x, const float* w, const float* bias, float* const* outs,
                       int n_outs, int M, int IN, int OUT, int relu, void* ws, uint32_t* status,
-                      cudaStream_t s);
+                      cudaStream_t s, void* kept = nullptr);
 int launch_linear_bwd(const float* x, const float* w, const float* const* dy_parts, int n_parts,
                       const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
-                      int OUT, void* ws, uint32_t* status, cudaStream_t s);
+                      int OUT, void* ws, uint32_t* status, cudaStream_t s,
+                      const void* kept = nullptr);
+size_t linear_kept_bytes(int M, int IN, int mode);
 
 // training.cu
 int launch_relu_fwd(const float* x, float* y, size_t n, cudaStream_t s);

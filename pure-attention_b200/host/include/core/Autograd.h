@@ -62,6 +62,11 @@ struct LinearFunction : public Function {
   std::shared_ptr<Tensor> bias_input;
   std::vector<std::weak_ptr<Tensor>> Outputs;
   bool relu;
+  // X's operand planes written by the forward (pa_linear_fwd_keep) for the
+  // backward, with the f32 math mode they were made under
+  std::shared_ptr<void> kept;
+  size_t kept_bytes = 0;
+  int kept_mode = 0;
   LinearFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w, std::shared_ptr<Tensor> b,
                  std::vector<std::shared_ptr<Tensor>> outs, bool relu_ = false);
   void apply_backward() override;

@@ -108,9 +108,10 @@ void LinearFunction::apply_backward() {
     auto Y = Outputs[0].lock();
     if (!Y || !Y->get_gradient_ptr()) return;
     Scratch ws(pa_linear_workspace_size(M, K, N), stream());
-    check_status(pa_linear_relu_bwd(X_input->get_data_ptr(), W_input->get_data_ptr(),
-                                    Y->get_data_ptr(), Y->get_gradient_ptr(), dX, dW, db, M, K, N,
-                                    ws.get(), ws.size(), ps(stream())),
+    const float* dy = Y->get_gradient_ptr();
+    check_status(pa_linear_bwd_kept(X_input->get_data_ptr(), W_input->get_data_ptr(), kept.get(),
+                                    kept_bytes, kept_mode, Y->get_data_ptr(), &dy, 1, dX, dW, db,
+                                    M, K, N, ws.get(), ws.size(), ps(stream())),
                  "linear + ReLU backward");
     return;
   }
@@ -130,8 +131,9 @@ void LinearFunction::apply_backward() {
   }
   if (!any) return;
   Scratch ws(pa_linear_workspace_size(M, K, N), stream());
-  check_status(pa_linear_bwd(X_input->get_data_ptr(), W_input->get_data_ptr(), grads.data(), parts,
-                             dX, dW, db, M, K, N, ws.get(), ws.size(), ps(stream())),
+  check_status(pa_linear_bwd_kept(X_input->get_data_ptr(), W_input->get_data_ptr(), kept.get(),
+                                  kept_bytes, kept_mode, nullptr, grads.data(), parts, dX, dW, db,
+                                  M, K, N, ws.get(), ws.size(), ps(stream())),
                "linear backward");
 }
 

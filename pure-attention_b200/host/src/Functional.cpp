@@ -112,17 +112,32 @@ void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
     outs.push_back(mine.back()->get_data_ptr());
   }
   Scratch ws(pa_linear_workspace_size(M, K, N), stream);
-  if (relu)
+  std::shared_ptr<LinearFunction> node;
+  if (g) {
+    // the backward needs X's operand planes again: keep the forward's in the node
+    node = std::make_shared<LinearFunction>(A, W, bias, mine, relu);
+    node->kept_bytes = pa_linear_kept_size(M, K);
+    node->kept_mode = pa_get_f32_math();
+    void* p = nullptr;
+    retain_pool_memory();
+    if (cudaMallocAsync(&p, node->kept_bytes, stream) != cudaSuccess)
+      throw std::runtime_error("Linear: cannot allocate the kept operand planes");
+    node->kept = std::shared_ptr<void>(p, [](void* q) { cudaFreeAsync(q, CudaContext::getStream()); });
+    check_status(pa_linear_fwd_keep(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
+                                    outs.data(), static_cast<int>(num_parts), relu ? 1 : 0, M, K, N,
+                                    p, node->kept_bytes, ws.get(), ws.size(), ps(stream)),
+                 relu ? "Linear + ReLU" : "Linear");
+  } else if (relu) {
     check_status(pa_linear_relu_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
                                     outs[0], M, K, N, ws.get(), ws.size(), ps(stream)),
                  "Linear + ReLU");
-  else
+  } else {
     check_status(pa_linear_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
                                outs.data(), static_cast<int>(num_parts), M, K, N, ws.get(),
                                ws.size(), ps(stream)),
                  "Linear");
+  }
   if (g) {
-    auto node = std::make_shared<LinearFunction>(A, W, bias, mine, relu);
     for (auto& p : mine) p->set_grad_fn(node);
   }
   parts.insert(parts.end(), mine.begin(), mine.end());

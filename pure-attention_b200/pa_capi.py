@@ -28,7 +28,7 @@ EXPORTS = [
     "pa_layer_norm_bwd_accumulate",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
-    "pa_linear_relu_bwd",
+    "pa_linear_relu_bwd", "pa_linear_kept_size", "pa_linear_fwd_keep", "pa_linear_bwd_kept",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad", "pa_bias_grad_workspace_size", "pa_bias_grad_ws",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
     "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_fwd_workspace_size", "pa_mse_fwd_ws", "pa_mse_bwd", "pa_adam_step", "pa_adam_step_multi",
@@ -77,6 +77,10 @@ _SIGS = {
     "pa_linear_workspace_size": (_sz, [_int] * 3),
     "pa_linear_relu_fwd": (_int, [_vp] * 4 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_linear_relu_bwd": (_int, [_vp] * 7 + [_int] * 3 + [_vp, _sz, _vp]),
+    "pa_linear_kept_size": (_sz, [_int, _int]),
+    "pa_linear_fwd_keep": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp)] + [_int] * 5 + [_vp, _sz, _vp, _sz, _vp]),
+    "pa_linear_bwd_kept": (_int, [_vp, _vp, _vp, _sz, _int, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp]
+                           + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_linear_fwd": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp), _int, _int, _int, _int, _vp, _sz, _vp]),
     "pa_linear_bwd": (_int, [_vp, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp, _int, _int, _int,
                              _vp, _sz, _vp]),
@@ -364,6 +368,33 @@ def linear_relu_bwd(x, w, y, dy, dx, dw, dbias, M, in_features, out_features, wo
     _check("pa_linear_relu_bwd", load().pa_linear_relu_bwd(
         _ptr(x), _ptr(w), _ptr(y), _ptr(dy), opt(dx), opt(dw), opt(dbias), M, in_features,
         out_features, _ptr(ws), nb, _stream() if stream is None else stream))
+
+
+def linear_kept_size(M, in_features):
+    return load().pa_linear_kept_size(M, in_features)
+
+
+def linear_fwd_keep(x, w, bias, outs, M, in_features, out_features, kept, relu=False,
+                    workspace=None, stream=None):
+    """linear_fwd / linear_relu_fwd that also leaves x's operand planes in `kept`."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    arr = (_vp * len(outs))(*[_ptr(o) for o in outs])
+    _check("pa_linear_fwd_keep", load().pa_linear_fwd_keep(
+        _ptr(x), _ptr(w), _ptr(bias) if bias is not None else None, arr, len(outs), int(relu), M,
+        in_features, out_features, _ptr(kept), kept.numel() * kept.element_size(), _ptr(ws), nb,
+        _stream() if stream is None else stream))
+
+
+def linear_bwd_kept(x, w, kept, kept_mode, y, dy_parts, dx, dw, dbias, M, in_features, out_features,
+                    workspace=None, stream=None):
+    """linear_bwd (y None) / linear_relu_bwd (y = ReLU output) using the kept planes of x."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    arr = (_vp * len(dy_parts))(*[_ptr(t) for t in dy_parts])
+    opt = lambda t: _ptr(t) if t is not None else None
+    _check("pa_linear_bwd_kept", load().pa_linear_bwd_kept(
+        _ptr(x), _ptr(w), _ptr(kept), kept.numel() * kept.element_size(), F32_MATH[kept_mode],
+        opt(y), arr, len(dy_parts), opt(dx), opt(dw), opt(dbias), M, in_features, out_features,
+        _ptr(ws), nb, _stream() if stream is None else stream))
 
 
 def split_last_dim(inp, outs, rows, width, stream=None):

@@ -377,3 +377,45 @@ def test_adam_multi_tensor_matches_single_tensor_updates():
     assert pa_capi.device_status() == 0
     for a, b in zip(w1 + m1 + v1, w2 + m2 + v2):
         np.testing.assert_allclose(_np(b), _np(a), rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fwd_mode,bwd_mode", [("split3", "split3"), ("bf16", "bf16"),
+                                               ("split3", "bf16"), ("bf16", "split3")])
+def test_linear_kept_planes_match_plain_calls(fwd_mode, bwd_mode):
+    """pa_linear_fwd_keep / pa_linear_bwd_kept (X's operand planes kept from the
+    forward) give the plain calls' results, also when the math mode changed in
+    between (split3 planes serve bf16; bf16 planes make a split3 backward
+    convert X again); ReLU form included."""
+    import pa_capi
+    M, IN, OUT = 1024, 256, 384
+    x, w, bias = seeded_normal(51, (M, IN)), seeded_normal(52, (IN, OUT), 0.1), seeded_normal(53, (OUT,))
+    dy = seeded_normal(54, (M, OUT))
+    ws = torch.empty(pa_capi.linear_workspace_size(M, IN, OUT), dtype=torch.uint8, device="cuda")
+    try:
+        for relu in (False, True):
+            pa_capi.set_f32_math(fwd_mode)
+            kept = torch.empty(pa_capi.linear_kept_size(M, IN), dtype=torch.uint8, device="cuda")
+            y_keep, y_ref = (torch.empty(M, OUT, device="cuda") for _ in range(2))
+            pa_capi.linear_fwd_keep(_cu(x), _cu(w), _cu(bias), [y_keep], M, IN, OUT, kept, relu=relu,
+                                    workspace=ws)
+            if relu:
+                pa_capi.linear_relu_fwd(_cu(x), _cu(w), _cu(bias), y_ref, M, IN, OUT, ws)
+            else:
+                pa_capi.linear_fwd(_cu(x), _cu(w), _cu(bias), [y_ref], M, IN, OUT, ws)
+            np.testing.assert_array_equal(_np(y_keep), _np(y_ref))
+            pa_capi.set_f32_math(bwd_mode)
+            g1 = [torch.zeros(M, IN, device="cuda"), torch.zeros(IN, OUT, device="cuda"),
+                  torch.zeros(OUT, device="cuda")]
+            g2 = [torch.zeros_like(t) for t in g1]
+            pa_capi.linear_bwd_kept(_cu(x), _cu(w), kept, fwd_mode, y_keep if relu else None, [_cu(dy)],
+                                    *g1, M, IN, OUT, workspace=ws)
+            if relu:
+                pa_capi.linear_relu_bwd(_cu(x), _cu(w), y_ref, _cu(dy), *g2, M, IN, OUT, ws)
+            else:
+                pa_capi.linear_bwd(_cu(x), _cu(w), [_cu(dy)], *g2, M, IN, OUT, ws)
+            for a, b in zip(g1, g2):
+                assert rel_err(_np(a), _np(b)) < 1e-6
+    finally:
+        pa_capi.set_f32_math("split3")
+    assert pa_capi.device_status() == 0
