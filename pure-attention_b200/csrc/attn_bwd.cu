@@ -665,7 +665,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
                         const __grid_constant__ CUtensorMap mapdO, float* __restrict__ dq_acc,
                         OutT* __restrict__ dk, OutT* __restrict__ dv,
                         const uint8_t* __restrict__ ext, int L, int Lp, int H, float scale,
-                        float scale_log2, int accumulate, uint32_t* status) {
+                        float scale_log2, int accumulate, int n_pairs, int n_items,
+                        uint32_t* status) {
   using C = Bwd64Cfg;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[24];
@@ -714,17 +715,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
   const uint32_t kv_done = smem_u32(&bars[16]);
   const uint32_t rx_full = smem_u32(&bars[22]);  // partner's dQ half is in sRX (16 KB of st.async)
   const uint32_t tx_free = smem_u32(&bars[23]);  // partner has read what this CTA sent
+  const uint32_t acc_free = smem_u32(&bars[12]);  // the epilogue has read an item's dV and dK
 
   const int warp = warp_id();
-  const int bh = blockIdx.y;
-  const int b = bh / H, h = bh % H;
-  const int k0 = blockIdx.x * 128;
   const int n_q = Lp / 128;
-  // Query tiles are visited from tile blockIdx.x onwards (mod n_q): the CTAs of
-  // one (batch, head) then reduce into different dQ rows at any moment instead
-  // of all into the same tile. jq(j) = query tile of iteration j.
-  const int q_first = (blockIdx.x >> 1) % n_q;  // same order in both CTAs of a cluster
-  auto jq = [&](int j) { const int t = j + q_first; return t < n_q ? t : t - n_q; };
+  // Persistent clusters: cluster cl takes work items cl, cl + n_cl, ...; an item
+  // is (batch*head, pair of adjacent key tiles), this CTA's tile of the pair
+  // being its rank. Every role walks the same items; barrier phases and ring
+  // slots count query tiles over all of them (g = items done * n_q + j).
+  const int cl = static_cast<int>(blockIdx.x >> 1), n_cl = static_cast<int>(gridDim.x >> 1);
+  const int rank_x = static_cast<int>(blockIdx.x & 1);
+  struct Item {
+    int bh, b, h, k0, q_first;
+  };
+  auto item_of = [&](int item) {
+    Item w;
+    w.bh = item / n_pairs;
+    const int pair = item % n_pairs;
+    w.b = w.bh / H;
+    w.h = w.bh % H;
+    w.k0 = (2 * pair + rank_x) * 128;
+    // Query tiles are visited from tile `pair` onwards (mod n_q): the clusters
+    // of one (batch, head) then reduce into different dQ rows at any moment
+    // instead of all into the same tile. Same order in both CTAs of a cluster.
+    w.q_first = pair % n_q;
+    return w;
+  };
+  auto jq = [&](const Item& w, int j) { const int t = j + w.q_first; return t < n_q ? t : t - n_q; };
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -746,6 +763,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(kv_done, 1);
+    mbar_init(acc_free, C::NEW);
     mbar_init(rx_full, 1);
     mbar_init(tx_free, 128);
     fence_mbar_init();
@@ -766,23 +784,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
     if (elect_one()) {
       tma_prefetch_desc(&mapQ);
       tma_prefetch_desc(&mapdO);
-      mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
-      tma_load_4d(smem_u32(sK), &mapK, kv_full, 0, h, k0, b);
-      tma_load_4d(smem_u32(sV), &mapV, kv_full, 0, h, k0, b);
-      // buffers free up in the order dK(j-3) < dV(j-2) < dK(j-2) < ..., so the
-      // loads below are requested in the order they can be granted
-      for (int j = 0; j < n_q; ++j) {
-        const int s = j % C::QSTAGES, t = j % C::OSTAGES;
-        if (j >= C::QSTAGES && !mbar_wait(q_empty(s), ((j / C::QSTAGES) - 1) & 1, status)) break;
-        uint8_t* sq = sQ + s * C::QSTAGE_BYTES;
-        mbar_arrive_expect_tx(q_full(s), C::QT_BYTES + C::EXT_BYTES);
-        tma_load_4d(smem_u32(sq), &mapQ, q_full(s), 0, h, jq(j) * 128, b);
-        bulk_load(smem_u32(sq + C::QT_BYTES),
-                  ext + (static_cast<size_t>(bh) * n_q + jq(j)) * C::EXT_BYTES, C::EXT_BYTES,
-                  q_full(s));
-        if (j >= C::OSTAGES && !mbar_wait(o_empty(t), ((j / C::OSTAGES) - 1) & 1, status)) break;
-        mbar_arrive_expect_tx(o_full(t), C::QT_BYTES);
-        tma_load_4d(smem_u32(sO + t * C::QT_BYTES), &mapdO, o_full(t), 0, h, jq(j) * 128, b);
+      bool ok = true;
+      for (int item = cl, it = 0; ok && item < n_items; item += n_cl, ++it) {
+        const Item w = item_of(item);
+        // buffers free up in the order dK(g-3) < dV(g-2) < dK(g-2) < ..., so the
+        // loads below are requested in the order they can be granted
+        for (int j = 0; j < n_q; ++j) {
+          const int g = it * n_q + j;
+          const int s = g % C::QSTAGES, t = g % C::OSTAGES;
+          if (g >= C::QSTAGES && !(ok = mbar_wait(q_empty(s), ((g / C::QSTAGES) - 1) & 1, status)))
+            break;
+          uint8_t* sq = sQ + s * C::QSTAGE_BYTES;
+          mbar_arrive_expect_tx(q_full(s), C::QT_BYTES + C::EXT_BYTES);
+          tma_load_4d(smem_u32(sq), &mapQ, q_full(s), 0, w.h, jq(w, j) * 128, w.b);
+          bulk_load(smem_u32(sq + C::QT_BYTES),
+                    ext + (static_cast<size_t>(w.bh) * n_q + jq(w, j)) * C::EXT_BYTES,
+                    C::EXT_BYTES, q_full(s));
+          if (g >= C::OSTAGES && !(ok = mbar_wait(o_empty(t), ((g / C::OSTAGES) - 1) & 1, status)))
+            break;
+          mbar_arrive_expect_tx(o_full(t), C::QT_BYTES);
+          tma_load_4d(smem_u32(sO + t * C::QT_BYTES), &mapdO, o_full(t), 0, w.h, jq(w, j) * 128,
+                      w.b);
+          if (j == 0) {
+            // K and V of this item, once every MMA of the previous item is done with them
+            if (it > 0 && !(ok = mbar_wait(kv_done, (it - 1) & 1, status))) break;
+            mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
+            tma_load_4d(smem_u32(sK), &mapK, kv_full, 0, w.h, w.k0, w.b);
+            tma_load_4d(smem_u32(sV), &mapV, kv_full, 0, w.h, w.k0, w.b);
+          }
+        }
       }
     }
   } else if (warp == 1) {
@@ -803,88 +833,96 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       const uint64_t dOnesS = make_sdesc(smem_u32(sOnesS), 128, 0, 0);
       const uint64_t dOnesP = make_sdesc(smem_u32(sOnesP), 128, 0, 0);
       const uint64_t dExt = make_sdesc(smem_u32(sQ + C::QT_BYTES), 128, 256, 0);
-      auto q_off = [&](int j) { return static_cast<uint32_t>(((j % C::QSTAGES) * C::QSTAGE_BYTES) >> 4); };
-      auto o_off = [&](int j) { return static_cast<uint32_t>(((j % C::OSTAGES) * C::QT_BYTES) >> 4); };
-      auto issue_S = [&](int j) {  // S'^T = K Q^T - LSE/scale
-        const uint32_t so = q_off(j);
+      // g: query tile counted over all items (ring slots, dS buffer); j: within the item
+      auto q_off = [&](int g) { return static_cast<uint32_t>(((g % C::QSTAGES) * C::QSTAGE_BYTES) >> 4); };
+      auto o_off = [&](int g) { return static_cast<uint32_t>(((g % C::OSTAGES) * C::QT_BYTES) >> 4); };
+      auto issue_S = [&](int g) {  // S'^T = K Q^T - LSE/scale
+        const uint32_t so = q_off(g);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16_ss(tmem + C::T_S, dK_K + ((k * 32) >> 4), dQ_K + so + ((k * 32) >> 4), idSP,
                       k > 0 ? 1u : 0u);
         umma_f16_ss(tmem + C::T_S, dOnesS, dExt + so, idSP, 1u);
       };
-      auto issue_dP = [&](int j) {  // dP'^T = V dO^T - Delta
-        const uint32_t so = o_off(j);
+      auto issue_dP = [&](int g) {  // dP'^T = V dO^T - Delta
+        const uint32_t so = o_off(g);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16_ss(tmem + C::T_DP, dV_K + ((k * 32) >> 4), dO_K + so + ((k * 32) >> 4), idSP,
                       k > 0 ? 1u : 0u);
-        umma_f16_ss(tmem + C::T_DP, dOnesP, dExt + q_off(j), idSP, 1u);
+        umma_f16_ss(tmem + C::T_DP, dOnesP, dExt + q_off(g), idSP, 1u);
       };
-      auto issue_dV = [&](int j) {  // dV += P^T dO  (P^T from TMEM)
-        const uint32_t so = o_off(j);
+      auto issue_dV = [&](int g, int j) {  // dV += P^T dO  (P^T from TMEM)
+        const uint32_t so = o_off(g);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           umma_f16_ts(tmem + C::T_DV, tmem + C::T_PT + 8 * k, dO_MN + so + ((k * 2048) >> 4), idKV,
                       (j > 0 || k > 0) ? 1u : 0u);
       };
-      auto issue_dK = [&](int j) {  // dK += dS^T Q  (dS^T packed over the dP columns)
-        const uint32_t so = q_off(j);
+      auto issue_dK = [&](int g, int j) {  // dK += dS^T Q  (dS^T packed over the dP columns)
+        const uint32_t so = q_off(g);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           umma_f16_ts(tmem + C::T_DK, tmem + C::T_DP + 32 * (k / 2) + 8 * (k % 2),
                       dQ_MN + so + ((k * 2048) >> 4), idKV, (j > 0 || k > 0) ? 1u : 0u);
       };
-      auto issue_dQ = [&](int j) {  // dQ = dS K
-        const uint32_t bo = ((j & 1) * C::DS_BYTES) >> 4;
+      auto issue_dQ = [&](int g) {  // dQ = dS K
+        const uint32_t bo = ((g & 1) * C::DS_BYTES) >> 4;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           umma_f16_ss(tmem + C::T_DQ, dDS_MN + bo + ((k * 2048) >> 4), dK_MN + ((k * 2048) >> 4), idQ,
                       k > 0 ? 1u : 0u);
       };
-      bool ok = mbar_wait(kv_full, 0, status) && mbar_wait(q_full(0), 0, status) &&
-                mbar_wait(o_full(0), 0, status);
-      if (ok) {
+      bool ok = true;
+      for (int item = cl, it = 0; ok && item < n_items; item += n_cl, ++it) {
+        const int gb = it * n_q;
+        ok = mbar_wait(kv_full, it & 1, status) &&
+             mbar_wait(q_full(gb % C::QSTAGES), (gb / C::QSTAGES) & 1, status) &&
+             mbar_wait(o_full(gb % C::OSTAGES), (gb / C::OSTAGES) & 1, status);
+        if (!ok) break;
         tc_fence_after();
-        issue_S(0);
+        issue_S(gb);
         umma_commit(s_full);
-        issue_dP(0);
+        issue_dP(gb);
         umma_commit(dp_full);
+        for (int j = 0; ok && j < n_q; ++j) {
+          const int g = gb + j;
+          const bool more = j + 1 < n_q;
+          if (!(ok = mbar_wait(s_free, g & 1, status))) break;
+          if (more) {
+            if (!(ok = mbar_wait(q_full((g + 1) % C::QSTAGES), ((g + 1) / C::QSTAGES) & 1, status)))
+              break;
+            tc_fence_after();
+            issue_S(g + 1);
+            umma_commit(s_full);
+          }
+          if (!(ok = mbar_wait(pt_full, g & 1, status))) break;
+          // dV and dK restart from zero: the previous item's epilogue must have read them
+          if (j == 0 && it > 0 && !(ok = mbar_wait(acc_free, (it - 1) & 1, status))) break;
+          tc_fence_after();
+          issue_dV(g, j);
+          umma_commit(pt_free);
+          umma_commit(o_empty(g % C::OSTAGES));
+          if (!(ok = mbar_wait(p_full(g), (g >> 1) & 1, status))) break;
+          tc_fence_after();
+          issue_dK(g, j);  // reads dS^T(g) from the dP columns before dP(g+1) overwrites them
+          umma_commit(q_empty(g % C::QSTAGES));
+          if (more) {
+            if (!(ok = mbar_wait(o_full((g + 1) % C::OSTAGES), ((g + 1) / C::OSTAGES) & 1, status)))
+              break;
+            tc_fence_after();
+            issue_dP(g + 1);
+            umma_commit(dp_full);
+          }
+          if (g > 0) {
+            if (!(ok = mbar_wait(dq_empty, (g - 1) & 1, status))) break;
+            tc_fence_after();
+          }
+          issue_dQ(g);
+          umma_commit(dq_full);
+        }
+        if (ok) umma_commit(kv_done);  // K, V free; dV, dK final
       }
-      for (int j = 0; ok && j < n_q; ++j) {
-        const bool more = j + 1 < n_q;
-        if (!(ok = mbar_wait(s_free, j & 1, status))) break;
-        if (more) {
-          if (!(ok = mbar_wait(q_full((j + 1) % C::QSTAGES), ((j + 1) / C::QSTAGES) & 1, status)))
-            break;
-          tc_fence_after();
-          issue_S(j + 1);
-          umma_commit(s_full);
-        }
-        if (!(ok = mbar_wait(pt_full, j & 1, status))) break;
-        tc_fence_after();
-        issue_dV(j);
-        umma_commit(pt_free);
-        umma_commit(o_empty(j % C::OSTAGES));
-        if (!(ok = mbar_wait(p_full(j), (j >> 1) & 1, status))) break;
-        tc_fence_after();
-        issue_dK(j);  // reads dS^T(j) from the dP columns before dP(j+1) overwrites them
-        umma_commit(q_empty(j % C::QSTAGES));
-        if (more) {
-          if (!(ok = mbar_wait(o_full((j + 1) % C::OSTAGES), ((j + 1) / C::OSTAGES) & 1, status)))
-            break;
-          tc_fence_after();
-          issue_dP(j + 1);
-          umma_commit(dp_full);
-        }
-        if (j > 0) {
-          if (!(ok = mbar_wait(dq_empty, (j - 1) & 1, status))) break;
-          tc_fence_after();
-        }
-        issue_dQ(j);
-        umma_commit(dq_full);
-      }
-      if (ok) umma_commit(kv_done);
     }
   } else if (warp >= C::EW_WARP && warp < C::READOUT_WARP) {
     // ------------------------------------------------------------ P / dS
@@ -892,9 +930,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
     // queries [32 grp, 32 grp + 32) of each tile; thread = key row.
     const int grp = (warp - C::EW_WARP) >> 2;
     const int kr = ((warp & 3) << 5) + static_cast<int>(lane_id());  // key row == TMEM lane
-    const int key = k0 + kr;
-    const bool valid = key < L;
-    const bool full_tile = k0 + 128 <= L;  // CTA-uniform: no key masking needed
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + C::T_S + lane_base + grp * C::QPG;
     const uint32_t tdP = tmem + C::T_DP + lane_base + grp * C::QPG;
@@ -902,9 +937,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
     // this group's 32 queries: 64 bytes of a key row in dS chunk grp / 2, from byte 64 (grp % 2)
     const int dsb0 = 64 * (grp & 1);
     bool ok = true;
+    for (int item = cl, it = 0; ok && item < n_items; item += n_cl, ++it) {
+    const Item w = item_of(item);
+    const int key = w.k0 + kr;
+    const bool valid = key < L;
+    const bool full_tile = w.k0 + 128 <= L;  // CTA-uniform: no key masking needed
     for (int j = 0; j < n_q; ++j) {
+      const int g = it * n_q + j;
       // P phase
-      if (!(ok = mbar_wait_warp(s_full, j & 1, status))) break;
+      if (!(ok = mbar_wait_warp(s_full, g & 1, status))) break;
       tc_fence_after();
       uint32_t va[16], vb[16];
       tmem_ld16(tS, va);
@@ -928,8 +969,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
         pk0[i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
         pk1[i] = pack_bf16x2(p[16 + 2 * i], p[16 + 2 * i + 1]);
       }
-      if (j > 0) {  // P^T columns are free once the previous tile's dV MMA has read them
-        if (!(ok = mbar_wait_warp(pt_free, (j - 1) & 1, status))) break;
+      if (g > 0) {  // P^T columns are free once the previous tile's dV MMA has read them
+        if (!(ok = mbar_wait_warp(pt_free, (g - 1) & 1, status))) break;
         tc_fence_after();
       }
       PA_TMEM_ST_X8(tPT, pk0);
@@ -938,7 +979,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       tc_fence_before();
       mbar_arrive(pt_full);
       // dS phase
-      if (!(ok = mbar_wait_warp(dp_full, j & 1, status))) break;
+      if (!(ok = mbar_wait_warp(dp_full, g & 1, status))) break;
       tc_fence_after();
       tmem_ld16(tdP, va);
       tmem_ld16(tdP + 16, vb);
@@ -954,7 +995,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       // dS^T packed over the first 16 of this group's 32 dP columns (read above)
       PA_TMEM_ST_X8(tdP, ds);
       PA_TMEM_ST_X8(tdP + 8, (ds + 8));
-      uint8_t* dsrow = sdS + (j & 1) * C::DS_BYTES + (grp >> 1) * C::CHUNK;
+      uint8_t* dsrow = sdS + (g & 1) * C::DS_BYTES + (grp >> 1) * C::CHUNK;
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         *reinterpret_cast<uint4*>(dsrow + sw128_offset(kr, dsb0 + 16 * u)) =
@@ -962,17 +1003,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full(j));
+      mbar_arrive(p_full(g));
     }
     // dV and dK (x scale) epilogue: groups 0, 1 write dV columns [0,32), [32,64);
     // groups 2, 3 the same columns of dK.
-    if (ok && mbar_wait_warp(kv_done, 0, status)) {
+    if (!ok || !(ok = mbar_wait_warp(kv_done, it & 1, status))) break;
+    {
       tc_fence_after();
       const bool is_dv = grp < 2;
       const int c = grp & 1;
+      const int b = w.b, h = w.h;
       uint32_t o[32];
       tmem_ld32(tmem + (is_dv ? C::T_DV : C::T_DK) + lane_base + c * 32, o);
       tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(acc_free);  // the next item's first dV / dK MMAs may overwrite them
       if (valid && std::is_same<OutT, float>::value) {
         const float mul = is_dv ? 1.f : scale;
         float4* d4 = reinterpret_cast<float4*>((is_dv ? dv : dk) +
@@ -1014,6 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
         }
       }
     }
+    }  // item
   } else if (warp >= C::READOUT_WARP) {
     // ------------------------------------------------------------ dQ readout
     const int lane = static_cast<int>(lane_id());
@@ -1025,10 +1071,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
     const uint8_t* rx_slot = sRX + tid * 16;
     const uint32_t rx_full_peer = mapa_shared(rx_full, peer);
     const uint32_t tx_free_peer = mapa_shared(tx_free, peer);
+    bool ok = true;
+    for (int item = cl, it = 0; ok && item < n_items; item += n_cl, ++it) {
+    const Item w = item_of(item);
     for (int j = 0; j < n_q; ++j) {
-      if (!mbar_wait_warp(dq_full, j & 1, status)) break;
+      const int g = it * n_q + j;
+      if (!(ok = mbar_wait_warp(dq_full, g & 1, status))) break;
       // the partner has read what this CTA sent for the previous tile
-      if (j > 0 && !mbar_wait_cluster_warp(tx_free, (j - 1) & 1, status)) break;
+      if (g > 0 && !(ok = mbar_wait_cluster_warp(tx_free, (g - 1) & 1, status))) break;
       if (tid == 0) mbar_arrive_expect_tx(rx_full, C::RX_BYTES);  // this tile's incoming bytes
       tc_fence_after();
       uint32_t own0[16], own1[16];
@@ -1049,15 +1099,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
         else dq_split<1>(r, own1, peer_slot, rx_full_peer, 4);
       }
       // add the partner's contribution to this CTA's columns, then reduce them
-      if (!mbar_wait_cluster_warp(rx_full, j & 1, status)) break;
+      if (!(ok = mbar_wait_cluster_warp(rx_full, g & 1, status))) break;
       dq_add_slots(own0, rx_slot, 0);
       dq_add_slots(own1, rx_slot, 4);
       mbar_arrive_cluster_relaxed(tx_free_peer);  // the values read above are consumed
-      float* row = dq_acc + (static_cast<size_t>(bh) * Lp + jq(j) * 128 + wl + (lane >> 2)) * 64 +
+      float* row = dq_acc + (static_cast<size_t>(w.bh) * Lp + jq(w, j) * 128 + wl + (lane >> 2)) * 64 +
                    32 * rank + 2 * (lane & 3);
       dq_reduce_own(own0, row);
       dq_reduce_own(own1, row + 16 * 64);
     }
+    }  // item
   }
 
   tc_fence_before();
@@ -1186,12 +1237,35 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
   if constexpr (D == 64 && !SPLIT) {
     using C64 = Bwd64Cfg;
-    grid.x = (grid.x + 1) & ~1u;  // clusters of two key tiles (a tile past L has no keys)
     static uint64_t attr64 = 0;
     ensure_smem_attr(attn_bwd_d64_kernel<T>, C64::SMEM, attr64);
-    attn_bwd_d64_kernel<T><<<grid, C64::THREADS, C64::SMEM, stream>>>(
+    // Persistent clusters of two CTAs, as many as fit on the device at once;
+    // work items are (batch*head, pair of adjacent key tiles; a tile past L
+    // has no keys).
+    const int n_pairs = (static_cast<int>(grid.x) + 1) / 2;
+    const int n_items = n_pairs * static_cast<int>(bh);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int max_clusters[64] = {0};
+    int& mc = max_clusters[dev & 63];
+    if (mc <= 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * 4096, 1, 1);
+      cfg.blockDim = dim3(C64::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = C64::SMEM;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_bwd_d64_kernel<T>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();  // clear a failed query; fall back to one cluster per two SMs
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        n = sms / 2;
+      }
+      mc = n;
+    }
+    const int n_cl = n_items < mc ? n_items : mc;
+    attn_bwd_d64_kernel<T><<<dim3(2 * n_cl, 1, 1), C64::THREADS, C64::SMEM, stream>>>(
         m[0], m[1], m[2], m[3], dq_acc, static_cast<T*>(dk), static_cast<T*>(dv), ext, sh.L, Lp,
-        sh.H, sh.scale, sh.scale * kLog2e, accumulate, status);
+        sh.H, sh.scale, sh.scale * kLog2e, accumulate, n_pairs, n_items, status);
   } else {
     static uint64_t attr = 0;
     ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr);
