@@ -948,9 +948,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       if (!(ok = mbar_wait_warp(s_full, g & 1, status))) break;
       tc_fence_after();
       uint32_t va[16], vb[16];
-      tmem_ld16(tS, va);
-      tmem_ld16(tS + 16, vb);
-      tmem_ld_wait();
+      tmem_ld16x2_sync(tS, tS + 16, va, vb);
       tc_fence_before();
       mbar_arrive(s_free);
       float p[32];
@@ -981,9 +979,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       // dS phase
       if (!(ok = mbar_wait_warp(dp_full, g & 1, status))) break;
       tc_fence_after();
-      tmem_ld16(tdP, va);
-      tmem_ld16(tdP + 16, vb);
-      tmem_ld_wait();
+      tmem_ld16x2_sync(tdP, tdP + 16, va, vb);
       uint32_t ds[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -1014,8 +1010,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       const int c = grp & 1;
       const int b = w.b, h = w.h;
       uint32_t o[32];
-      tmem_ld32(tmem + (is_dv ? C::T_DV : C::T_DK) + lane_base + c * 32, o);
-      tmem_ld_wait();
+      tmem_ld32_sync(tmem + (is_dv ? C::T_DV : C::T_DK) + lane_base + c * 32, o);
       tc_fence_before();
       mbar_arrive(acc_free);  // the next item's first dV / dK MMAs may overwrite them
       if (valid && std::is_same<OutT, float>::value) {
@@ -1084,15 +1079,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       uint32_t own0[16], own1[16];
       {
         uint32_t r[32];
-        tmem_ld_16x256b_x8(tdQ, r);  // rows wl .. wl+15
-        tmem_ld_wait();
+        tmem_ld_16x256b_x8_sync(tdQ, r);  // rows wl .. wl+15
         if (rank == 0) dq_split<0>(r, own0, peer_slot, rx_full_peer, 0);
         else dq_split<1>(r, own0, peer_slot, rx_full_peer, 0);
       }
       {
         uint32_t r[32];
-        tmem_ld_16x256b_x8(tdQ + (16u << 16), r);  // rows wl+16 .. wl+31
-        tmem_ld_wait();
+        tmem_ld_16x256b_x8_sync(tdQ + (16u << 16), r);  // rows wl+16 .. wl+31
         tc_fence_before();
         mbar_arrive(dq_empty);  // dQ's TMEM columns are free for the next tile
         if (rank == 0) dq_split<0>(r, own1, peer_slot, rx_full_peer, 4);
@@ -1102,7 +1095,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Bwd64Cfg::THREADS, 1
       if (!(ok = mbar_wait_cluster_warp(rx_full, g & 1, status))) break;
       dq_add_slots(own0, rx_slot, 0);
       dq_add_slots(own1, rx_slot, 4);
-      mbar_arrive_cluster_relaxed(tx_free_peer);  // the values read above are consumed
+      // The partner may now overwrite sRX. The fence orders this thread's reads
+      // of sRX before the arrive (a bare relaxed arrive may be issued before
+      // those loads return); restricted to shared::cta accesses, it does not
+      // wait for the reductions still in flight, as a full release would.
+      fence_release_shared_cta_cluster();
+      mbar_arrive_cluster_relaxed(tx_free_peer);
       float* row = dq_acc + (static_cast<size_t>(w.bh) * Lp + jq(w, j) * 128 + wl + (lane >> 2)) * 64 +
                    32 * rank + 2 * (lane & 3);
       dq_reduce_own(own0, row);
