@@ -5,8 +5,12 @@
 // O = softmax(S) V and LSE = rowmax + log(rowsum) (natural log). Unlike the
 // reference, O is divided by the row sum exactly (no +1e-6).
 //
-// One CTA = one (batch, head) and two 128-row query tiles (256 rows).
-//   warp 0      : TMA producer (Q once, K/V ring of STAGES stages)
+// Persistent: one CTA per SM walks work items (batch*head, block of two
+// 128-row query tiles = 256 rows), item = blockIdx.x + k * gridDim.x; the K/V
+// ring, the barrier phases and (where shared memory allows) a double-buffered
+// Q carry across items, so the next item's first S MMAs and loads overlap the
+// current item's last tiles and its O write-back.
+//   warp 0      : TMA producer (Q per item, K/V ring of STAGES stages)
 //   warp 1      : TMEM allocator + tcgen05.mma issuer (single elected lane)
 //   warps 4-7   : softmax of query tile 0   (thread = one query row)
 //   warps 8-11  : softmax of query tile 1
@@ -45,7 +49,12 @@ struct FwdCfg {
   static constexpr int CHUNK = 128 * 128;        // bytes of one 128-row x 128-byte box
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int SMEM = NP * (2 * Q_BYTES + STAGES * 2 * KV_BYTES) + 1024;
+  static constexpr int KV_RING = NP * STAGES * 2 * KV_BYTES;
+  static constexpr int Q_ITEM = NP * 2 * Q_BYTES;  // both query tiles of an item
+  // Q buffers: two where they fit next to the K/V ring (the next item's Q then
+  // loads while the current item still runs), else one.
+  static constexpr int QBUF = (2 * Q_ITEM + KV_RING + 1024 <= 227 * 1024) ? 2 : 1;
+  static constexpr int SMEM = QBUF * Q_ITEM + KV_RING + 1024;
   static constexpr int THREADS = 384;
   static constexpr bool SEP_P = (D == 64 && !SPLIT);  // P in its own TMEM columns
   static constexpr uint32_t T_S = 0, T_O = 256;
@@ -53,13 +62,14 @@ struct FwdCfg {
 };
 
 // OutT: __nv_bfloat16 (bf16 path) or float (SPLIT). d_out: head dim of O.
+// n_qb: 256-row query blocks per (batch, head); n_items = n_qb * B * H.
 template <int D, bool SPLIT, typename OutT>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapQl,
                     const __grid_constant__ CUtensorMap mapKl, const __grid_constant__ CUtensorMap mapVl,
                     OutT* __restrict__ O, float* __restrict__ lse, int L, int H, int d_out,
-                    float scale_log2, uint32_t* status) {
+                    float scale_log2, int n_qb, int n_items, uint32_t* status) {
   using C = FwdCfg<D, SPLIT>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bars[24];
@@ -68,28 +78,33 @@ __global__ void __launch_bounds__(384, 1)
   if (cta_aborted(status, &abort_flag)) return;
 
   uint8_t* smem = align1024(smem_raw);
-  // plane p of query tile t at sQ + (t * NP + p) * Q_BYTES; K/V likewise per stage
+  // plane p of query tile t of Q buffer u at sQ + u * Q_ITEM + (t * NP + p) * Q_BYTES;
+  // K/V plane p of stage s at sK / sV + (s * NP + p) * KV_BYTES
   uint8_t* sQ = smem;
-  uint8_t* sK = smem + C::NP * 2 * C::Q_BYTES;
+  uint8_t* sK = smem + C::QBUF * C::Q_ITEM;
   uint8_t* sV = sK + C::NP * C::STAGES * C::KV_BYTES;
 
-  const uint32_t q_full = smem_u32(&bars[0]);
-  auto kv_full = [&](int s) { return smem_u32(&bars[1 + s]); };
-  auto kv_empty = [&](int s) { return smem_u32(&bars[4 + s]); };
-  auto s_full = [&](int t) { return smem_u32(&bars[7 + t]); };
-  auto p_full = [&](int t) { return smem_u32(&bars[9 + t]); };
-  auto o_done = [&](int t) { return smem_u32(&bars[11 + t]); };
-  auto s_free = [&](int t) { return smem_u32(&bars[13 + t]); };
-  auto pv_done = [&](int t) { return smem_u32(&bars[15 + t]); };
+  auto q_full = [&](int u) { return smem_u32(&bars[0 + u]); };
+  auto q_empty = [&](int u) { return smem_u32(&bars[2 + u]); };
+  auto kv_full = [&](int s) { return smem_u32(&bars[4 + s]); };
+  auto kv_empty = [&](int s) { return smem_u32(&bars[7 + s]); };
+  auto s_full = [&](int t) { return smem_u32(&bars[10 + t]); };
+  auto p_full = [&](int t) { return smem_u32(&bars[12 + t]); };
+  auto o_done = [&](int t) { return smem_u32(&bars[14 + t]); };
+  auto s_free = [&](int t) { return smem_u32(&bars[16 + t]); };
+  auto pv_done = [&](int t) { return smem_u32(&bars[18 + t]); };
 
   const int warp = warp_id();
-  const int bh = blockIdx.y;
-  const int b = bh / H, h = bh % H;
-  const int q0 = blockIdx.x * 256;
   const int n_kv = (L + C::BN - 1) / C::BN;
+  // Items in launch order: consecutive items share (batch, head), so the CTAs
+  // running at one time read the K/V of a few heads, which stay in L2.
+  const int item0 = static_cast<int>(blockIdx.x), n_cta = static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int u = 0; u < C::QBUF; ++u) {
+      mbar_init(q_full(u), 1);
+      mbar_init(q_empty(u), 1);
+    }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
@@ -112,29 +127,40 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
+  // it: items done by this CTA; g: KV tiles done over all its items (ring slot
+  // and barrier phase); j: KV tile within the item.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&mapQ);
       tma_prefetch_desc(&mapK);
       tma_prefetch_desc(&mapV);
-      mbar_arrive_expect_tx(q_full, C::NP * 2 * C::Q_BYTES);
-      for (int t = 0; t < 2; ++t)
-        for (int p = 0; p < C::NP; ++p)
-          for (int c = 0; c < C::KCH; ++c)
-            tma_load_4d(smem_u32(sQ + (t * C::NP + p) * C::Q_BYTES + c * C::CHUNK),
-                        p ? &mapQl : &mapQ, q_full, c * 64, h, q0 + t * C::BM, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % C::STAGES;
-        if (j >= C::STAGES && !mbar_wait(kv_empty(s), ((j / C::STAGES) - 1) & 1, status)) break;
-        mbar_arrive_expect_tx(kv_full(s), C::NP * 2 * C::KV_BYTES);
-        for (int p = 0; p < C::NP; ++p)
-          for (int c = 0; c < C::KCH; ++c) {
-            tma_load_4d(smem_u32(sK + (s * C::NP + p) * C::KV_BYTES + c * C::CHUNK),
-                        p ? &mapKl : &mapK, kv_full(s), c * 64, h, j * C::BN, b);
-            tma_load_4d(smem_u32(sV + (s * C::NP + p) * C::KV_BYTES + c * C::CHUNK),
-                        p ? &mapVl : &mapV, kv_full(s), c * 64, h, j * C::BN, b);
-          }
+      bool ok = true;
+      for (int item = item0, it = 0; ok && item < n_items; item += n_cta, ++it) {
+        const int bh = item / n_qb;
+        const int b = bh / H, h = bh % H;
+        const int q0 = (item % n_qb) * 256;
+        const int u = it % C::QBUF, k = it / C::QBUF;
+        if (k > 0 && !(ok = mbar_wait(q_empty(u), (k - 1) & 1, status))) break;
+        mbar_arrive_expect_tx(q_full(u), C::Q_ITEM);
+        for (int t = 0; t < 2; ++t)
+          for (int p = 0; p < C::NP; ++p)
+            for (int c = 0; c < C::KCH; ++c)
+              tma_load_4d(smem_u32(sQ + u * C::Q_ITEM + (t * C::NP + p) * C::Q_BYTES + c * C::CHUNK),
+                          p ? &mapQl : &mapQ, q_full(u), c * 64, h, q0 + t * C::BM, b);
+        for (int j = 0; j < n_kv; ++j) {
+          const int g = it * n_kv + j;
+          const int s = g % C::STAGES;
+          if (g >= C::STAGES && !(ok = mbar_wait(kv_empty(s), ((g / C::STAGES) - 1) & 1, status))) break;
+          mbar_arrive_expect_tx(kv_full(s), C::NP * 2 * C::KV_BYTES);
+          for (int p = 0; p < C::NP; ++p)
+            for (int c = 0; c < C::KCH; ++c) {
+              tma_load_4d(smem_u32(sK + (s * C::NP + p) * C::KV_BYTES + c * C::CHUNK),
+                          p ? &mapKl : &mapK, kv_full(s), c * 64, h, j * C::BN, b);
+              tma_load_4d(smem_u32(sV + (s * C::NP + p) * C::KV_BYTES + c * C::CHUNK),
+                          p ? &mapVl : &mapV, kv_full(s), c * 64, h, j * C::BN, b);
+            }
+        }
       }
     }
   } else if (warp == 1) {
@@ -148,12 +174,12 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t dV0 = make_sdesc(smem_u32(sV), C::CHUNK, 1024);
       // SPLIT: product terms (A plane, B plane) = (hi,hi), (hi,lo), (lo,hi)
       constexpr int NTERM = SPLIT ? 3 : 1;
-      auto issue_S = [&](int t, int j) {
+      auto issue_S = [&](int t, int u, int g) {
 #pragma unroll
         for (int term = 0; term < NTERM; ++term) {
           const int pa = term == 2 ? 1 : 0, pb = term == 1 ? 1 : 0;
-          const uint64_t qd = dQ0 + (((t * C::NP + pa) * C::Q_BYTES) >> 4);
-          const uint64_t kd = dK0 + ((((j % C::STAGES) * C::NP + pb) * C::KV_BYTES) >> 4);
+          const uint64_t qd = dQ0 + ((u * C::Q_ITEM + (t * C::NP + pa) * C::Q_BYTES) >> 4);
+          const uint64_t kd = dK0 + ((((g % C::STAGES) * C::NP + pb) * C::KV_BYTES) >> 4);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t off = ((k / 4) * C::CHUNK + (k % 4) * 32) >> 4;
@@ -161,58 +187,72 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
       };
-      auto issue_PV = [&](int t, int j) {
+      // P*V of KV tile g (j-th of the item: j == 0 starts O from zero)
+      auto issue_PV = [&](int t, int g, int j) {
         const uint32_t tp = C::SEP_P ? (tmem + C::T_P + t * 64) : (tmem + C::T_S + t * 128);
 #pragma unroll
         for (int term = 0; term < NTERM; ++term) {
           const int pa = term == 2 ? 1 : 0, pb = term == 1 ? 1 : 0;
-          const uint64_t vd = dV0 + ((((j % C::STAGES) * C::NP + pb) * C::KV_BYTES) >> 4);
+          const uint64_t vd = dV0 + ((((g % C::STAGES) * C::NP + pb) * C::KV_BYTES) >> 4);
 #pragma unroll
           for (int k = 0; k < C::BN / 16; ++k)
             umma_f16_ts(tmem + C::T_O + t * D, tp + pa * 64 + k * 8, vd + ((k * 2048) >> 4), idO,
                         (j > 0 || term > 0 || k > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(q_full, 0, status) && mbar_wait(kv_full(0), 0, status);
-      if (ok) {
-        tc_fence_after();
-        issue_S(0, 0);
-        umma_commit(s_full(0));
-        issue_S(1, 0);
-        umma_commit(s_full(1));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j % C::STAGES;
-        const bool more = j + 1 < n_kv;
-        if (more && !(ok = mbar_wait(kv_full((j + 1) % C::STAGES), ((j + 1) / C::STAGES) & 1,
-                                     status)))
-          break;
+      bool ok = true;
+      for (int item = item0, it = 0; ok && item < n_items; item += n_cta, ++it) {
+        const int u = it % C::QBUF, g0 = it * n_kv;
+        ok = mbar_wait(q_full(u), (it / C::QBUF) & 1, status) &&
+             mbar_wait(kv_full(g0 % C::STAGES), (g0 / C::STAGES) & 1, status);
+        if (!ok) break;
+        // S of the item's first KV tile. Separate P: S's columns are free once
+        // the softmax has loaded the previous tile's S. P over S: the previous
+        // tile's P*V, which reads them, was issued before (in order).
         for (int t = 0; t < 2; ++t) {
-          if (C::SEP_P) {
-            // next S first (its columns were released by s_free), then P*V
-            if (more) {
-              if (!(ok = mbar_wait(s_free(t), j & 1, status))) break;
+          if (C::SEP_P && g0 > 0 && !(ok = mbar_wait(s_free(t), (g0 - 1) & 1, status))) break;
+          tc_fence_after();
+          issue_S(t, u, g0);
+          umma_commit(s_full(t));
+        }
+        if (!ok) break;
+        if (n_kv == 1) umma_commit(q_empty(u));
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int g = g0 + j;
+          const bool more = j + 1 < n_kv;
+          if (more && !(ok = mbar_wait(kv_full((g + 1) % C::STAGES), ((g + 1) / C::STAGES) & 1, status)))
+            break;
+          // P*V of tile j starts O from zero at j == 0: p_full of this item's
+          // first tile is arrived only after the softmax has read the previous
+          // item's O (its write-back comes first), so O is free then.
+          for (int t = 0; t < 2; ++t) {
+            if (C::SEP_P) {
+              // next S first (its columns were released by s_free), then P*V
+              if (more) {
+                if (!(ok = mbar_wait(s_free(t), g & 1, status))) break;
+                tc_fence_after();
+                issue_S(t, u, g + 1);
+                umma_commit(s_full(t));
+              }
+              if (!(ok = mbar_wait(p_full(t), g & 1, status))) break;
               tc_fence_after();
-              issue_S(t, j + 1);
-              umma_commit(s_full(t));
+              issue_PV(t, g, j);
+              umma_commit(pv_done(t));
+            } else {
+              // P lives in S's columns: P*V first, then the next S overwrites them
+              if (!(ok = mbar_wait(p_full(t), g & 1, status))) break;
+              tc_fence_after();
+              issue_PV(t, g, j);
+              umma_commit(pv_done(t));
+              if (more) {
+                issue_S(t, u, g + 1);
+                umma_commit(s_full(t));
+              }
             }
-            if (!(ok = mbar_wait(p_full(t), j & 1, status))) break;
-            tc_fence_after();
-            issue_PV(t, j);
-            umma_commit(pv_done(t));
-          } else {
-            // P lives in S's columns: P*V first, then the next S overwrites them
-            if (!(ok = mbar_wait(p_full(t), j & 1, status))) break;
-            tc_fence_after();
-            issue_PV(t, j);
-            umma_commit(pv_done(t));
-            if (more) {
-              issue_S(t, j + 1);
-              umma_commit(s_full(t));
-            }
+            if (t == 1) umma_commit(kv_empty(g % C::STAGES));
+            if (!more) umma_commit(o_done(t));
           }
-          if (t == 1) umma_commit(kv_empty(s));
-          if (!more) umma_commit(o_done(t));
+          if (j + 2 == n_kv) umma_commit(q_empty(u));  // the item's last S MMAs are issued
         }
       }
     }
@@ -224,12 +264,16 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tS = tmem + C::T_S + t * 128 + lane_base;
     const uint32_t tO = tmem + C::T_O + t * D + lane_base;
     const uint32_t tP = C::SEP_P ? (tmem + C::T_P + t * 64 + lane_base) : tS;
-    const int row = q0 + t * C::BM + r;
+    bool ok = true;
+    for (int item = item0, it = 0; ok && item < n_items; item += n_cta, ++it) {
+    const int bh = item / n_qb;
+    const int b = bh / H, h = bh % H;
+    const int row = (item % n_qb) * 256 + t * C::BM + r;
     float m = -INFINITY;  // running max of S * scale * log2(e)
     float l = 0.f;        // running row sum (relative to m)
-    bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = mbar_wait_warp(s_full(t), j & 1, status))) break;
+      const int g = it * n_kv + j;
+      if (!(ok = mbar_wait_warp(s_full(t), g & 1, status))) break;
       tc_fence_after();
       float s[128];
 #pragma unroll
@@ -258,8 +302,8 @@ __global__ void __launch_bounds__(384, 1)
       }
       // P of the previous tile and O are read / accumulated by its P*V MMA:
       // wait for it before overwriting P or rescaling O (normally long done).
-      if (C::SEP_P && j > 0) {
-        if (!(ok = mbar_wait_warp(pv_done(t), (j - 1) & 1, status))) break;
+      if (C::SEP_P && g > 0) {
+        if (!(ok = mbar_wait_warp(pv_done(t), (g - 1) & 1, status))) break;
         tc_fence_after();
       }
       // P = exp2(S * scale * log2(e) - m), packed to bf16 pairs, 16 columns at a time.
@@ -297,38 +341,40 @@ __global__ void __launch_bounds__(384, 1)
       tc_fence_before();
       mbar_arrive(p_full(t));
     }
-    if (ok && mbar_wait_warp(o_done(t), 0, status)) {
-      tc_fence_after();
-      const float inv_l = 1.f / l;
-      OutT* orow = O + ((static_cast<size_t>(b) * L + row) * H + h) * d_out;
+    // O write-back. The TMEM loads complete (wait::ld) before this warpgroup's
+    // next p_full arrive, which the next item's first P*V waits for.
+    if (!ok || !(ok = mbar_wait_warp(o_done(t), it & 1, status))) break;
+    tc_fence_after();
+    const float inv_l = 1.f / l;
+    OutT* orow = O + ((static_cast<size_t>(b) * L + row) * H + h) * d_out;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_ld_wait();
-        if constexpr (std::is_same<OutT, float>::value) {
-          if (row < L && c * 32 < d_out) {
-            float4* dst = reinterpret_cast<float4*>(orow + c * 32);
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32(tO + c * 32, o);
+      tmem_ld_wait();
+      if constexpr (std::is_same<OutT, float>::value) {
+        if (row < L && c * 32 < d_out) {
+          float4* dst = reinterpret_cast<float4*>(orow + c * 32);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
-                                   __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
-          }
-        } else {
-          uint32_t pkd[16];
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                                 __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
+        }
+      } else {
+        uint32_t pkd[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pkd[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
-          if (row < L) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+        for (int i = 0; i < 16; ++i)
+          pkd[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+        if (row < L) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
-          }
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
         }
       }
-      if (row < L) lse[static_cast<size_t>(bh) * L + row] = (m + __log2f(l)) * kLn2;
     }
+    if (row < L) lse[static_cast<size_t>(bh) * L + row] = (m + __log2f(l)) * kLn2;
+    }  // item
   }
 
   tc_fence_before();
@@ -345,10 +391,30 @@ static int launch_fwd(const AttnShape& shp, const CUtensorMap* m, void* o, float
   using C = FwdCfg<D, SPLIT>;
   static uint64_t attr = 0;
   ensure_smem_attr(attn_fwd_kernel<D, SPLIT, OutT>, C::SMEM, attr);
-  dim3 grid((shp.L + 255) / 256, shp.B * shp.H);
+  // persistent: as many CTAs as fit on the device at once, at most one per item
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int resident[64] = {0};
+  int& res = resident[dev & 63];
+  if (res <= 0) {
+    int sms = 0, per_sm = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_fwd_kernel<D, SPLIT, OutT>, C::THREADS,
+                                                      C::SMEM) != cudaSuccess ||
+        per_sm <= 0) {
+      cudaGetLastError();  // clear a failed query; one CTA per SM
+      per_sm = 1;
+    }
+    res = (sms > 0 ? sms : 148) * per_sm;
+  }
+  const int n_qb = (shp.L + 255) / 256;
+  const long long items = static_cast<long long>(n_qb) * shp.B * shp.H;
+  if (items > 0x7fffffffLL) return PA_ERR_SHAPE;
+  const int n_items = static_cast<int>(items);
+  const int grid = n_items < res ? n_items : res;
   attn_fwd_kernel<D, SPLIT, OutT><<<grid, C::THREADS, C::SMEM, stream>>>(
       m[0], m[1], m[2], m[3], m[4], m[5], static_cast<OutT*>(o), lse, shp.L, shp.H, d_out,
-      shp.scale * kLog2e, status);
+      shp.scale * kLog2e, n_qb, n_items, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
