@@ -289,9 +289,16 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= kv_left) s[i] = -INFINITY;
       }
-      float mx = s[0];
+      // row max over eight independent chains (a single chain is 127 dependent steps)
+      float mk[8];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      for (int k = 0; k < 8; ++k) mk[k] = s[k];
+#pragma unroll
+      for (int i = 8; i < 128; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mk[k] = fmaxf(mk[k], s[i + k]);
+      const float mx = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
+                             fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
       const float m_new = fmaxf(m, mx * scale_log2);
       const bool need = m_new > m + 8.f;
       const bool warp_need = __any_sync(0xffffffffu, need);
