@@ -289,16 +289,16 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= kv_left) s[i] = -INFINITY;
       }
-      // row max over eight independent chains (a single chain is 127 dependent steps)
+      // row max over eight independent chains of three-input max (a single
+      // chain would be 127 dependent steps)
       float mk[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mk[k] = s[k];
+      for (int k = 0; k < 8; ++k) mk[k] = fmaxf(s[k], s[8 + k]);
 #pragma unroll
-      for (int i = 8; i < 128; i += 8)
+      for (int i = 16; i < 128; i += 16)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mk[k] = fmaxf(mk[k], s[i + k]);
-      const float mx = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
-                             fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
+        for (int k = 0; k < 8; ++k) mk[k] = max3f(mk[k], s[i + k], s[i + 8 + k]);
+      const float mx = max3f(max3f(mk[0], mk[1], mk[2]), max3f(mk[3], mk[4], mk[5]), fmaxf(mk[6], mk[7]));
       const float m_new = fmaxf(m, mx * scale_log2);
       const bool need = m_new > m + 8.f;
       const bool warp_need = __any_sync(0xffffffffu, need);

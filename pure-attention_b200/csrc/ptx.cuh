@@ -517,6 +517,13 @@ __device__ __forceinline__ void tmem_ld_16x256b_x8_sync(uint32_t taddr, uint32_t
       : "memory");
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Two fp32 additions into global memory (one 8-byte vector reduction).
 __device__ __forceinline__ void red_add_v2_f32(float* addr, float a, float b) {
   asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
