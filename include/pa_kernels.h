@@ -128,6 +128,17 @@ int pa_layer_norm_fwd(const float* x, const float* gamma, const float* beta, flo
                       float* mean, float* rstd, uint32_t M, uint32_t N, float epsilon,
                       pa_stream_t stream);
 
+/* sum = x + r (written), then y = LayerNorm(sum) as pa_layer_norm_fwd: a
+ * residual add fused in front of the norm, one pass over the rows instead of an
+ * add pass plus a norm pass. The reference builds the same value from its
+ * elementwise add launcher and launch_layer_norm_forward
+ * (include/backend/Launchers.cuh:178-189) in sequence. sum may alias neither
+ * x nor r. The backward is pa_layer_norm_bwd_accumulate with x = sum, into
+ * the gradient of sum, which the add then hands to x and r. */
+int pa_add_layer_norm_fwd(const float* x, const float* r, float* sum, const float* gamma,
+                          const float* beta, float* y, float* mean, float* rstd, uint32_t M,
+                          uint32_t N, float epsilon, pa_stream_t stream);
+
 size_t pa_layer_norm_bwd_workspace_size(uint32_t M, uint32_t N);
 
 /* dx (overwritten), dgamma and dbeta (accumulated); a NULL output is skipped.

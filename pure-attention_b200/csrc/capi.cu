@@ -166,7 +166,20 @@ int pa_layer_norm_fwd(const float* x, const float* gamma, const float* beta, flo
   if (M == 0 || N == 0) return PA_ERR_SHAPE;
   if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
   if (!al16(x) || !al16(gamma) || !al16(beta) || !al16(y)) return PA_ERR_ALIGN;
-  return pa::launch_layer_norm_fwd(x, gamma, beta, y, mean, rstd, M, N, epsilon,
+  return pa::launch_layer_norm_fwd(x, nullptr, nullptr, gamma, beta, y, mean, rstd, M, N, epsilon,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+int pa_add_layer_norm_fwd(const float* x, const float* r, float* sum, const float* gamma,
+                          const float* beta, float* y, float* mean, float* rstd, uint32_t M,
+                          uint32_t N, float epsilon, pa_stream_t stream) {
+  if (!x || !r || !sum || !gamma || !beta || !y || !mean || !rstd) return PA_ERR_NULL;
+  if (M == 0 || N == 0) return PA_ERR_SHAPE;
+  if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
+  if (!al16(x) || !al16(r) || !al16(sum) || !al16(gamma) || !al16(beta) || !al16(y))
+    return PA_ERR_ALIGN;
+  if (sum == x || sum == r) return PA_ERR_SHAPE;
+  return pa::launch_layer_norm_fwd(x, r, sum, gamma, beta, y, mean, rstd, M, N, epsilon,
                                    static_cast<cudaStream_t>(stream));
 }
 

@@ -48,8 +48,10 @@ int launch_attn_delta_f32(const AttnShape& sh, const void* dO, const void* o, fl
 namespace pa {
 
 // layernorm.cu
-int launch_layer_norm_fwd(const float* x, const float* g, const float* b, float* y, float* mu,
-                          float* rs, uint32_t M, uint32_t N, float eps, cudaStream_t s);
+// r == nullptr: y = LN(x); else sum = x + r and y = LN(sum)
+int launch_layer_norm_fwd(const float* x, const float* r, float* sum, const float* g,
+                          const float* b, float* y, float* mu, float* rs, uint32_t M, uint32_t N,
+                          float eps, cudaStream_t s);
 size_t layer_norm_bwd_workspace_bytes(uint32_t M, uint32_t N);
 int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, const float* rs,
                           const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,

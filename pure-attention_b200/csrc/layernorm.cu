@@ -29,9 +29,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 constexpr int LN_WARPS = 8;  // rows in flight per CTA
 
 // VPL = float4 vectors per lane (row length N <= 128 * VPL, N % 4 == 0).
-template <int VPL>
+// ADD: the row is x + r (a residual add fused in front of the norm), also
+// written to sum, which the backward and the next residual add read.
+template <int VPL, bool ADD>
 __global__ void __launch_bounds__(LN_WARPS * 32)
-    ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+    ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ r,
+                  float* __restrict__ sum, const float* __restrict__ gamma,
                   const float* __restrict__ beta, float* __restrict__ y, float* __restrict__ mean,
                   float* __restrict__ rstd, uint32_t M, uint32_t N, float eps) {
   const uint32_t lane = threadIdx.x & 31;
@@ -39,12 +42,19 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
   for (uint32_t row = blockIdx.x * LN_WARPS + threadIdx.x / 32; row < M;
        row += gridDim.x * LN_WARPS) {
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * N);
+    const float4* rr = reinterpret_cast<const float4*>(r + static_cast<size_t>(row) * N);
+    float4* sr = reinterpret_cast<float4*>(sum + static_cast<size_t>(row) * N);
     float4 v[VPL];
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const uint32_t c = lane + 32 * i;
       v[i] = c < nvec ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ADD && c < nvec) {
+        const float4 w = rr[c];
+        v[i] = make_float4(v[i].x + w.x, v[i].y + w.y, v[i].z + w.z, v[i].w + w.w);
+        sr[c] = v[i];
+      }
       s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
     }
     const float mu = warp_sum(s) / N;
@@ -204,10 +214,14 @@ uint32_t ln_bwd_blocks(uint32_t M, uint32_t N) {
 }
 
 template <int VPL>
-int ln_fwd_launch(const float* x, const float* g, const float* b, float* y, float* mu, float* rs,
-                  uint32_t M, uint32_t N, float eps, cudaStream_t s) {
+int ln_fwd_launch(const float* x, const float* r, float* sum, const float* g, const float* b,
+                  float* y, float* mu, float* rs, uint32_t M, uint32_t N, float eps, cudaStream_t s) {
   const uint32_t blocks = (M + LN_WARPS - 1) / LN_WARPS;
-  ln_fwd_kernel<VPL><<<blocks, LN_WARPS * 32, 0, s>>>(x, g, b, y, mu, rs, M, N, eps);
+  if (r)
+    ln_fwd_kernel<VPL, true><<<blocks, LN_WARPS * 32, 0, s>>>(x, r, sum, g, b, y, mu, rs, M, N, eps);
+  else
+    ln_fwd_kernel<VPL, false><<<blocks, LN_WARPS * 32, 0, s>>>(x, nullptr, nullptr, g, b, y, mu, rs,
+                                                               M, N, eps);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
@@ -240,14 +254,16 @@ int ln_bwd_launch(const float* dy, const float* x, const float* mu, const float*
 
 }  // namespace
 
-int launch_layer_norm_fwd(const float* x, const float* g, const float* b, float* y, float* mu,
-                          float* rs, uint32_t M, uint32_t N, float eps, cudaStream_t s) {
-  if (N <= 128) return ln_fwd_launch<1>(x, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 256) return ln_fwd_launch<2>(x, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 512) return ln_fwd_launch<4>(x, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 1024) return ln_fwd_launch<8>(x, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 2048) return ln_fwd_launch<16>(x, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 4096) return ln_fwd_launch<32>(x, g, b, y, mu, rs, M, N, eps, s);
+// r == nullptr: y = LN(x); else sum = x + r and y = LN(sum).
+int launch_layer_norm_fwd(const float* x, const float* r, float* sum, const float* g,
+                          const float* b, float* y, float* mu, float* rs, uint32_t M, uint32_t N,
+                          float eps, cudaStream_t s) {
+  if (N <= 128) return ln_fwd_launch<1>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
+  if (N <= 256) return ln_fwd_launch<2>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
+  if (N <= 512) return ln_fwd_launch<4>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
+  if (N <= 1024) return ln_fwd_launch<8>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
+  if (N <= 2048) return ln_fwd_launch<16>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
+  if (N <= 4096) return ln_fwd_launch<32>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
   return PA_ERR_UNSUPPORTED;
 }
 

@@ -75,9 +75,10 @@ class TransformerLayer(pa.Module):
 
     def forward(self, x):
         x_norm = self.ln1.forward(x)
-        x = pa.add(x, self.mha.forward(x_norm, x_norm, x_norm))
-        x = pa.add(x, self.ffn.forward(self.ln2.forward(x)))
-        return self.ln_final.forward(x)
+        # each residual add is fused with the LayerNorm that reads its sum
+        x, h = self.ln2.forward_add(x, self.mha.forward(x_norm, x_norm, x_norm))
+        _, out = self.ln_final.forward_add(x, self.ffn.forward(h))
+        return out
 
     def parameters(self):
         return (self.mha.parameters() + self.ln1.parameters() + self.ffn.parameters()

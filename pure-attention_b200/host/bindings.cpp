@@ -124,6 +124,8 @@ PYBIND11_MODULE(PureAttention, m) {
   py::class_<layers::LayerNorm, layers::Module, std::shared_ptr<layers::LayerNorm>>(m, "LayerNorm")
       .def(py::init<uint32_t, float>(), py::arg("normalized_shape"), py::arg("epsilon") = 1e-5f)
       .def("forward", &layers::LayerNorm::forward)
+      .def("forward_add", &layers::LayerNorm::forward_add,
+           "(x + r, LayerNorm(x + r)) from one fused kernel")
       .def("parameters", &layers::LayerNorm::parameters)
       .def_property_readonly("gamma", &layers::LayerNorm::get_gamma)
       .def_property_readonly("beta", &layers::LayerNorm::get_beta);

@@ -4,6 +4,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <memory>
+#include <utility>
 #include <vector>
 #include "core/Tensor.h"
 
@@ -44,4 +45,10 @@ std::shared_ptr<Tensor> layer_norm(const std::shared_ptr<Tensor>& input,
                                    const std::shared_ptr<Tensor>& gamma,
                                    const std::shared_ptr<Tensor>& beta, float epsilon,
                                    const cudaStream_t& stream);
+// sum = x + r and y = LayerNorm(sum) in one kernel; returns {sum, y}. sum's
+// node is the add (its gradient goes to x and r), y's the norm over sum.
+std::pair<std::shared_ptr<Tensor>, std::shared_ptr<Tensor>> add_layer_norm(
+    const std::shared_ptr<Tensor>& x, const std::shared_ptr<Tensor>& r,
+    const std::shared_ptr<Tensor>& gamma, const std::shared_ptr<Tensor>& beta, float epsilon,
+    const cudaStream_t& stream);
 }  // namespace core

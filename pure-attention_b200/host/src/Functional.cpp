@@ -215,4 +215,32 @@ std::shared_ptr<Tensor> layer_norm(const std::shared_ptr<Tensor>& input,
   return output;
 }
 
+std::pair<std::shared_ptr<Tensor>, std::shared_ptr<Tensor>> add_layer_norm(
+    const std::shared_ptr<Tensor>& x, const std::shared_ptr<Tensor>& r,
+    const std::shared_ptr<Tensor>& gamma, const std::shared_ptr<Tensor>& beta, float epsilon,
+    const cudaStream_t& stream) {
+  const uint32_t N = static_cast<uint32_t>(last_dim(*x));
+  const uint32_t M = static_cast<uint32_t>(x->numel() / N);
+  if (r->numel() != x->numel())
+    throw std::runtime_error("Add+LayerNorm: the residual must have the input's size");
+  if (gamma->numel() != N || beta->numel() != N)
+    throw std::runtime_error("LayerNorm: gamma/beta must have the normalized size");
+  const bool gs = x->requires_grad() || r->requires_grad();
+  const bool g = gs || gamma->requires_grad() || beta->requires_grad();
+  auto sum = std::make_shared<Tensor>(x->get_shape(), g, false);
+  auto output = std::make_shared<Tensor>(x->get_shape(), g, false);
+  auto mean = std::make_shared<Tensor>(std::vector<uint32_t>{M}, false);
+  auto rstd = std::make_shared<Tensor>(std::vector<uint32_t>{M}, false);
+  check_status(pa_add_layer_norm_fwd(x->get_data_ptr(), r->get_data_ptr(), sum->get_data_ptr(),
+                                     gamma->get_data_ptr(), beta->get_data_ptr(),
+                                     output->get_data_ptr(), mean->get_data_ptr(),
+                                     rstd->get_data_ptr(), M, N, epsilon, ps(stream)),
+               "Add+LayerNorm");
+  if (gs) sum->set_grad_fn(std::make_shared<AddFunction>(x, r, sum));
+  if (g)
+    output->set_grad_fn(
+        std::make_shared<LayerNormFunction>(sum, gamma, beta, output, mean, rstd, M, N));
+  return {sum, output};
+}
+
 }  // namespace core

@@ -48,6 +48,11 @@ std::shared_ptr<core::Tensor> LayerNorm::forward(const std::shared_ptr<core::Ten
   return core::layer_norm(input, gamma, beta, epsilon, stream());
 }
 
+std::pair<std::shared_ptr<core::Tensor>, std::shared_ptr<core::Tensor>> LayerNorm::forward_add(
+    const std::shared_ptr<core::Tensor>& x, const std::shared_ptr<core::Tensor>& r) {
+  return core::add_layer_norm(x, r, gamma, beta, epsilon, stream());
+}
+
 std::vector<std::shared_ptr<core::Tensor>> LayerNorm::parameters() { return {gamma, beta}; }
 
 // Same parameter shapes and He-normal init as MHA.cpp:10-28.

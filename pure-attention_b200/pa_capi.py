@@ -24,7 +24,7 @@ EXPORTS = [
     "pa_abi_version", "pa_status_string", "pa_device_status", "pa_set_f32_math", "pa_get_f32_math",
     "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
-    "pa_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
+    "pa_layer_norm_fwd", "pa_add_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
     "pa_layer_norm_bwd_accumulate",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
@@ -67,6 +67,7 @@ _SIGS = {
     "pa_attn_bwd_noalloc": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp]),
     "pa_attn_delta": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp]),
     "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
+    "pa_add_layer_norm_fwd": (_int, [_vp] * 8 + [_u32, _u32, _flt, _vp]),
     "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
     "pa_layer_norm_bwd": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
     "pa_layer_norm_bwd_accumulate": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
@@ -239,6 +240,16 @@ def layer_norm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5, stream=None):
                                   _ptr(rstd), M, N, float(eps),
                                   _stream() if stream is None else stream)
     _check("pa_layer_norm_fwd", st)
+
+
+def add_layer_norm_fwd(x, r, out_sum, gamma, beta, y, mean, rstd, eps=1e-5, stream=None):
+    """out_sum = x + r, y = LayerNorm(out_sum) in one pass."""
+    M = x.numel() // x.shape[-1]
+    N = x.shape[-1]
+    st = load().pa_add_layer_norm_fwd(_ptr(x), _ptr(r), _ptr(out_sum), _ptr(gamma), _ptr(beta),
+                                      _ptr(y), _ptr(mean), _ptr(rstd), M, N, float(eps),
+                                      _stream() if stream is None else stream)
+    _check("pa_add_layer_norm_fwd", st)
 
 
 def layer_norm_bwd_workspace_size(M, N):

@@ -105,6 +105,34 @@ def test_layer_norm_matches_oracle(M, N):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M,N", [(8192, 1024), (37, 128), (5, 12)])
+def test_add_layer_norm_matches_oracle(M, N):
+    """sum = x + r exactly (one fp32 add per element), y = LayerNorm(sum) as the
+    oracle's forward of the sum, and identical to the unfused kernel on it."""
+    import oracle
+    import pa_capi
+    x = seeded_normal(M + 20, (M, N))
+    r = seeded_normal(M + 21, (M, N))
+    gamma = 1.0 + 0.1 * seeded_normal(N + 22, (N,))
+    beta = 0.1 * seeded_normal(N + 23, (N,))
+    s = torch.empty(M, N, device="cuda")
+    y = torch.empty(M, N, device="cuda")
+    mean = torch.empty(M, device="cuda")
+    rstd = torch.empty(M, device="cuda")
+    pa_capi.add_layer_norm_fwd(_cu(x), _cu(r), s, _cu(gamma), _cu(beta), y, mean, rstd)
+    want_s = (x.astype(np.float32) + r.astype(np.float32)).astype(np.float64)
+    np.testing.assert_array_equal(_np(s), want_s)
+    oy, om, ors = oracle.layer_norm_fwd(want_s, gamma, beta)
+    assert rel_err(_np(y), oy) < 1e-5
+    assert rel_err(_np(mean), om) < 1e-5
+    assert rel_err(_np(rstd), ors) < 1e-5
+    y2, m2, r2 = torch.empty_like(y), torch.empty_like(mean), torch.empty_like(rstd)
+    pa_capi.layer_norm_fwd(s, _cu(gamma), _cu(beta), y2, m2, r2)
+    np.testing.assert_array_equal(_np(y), _np(y2))
+    np.testing.assert_array_equal(_np(mean), _np(m2))
+
+
+@pytest.mark.gpu
 def test_layer_norm_backward_is_deterministic():
     import pa_capi
     M, N = 4096, 512

@@ -71,6 +71,12 @@ def test_layer_norm_and_matmul_validation_without_gpu():
     assert lib.pa_layer_norm_fwd(16, 16, 16, 16, 16, 16, 0, 8, 1e-5, None) == 1
     assert lib.pa_layer_norm_fwd(16, 16, 16, 16, 16, 16, 4, 6, 1e-5, None) == 4
     assert lib.pa_layer_norm_bwd(16, 16, 16, 16, 16, 16, 16, 16, 4, 8, None, 0, None) == 7
+    # fused residual add: NULL sum, zero rows, N not a multiple of 4, misaligned r, sum aliasing x
+    assert lib.pa_add_layer_norm_fwd(16, 16, None, 16, 16, 16, 16, 16, 4, 8, 1e-5, None) == 8
+    assert lib.pa_add_layer_norm_fwd(16, 32, 48, 16, 16, 16, 16, 16, 0, 8, 1e-5, None) == 1
+    assert lib.pa_add_layer_norm_fwd(16, 32, 48, 16, 16, 16, 16, 16, 4, 6, 1e-5, None) == 4
+    assert lib.pa_add_layer_norm_fwd(16, 36, 48, 16, 16, 16, 16, 16, 4, 8, 1e-5, None) == 3
+    assert lib.pa_add_layer_norm_fwd(16, 32, 16, 16, 16, 16, 16, 16, 4, 8, 1e-5, None) == 1
     assert lib.pa_matmul(16, 16, 16, 0, 4, 4, None, 0, None) == 1
     assert lib.pa_matmul_grad_x(None, 16, 16, 4, 4, 4, None, 0, None) == 8
     assert lib.pa_matmul_grad_w(16, 16, 16, 4, 4, 4, None, 0, None) == 7   # no workspace

@@ -72,6 +72,34 @@ def test_fan_out_gradients_accumulate_once(pa):
 
 
 @pytest.mark.gpu
+def test_fused_add_layer_norm_matches_unfused_graph(pa):
+    """LayerNorm.forward_add(x, r) gives (x + r, LN(x + r)) with the same values
+    and the same gradients for x, r, gamma, beta as pa.add followed by
+    LayerNorm.forward, when both the sum and the norm feed the loss."""
+    x, r, t1, t2 = (seeded_normal(40 + i, (6, 24, 32)) for i in range(4))
+    ln = pa.LayerNorm(32)
+    g0 = 1.0 + 0.1 * seeded_normal(44, (1, 32))
+    b0 = 0.1 * seeded_normal(45, (1, 32))
+    outs = []
+    for fused in (True, False):
+        ln.gamma.to_device(g0.astype(np.float32).ravel().tolist())
+        ln.beta.to_device(b0.astype(np.float32).ravel().tolist())
+        for p in ln.parameters():
+            p.zero_grad()
+        X, R = _t(pa, x, True), _t(pa, r, True)
+        if fused:
+            s, y = ln.forward_add(X, R)
+        else:
+            s = pa.add(X, R)
+            y = ln.forward(s)
+        loss = pa.add(pa.MSE()(s, _t(pa, t1)), pa.MSE()(y, _t(pa, t2)))
+        loss.backward()
+        outs.append([_h(s), _h(y), _h(loss), _g(X), _g(R), _g(ln.gamma), _g(ln.beta)])
+    for a, b in zip(*outs):
+        assert rel_err(a, b) < 1e-6
+
+
+@pytest.mark.gpu
 def test_mlp_relu_mse_adam_matches_torch(pa):
     x = seeded_normal(4, (128, 24))
     t = seeded_normal(5, (128, 8))
