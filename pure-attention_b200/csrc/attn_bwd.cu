@@ -575,7 +575,12 @@ __global__ void __launch_bounds__(512, 1)
 // (an extension tile written by the prep kernel, against tiles of ones), so
 // S' = S - LSE/scale and dP' = dP - Delta come out of the tensor core and the
 // elementwise step needs no per-query loads: P = exp2(S' * scale * log2 e),
-// dS = P * dP'.
+// dS = P * dP'. (The extra K-step is 6% more tensor-pipe work, but loading
+// LSE and Delta per query in the elementwise step, whose instruction stream is
+// on the critical path, measured 23% slower.)
+// Persistent: one two-CTA cluster per SM pair walks (batch*head, pair of key
+// tiles) work items; rings, barrier phases and the dS buffers continue across
+// items, and the dV/dK write-back of one item overlaps the next item's MMAs.
 // Each tile's elementwise work runs in two phases:
 //   P phase:  load S (s_free: the next S may start) -> P in registers ->
 //             P^T to its own TMEM columns (pt_full: dV may start)
