@@ -144,9 +144,17 @@ class GradAllReduce:
     bucket into it, all-reduces it and scatters the averaged values back.
     NCCL averages in the collective (ReduceOp.AVG); other backends sum and the
     scatter divides by the world size.
+
+    Overlapped use: begin(), then ready(key) for each gradient once it is
+    final (keys[i] names grads[i]; by default its data pointer), then
+    finish(). A bucket is reduced as soon as all of its gradients are ready,
+    buckets strictly in index order so that every rank issues the same
+    collectives in the same order; CUDA buckets run on a side stream that
+    waits for the point in the default stream where the bucket became ready,
+    and finish() makes the default stream wait for them.
     """
 
-    def __init__(self, grads, bucket_bytes=25 << 20, group=None):
+    def __init__(self, grads, bucket_bytes=25 << 20, group=None, keys=None):
         torch = _torch()
         import torch.distributed as dist
         self.dist, self.group = dist, group
@@ -166,16 +174,68 @@ class GradAllReduce:
         self.flat = [torch.empty(sum(v.numel() for v in b), dtype=b[0].dtype, device=b[0].device)
                      for b in self.buckets]
         self.sizes = [[v.numel() for v in b] for b in self.buckets]
+        grads = list(grads)
+        keys = [g.data_ptr() for g in grads] if keys is None else list(keys)
+        if len(keys) != len(grads):
+            raise ValueError("one key per gradient")
+        # bucket of grads[i]: buckets hold the gradients in reverse order
+        self.where = {}
+        i = len(grads) - 1
+        for b, views in enumerate(self.buckets):
+            for _ in views:
+                self.where[keys[i]] = b
+                i -= 1
+        cuda = grads[0].device.type == "cuda"
+        self.comm = torch.cuda.Stream(device=grads[0].device) if cuda else None
+        self.pending = None
 
-    def __call__(self):
+    def _reduce(self, b):
         torch = _torch()
         op = self.dist.ReduceOp.AVG if self.avg_in_collective else self.dist.ReduceOp.SUM
-        for views, flat, sizes in zip(self.buckets, self.flat, self.sizes):
-            torch.cat(views, out=flat)
-            self.dist.all_reduce(flat, op=op, group=self.group)
-            if not self.avg_in_collective:
-                flat.div_(self.world)
-            torch._foreach_copy_(views, list(torch.split(flat, sizes)))
+        views, flat, sizes = self.buckets[b], self.flat[b], self.sizes[b]
+        torch.cat(views, out=flat)
+        self.dist.all_reduce(flat, op=op, group=self.group)
+        if not self.avg_in_collective:
+            flat.div_(self.world)
+        torch._foreach_copy_(views, list(torch.split(flat, sizes)))
+
+    def __call__(self):
+        for b in range(len(self.buckets)):
+            self._reduce(b)
+
+    def begin(self):
+        self.pending = [len(v) for v in self.buckets]
+        self.launched = 0  # buckets 0 .. launched-1 are reduced or queued
+
+    def _launch(self, b):
+        if self.comm is None:
+            self._reduce(b)
+            return
+        torch = _torch()
+        ready = torch.cuda.Event()
+        ready.record()  # the current stream, where this bucket's gradients were written
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(ready)
+            self._reduce(b)
+
+    def ready(self, key):
+        b = self.where.get(key)
+        if b is None or self.pending is None:
+            return
+        self.pending[b] -= 1
+        while self.launched < len(self.buckets) and self.pending[self.launched] == 0:
+            self._launch(self.launched)
+            self.launched += 1
+
+    def finish(self):
+        """Reduce the buckets not reduced yet (gradients no node wrote) and
+        make the current stream wait for every reduction."""
+        while self.launched < len(self.buckets):
+            self._launch(self.launched)
+            self.launched += 1
+        self.pending = None
+        if self.comm is not None:
+            _torch().cuda.current_stream().wait_stream(self.comm)
 
     @property
     def nbytes(self):
@@ -212,6 +272,10 @@ class DenoiseTrainer:
             for p in self.params:
                 dist.broadcast(device_view(p), src=src, group=group)
             self.reducer = GradAllReduce([grad_view(p) for p in self.params], bucket_bytes, group)
+        self.overlap = True  # all-reduce each bucket while the rest of the backward runs
+
+    def _leaf_ready(self, t):
+        self.reducer.ready(t.grad_view().__cuda_array_interface__["data"][0])
 
     @property
     def num_parameters(self):
@@ -228,10 +292,15 @@ class DenoiseTrainer:
         self.opt.zero_grad()
         out = self.model.forward(self.x)
         loss = self.criterion(out, self.t)
-        loss.backward()
+        if self.reducer is not None and self.overlap:
+            self.reducer.begin()
+            loss.backward(True, self._leaf_ready)
+            self.reducer.finish()
+        else:
+            loss.backward()
+            if self.reducer is not None:
+                self.reducer()
         del out
-        if self.reducer is not None:
-            self.reducer()
         self.opt.step()
         return loss  # holds this step's graph until the caller drops it
 

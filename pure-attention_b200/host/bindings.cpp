@@ -3,6 +3,7 @@
 // are set_seed, device_status and Tensor.zero_grad.
 #include <pybind11/pybind11.h>
 #include <string>
+#include <pybind11/functional.h>
 #include <pybind11/stl.h>
 
 #include <algorithm>
@@ -65,7 +66,12 @@ PYBIND11_MODULE(PureAttention, m) {
              return std::make_shared<Tensor>(shape, requires_grad);
            }),
            py::arg("shape"), py::arg("requires_grad") = false)
-      .def("backward", &Tensor::backward, py::arg("seed_with_ones") = true)
+      .def("backward", py::overload_cast<bool>(&Tensor::backward, py::const_),
+           py::arg("seed_with_ones") = true)
+      .def("backward", py::overload_cast<bool, const Tensor::LeafHook&>(&Tensor::backward, py::const_),
+           py::arg("seed_with_ones"), py::arg("leaf_ready"),
+           "backward(), calling leaf_ready(t) for each gradient-requiring leaf t as soon as its "
+           "gradient is final on the stream")
       .def("to_host", &Tensor::to_host)
       .def("to_device", &Tensor::to_device)
       .def("grad_to_host", &Tensor::grad_to_host)

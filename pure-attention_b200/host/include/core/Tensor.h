@@ -4,6 +4,7 @@
 // the context stream) and gradients start at zero.
 #pragma once
 #include <cstdint>
+#include <functional>
 #include <memory>
 #include <vector>
 
@@ -40,6 +41,12 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
   // reverse topological order, so shared inputs receive the sum of all
   // contributions before their own node runs.
   void backward(bool seed_with_ones = true) const;
+  // As backward(), and `leaf_ready` is called for each gradient-requiring leaf
+  // of the graph (a parameter or input) right after the last node that adds to
+  // its gradient has been enqueued: its gradient is then final on the stream,
+  // so a caller can start reducing it while the rest of the backward runs.
+  using LeafHook = std::function<void(const std::shared_ptr<Tensor>&)>;
+  void backward(bool seed_with_ones, const LeafHook& leaf_ready) const;
 
  private:
   float32_t* data_ptr = nullptr;

@@ -1,6 +1,7 @@
 #include "core/Tensor.h"
 
 #include <algorithm>
+#include <unordered_map>
 #include <stdexcept>
 #include <string>
 #include <unordered_set>
@@ -82,7 +83,9 @@ void Tensor::zero_grad() const {
     cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), CudaContext::getStream());
 }
 
-void Tensor::backward(bool seed_with_ones) const {
+void Tensor::backward(bool seed_with_ones) const { backward(seed_with_ones, LeafHook()); }
+
+void Tensor::backward(bool seed_with_ones, const LeafHook& leaf_ready) const {
   if (!requires_gradient)
     throw std::runtime_error("Called backward() on a tensor that does not require gradients.");
   if (seed_with_ones)
@@ -108,7 +111,28 @@ void Tensor::backward(bool seed_with_ones) const {
       stack.pop_back();
     }
   }
-  for (auto it = order.rbegin(); it != order.rend(); ++it) (*it)->apply_backward();
+  if (!leaf_ready) {
+    for (auto it = order.rbegin(); it != order.rend(); ++it) (*it)->apply_backward();
+    return;
+  }
+  // For each gradient-requiring leaf, the last node (in execution order) that
+  // takes it as an input; after that node the leaf's gradient is complete.
+  std::vector<Function*> exec(order.rbegin(), order.rend());
+  std::unordered_map<const Tensor*, size_t> last;
+  std::vector<std::vector<std::shared_ptr<Tensor>>> ready_after(exec.size());
+  for (size_t i = 0; i < exec.size(); ++i)
+    for (const auto& in : exec[i]->inputs())
+      if (in && in->requires_grad() && !in->grad_fn()) last[in.get()] = i;
+  std::unordered_set<const Tensor*> queued;
+  for (size_t i = 0; i < exec.size(); ++i)
+    for (const auto& in : exec[i]->inputs())
+      if (in && in->requires_grad() && !in->grad_fn() && last[in.get()] == i &&
+          queued.insert(in.get()).second)
+        ready_after[i].push_back(in);
+  for (size_t i = 0; i < exec.size(); ++i) {
+    exec[i]->apply_backward();
+    for (const auto& leaf : ready_after[i]) leaf_ready(leaf);
+  }
 }
 
 }  // namespace core

@@ -1,7 +1,9 @@
 """Host logic of the data-parallel denoise training step, on CPU: the bucketed
 gradient all-reduce averages every gradient over world-size-2 gloo ranks
 (buckets split at the byte limit, a tensor larger than the limit alone in its
-bucket, views written in place), and the synthetic denoise data has the stated
+bucket, views written in place), also when buckets are reduced as their
+gradients become ready (in bucket order whatever the readiness order, the
+rest flushed by finish()), and the synthetic denoise data has the stated
 shapes, ranges and per-seed determinism."""
 import os
 import socket
@@ -47,9 +49,28 @@ def _worker(rank, world, port, out_dir, bucket_bytes):
         red()
         red()  # averaging twice leaves equal buffers unchanged
         nb = [[v.numel() for v in b] for b in red.buckets]
-        np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
-                 *[s.numpy() for s in storage], buckets=np.array(repr(nb)))
         assert all(s.data_ptr() == v.data_ptr() for s, v in zip(storage, views))
+        # overlapped form: gradients become ready in forward order (the last
+        # bucket's first), one never does; unknown keys are ignored
+        storage2 = [g.clone() for g in grads]
+        keys = ["g%d" % i for i in range(len(storage2))]
+        red2 = denoise.GradAllReduce([s.view(-1) for s in storage2], bucket_bytes=bucket_bytes,
+                                     keys=keys)
+        launched = []
+        orig = red2._launch
+        red2._launch = lambda b: (launched.append(b), orig(b))
+        red2.begin()
+        red2.ready("not a gradient")
+        for k in keys[1:]:
+            red2.ready(k)
+        before_finish = list(launched)
+        red2.finish()
+        assert launched == list(range(len(red2.buckets)))
+        # grads[0] sits in the last bucket, which only finish() reduces
+        assert len(before_finish) == len(red2.buckets) - 1
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
+                 *[s.numpy() for s in storage], *[s.numpy() for s in storage2],
+                 buckets=np.array(repr(nb)))
     finally:
         dist.destroy_process_group()
 
@@ -70,6 +91,7 @@ def _run(tmp_path, bucket_bytes):
     for r in range(world):
         for i, w in enumerate(want):
             np.testing.assert_allclose(outs[r][f"arr_{i}"], w, rtol=1e-6, atol=1e-6)
+            np.testing.assert_allclose(outs[r][f"arr_{len(want) + i}"], w, rtol=1e-6, atol=1e-6)
     np.testing.assert_array_equal(outs[0]["arr_3"], outs[1]["arr_3"])
     return eval(str(outs[0]["buckets"]))
 

@@ -100,6 +100,32 @@ def test_fused_add_layer_norm_matches_unfused_graph(pa):
 
 
 @pytest.mark.gpu
+def test_backward_leaf_hook_reports_final_gradients(pa):
+    """backward(seed, hook) calls hook(t) once per gradient-requiring leaf
+    (every parameter of a denoise layer and the input), after the last node
+    that writes its gradient: a copy taken in the hook, on the operators'
+    stream, equals the gradient after the whole backward."""
+    import denoise as dn
+    model = dn.DenoiseTransformer(1, 128, 4, 256)  # head dim 32
+    params = model.parameters()
+    X = _t(pa, seeded_normal(50, (2, 48, 128)), True)
+    loss = pa.MSE()(model.forward(X), _t(pa, seeded_normal(51, (2, 48, 128))))
+    ptr = lambda t: t.grad_view().__cuda_array_interface__["data"][0]
+    snaps, calls = {}, []
+
+    def hook(t):
+        calls.append(ptr(t))
+        snaps[ptr(t)] = torch.as_tensor(t.grad_view(), device="cuda").clone()
+
+    loss.backward(True, hook)
+    torch.cuda.synchronize()
+    leaves = params + [X]
+    assert sorted(calls) == sorted(ptr(t) for t in leaves)
+    for t in leaves:
+        np.testing.assert_array_equal(snaps[ptr(t)].cpu().numpy(), _g(t).astype(np.float32))
+
+
+@pytest.mark.gpu
 def test_mlp_relu_mse_adam_matches_torch(pa):
     x = seeded_normal(4, (128, 24))
     t = seeded_normal(5, (128, 8))
