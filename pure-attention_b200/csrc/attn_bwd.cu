@@ -576,8 +576,9 @@ __global__ void __launch_bounds__(512, 1)
 // S' = S - LSE/scale and dP' = dP - Delta come out of the tensor core and the
 // elementwise step needs no per-query loads: P = exp2(S' * scale * log2 e),
 // dS = P * dP'. (The extra K-step is 6% more tensor-pipe work, but loading
-// LSE and Delta per query in the elementwise step, whose instruction stream is
-// on the critical path, measured 23% slower.)
+// LSE and Delta per query from shared memory in the elementwise step measured
+// 23% slower: the MMAs' shared-memory operand reads are what this kernel is
+// sensitive to.)
 // Persistent: one two-CTA cluster per SM pair walks (batch*head, pair of key
 // tiles) work items; rings, barrier phases and the dS buffers continue across
 // items, and the dV/dK write-back of one item overlaps the next item's MMAs.
