@@ -40,6 +40,9 @@ def lib():
             getattr(_lib, n).argtypes = [_dp] * 5 + [_i] * 4 + [ctypes.c_double]
         _lib.oracle_attn_bwd.argtypes = [_dp] * 10 + [_i] * 4 + [ctypes.c_double]
         _lib.oracle_attn_delta.argtypes = [_dp] * 3 + [_i] * 4
+        _ip = ctypes.POINTER(ctypes.c_int)
+        _lib.oracle_attn_sampled.argtypes = ([_dp] * 4 + [_i, _i, ctypes.c_double, _ip, _i, _ip, _i]
+                                             + [_dp] * 5)
         _lib.oracle_layer_norm_fwd.argtypes = [_dp] * 6 + [_i] * 2 + [ctypes.c_double]
         _lib.oracle_layer_norm_bwd.argtypes = [_dp] * 8 + [_i] * 2
         for n in ("oracle_matmul", "oracle_matmul_grad_x", "oracle_matmul_grad_w"):
@@ -88,6 +91,27 @@ def attn_bwd(q, k, v, o, dO, lse, scale=None):
                           dv.ctypes.data_as(_dp), delta.ctypes.data_as(_dp), B, L, H, D,
                           float(scale))
     return dq, dk, dv, delta
+
+
+def attn_sampled(q, k, v, dO, qrows, krows, scale=None):
+    """One (batch, head) slice, q/k/v/dO as [L, D]: LSE of every query row,
+    and O, dQ of the query rows `qrows`, dK, dV of the key rows `krows`, in
+    float64. Returns (lse[L], o[nq, D], dq[nq, D], dk[nk, D], dv[nk, D])."""
+    L, D = q.shape
+    scale = 1.0 / np.sqrt(D) if scale is None else scale
+    arrs = [_d(x) for x in (q, k, v, dO)]
+    qr = np.ascontiguousarray(qrows, dtype=np.int32)
+    kr = np.ascontiguousarray(krows, dtype=np.int32)
+    if qr.size and (qr.min() < 0 or qr.max() >= L) or kr.size and (kr.min() < 0 or kr.max() >= L):
+        raise ValueError("sampled row out of range")
+    ip = ctypes.POINTER(ctypes.c_int)
+    lse = np.zeros(L)
+    o, dq = np.zeros((qr.size, D)), np.zeros((qr.size, D))
+    dk, dv = np.zeros((kr.size, D)), np.zeros((kr.size, D))
+    lib().oracle_attn_sampled(*[p for _, p in arrs], L, D, float(scale), qr.ctypes.data_as(ip),
+                              int(qr.size), kr.ctypes.data_as(ip), int(kr.size),
+                              *[a.ctypes.data_as(_dp) for a in (lse, o, dq, dk, dv)])
+    return lse, o, dq, dk, dv
 
 
 # ------------------------------------------------------------------ layer norm
@@ -185,10 +209,25 @@ def concat_last_dim_grad(parts_grad, grad_in0=None):
 
 
 # ------------------------------------------------------------------ CPU baseline
+_AVX512 = ("avx512f", "avx512bw", "avx512dq", "avx512vl")
+
+
+def cpu_isa():
+    """'avx512' when every host core reports AVX-512 F/BW/DQ/VL (and that
+    build exists), else 'avx2'."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = [ln.split(":", 1)[1].split() for ln in f if ln.startswith("flags")]
+    except OSError:
+        flags = []
+    ok = flags and all(all(x in fl for x in _AVX512) for fl in flags)
+    return "avx512" if ok and os.path.exists(os.path.join(HERE, "libcpuattn_avx512.so")) else "avx2"
+
+
 def cpu():
     global _cpu
     if _cpu is None:
-        _cpu = _load("libcpuattn.so")
+        _cpu = _load("libcpuattn_avx512.so" if cpu_isa() == "avx512" else "libcpuattn.so")
         _cpu.cpu_attn_fwd_bwd.argtypes = [_fp] * 9 + [_i] * 4 + [ctypes.c_float] + [_i] * 3
         _cpu.cpu_attn_fwd_bwd.restype = _i
         _cpu.cpu_hardware_threads.restype = _i
@@ -230,6 +269,8 @@ def ref():
         _ref.ref_layer_norm_bwd.argtypes = [_fp] * 8 + [_i] * 2
         for n in ("ref_matmul", "ref_matmul_grad_x", "ref_matmul_grad_w"):
             getattr(_ref, n).argtypes = [_fp] * 3 + [_i] * 3
+        if hasattr(_ref, "ref_time_flash"):
+            _ref.ref_time_flash.argtypes = [_fp] * 4 + [_i] * 5 + [_fp] * 2
     return _ref
 
 
@@ -320,3 +361,16 @@ def ref_matmul_grad_w(x, dy, dw0):
     dw = np.array(dw0, dtype=np.float32, copy=True)
     _chk(ref().ref_matmul_grad_w(xp, dyp, dw.ctypes.data_as(_fp), M, N, K), "matmul grad W")
     return dw
+
+
+def ref_time_flash(q, k, v, dO, reps):
+    """Milliseconds per call of the reference's flash forward and backward on
+    the GPU (inputs [B, L, H, D] fp32; D = 32 shipped backward, D = 64 the
+    in-bounds relaunch). Returns (fwd_ms, bwd_ms)."""
+    B, L, H, D = q.shape
+    arrs = [_f(a) for a in (q, k, v, dO)]
+    fwd = ctypes.c_float(0.0)
+    bwd = ctypes.c_float(0.0)
+    _chk(ref().ref_time_flash(*[p for _, p in arrs], B, L, H, D, int(reps),
+                              ctypes.byref(fwd), ctypes.byref(bwd)), "flash timing")
+    return float(fwd.value), float(bwd.value)

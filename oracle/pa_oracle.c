@@ -135,6 +135,113 @@ void oracle_attn_bwd(const double* q, const double* k, const double* v, const do
   free(delta);
 }
 
+/* One (batch, head) slice at sequence lengths too long for the full backward
+ * above: the same math, evaluated for sampled rows only. Inputs are the
+ * slice's rows, q, k, v, dO as [L, D] (row-major, contiguous).
+ *   - every query row: the two-pass forward of oracle_attn_fwd
+ *     (flash_attn_forward_kernel.cu:105-185), giving lse_all[L], the row's O
+ *     and Delta_i = dO_i . O_i (flash_attn_backward_kernel.cu:25-41);
+ *   - sampled queries qrows[0..nq): O_i (o_rows) and
+ *     dQ_i = sum_j dS_ij K_j with dS_ij = P_ij (dP_ij - Delta_i) * scale,
+ *     P_ij = exp(S_ij*scale - LSE_i), dP_ij = dO_i . V_j (doc/flash_backward.md
+ *     section 5; flash_attn_backward_kernel.cu:153-197);
+ *   - sampled keys krows[0..nk): dV_j = sum_i P_ij dO_i and dK_j = sum_i dS_ij Q_i
+ *     (:193-197), which need column j of P and dS over every query.
+ * Outputs are [nq, D] / [nk, D] float64, overwritten. */
+void oracle_attn_sampled(const double* q, const double* k, const double* v, const double* dO,
+                         int L, int D, double scale, const int* qrows, int nq, const int* krows,
+                         int nk, double* lse_all, double* o_rows, double* dq_rows, double* dk_rows,
+                         double* dv_rows) {
+  double* delta = (double*)malloc(sizeof(double) * (size_t)L);
+  int* qpos = (int*)malloc(sizeof(int) * (size_t)L); /* query row -> sample index, or -1 */
+  for (int i = 0; i < L; ++i) qpos[i] = -1;
+  for (int t = 0; t < nq; ++t) qpos[qrows[t]] = t;
+#pragma omp parallel
+  {
+    double* s = (double*)malloc(sizeof(double) * (size_t)L);
+    double* oi = (double*)malloc(sizeof(double) * (size_t)D);
+#pragma omp for schedule(dynamic, 16)
+    for (int i = 0; i < L; ++i) {
+      const double* qi = q + (size_t)i * D;
+      double m = -INFINITY;
+      for (int j = 0; j < L; ++j) {
+        const double* kj = k + (size_t)j * D;
+        double acc = 0.0;
+        for (int x = 0; x < D; ++x) acc += qi[x] * kj[x];
+        s[j] = acc * scale;
+        if (s[j] > m) m = s[j];
+      }
+      double l = 0.0;
+      for (int j = 0; j < L; ++j) {
+        s[j] = exp(s[j] - m);
+        l += s[j];
+      }
+      for (int x = 0; x < D; ++x) oi[x] = 0.0;
+      for (int j = 0; j < L; ++j) {
+        const double* vj = v + (size_t)j * D;
+        const double pj = s[j] / l;
+        for (int x = 0; x < D; ++x) oi[x] += pj * vj[x];
+      }
+      lse_all[i] = m + log(l);
+      const double* doi = dO + (size_t)i * D;
+      double d = 0.0;
+      for (int x = 0; x < D; ++x) d += doi[x] * oi[x];
+      delta[i] = d;
+      if (qpos[i] >= 0) memcpy(o_rows + (size_t)qpos[i] * D, oi, sizeof(double) * (size_t)D);
+    }
+    free(s);
+    free(oi);
+  }
+  /* dQ of the sampled queries */
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int t = 0; t < nq; ++t) {
+    const int i = qrows[t];
+    const double* qi = q + (size_t)i * D;
+    const double* doi = dO + (size_t)i * D;
+    double* dqi = dq_rows + (size_t)t * D;
+    for (int x = 0; x < D; ++x) dqi[x] = 0.0;
+    for (int j = 0; j < L; ++j) {
+      const double* kj = k + (size_t)j * D;
+      const double* vj = v + (size_t)j * D;
+      double sacc = 0.0, dpacc = 0.0;
+      for (int x = 0; x < D; ++x) {
+        sacc += qi[x] * kj[x];
+        dpacc += doi[x] * vj[x];
+      }
+      const double p = exp(sacc * scale - lse_all[i]);
+      const double ds = p * (dpacc - delta[i]) * scale;
+      for (int x = 0; x < D; ++x) dqi[x] += ds * kj[x];
+    }
+  }
+  /* dK, dV of the sampled keys */
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int t = 0; t < nk; ++t) {
+    const int j = krows[t];
+    const double* kj = k + (size_t)j * D;
+    const double* vj = v + (size_t)j * D;
+    double* dkj = dk_rows + (size_t)t * D;
+    double* dvj = dv_rows + (size_t)t * D;
+    for (int x = 0; x < D; ++x) dkj[x] = dvj[x] = 0.0;
+    for (int i = 0; i < L; ++i) {
+      const double* qi = q + (size_t)i * D;
+      const double* doi = dO + (size_t)i * D;
+      double sacc = 0.0, dpacc = 0.0;
+      for (int x = 0; x < D; ++x) {
+        sacc += qi[x] * kj[x];
+        dpacc += doi[x] * vj[x];
+      }
+      const double p = exp(sacc * scale - lse_all[i]);
+      const double ds = p * (dpacc - delta[i]) * scale;
+      for (int x = 0; x < D; ++x) {
+        dvj[x] += p * doi[x];
+        dkj[x] += ds * qi[x];
+      }
+    }
+  }
+  free(delta);
+  free(qpos);
+}
+
 /* LayerNorm forward, layer_norm_forward_kernel.cu:40-82: mean, biased variance
  * var = E[x^2] - mean^2 (:63-64), rstd = 1/sqrt(var + eps) (:65),
  * y = gamma * (x - mean) * rstd + beta (:79-82). */

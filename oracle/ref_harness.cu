@@ -183,3 +183,76 @@ int ref_matmul_grad_w(const float* x, const float* dy, float* dw, int M, int N, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- timing
+// The reference's attention kernels timed on the GPU (CUDA events, after one
+// untimed launch): launch_flash_attention, then the backward - the shipped
+// launch_flash_backward at D = 32 (which allocates its temporaries inside each
+// call), or at D = 64 compute_delta_kernel plus flash_attn_backward_kernel<64,16,64>
+// with the in-bounds Bc = 64 geometry of ref_flash_bwd_relaunch_d64. Inputs are
+// host fp32 [B, L, H*D]; the average milliseconds per call are written to
+// fwd_ms and bwd_ms. Returns 0 or a CUDA error code.
+extern "C" int ref_time_flash(const float* q, const float* k, const float* v, const float* dO,
+                              int B, int L, int H, int D, int reps, float* fwd_ms,
+                              float* bwd_ms) {
+  if ((D != 32 && D != 64) || reps <= 0) return -1;
+  if (D == 64 && L % 64 != 0) return -1;
+  const uint32_t E = static_cast<uint32_t>(H * D);
+  const std::vector<uint32_t> shp = {static_cast<uint32_t>(B), static_cast<uint32_t>(L), E};
+  const size_t n = static_cast<size_t>(B) * L * E;
+  auto Q = std::make_shared<core::Tensor>(shp, false);
+  auto K = std::make_shared<core::Tensor>(shp, false);
+  auto V = std::make_shared<core::Tensor>(shp, false);
+  auto O = std::make_shared<core::Tensor>(shp, false);
+  auto Lc = std::make_shared<core::Tensor>(
+      std::vector<uint32_t>{static_cast<uint32_t>(B * H), static_cast<uint32_t>(L)}, false);
+  Q->to_device(std::vector<float>(q, q + n));
+  K->to_device(std::vector<float>(k, k + n));
+  V->to_device(std::vector<float>(v, v + n));
+  float* G = up(dO, n);
+  float *dQ = up(nullptr, n), *dK = up(nullptr, n), *dV = up(nullptr, n);
+  float* Delta = up(nullptr, static_cast<size_t>(B) * H * L);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  auto bwd = [&]() {
+    if (D == 32) {
+      launch_flash_backward(Q->get_data_ptr(), K->get_data_ptr(), V->get_data_ptr(),
+                            O->get_data_ptr(), G, Lc->get_data_ptr(), dQ, dK, dV, B, H, L, H * D,
+                            nullptr);
+      return;
+    }
+    const int Bc = 64, Br = 16, PAD = 8;
+    const int blocks = (B * H * L + 255) / 256;
+    compute_delta_kernel<<<blocks, 256>>>(G, O->get_data_ptr(), Delta, B, H, L, D);
+    const size_t smem = (4 * Bc * (D + PAD) + 2 * Br * (D + PAD)) * sizeof(float);
+    cudaFuncSetAttribute(flash_attn_backward_kernel<64, 16, 64>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    flash_attn_backward_kernel<64, 16, 64><<<dim3(L / Bc, B * H), 64, smem>>>(
+        Q->get_data_ptr(), K->get_data_ptr(), V->get_data_ptr(), O->get_data_ptr(), G,
+        Lc->get_data_ptr(), Delta, dQ, dK, dV, L * H * D, D, H * D, L, 1.0f / 8.0f);
+  };
+  launch_flash_attention(Q, K, V, O, Lc, H, nullptr);
+  bwd();
+  int st = finish();
+  if (st == 0) {
+    cudaEventRecord(e0);
+    for (int i = 0; i < reps; ++i) launch_flash_attention(Q, K, V, O, Lc, H, nullptr);
+    cudaEventRecord(e1);
+    st = finish();
+    cudaEventElapsedTime(fwd_ms, e0, e1);
+    *fwd_ms /= reps;
+  }
+  if (st == 0) {
+    cudaEventRecord(e0);
+    for (int i = 0; i < reps; ++i) bwd();
+    cudaEventRecord(e1);
+    st = finish();
+    cudaEventElapsedTime(bwd_ms, e0, e1);
+    *bwd_ms /= reps;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  for (float* p : {G, dQ, dK, dV, Delta}) cudaFree(p);
+  return st;
+}

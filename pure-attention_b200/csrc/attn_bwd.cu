@@ -1241,18 +1241,17 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));
   if constexpr (D == 64 && !SPLIT) {
     using C64 = Bwd64Cfg;
-    static uint64_t attr64 = 0;
-    ensure_smem_attr(attn_bwd_d64_kernel<T>, C64::SMEM, attr64);
+    static std::atomic<uint64_t> attr64{0};
+    if (!ensure_smem_attr(attn_bwd_d64_kernel<T>, C64::SMEM, attr64)) return PA_ERR_LAUNCH;
     // Persistent clusters of two CTAs, as many as fit on the device at once;
     // work items are (batch*head, pair of adjacent key tiles; a tile past L
     // has no keys).
     const int n_pairs = (static_cast<int>(grid.x) + 1) / 2;
     const int n_items = n_pairs * static_cast<int>(bh);
-    int dev = 0;
-    cudaGetDevice(&dev);
-    static int max_clusters[64] = {0};
-    int& mc = max_clusters[dev & 63];
-    if (mc <= 0) {
+    const int dev = current_device();
+    if (dev < 0) return PA_ERR_DEVICE;
+    static std::atomic<int> max_clusters[kMaxDevices];
+    const int mc = cached_per_device(max_clusters, dev, [] {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * 4096, 1, 1);
       cfg.blockDim = dim3(C64::THREADS, 1, 1);
@@ -1260,19 +1259,17 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
       int n = 0;
       if (cudaOccupancyMaxActiveClusters(&n, attn_bwd_d64_kernel<T>, &cfg) != cudaSuccess || n <= 0) {
         cudaGetLastError();  // clear a failed query; fall back to one cluster per two SMs
-        int sms = 148;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        n = sms / 2;
+        n = device_sm_count() / 2;
       }
-      mc = n;
-    }
+      return n;
+    });
     const int n_cl = n_items < mc ? n_items : mc;
     attn_bwd_d64_kernel<T><<<dim3(2 * n_cl, 1, 1), C64::THREADS, C64::SMEM, stream>>>(
         m[0], m[1], m[2], m[3], dq_acc, static_cast<T*>(dk), static_cast<T*>(dv), ext, sh.L, Lp,
         sh.H, sh.scale, sh.scale * kLog2e, accumulate, n_pairs, n_items, status);
   } else {
-    static uint64_t attr = 0;
-    ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr);
+    static std::atomic<uint64_t> attr{0};
+    if (!ensure_smem_attr(attn_bwd_kernel<D, SPLIT, T>, C::SMEM, attr)) return PA_ERR_LAUNCH;
     attn_bwd_kernel<D, SPLIT, T><<<grid, 512, C::SMEM, stream>>>(
         m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], mdq, static_cast<T*>(dk),
         static_cast<T*>(dv), lse2, delta_t, sh.L, Lp, sh.H, sh.D, sh.scale, sh.scale * kLog2e,

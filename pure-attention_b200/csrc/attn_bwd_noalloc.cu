@@ -10,8 +10,13 @@
 //
 // The array holds PA_ATTN_BWD_NOALLOC_MAX_WORKSPACE bytes (32 MiB). A shape
 // whose backward workspace (pa_attn_bwd_workspace_size) is larger is rejected
-// with PA_ERR_WORKSPACE. At head_dim 64 that is about 127 000 (batch*head,
-// padded query) rows, e.g. B=1, H=16, L=4096 fits and B=8, H=16, L=4096 does not.
+// with PA_ERR_WORKSPACE. The bf16 head-dim-64 backward needs 296 bytes per
+// (batch*head, padded query) row - LSE, Delta, a 64-float dQ accumulator row
+// and its share of the 4 KB key-extension tile per 128 rows - so about
+// 113 000 rows fit: B=1, H=16, L=4096 does, B=8, H=16, L=4096 does not. The
+// fp32 path also keeps eight bf16 operand planes, about 1.3 KB per row in all,
+// so only about 25 000 rows fit (B=1, H=4, L=4096, say). pa_attn_bwd_workspace_size
+// gives the exact figure for a shape.
 //
 // All calls on a device share the one array, and it keeps whatever the last
 // call left in it. The backward clears what must start at zero (the fp32 dQ
@@ -23,9 +28,10 @@
 // The device address of the array is looked up (cudaGetSymbolAddress) on the
 // first call made while a given device is current; make that first call before
 // any stream capture on that device.
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
-#include "pa_kernels.h"
+#include "attn_common.cuh"
 
 namespace {
 
@@ -34,18 +40,19 @@ constexpr size_t kMaxWorkspace = PA_ATTN_BWD_NOALLOC_MAX_WORKSPACE;
 static __device__ __align__(256) unsigned char g_attn_bwd_scratch[kMaxWorkspace];
 
 // Device address of g_attn_bwd_scratch on the current device (set up once per
-// device). In host code the symbol itself is only a stand-in, never a device
-// address, so it must not be passed to a kernel.
+// device; atomically cached, since host threads driving different GPUs may
+// make their first calls at the same time). In host code the symbol itself is
+// only a stand-in, never a device address, so it must not be passed to a kernel.
 void* scratch_address() {
-  static void* ptrs[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!ptrs[dev]) {
-    void* p = nullptr;
+  static std::atomic<void*> ptrs[pa::kMaxDevices];
+  const int dev = pa::current_device();
+  if (dev < 0) return nullptr;
+  void* p = ptrs[dev].load(std::memory_order_acquire);
+  if (!p) {
     if (cudaGetSymbolAddress(&p, g_attn_bwd_scratch) != cudaSuccess) return nullptr;
-    ptrs[dev] = p;
+    ptrs[dev].store(p, std::memory_order_release);
   }
-  return ptrs[dev];
+  return p;
 }
 
 }  // namespace

@@ -1,5 +1,6 @@
 // Shared pieces of the attention kernels: problem shape, constants, TMA maps.
 #pragma once
+#include <atomic>
 #include <cuda_runtime.h>
 #include "pa_kernels.h"
 #include "ptx.cuh"
@@ -33,16 +34,59 @@ inline bool make_qkv_map(CUtensorMap* m, const void* base, const AttnShape& sh, 
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// Raise a kernel's dynamic shared memory limit once per device.
-template <typename K>
-inline void ensure_smem_attr(K kernel, int bytes, uint64_t& done_mask) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(done_mask & bit)) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    done_mask |= bit;
+// ---------------------------------------------------------------- per-device host caches
+// The C ABI may be called from one host thread per GPU at the same time, so
+// every value cached per device is an atomic: concurrent first calls compute
+// the same value and store it without a data race.
+constexpr int kMaxDevices = 64;
+
+// The calling thread's current device, or -1 (no device, or beyond the caches).
+inline int current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  return dev;
+}
+
+// cache[dev], computed by `compute` on first use; a value <= 0 is not kept.
+template <typename F>
+inline int cached_per_device(std::atomic<int> (&cache)[kMaxDevices], int dev, F compute) {
+  int v = cache[dev].load(std::memory_order_acquire);
+  if (v <= 0) {
+    v = compute();
+    if (v > 0) cache[dev].store(v, std::memory_order_release);
   }
+  return v;
+}
+
+// Streaming multiprocessors of the current device (148 if it cannot be read).
+inline int device_sm_count() {
+  static std::atomic<int> cache[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0) return 148;
+  const int n = cached_per_device(cache, dev, [dev] {
+    int sms = 0;
+    return cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess ? sms : 0;
+  });
+  return n > 0 ? n : 148;
+}
+
+// Raise a kernel's dynamic shared memory limit on the current device, once per
+// device. The bit is set only after cudaFuncSetAttribute succeeded; two
+// threads may both set the attribute, which is harmless. Returns false when
+// the attribute could not be set (the launch would fail).
+template <typename K>
+inline bool ensure_smem_attr(K kernel, int bytes, std::atomic<uint64_t>& done_mask) {
+  const int dev = current_device();
+  if (dev < 0) return false;
+  const uint64_t bit = 1ull << dev;
+  if (done_mask.load(std::memory_order_acquire) & bit) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();  // do not leave the error for the caller's launch check
+    return false;
+  }
+  done_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
 }
 
 }  // namespace pa

@@ -396,24 +396,22 @@ template <int D, bool SPLIT, typename OutT>
 static int launch_fwd(const AttnShape& shp, const CUtensorMap* m, void* o, float* lse, int d_out,
                       uint32_t* status, cudaStream_t stream) {
   using C = FwdCfg<D, SPLIT>;
-  static uint64_t attr = 0;
-  ensure_smem_attr(attn_fwd_kernel<D, SPLIT, OutT>, C::SMEM, attr);
+  static std::atomic<uint64_t> attr{0};
+  if (!ensure_smem_attr(attn_fwd_kernel<D, SPLIT, OutT>, C::SMEM, attr)) return PA_ERR_LAUNCH;
   // persistent: as many CTAs as fit on the device at once, at most one per item
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static int resident[64] = {0};
-  int& res = resident[dev & 63];
-  if (res <= 0) {
-    int sms = 0, per_sm = 0;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int dev = current_device();
+  if (dev < 0) return PA_ERR_DEVICE;
+  static std::atomic<int> resident[kMaxDevices];
+  const int res = cached_per_device(resident, dev, [] {
+    int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_fwd_kernel<D, SPLIT, OutT>, C::THREADS,
                                                       C::SMEM) != cudaSuccess ||
         per_sm <= 0) {
       cudaGetLastError();  // clear a failed query; one CTA per SM
       per_sm = 1;
     }
-    res = (sms > 0 ? sms : 148) * per_sm;
-  }
+    return device_sm_count() * per_sm;
+  });
   const int n_qb = (shp.L + 255) / 256;
   const long long items = static_cast<long long>(n_qb) * shp.B * shp.H;
   if (items > 0x7fffffffLL) return PA_ERR_SHAPE;

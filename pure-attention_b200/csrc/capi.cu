@@ -11,16 +11,21 @@ namespace {
 // First error recorded by a bounded wait in any kernel on this device.
 __device__ uint32_t g_pa_status = 0;
 
+// Device address of g_pa_status on the current device, looked up once per
+// device (atomically cached: host threads driving different GPUs may make
+// their first calls at the same time).
 uint32_t* status_word() {
-  static uint32_t* ptrs[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!ptrs[dev]) {
+  static std::atomic<uint32_t*> ptrs[pa::kMaxDevices];
+  const int dev = pa::current_device();
+  if (dev < 0) return nullptr;
+  uint32_t* w = ptrs[dev].load(std::memory_order_acquire);
+  if (!w) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_pa_status) != cudaSuccess) return nullptr;
-    ptrs[dev] = static_cast<uint32_t*>(p);
+    w = static_cast<uint32_t*>(p);
+    ptrs[dev].store(w, std::memory_order_release);
   }
-  return ptrs[dev];
+  return w;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -81,6 +86,34 @@ int pa_device_status(pa_stream_t stream, int clear) {
   if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return PA_ERR_DEVICE;
   if (clear && v != 0 && cudaMemset(w, 0, sizeof(v)) != cudaSuccess) return PA_ERR_DEVICE;
   return v == 0 ? PA_OK : PA_ERR_TIMEOUT;
+}
+
+}  // extern "C"
+
+namespace {
+// One thread waits on an mbarrier of arrival count 1 with the kernels' bounded
+// wait. Without the arrival nothing completes the phase: the wait gives up
+// after limit_ns, records the timeout in the status word and the kernel ends.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int arrive, uint32_t* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  const uint32_t b = pa::smem_u32(&bar);
+  pa::mbar_init(b, 1);
+  pa::fence_mbar_init();
+  if (arrive) pa::mbar_arrive(b);
+  pa::mbar_wait_for(b, 0, status, limit_ns);
+}
+}  // namespace
+
+extern "C" {
+
+int pa_wait_selftest(uint64_t limit_ns, int arrive, pa_stream_t stream) {
+  constexpr uint64_t kMaxLimitNs = 5000000000ull;
+  if (limit_ns == 0 || limit_ns > kMaxLimitNs) return PA_ERR_SHAPE;
+  uint32_t* w = status_word();
+  if (!w) return PA_ERR_DEVICE;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, arrive, w);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
 size_t pa_attn_fwd_workspace_size(const pa_attn_desc* desc) {

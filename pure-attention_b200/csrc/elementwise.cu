@@ -15,14 +15,7 @@ namespace pa {
 
 namespace {
 
-int sm_count() {
-  static int sms[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 63;
-  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  return sms[dev] > 0 ? sms[dev] : 148;
-}
+int sm_count() { return device_sm_count(); }
 
 unsigned grid_for(size_t work, int threads) {
   const size_t want = (work + threads - 1) / threads;

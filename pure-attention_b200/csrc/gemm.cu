@@ -353,14 +353,7 @@ struct Epilogue {
 };
 
 
-int sm_count() {
-  static int n[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 63;
-  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return n[dev] > 0 ? n[dev] : 148;
-}
+int sm_count() { return device_sm_count(); }
 
 // bf16 math: maps over the hi planes, A boxes of 128 rows and B boxes of 256.
 // fp32 [rows, cols] output with row pitch ld, as 128-row x 32-column TMA boxes.
@@ -376,8 +369,9 @@ template <bool A_MN, bool B_MN, int NT>
 int run_gemm_persist(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred,
                      int accumulate, const Epilogue& ep, uint32_t* status, cudaStream_t s) {
   const CUtensorMap& mA = m[0];
-  static uint64_t attr = 0;
-  ensure_smem_attr(gemm_persist_kernel<A_MN, B_MN, NT>, PersistCfg<NT>::SMEM, attr);
+  static std::atomic<uint64_t> attr{0};
+  if (!ensure_smem_attr(gemm_persist_kernel<A_MN, B_MN, NT>, PersistCfg<NT>::SMEM, attr))
+    return PA_ERR_LAUNCH;
   // TMA-store epilogue when every output is 16-byte aligned with a 16-byte row
   // pitch and column blocks hold whole 32-column chunks
   CUtensorMap mc[3];

@@ -196,14 +196,7 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-int num_sms() {
-  static int sms[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 63;
-  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  return sms[dev] > 0 ? sms[dev] : 148;
-}
+int num_sms() { return device_sm_count(); }
 
 // One wave of CTAs: two per SM for rows of up to 1024 values (about 100-130
 // registers per thread, 64 KB of partials), three for shorter rows.
@@ -233,14 +226,17 @@ int ln_bwd_launch(const float* dy, const float* x, const float* mu, const float*
   const size_t smem = static_cast<size_t>(LN_WARPS) * 2 * N * sizeof(float);
   float* p = (dg || db) ? part : nullptr;
   if (accumulate && dx) {
-    static uint64_t attr = 0;
-    ensure_smem_attr(ln_bwd_kernel<VPL, true>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4), attr);
+    static std::atomic<uint64_t> attr{0};
+    if (!ensure_smem_attr(ln_bwd_kernel<VPL, true>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4),
+                          attr))
+      return PA_ERR_LAUNCH;
     ln_bwd_kernel<VPL, true><<<blocks, LN_WARPS * 32, p ? smem : 0, s>>>(dy, x, mu, rs, g, dx, p,
                                                                           M, N);
   } else {
-    static uint64_t attr = 0;
-    ensure_smem_attr(ln_bwd_kernel<VPL, false>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4),
-                     attr);
+    static std::atomic<uint64_t> attr{0};
+    if (!ensure_smem_attr(ln_bwd_kernel<VPL, false>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4),
+                          attr))
+      return PA_ERR_LAUNCH;
     ln_bwd_kernel<VPL, false><<<blocks, LN_WARPS * 32, p ? smem : 0, s>>>(dy, x, mu, rs, g, dx, p,
                                                                            M, N);
   }

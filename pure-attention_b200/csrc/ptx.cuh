@@ -80,20 +80,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* status) {
+// Bounded wait for the phase with the given parity to complete: gives up after
+// limit_ns of wall time (recording PA_DEV_ERR_TIMEOUT), or as soon as another
+// wait of this or an earlier kernel has recorded an error.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint32_t* status,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > PA_WAIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       record_error(status, PA_DEV_ERR_TIMEOUT);
       return false;
     }
     if (aborted(status)) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* status) {
+  return mbar_wait_for(bar, parity, status, PA_WAIT_NS);
 }
 
 // Every lane waits, then the warp agrees: true only if all lanes saw the phase

@@ -15,14 +15,7 @@ namespace pa {
 
 namespace {
 
-int sms() {
-  static int n[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 63;
-  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return n[dev] > 0 ? n[dev] : 148;
-}
+int sms() { return device_sm_count(); }
 unsigned grid(size_t n) {
   const size_t want = (n + 255) / 256, cap = static_cast<size_t>(sms()) * 8;
   return static_cast<unsigned>(want < cap ? (want ? want : 1) : cap);

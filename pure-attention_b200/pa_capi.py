@@ -21,7 +21,8 @@ STATUS = {
 
 # Every symbol include/pa_kernels.h declares.
 EXPORTS = [
-    "pa_abi_version", "pa_status_string", "pa_device_status", "pa_set_f32_math", "pa_get_f32_math",
+    "pa_abi_version", "pa_status_string", "pa_device_status", "pa_wait_selftest", "pa_set_f32_math",
+    "pa_get_f32_math",
     "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_add_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
@@ -60,6 +61,7 @@ _SIGS = {
     "pa_get_f32_math": (_int, []),
     "pa_status_string": (ctypes.c_char_p, [_int]),
     "pa_device_status": (_int, [_vp, _int]),
+    "pa_wait_selftest": (_int, [ctypes.c_uint64, _int, _vp]),
     "pa_attn_fwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
     "pa_attn_fwd": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "pa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
@@ -231,6 +233,13 @@ def attn_delta(dO, o, delta, desc=None, stream=None):
 def device_status(clear=True, stream=None):
     """Synchronise and return the device status word (0 = no kernel timed out)."""
     return load().pa_device_status(_stream() if stream is None else stream, int(clear))
+
+
+def wait_selftest(limit_ns, arrive, stream=None):
+    """Enqueue the failure-detection self-test: one bounded mbarrier wait of
+    limit_ns that completes (arrive=True) or runs out (arrive=False)."""
+    _check("pa_wait_selftest", load().pa_wait_selftest(int(limit_ns), int(bool(arrive)),
+                                                        _stream() if stream is None else stream))
 
 
 def layer_norm_fwd(x, gamma, beta, y, mean, rstd, eps=1e-5, stream=None):

@@ -109,9 +109,13 @@ def test_attention_bf16_accumulate_adds_into_grads():
 
 @pytest.mark.gpu
 def test_attention_bf16_headline_shape_slices():
-    """B=8, H=16, L=4096, d=64 (the headline shape): two (b, h) slices against the oracle."""
+    """B=8, H=16, L=4096, d=64 (the headline shape): six (b, h) slices spread
+    over batches and heads against the full float64 oracle, and LSE / O / dQ /
+    dK / dV on sampled rows of six more."""
     inputs, outs = _run(8, 4096, 16, 64, seed=3)
-    _check(inputs, outs, heads=[(0, 0), (7, 15)])
+    _check(inputs, outs, heads=[(0, 0), (1, 7), (3, 3), (4, 12), (6, 9), (7, 15)])
+    _check_sampled(inputs, outs, heads=[(0, 15), (2, 1), (3, 14), (5, 5), (6, 0), (7, 8)],
+                   n_rows=128)
 
 
 @pytest.mark.gpu
@@ -121,20 +125,50 @@ def test_attention_bf16_d128_two_heads_oracle():
     _check(inputs, outs)
 
 
+def _sampled_rows(L, n, seed):
+    """n distinct rows of [0, L): both ends (tile edges), the rest spread at random."""
+    rng = np.random.default_rng(seed)
+    ends = [0, 1, 127, 128, L // 2, L - 129, L - 128, L - 2, L - 1]
+    rest = rng.choice(np.setdiff1d(np.arange(L), ends), size=n - len(ends), replace=False)
+    return np.sort(np.concatenate([ends, rest])).astype(np.int32)
+
+
+def _check_sampled(inputs, outs, heads, n_rows=256):
+    """Oracle parity at lengths where the full float64 backward is too slow:
+    for each (b, h), LSE of every query row, and O / dQ on n_rows sampled query
+    rows, dK / dV on n_rows sampled key rows (oracle.attn_sampled)."""
+    import oracle
+    qn, kn, vn, gn = inputs
+    o, lse, dq, dk, dv = outs
+    B, L, H, D = qn.shape
+    for (b, h) in heads:
+        sl = lambda a: np.ascontiguousarray(a[b, :, h, :])
+        qr = _sampled_rows(L, n_rows, 17 * b + h)
+        kr = _sampled_rows(L, n_rows, 1000 + 17 * b + h)
+        rl, ro, rdq, rdk, rdv = oracle.attn_sampled(sl(qn), sl(kn), sl(vn), sl(gn), qr, kr)
+        errs = {"o": rel_err(sl(o)[qr], ro), "dq": rel_err(sl(dq)[qr], rdq),
+                "dk": rel_err(sl(dk)[kr], rdk), "dv": rel_err(sl(dv)[kr], rdv)}
+        lse_err = float(np.max(np.abs(lse[b * H + h] - rl)))
+        print(f"(b={b},h={h}) L={L} D={D} sampled rel errs {errs} lse (all rows) max abs {lse_err:.2e}")
+        for name, e in errs.items():
+            assert e <= BF16_TOL, (b, h, name, e)
+        assert lse_err <= LSE_TOL, (b, h, lse_err)
+
+
 @pytest.mark.gpu
-def test_attention_bf16_long_sequence_d128_properties():
-    """B=2, H=16, L=16384, d=128 (long-sequence shape), checked through exact
-    identities of the math that hold at any size:
+def test_attention_bf16_long_sequence_d128_oracle():
+    """B=2, H=16, L=16384, d=128 (the long-sequence shape): 128 query tiles per
+    key tile, LSE / Delta over 16 384 rows. Against the float64 oracle on two
+    (b, h) slices: LSE of every row, O and dQ on 256 sampled query rows, dK and
+    dV on 256 sampled key rows. Then identities of the math over every head:
       sum_j dV_j = sum_i dO_i   (rows of P sum to 1)
       sum_j dK_j = 0            (rows of dS sum to 0)
       O rows lie in the range of V's columns (convex combinations)."""
-    (qn, kn, vn, gn), (o, lse, dq, dk, dv) = _run(2, 16384, 16, 128, seed=4)
-    sdv = dv.sum(axis=1)           # [B, H, D]
-    sdo = gn.sum(axis=1)
-    assert rel_err(sdv, sdo) < 2e-2
-    sdk = np.abs(dk.sum(axis=1)).max()
-    scale = np.abs(dk).sum(axis=1).max()
-    assert sdk <= 2e-2 * scale
+    inputs, outs = _run(2, 16384, 16, 128, seed=4)
+    _check_sampled(inputs, outs, heads=[(0, 0), (1, 15)])
+    (qn, kn, vn, gn), (o, lse, dq, dk, dv) = inputs, outs
+    assert rel_err(dv.sum(axis=1), gn.sum(axis=1)) < 2e-2
+    assert np.abs(dk.sum(axis=1)).max() <= 2e-2 * np.abs(dk).sum(axis=1).max()
     assert np.all(o <= vn.max(axis=1, keepdims=True) + 1e-2)
     assert np.all(o >= vn.min(axis=1, keepdims=True) - 1e-2)
     assert np.all(np.isfinite(dq)) and np.all(np.isfinite(lse))
@@ -143,9 +177,11 @@ def test_attention_bf16_long_sequence_d128_properties():
 @pytest.mark.gpu
 def test_attention_bf16_long_sequence_d64_properties():
     """B=1, H=4, L=16384, d=64: 128 query tiles per key tile, so the per-cluster
-    query-tile order wraps around; exact identities as for d=128, plus two
-    (b, h) slices at the start against the oracle would be too slow in float64."""
-    (qn, kn, vn, gn), (o, lse, dq, dk, dv) = _run(1, 16384, 4, 64, seed=6)
+    query-tile order wraps around. Sampled-row oracle parity on two heads, and
+    the exact identities of the d=128 test over every head."""
+    inputs, outs = _run(1, 16384, 4, 64, seed=6)
+    _check_sampled(inputs, outs, heads=[(0, 0), (0, 3)])
+    (qn, kn, vn, gn), (o, lse, dq, dk, dv) = inputs, outs
     assert rel_err(dv.sum(axis=1), gn.sum(axis=1)) < 2e-2
     assert np.abs(dk.sum(axis=1)).max() <= 2e-2 * np.abs(dk).sum(axis=1).max()
     assert np.all(o <= vn.max(axis=1, keepdims=True) + 1e-2)

@@ -101,3 +101,24 @@ def test_cpu_baseline_matches_oracle(oracle):
     assert rel_err(lse, rl) < 1e-6
     for a, b in ((dq, rdq), (dk, rdk), (dv, rdv)):
         assert rel_err(a, b) < 1e-4
+
+
+def test_sampled_row_oracle_equals_full_oracle(oracle):
+    """oracle.attn_sampled (LSE of every row; O, dQ of sampled queries; dK, dV of
+    sampled keys) computes the same numbers as the full float64 forward and
+    backward, at a ragged length."""
+    B, L, H, D = 1, 300, 2, 64
+    q, k, v, g = (seeded_normal(s, (B, L, H, D), 0.5).astype(np.float64) for s in (41, 42, 43, 44))
+    o, lse = oracle.attn_fwd(q, k, v)
+    dq, dk, dv, _ = oracle.attn_bwd(q, k, v, o, g, lse)
+    h = 1
+    sl = lambda a: np.ascontiguousarray(a[0, :, h, :])
+    qr, kr = [0, 5, 127, 128, 299], [1, 2, 150, 298, 299]
+    rl, ro, rdq, rdk, rdv = oracle.attn_sampled(sl(q), sl(k), sl(v), sl(g), qr, kr)
+    np.testing.assert_allclose(rl, lse[h], rtol=0, atol=1e-12)
+    np.testing.assert_allclose(ro, sl(o)[qr], rtol=1e-12, atol=1e-13)
+    np.testing.assert_allclose(rdq, sl(dq)[qr], rtol=1e-10, atol=1e-13)
+    np.testing.assert_allclose(rdk, sl(dk)[kr], rtol=1e-10, atol=1e-13)
+    np.testing.assert_allclose(rdv, sl(dv)[kr], rtol=1e-10, atol=1e-13)
+    with pytest.raises(ValueError):
+        oracle.attn_sampled(sl(q), sl(k), sl(v), sl(g), [L], [])
