@@ -115,6 +115,12 @@ def parse():
                     help="instead of the attention step: the data-parallel denoise training step "
                          "(6 layers, E1024 H16 FFN4096, N2048, 8 sequences per GPU, fp32 weights), "
                          "gradients averaged over the ranks with NCCL")
+    ap.add_argument("--bucket-mb", type=float, default=25.0,
+                    help="--train: gradient bucket size of the all-reduce")
+    ap.add_argument("--tail-mb", type=float, default=0.0,
+                    help="--train: the gradients backward finishes last (this many MB) go into "
+                         "smaller buckets of --tail-bucket-mb")
+    ap.add_argument("--tail-bucket-mb", type=float, default=4.0)
     return ap.parse_args()
 
 
@@ -703,7 +709,11 @@ def run_train(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     import denoise
     peak, peak_sus, _, peak_src = peaks()
-    tr = denoise.DenoiseTrainer(lr=1e-4, math="bf16", **TRAIN)
+    mb = lambda x: int(x * (1 << 20))
+    tr = denoise.DenoiseTrainer(lr=1e-4, math="bf16", bucket_bytes=mb(args.bucket_mb),
+                                tail_bytes=mb(args.tail_mb),
+                                tail_bucket_bytes=mb(args.tail_bucket_mb) if args.tail_mb else None,
+                                **TRAIN)
     lift = denoise.embedding(TRAIN["embed"], 5)
     rng = np.random.default_rng(5 + rank)
     data = [tuple(torch.from_numpy(a).pin_memory()
@@ -779,6 +789,10 @@ def run_train(args):
         "allreduce_ms": None if ms_ar is None else round(ms_ar / args.steps, 3),
         "split3_ms_per_step": round(ms_split3 / args.steps, 3),
         "allreduce_bytes": None if tr.reducer is None else tr.reducer.nbytes,
+        "allreduce_buckets": None if tr.reducer is None else {
+            "count": len(tr.reducer.buckets), "bucket_mb": args.bucket_mb, "tail_mb": args.tail_mb,
+            "tail_bucket_mb": args.tail_bucket_mb if args.tail_mb else None,
+            "in_place": tr.reducer.inplace},
         "e2e": {"value": round(tokens / (e2e_step * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_step, 3),

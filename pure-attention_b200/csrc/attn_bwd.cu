@@ -96,57 +96,75 @@ __device__ __forceinline__ void write_ext_rows(uint8_t* ext, size_t bh, int Lp, 
   *reinterpret_cast<uint4*>(t + off + 128) = make_uint4(d.x, d.y, 0u, 0u);
 }
 
-// G = D/8 threads per (b, l, h) row, each reading 8 values of dO and O.
+// One thread per (batch*head, query row); a block holds the 128 rows of one
+// query tile, so the extension tile, LSE and Delta of a block are contiguous
+// and every warp writes them as whole 128-byte lines. Each thread reads its
+// rows of dO and O (D values each) with up to 16 independent 16-byte loads in
+// flight. With dq_zero the block also clears its tile of the fp32 dQ
+// accumulator (128 rows x dq_width floats), which the main kernel reduces into.
 template <int D, typename InT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(128)
     attn_bwd_prep_kernel(const InT* __restrict__ dO, const InT* __restrict__ O,
                          const float* __restrict__ lse, float* __restrict__ lse2_t,
                          float* __restrict__ delta_t, float* __restrict__ delta_ref,
-                         uint8_t* __restrict__ ext, float inv_scale, int B, int L, int Lp, int H) {
-  constexpr int G = D / 8;
-  const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t rowi = gt / G;  // over B * Lp * H, ordered (b, l, h)
-  const int g = static_cast<int>(gt % G);
-  const size_t nrows = static_cast<size_t>(B) * Lp * H;
-  const bool in_range = rowi < nrows;
-  const int h = in_range ? static_cast<int>(rowi % H) : 0;
-  const int l = in_range ? static_cast<int>((rowi / H) % Lp) : 0;
-  const int b = in_range ? static_cast<int>(rowi / (static_cast<size_t>(H) * Lp)) : 0;
-  float acc = 0.f;
-  const bool real = in_range && l < L;
+                         uint8_t* __restrict__ ext, float* __restrict__ dq_zero, int dq_width,
+                         float inv_scale, int L, int Lp, int H) {
+  constexpr int NV = D * static_cast<int>(sizeof(InT)) / 16;  // 16-byte vectors per row
+  constexpr int CH = NV < 8 ? NV : 8;                           // vectors loaded per batch
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int l = blockIdx.x * 128 + static_cast<int>(threadIdx.x);
+  const bool real = l < L;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (real) {
-    const size_t off = ((static_cast<size_t>(b) * L + l) * H + h) * D + g * 8;
-    if constexpr (sizeof(InT) == 2) {
-      const uint4 a = *reinterpret_cast<const uint4*>(dO + off);
-      const uint4 c = *reinterpret_cast<const uint4*>(O + off);
-      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+    const size_t off = ((static_cast<size_t>(b) * L + l) * H + h) * D;
+    const uint4* a4 = reinterpret_cast<const uint4*>(dO + off);
+    const uint4* c4 = reinterpret_cast<const uint4*>(O + off);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 fa = __bfloat1622float2(a2[i]);
-        const float2 fc = __bfloat1622float2(c2[i]);
-        acc = fmaf(fa.x, fc.x, acc);
-        acc = fmaf(fa.y, fc.y, acc);
+    for (int v0 = 0; v0 < NV; v0 += CH) {
+      uint4 va[CH], vc[CH];
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        va[i] = a4[v0 + i];
+        vc[i] = c4[v0 + i];
       }
-    } else {
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const float4 fa = *reinterpret_cast<const float4*>(dO + off + 4 * i);
-        const float4 fc = *reinterpret_cast<const float4*>(O + off + 4 * i);
-        acc = fmaf(fa.x, fc.x, fmaf(fa.y, fc.y, fmaf(fa.z, fc.z, fmaf(fa.w, fc.w, acc))));
+      for (int i = 0; i < CH; ++i) {
+        if constexpr (sizeof(InT) == 2) {
+          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&va[i]);
+          const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&vc[i]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fx = __bfloat1622float2(x2[e]);
+            const float2 fy = __bfloat1622float2(y2[e]);
+            acc[e] = fmaf(fx.x, fy.x, fmaf(fx.y, fy.y, acc[e]));
+          }
+        } else {
+          const float* x = reinterpret_cast<const float*>(&va[i]);
+          const float* y = reinterpret_cast<const float*>(&vc[i]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] = fmaf(x[e], y[e], acc[e]);
+        }
       }
     }
   }
-#pragma unroll
-  for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (in_range && g == 0) {
-    const size_t bh = static_cast<size_t>(b) * H + h;
-    if (lse2_t) lse2_t[bh * Lp + l] = real ? lse[bh * L + l] * kLog2e : INFINITY;
-    if (delta_t) delta_t[bh * Lp + l] = real ? acc : 0.f;
-    if (delta_ref && real) delta_ref[(static_cast<size_t>(b) * L + l) * H + h] = acc;
+  const float delta = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  const size_t row = static_cast<size_t>(bh) * Lp + l;  // rows [B*H, Lp]
+  if (l < Lp) {
+    if (lse2_t) lse2_t[row] = real ? lse[static_cast<size_t>(bh) * L + l] * kLog2e : INFINITY;
+    if (delta_t) delta_t[row] = real ? delta : 0.f;
     if (ext)
-      write_ext_rows(ext, bh, Lp, l, real ? -lse[bh * L + l] * inv_scale : 0.f, real ? -acc : 0.f,
-                     !real);
+      write_ext_rows(ext, bh, Lp, l, real ? -lse[static_cast<size_t>(bh) * L + l] * inv_scale : 0.f,
+                     real ? -delta : 0.f, !real);
+  }
+  if (delta_ref && real) delta_ref[(static_cast<size_t>(b) * L + l) * H + h] = delta;
+  if (dq_zero) {
+    float4* z = reinterpret_cast<float4*>(dq_zero + (static_cast<size_t>(bh) * Lp +
+                                                     static_cast<size_t>(blockIdx.x) * 128) * dq_width);
+    const int n4 = 128 * dq_width / 4;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int i = static_cast<int>(threadIdx.x); i < n4; i += 128) z[i] = zero;
   }
 }
 
@@ -1185,27 +1203,35 @@ size_t stats_bytes(const AttnShape& sh, int Dacc, bool ext = false) {
          (ext ? bh * (Lp / 128) * kExtTileBytes : 0);
 }
 
-// Delta (and LSE2) prep over rows of `Dreal` values of type InT.
+// Delta (and LSE2, extension tiles, the zeroed dQ accumulator) prep over rows
+// of `Dreal` values of type InT: one block per (batch*head, 128-row tile).
+// Lp: row pitch of the [B*H, Lp] outputs (a multiple of 128 for the backward;
+// L for Delta alone, where only rows < L are written).
 template <int Dreal, typename InT>
 int launch_prep(const AttnShape& sh, const void* dO, const void* o, const float* lse, float* lse2,
-                float* delta_t, float* delta_ref, uint8_t* ext, int Lp, cudaStream_t stream) {
-  const size_t rows = static_cast<size_t>(sh.B) * Lp * sh.H;
-  const size_t threads = rows * (Dreal / 8);
-  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  attn_bwd_prep_kernel<Dreal, InT><<<blocks, 256, 0, stream>>>(
+                float* delta_t, float* delta_ref, uint8_t* ext, float* dq_zero, int dq_width, int Lp,
+                cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>((Lp + 127) / 128), static_cast<unsigned>(sh.B * sh.H));
+  attn_bwd_prep_kernel<Dreal, InT><<<grid, 128, 0, stream>>>(
       static_cast<const InT*>(dO), static_cast<const InT*>(o), lse, lse2, delta_t, delta_ref, ext,
-      1.f / sh.scale, sh.B, sh.L, Lp, sh.H);
+      dq_zero, dq_width, 1.f / sh.scale, sh.L, Lp, sh.H);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
 template <typename InT>
 int prep_any(int Dreal, const AttnShape& sh, const void* dO, const void* o, const float* lse,
              float* lse2, float* delta_t, float* delta_ref, int Lp, cudaStream_t stream,
-             uint8_t* ext = nullptr) {
+             uint8_t* ext = nullptr, float* dq_zero = nullptr, int dq_width = 0) {
   switch (Dreal) {
-    case 32: return launch_prep<32, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, Lp, stream);
-    case 64: return launch_prep<64, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, Lp, stream);
-    case 128: return launch_prep<128, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, Lp, stream);
+    case 32:
+      return launch_prep<32, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, dq_zero, dq_width,
+                                  Lp, stream);
+    case 64:
+      return launch_prep<64, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, dq_zero, dq_width,
+                                  Lp, stream);
+    case 128:
+      return launch_prep<128, InT>(sh, dO, o, lse, lse2, delta_t, delta_ref, ext, dq_zero, dq_width,
+                                   Lp, stream);
     default: return PA_ERR_UNSUPPORTED;
   }
 }
@@ -1230,12 +1256,13 @@ int run_bwd(const AttnShape& sh, const CUtensorMap* m, const void* o, const void
   if (!make_tmap(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return PA_ERR_ALIGN;
-  if (cudaMemsetAsync(dq_acc, 0, bh * Lp * D * sizeof(float), stream) != cudaSuccess)
-    return PA_ERR_LAUNCH;
+  // the prep kernel also zeroes the dQ accumulator [B*H*Lp, D]
   constexpr bool kD64 = D == 64 && !SPLIT;
   uint8_t* ext = kD64 ? stats + 2 * up256(bh * Lp * 4) + up256(bh * Lp * D * 4) : nullptr;
-  int st = kD64 ? prep_any<T>(sh.D, sh, dO, o, lse, nullptr, nullptr, nullptr, Lp, stream, ext)
-                : prep_any<T>(sh.D, sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream);
+  int st = kD64 ? prep_any<T>(sh.D, sh, dO, o, lse, nullptr, nullptr, nullptr, Lp, stream, ext,
+                              dq_acc, D)
+                : prep_any<T>(sh.D, sh, dO, o, lse, lse2, delta_t, nullptr, Lp, stream, nullptr,
+                              dq_acc, D);
   if (st != PA_OK) return st;
 
   dim3 grid((sh.L + 127) / 128, static_cast<unsigned>(bh));

@@ -17,10 +17,10 @@ the target is the clean lift, so output and target have the reference's
 Data parallelism: every rank builds the model from the same seed and rank 0's
 parameters are broadcast once, so all replicas start identical. Each rank runs
 forward and backward on its own sequences; `GradAllReduce` then averages the
-weight gradients over ranks with NCCL all-reduce on zero-copy views of the
-host tensors' gradient buffers, in buckets (per bucket: one gather into a flat
-buffer, one all-reduce, one scatter back), and every rank takes the same Adam
-step.
+weight gradients over ranks with NCCL all-reduce, in buckets: the parameters'
+gradients are moved into one flat arena per bucket, so each bucket is one
+in-place all-reduce, started as soon as backward has finished its gradients;
+every rank then takes the same Adam step.
 
 Precision: weights, activations and gradients are fp32 tensors. math="split3"
 computes every product at fp32-level accuracy (bf16 hi/lo planes, three
@@ -134,16 +134,40 @@ def grad_view(t):
     return _torch().as_tensor(t.grad_view(), device="cuda")
 
 
+def plan_buckets(nbytes, bucket_bytes, tail_bytes=0, tail_bucket_bytes=None):
+    """Buckets (lists of indices into nbytes) in reverse index order - the
+    order in which backward finishes the gradients. Each bucket holds at most
+    bucket_bytes (a gradient larger than that gets a bucket of its own); the
+    last tail_bytes of that order (the gradients backward finishes last, whose
+    reduction cannot hide behind it) go into buckets of tail_bucket_bytes."""
+    order = list(range(len(nbytes)))[::-1]
+    total = sum(nbytes)
+    buckets, cur, cur_bytes, seen = [], [], 0, 0
+    for i in order:
+        limit = bucket_bytes
+        if tail_bucket_bytes and seen >= total - tail_bytes:
+            limit = tail_bucket_bytes
+        if cur and cur_bytes + nbytes[i] > limit:
+            buckets.append(cur)
+            cur, cur_bytes = [], 0
+        cur.append(i)
+        cur_bytes += nbytes[i]
+        seen += nbytes[i]
+    if cur:
+        buckets.append(cur)
+    return buckets
+
+
 class GradAllReduce:
     """Average gradients over the ranks of a process group, in buckets.
 
-    `grads` are flat-viewable torch tensors (views of the gradient buffers).
-    They are packed into buckets of at most `bucket_bytes` (a tensor larger
-    than that gets a bucket of its own) in reverse order, the order in which
-    backward finishes them. Each bucket owns a flat buffer; a call gathers the
-    bucket into it, all-reduces it and scatters the averaged values back.
-    NCCL averages in the collective (ReduceOp.AVG); other backends sum and the
-    scatter divides by the world size.
+    `grads` are flat-viewable torch tensors (views of the gradient buffers),
+    packed into buckets by plan_buckets. By default each bucket owns a flat
+    buffer; a call gathers the bucket into it, all-reduces it and scatters the
+    averaged values back. for_tensors() instead moves the gradients of
+    PureAttention tensors into one flat arena per bucket, so the all-reduce
+    runs in place with no gather or scatter. NCCL averages in the collective
+    (ReduceOp.AVG); other backends sum and then divide by the world size.
 
     Overlapped use: begin(), then ready(key) for each gradient once it is
     final (keys[i] names grads[i]; by default its data pointer), then
@@ -154,50 +178,68 @@ class GradAllReduce:
     and finish() makes the default stream wait for them.
     """
 
-    def __init__(self, grads, bucket_bytes=25 << 20, group=None, keys=None):
+    def __init__(self, grads, bucket_bytes=25 << 20, group=None, keys=None, tail_bytes=0,
+                 tail_bucket_bytes=None, arenas=None, plan=None):
         torch = _torch()
         import torch.distributed as dist
         self.dist, self.group = dist, group
         self.world = dist.get_world_size(group)
         self.avg_in_collective = dist.get_backend(group) == "nccl"
-        self.buckets = []
-        cur, cur_bytes = [], 0
-        for g in reversed(list(grads)):
-            nb = g.numel() * g.element_size()
-            if cur and cur_bytes + nb > bucket_bytes:
-                self.buckets.append(cur)
-                cur, cur_bytes = [], 0
-            cur.append(g.view(-1))
-            cur_bytes += nb
-        if cur:
-            self.buckets.append(cur)
-        self.flat = [torch.empty(sum(v.numel() for v in b), dtype=b[0].dtype, device=b[0].device)
-                     for b in self.buckets]
-        self.sizes = [[v.numel() for v in b] for b in self.buckets]
         grads = list(grads)
+        if plan is None:
+            plan = plan_buckets([g.numel() * g.element_size() for g in grads], bucket_bytes,
+                                tail_bytes, tail_bucket_bytes)
+        self.plan = plan
+        self.buckets = [[grads[i].view(-1) for i in b] for b in plan]
+        self.inplace = arenas is not None  # the views already are slices of the arenas
+        self.flat = (list(arenas) if self.inplace else
+                     [torch.empty(sum(v.numel() for v in b), dtype=b[0].dtype, device=b[0].device)
+                      for b in self.buckets])
+        self.sizes = [[v.numel() for v in b] for b in self.buckets]
         keys = [g.data_ptr() for g in grads] if keys is None else list(keys)
         if len(keys) != len(grads):
             raise ValueError("one key per gradient")
-        # bucket of grads[i]: buckets hold the gradients in reverse order
-        self.where = {}
-        i = len(grads) - 1
-        for b, views in enumerate(self.buckets):
-            for _ in views:
-                self.where[keys[i]] = b
-                i -= 1
+        self.where = {keys[i]: b for b, idx in enumerate(plan) for i in idx}
         cuda = grads[0].device.type == "cuda"
         self.comm = torch.cuda.Stream(device=grads[0].device) if cuda else None
         self.pending = None
+
+    @classmethod
+    def for_tensors(cls, tensors, bucket_bytes=25 << 20, group=None, tail_bytes=0,
+                    tail_bucket_bytes=None):
+        """Reducer over the gradients of PureAttention tensors, which are moved
+        (Tensor.set_grad_storage, zeroed) into one flat arena per bucket: each
+        gradient's slot starts on a 256-byte boundary, and the bucket's
+        all-reduce runs on its arena in place. The reducer owns the arenas and
+        must outlive the tensors' use of their gradients."""
+        torch = _torch()
+        numel = [int(np.prod(t.shape())) for t in tensors]
+        plan = plan_buckets([4 * n for n in numel], bucket_bytes, tail_bytes, tail_bucket_bytes)
+        pad = lambda n: (n + 63) // 64 * 64  # floats: 256-byte slots
+        arenas, views = [], [None] * len(tensors)
+        for idx in plan:
+            arena = torch.zeros(sum(pad(numel[i]) for i in idx), dtype=torch.float32, device="cuda")
+            off = 0
+            for i in idx:
+                tensors[i].set_grad_storage(arena.data_ptr() + 4 * off)
+                views[i] = arena[off:off + numel[i]]
+                off += pad(numel[i])
+            # the arena is reduced whole: padding stays zero on every rank
+            arenas.append(arena)
+        torch.cuda.synchronize()  # the rebinds' memsets ran on the operators' stream
+        return cls(views, group=group, arenas=arenas, plan=plan)
 
     def _reduce(self, b):
         torch = _torch()
         op = self.dist.ReduceOp.AVG if self.avg_in_collective else self.dist.ReduceOp.SUM
         views, flat, sizes = self.buckets[b], self.flat[b], self.sizes[b]
-        torch.cat(views, out=flat)
+        if not self.inplace:
+            torch.cat(views, out=flat)
         self.dist.all_reduce(flat, op=op, group=self.group)
         if not self.avg_in_collective:
             flat.div_(self.world)
-        torch._foreach_copy_(views, list(torch.split(flat, sizes)))
+        if not self.inplace:
+            torch._foreach_copy_(views, list(torch.split(flat, sizes)))
 
     def __call__(self):
         for b in range(len(self.buckets)):
@@ -253,7 +295,8 @@ class DenoiseTrainer:
     """
 
     def __init__(self, layers=6, embed=1024, heads=16, ffn=4096, seq=2048, batch=8, lr=1e-4,
-                 seed=5, bucket_bytes=25 << 20, group=None, math="split3"):
+                 seed=5, bucket_bytes=25 << 20, group=None, math="split3", tail_bytes=0,
+                 tail_bucket_bytes=None):
         import torch.distributed as dist
         self.shape = (batch, seq, embed)
         self.math = math
@@ -271,7 +314,9 @@ class DenoiseTrainer:
             src = dist.get_global_rank(group, 0) if group is not None else 0
             for p in self.params:
                 dist.broadcast(device_view(p), src=src, group=group)
-            self.reducer = GradAllReduce([grad_view(p) for p in self.params], bucket_bytes, group)
+            # gradients live in per-bucket arenas: each bucket is all-reduced in place
+            self.reducer = GradAllReduce.for_tensors(self.params, bucket_bytes, group, tail_bytes,
+                                                     tail_bucket_bytes)
         self.overlap = True  # all-reduce each bucket while the rest of the backward runs
 
     def _leaf_ready(self, t):

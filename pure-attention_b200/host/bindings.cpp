@@ -77,6 +77,11 @@ PYBIND11_MODULE(PureAttention, m) {
       .def("grad_to_host", &Tensor::grad_to_host)
       .def("shape", &Tensor::get_shape)
       .def("zero_grad", &Tensor::zero_grad)
+      .def("set_grad_storage",
+           [](Tensor& t, uintptr_t ptr) { t.set_gradient_storage(reinterpret_cast<float*>(ptr)); },
+           py::arg("device_ptr"),
+           "Move the gradient into caller-owned device memory (numel() floats, 16-byte aligned, "
+           "zeroed); the caller keeps it alive")
       .def_property_readonly("__cuda_array_interface__",
                              [cai](const Tensor& t) { return cai(t.get_data_ptr(), t.get_shape()); })
       .def("grad_view", [](const std::shared_ptr<Tensor>& t) { return GradView{t}; },

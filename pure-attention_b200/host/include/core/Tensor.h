@@ -35,6 +35,12 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
   void set_grad_fn(std::shared_ptr<Function> fn);
   std::shared_ptr<Function> grad_fn() const { return grad_function; }
   void zero_grad() const;
+  // Moves the gradient into caller-owned device memory of numel() floats
+  // (16-byte aligned), zeroed on the context stream; the tensor's own buffer
+  // is freed. The caller keeps that memory alive while the tensor uses it.
+  // Lets a data-parallel reducer keep many gradients in one flat buffer and
+  // all-reduce it in place.
+  void set_gradient_storage(float32_t* external);
 
   // Seeds this tensor's gradient with ones (or keeps the gradient already
   // written there) and runs every graph node reachable from it once, in
@@ -55,6 +61,7 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
   size_t size = 0;
   bool requires_gradient = false;
   bool is_leaf = true;
+  bool owns_gradient = true;
   std::shared_ptr<Function> grad_function;
 };
 

@@ -39,7 +39,7 @@ Tensor::Tensor(const std::vector<uint32_t>& shape_, bool requires_gradient_, boo
 Tensor::~Tensor() {
   const cudaStream_t s = CudaContext::getStream();
   if (data_ptr) cudaFreeAsync(data_ptr, s);
-  if (gradient_ptr) cudaFreeAsync(gradient_ptr, s);
+  if (gradient_ptr && owns_gradient) cudaFreeAsync(gradient_ptr, s);
 }
 
 void Tensor::to_device(const std::vector<float32_t>& host_data) const {
@@ -76,6 +76,18 @@ std::vector<float32_t> Tensor::grad_to_host() const {
 void Tensor::set_grad_fn(std::shared_ptr<Function> fn) {
   grad_function = std::move(fn);
   is_leaf = false;
+}
+
+void Tensor::set_gradient_storage(float32_t* external) {
+  if (!requires_gradient) throw std::runtime_error("set_gradient_storage: tensor has no gradient");
+  if (!external || (reinterpret_cast<uintptr_t>(external) & 15u) != 0)
+    throw std::runtime_error("set_gradient_storage: pointer must be non-null and 16-byte aligned");
+  const cudaStream_t s = CudaContext::getStream();
+  if (gradient_ptr && owns_gradient) cudaFreeAsync(gradient_ptr, s);
+  gradient_ptr = external;
+  owns_gradient = false;
+  if (cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), s) != cudaSuccess)
+    throw std::runtime_error("set_gradient_storage: cudaMemsetAsync failed");
 }
 
 void Tensor::zero_grad() const {

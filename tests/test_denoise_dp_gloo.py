@@ -68,8 +68,24 @@ def _worker(rank, world, port, out_dir, bucket_bytes):
         assert launched == list(range(len(red2.buckets)))
         # grads[0] sits in the last bucket, which only finish() reduces
         assert len(before_finish) == len(red2.buckets) - 1
+        # in place: the gradients are slices of one arena per bucket (what
+        # for_tensors builds around the trainer's parameters)
+        plan = denoise.plan_buckets([g.numel() * 4 for g in grads], bucket_bytes)
+        arenas, slices = [], [None] * len(grads)
+        for idx in plan:
+            arena = torch.zeros(sum(grads[i].numel() for i in idx))
+            off = 0
+            for i in idx:
+                slices[i] = arena[off:off + grads[i].numel()]
+                slices[i].copy_(grads[i].view(-1))
+                off += grads[i].numel()
+            arenas.append(arena)
+        red3 = denoise.GradAllReduce(slices, group=None, arenas=arenas, plan=plan)
+        red3()
+        assert all(f.data_ptr() == a.data_ptr() for f, a in zip(red3.flat, arenas))
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
                  *[s.numpy() for s in storage], *[s.numpy() for s in storage2],
+                 *[s.view(g.shape).numpy() for s, g in zip(slices, grads)],
                  buckets=np.array(repr(nb)))
     finally:
         dist.destroy_process_group()
@@ -92,6 +108,7 @@ def _run(tmp_path, bucket_bytes):
         for i, w in enumerate(want):
             np.testing.assert_allclose(outs[r][f"arr_{i}"], w, rtol=1e-6, atol=1e-6)
             np.testing.assert_allclose(outs[r][f"arr_{len(want) + i}"], w, rtol=1e-6, atol=1e-6)
+            np.testing.assert_allclose(outs[r][f"arr_{2 * len(want) + i}"], w, rtol=1e-6, atol=1e-6)
     np.testing.assert_array_equal(outs[0]["arr_3"], outs[1]["arr_3"])
     return eval(str(outs[0]["buckets"]))
 
@@ -129,3 +146,15 @@ def test_denoise_batch_shapes_and_determinism():
     assert abs(noise.std() - 0.1) < 0.01 and abs(noise.mean()) < 0.01
     x3, _ = denoise.denoise_batch(np.random.default_rng(6), 3, 64, lift)
     assert not np.array_equal(x1, x3)
+
+
+def test_plan_buckets_reverse_order_and_small_tail_buckets():
+    import denoise
+    sizes = [100, 100, 100, 100, 100, 100]
+    # reverse order, buckets of at most 250 B: [5, 4], [3, 2], [1, 0]
+    assert denoise.plan_buckets(sizes, 250) == [[5, 4], [3, 2], [1, 0]]
+    # the last 200 B in order (gradients 1 and 0, finished last) get 100 B buckets
+    assert denoise.plan_buckets(sizes, 250, tail_bytes=200, tail_bucket_bytes=100) == \
+        [[5, 4], [3, 2], [1], [0]]
+    # a gradient larger than the bucket size gets a bucket of its own
+    assert denoise.plan_buckets([10, 500, 10], 100) == [[2], [1], [0]]

@@ -249,3 +249,41 @@ def test_two_rank_data_parallel_matches_one_rank(dn, tmp_path):
     for i, (a, b) in enumerate(zip(dp, ref)):
         if np.linalg.norm(b) > 1e-3 * top:
             assert rel_err(a, b) < 1e-3, i
+
+
+@pytest.mark.gpu
+def test_gradient_arenas_reduce_in_place(dn):
+    """GradAllReduce.for_tensors moves every parameter's gradient into one flat
+    arena per bucket (the first layers' gradients, finished last, in small tail
+    buckets) and all-reduces each arena in place. With a one-rank NCCL group
+    the average is the identity, so a trainer whose gradients live in the
+    arenas takes the same steps as one without a reducer - up to the last bits
+    that differ between any two runs (the split-K weight-gradient GEMMs and
+    the dQ reductions add their parts in no fixed order)."""
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        x, t = dn.denoise_batch(np.random.default_rng(13), SMALL["batch"], SMALL["seq"],
+                                dn.embedding(SMALL["embed"], 5))
+        x, t = _pinned(x), _pinned(t)
+        a = dn.DenoiseTrainer(lr=1e-3, **SMALL)
+        b = dn.DenoiseTrainer(lr=1e-3, **SMALL)
+        assert a.reducer is None and b.reducer is None  # one rank: no reducer by default
+        b.reducer = dn.GradAllReduce.for_tensors(b.params, bucket_bytes=1 << 16,
+                                                 tail_bytes=1 << 16, tail_bucket_bytes=1 << 14)
+        spans = [(f.data_ptr(), f.data_ptr() + 4 * f.numel()) for f in b.reducer.flat]
+        for p in b.params:
+            ptr = dn.grad_view(p).data_ptr()
+            assert any(lo <= ptr < hi for lo, hi in spans)
+            assert ptr % 256 == 0
+        assert len(b.reducer.buckets) > 2
+        for _ in range(2):
+            la, lb = a.step(x, t), b.step(x, t)
+            assert abs(la - lb) <= 1e-6 * abs(la)
+        for p, q in zip(a.params, b.params):
+            assert rel_err(_h(q), _h(p)) < 1e-5
+            if np.linalg.norm(_g(p)) > 0:
+                assert rel_err(_g(q), _g(p)) < 1e-4
+    finally:
+        dist.destroy_process_group()
