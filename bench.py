@@ -115,6 +115,11 @@ def parse():
                     help="instead of the attention step: the data-parallel denoise training step "
                          "(6 layers, E1024 H16 FFN4096, N2048, 8 sequences per GPU, fp32 weights), "
                          "gradients averaged over the ranks with NCCL")
+    ap.add_argument("--kernels", action="store_true",
+                    help="instead of the attention step: each memory-bound kernel family (LayerNorm "
+                         "fwd / add+fwd / bwd / bwd-accumulate, multi-tensor Adam, the attention "
+                         "backward's prep and dQ-convert kernels) and the projection GEMM timed "
+                         "alone with CUDA events, as achieved GB/s (or TFLOP/s) against the peak")
     ap.add_argument("--bucket-mb", type=float, default=25.0,
                     help="--train: gradient bucket size of the all-reduce")
     ap.add_argument("--tail-mb", type=float, default=0.0,
@@ -803,6 +808,114 @@ def run_train(args):
     return 0
 
 
+def run_kernels(args):
+    """Each kernel family alone at a size whose inputs exceed L2, timed with
+    CUDA events over `steps` launches after `warmup`: algorithmic bytes (or
+    FLOPs) per launch over the mean launch time, against the measured peak.
+    Also the small-case driver of the per-kernel ncu captures."""
+    import ctypes
+    import torch
+    import pa_capi
+    torch.cuda.set_device(0)
+    lib = pa_capi.load()
+    peak, _, hbm, peak_src = peaks()
+    g = torch.Generator(device="cuda").manual_seed(17)
+    rnd = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    steps, warm = max(1, args.steps), args.warmup
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    rows = []
+
+    def hbm_row(kernel, shape, nbytes, ms):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        rows.append({"kernel": kernel, "shape": shape, "bound": "hbm", "us": round(ms * 1e3, 2),
+                     "algorithmic_bytes": int(nbytes), "achieved_gbs": round(gbs, 1),
+                     "frac_of_hbm": round(gbs / hbm, 4)})
+
+    # LayerNorm, rows of 1024 fp32 (the training step's width), 128 MiB per tensor
+    M, N = 32768, 1024
+    x, r, dy = rnd(M, N), rnd(M, N), rnd(M, N)
+    gam, bet = 1 + 0.1 * rnd(N), 0.1 * rnd(N)
+    y, s, dx = torch.empty_like(x), torch.empty_like(x), torch.zeros_like(x)
+    mu, rs = torch.empty(M, device="cuda"), torch.empty(M, device="cuda")
+    dg, db = torch.zeros(N, device="cuda"), torch.zeros(N, device="cuda")
+    ws = torch.empty(pa_capi.layer_norm_bwd_workspace_size(M, N), dtype=torch.uint8, device="cuda")
+    e = 4 * M * N
+    hbm_row("ln_fwd_kernel", f"M{M} N{N} fp32", 2 * e + 8 * M,
+            timed(lambda: pa_capi.layer_norm_fwd(x, gam, bet, y, mu, rs)))
+    hbm_row("ln_fwd_kernel (residual add fused)", f"M{M} N{N} fp32", 4 * e + 8 * M,
+            timed(lambda: pa_capi.add_layer_norm_fwd(x, r, s, gam, bet, y, mu, rs)))
+    hbm_row("ln_bwd_kernel + ln_param_reduce_kernel", f"M{M} N{N} fp32", 3 * e + 8 * M,
+            timed(lambda: pa_capi.layer_norm_bwd(dy, x, mu, rs, gam, dx, dg, db, ws)))
+    hbm_row("ln_bwd_kernel (accumulate into dX) + reduce", f"M{M} N{N} fp32", 4 * e + 8 * M,
+            timed(lambda: pa_capi.layer_norm_bwd(dy, x, mu, rs, gam, dx, dg, db, ws,
+                                                 accumulate=True)))
+    del x, r, dy, y, s, dx
+
+    # multi-tensor Adam over the training step's 75.6 M parameters (48 tensors of its shapes)
+    shapes = [(1024, 3072), (3072,), (1024, 1024), (1024,), (1024, 4096), (4096,), (4096, 1024),
+              (1024,)] * 6
+    ps = [rnd(*sh) for sh in shapes]
+    gs = [rnd(*sh) for sh in shapes]
+    ms_, vs_ = [torch.zeros_like(t) for t in ps], [torch.zeros_like(t) for t in ps]
+    arr = lambda ts: (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+    P, G, Mm, V = arr(ps), arr(gs), arr(ms_), arr(vs_)
+    sizes = (ctypes.c_size_t * len(ps))(*[t.numel() for t in ps])
+    n_par = sum(t.numel() for t in ps)
+    st = torch.cuda.current_stream().cuda_stream
+
+    def adam():
+        rc = lib.pa_adam_step_multi(P, G, Mm, V, sizes, len(ps), 1e-4, 0.9, 0.999, 1e-8, 0.1, 0.001, st)
+        assert rc == 0, rc
+
+    hbm_row("adam_multi_kernel", f"{len(ps)} tensors, {n_par / 1e6:.1f} M params", 28 * n_par,
+            timed(adam))
+    del ps, gs, ms_, vs_
+
+    # projection GEMM of the training step, fp32 tensors, bf16 products (includes the
+    # operand conversion to bf16 planes)
+    pa_capi.set_f32_math("bf16")
+    Mg, IN, OUT = 16384, 1024, 3072
+    xg, wg, bg = rnd(Mg, IN), rnd(IN, OUT) * 0.03, rnd(OUT)
+    yg = torch.empty(Mg, OUT, device="cuda")
+    wsg = torch.empty(pa_capi.linear_workspace_size(Mg, IN, OUT), dtype=torch.uint8, device="cuda")
+    ms_g = timed(lambda: pa_capi.linear_fwd(xg, wg, bg, [yg], Mg, IN, OUT, wsg))
+    fl = 2 * Mg * IN * OUT
+    rows.append({"kernel": "split_planes_kernel x2 + gemm_persist_kernel (pa_linear_fwd)",
+                 "shape": f"{Mg}x{IN} @ {IN}x{OUT} fp32 in/out, bf16 products", "bound": "tensor",
+                 "us": round(ms_g * 1e3, 2), "algorithmic_flops": fl,
+                 "achieved_tflops": round(fl / (ms_g * 1e-3) / 1e12, 1),
+                 "frac_of_tensor_peak": round(fl / (ms_g * 1e-3) / 1e12 / peak, 4)})
+    pa_capi.set_f32_math("split3")
+    del xg, wg, yg, wsg
+
+    # pa_attn_delta runs the backward's prep kernel alone, in its Delta-only form (no
+    # extension tiles, no dQ-accumulator clear); inside pa_attn_bwd the same kernel also
+    # writes those, and its share of the step is in the ncu launch list
+    B, L, H, D = 8, 4096, 16, 64
+    o_, do_ = (rnd(B, L, H, D).bfloat16() for _ in range(2))
+    delta = torch.empty(B, L, H, device="cuda")
+    hbm_row("attn_bwd_prep_kernel<64, bf16> (Delta only, pa_attn_delta)", f"B{B} L{L} H{H} d{D} bf16",
+            2 * B * L * H * D * 2 + 4 * B * L * H,
+            timed(lambda: pa_capi.attn_delta(do_, o_, delta)))
+    print(json.dumps({"metric": "per-kernel achieved bandwidth / throughput (1 x B200)",
+                      "peak_hbm_gbs": hbm, "peak_bf16_tflops": peak, "peak_source": peak_src,
+                      "steps": steps, "warmup": warm, "rows": rows,
+                      "device_status": pa_capi.device_status()}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -811,6 +924,8 @@ def main():
         return run_linear(args)
     if args.train:
         return run_train(args)
+    if args.kernels:
+        return run_kernels(args)
     return run_attention(args)
 
 
