@@ -146,8 +146,7 @@ int pa_layer_norm_fwd(const float* x, const float* gamma, const float* beta, flo
  * add pass plus a norm pass. The reference builds the same value from its
  * elementwise add launcher and launch_layer_norm_forward
  * (include/backend/Launchers.cuh:178-189) in sequence. sum may alias neither
- * x nor r. The backward is pa_layer_norm_bwd_accumulate with x = sum, into
- * the gradient of sum, which the add then hands to x and r. */
+ * x nor r. The backward is pa_add_layer_norm_bwd. */
 int pa_add_layer_norm_fwd(const float* x, const float* r, float* sum, const float* gamma,
                           const float* beta, float* y, float* mean, float* rstd, uint32_t M,
                           uint32_t N, float epsilon, pa_stream_t stream);
@@ -169,6 +168,22 @@ int pa_layer_norm_bwd_accumulate(const float* dy, const float* x, const float* m
                                  const float* rstd, const float* gamma, float* dx, float* dgamma,
                                  float* dbeta, uint32_t M, uint32_t N, void* workspace,
                                  size_t workspace_bytes, pa_stream_t stream);
+
+/* Backward of pa_add_layer_norm_fwd in one pass over the rows: with
+ * G = dL/dsum = LayerNorm_bwd(dy) + dsum, where dsum is the gradient that
+ * reached sum from its other consumers (NULL: none),
+ *   dx = G (flags & PA_ADD_LN_ACC_DX: dx += G), dr likewise (PA_ADD_LN_ACC_DR),
+ * and dgamma, dbeta accumulated as in pa_layer_norm_bwd; any output may be
+ * NULL, and dx and dr may be the same buffer (sum = x + x). Replaces the
+ * reference's LayerNorm backward (include/backend/Launchers.cuh:191-203)
+ * followed by its two gradient-accumulate launches for the add
+ * (tensor_add_grad_kernel.cu:4-9): the sum's gradient is never written. */
+#define PA_ADD_LN_ACC_DX 1
+#define PA_ADD_LN_ACC_DR 2
+int pa_add_layer_norm_bwd(const float* dy, const float* dsum, const float* sum,
+                          const float* mean, const float* rstd, const float* gamma, float* dx,
+                          float* dr, float* dgamma, float* dbeta, uint32_t M, uint32_t N,
+                          int flags, void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
 /* ---------------------------------------------------------------- matmul */
 
@@ -244,11 +259,14 @@ int pa_linear_fwd_keep(const float* X, const float* W, const float* bias, float*
  * n_parts = 1) reading X's planes from `kept`, written by pa_linear_fwd_keep
  * under f32 math mode `kept_mode`. Where they cannot serve the current mode
  * (a bf16 forward keeps no lo plane for a split3 backward) X is converted
- * again, as pa_linear_bwd does. */
+ * again, as pa_linear_bwd does. flags & PA_LINEAR_DX_OVERWRITE: dX = dY W^T
+ * (its old contents are neither read nor kept; for a gradient buffer nothing
+ * has written yet, which then needs no zeroing) instead of dX += dY W^T. */
+#define PA_LINEAR_DX_OVERWRITE 1
 int pa_linear_bwd_kept(const float* X, const float* W, const void* kept, size_t kept_bytes,
                        int kept_mode, const float* Y, const float* const* dy_parts, int n_parts,
                        float* dX, float* dW, float* dbias, int M, int in_features,
-                       int out_features, void* workspace, size_t workspace_bytes,
+                       int out_features, int flags, void* workspace, size_t workspace_bytes,
                        pa_stream_t stream);
 
 /* ---------------------------------------------------------------- elementwise */

@@ -251,6 +251,27 @@ int pa_layer_norm_bwd_accumulate(const float* dy, const float* x, const float* m
                         workspace_bytes, 1, stream);
 }
 
+int pa_add_layer_norm_bwd(const float* dy, const float* dsum, const float* sum,
+                          const float* mean, const float* rstd, const float* gamma, float* dx,
+                          float* dr, float* dgamma, float* dbeta, uint32_t M, uint32_t N,
+                          int flags, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  if (!dy || !sum || !mean || !rstd || !gamma) return PA_ERR_NULL;
+  if (M == 0 || N == 0) return PA_ERR_SHAPE;
+  if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
+  if ((flags & ~(PA_ADD_LN_ACC_DX | PA_ADD_LN_ACC_DR)) != 0) return PA_ERR_SHAPE;
+  if (!al16(dy) || !al16(sum) || !al16(gamma) || (dsum && !al16(dsum)) || (dx && !al16(dx)) ||
+      (dr && !al16(dr)))
+    return PA_ERR_ALIGN;
+  if ((dgamma || dbeta) &&
+      (!workspace || workspace_bytes < pa::layer_norm_bwd_workspace_bytes(M, N)))
+    return PA_ERR_WORKSPACE;
+  return pa::launch_add_layer_norm_bwd(dy, dsum, sum, mean, rstd, gamma, dx,
+                                       (flags & PA_ADD_LN_ACC_DX) ? 1 : 0, dr,
+                                       (flags & PA_ADD_LN_ACC_DR) ? 1 : 0, dgamma, dbeta, M, N,
+                                       static_cast<float*>(workspace),
+                                       static_cast<cudaStream_t>(stream));
+}
+
 size_t pa_matmul_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   return pa::gemm_workspace_bytes(M, N, K);
@@ -361,9 +382,10 @@ int pa_linear_fwd_keep(const float* X, const float* W, const float* bias, float*
 int pa_linear_bwd_kept(const float* X, const float* W, const void* kept, size_t kept_bytes,
                        int kept_mode, const float* Y, const float* const* dy_parts, int n_parts,
                        float* dX, float* dW, float* dbias, int M, int in_features,
-                       int out_features, void* workspace, size_t workspace_bytes,
+                       int out_features, int flags, void* workspace, size_t workspace_bytes,
                        pa_stream_t stream) {
   if (!X || !W || !dy_parts) return PA_ERR_NULL;
+  if ((flags & ~PA_LINEAR_DX_OVERWRITE) != 0) return PA_ERR_SHAPE;
   const int st = linear_check(M, in_features, out_features, n_parts, workspace, workspace_bytes);
   if (st != PA_OK) return st;
   if (Y && n_parts != 1) return PA_ERR_SHAPE;
@@ -378,7 +400,8 @@ int pa_linear_bwd_kept(const float* X, const float* W, const void* kept, size_t 
   if (!status) return PA_ERR_DEVICE;
   return pa::launch_linear_bwd(X, W, dy_parts, n_parts, Y, dX, dW, dbias, M, in_features,
                                out_features, workspace, status, static_cast<cudaStream_t>(stream),
-                               usable ? kept : nullptr);
+                               usable ? kept : nullptr,
+                               (flags & PA_LINEAR_DX_OVERWRITE) ? 0 : 1);
 }
 
 int pa_linear_relu_bwd(const float* X, const float* W, const float* Y, const float* dY, float* dX,

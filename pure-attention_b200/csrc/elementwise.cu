@@ -7,6 +7,7 @@
 //   split / concat    split_forward_kernel.cu:4-21, split_backward_kernel.cu:4-22
 // Vectorised with 16-byte accesses where the sizes allow; grids are sized in
 // multiples of the SM count with grid-stride loops.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "host_launchers.h"
@@ -117,6 +118,62 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// colsum_partial_kernel fused with the bf16 gather of the same values: the
+// projection backward's dY column block [M, D] (zero where mask <= 0) goes to
+// columns [c0, c0 + Dp) of the hi (and lo) planes with row pitch ldp, columns
+// D..Dp-1 as zeros, and its fp32 column sums per row chunk to part[y][D], in
+// the same order as colsum_partial_kernel (so the bias gradient is the same
+// bits). One read of dY (and the mask) serves both.
+__global__ void __launch_bounds__(256)
+    split_colsum_kernel(const float* __restrict__ dy, const float* __restrict__ mask,
+                        __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
+                        float* __restrict__ part, uint32_t M, uint32_t D, uint32_t Dp, size_t ldp,
+                        uint32_t c0, uint32_t rows_per) {
+  __shared__ float4 red[8][32];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t c = (blockIdx.x * 32 + lane) * 4;
+  const uint32_t r0 = blockIdx.y * rows_per, r1 = min(M, r0 + rows_per);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c < Dp) {
+#pragma unroll 4
+    for (uint32_t r = r0 + warp; r < r1; r += 8) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < D) {
+        v = *reinterpret_cast<const float4*>(dy + static_cast<size_t>(r) * D + c);
+        if (mask) {
+          const float4 m = *reinterpret_cast<const float4*>(mask + static_cast<size_t>(r) * D + c);
+          v.x = m.x > 0.f ? v.x : 0.f;
+          v.y = m.y > 0.f ? v.y : 0.f;
+          v.z = m.z > 0.f ? v.z : 0.f;
+          v.w = m.w > 0.f ? v.w : 0.f;
+        }
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      const uint32_t h01 = pack_bf16x2(v.x, v.y), h23 = pack_bf16x2(v.z, v.w);
+      const size_t o = static_cast<size_t>(r) * ldp + c0 + c;
+      *reinterpret_cast<uint2*>(hi + o) = make_uint2(h01, h23);
+      if (lo) {
+        const uint32_t l01 = pack_bf16x2(v.x - __uint_as_float(h01 << 16),
+                                         v.y - __uint_as_float(h01 & 0xffff0000u));
+        const uint32_t l23 = pack_bf16x2(v.z - __uint_as_float(h23 << 16),
+                                         v.w - __uint_as_float(h23 & 0xffff0000u));
+        *reinterpret_cast<uint2*>(lo + o) = make_uint2(l01, l23);
+      }
+    }
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < D) {
+    float4 t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 v = red[w][lane];
+      t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+    }
+    *reinterpret_cast<float4*>(part + static_cast<size_t>(blockIdx.y) * D + c) = t;
+  }
+}
+
 struct PtrPack {
   float* p[8];
 };
@@ -216,6 +273,30 @@ int launch_bias_grad_masked(const float* dy, const float* mask, float* db, uint3
   }
   colsum_partial_kernel<<<dim3((N + 127) / 128, R), 256, 0, s>>>(dy, mask, ws, M, N, rows_per);
   bias_grad_kernel<<<(N + 31) / 32, 1024, 0, s>>>(ws, nullptr, db, R, N);
+  return done();
+}
+
+// The masked bf16 gather of launch_split_planes_masked and the bias gradient of
+// launch_bias_grad_masked over the same dY block, in one read of dY: db[0, D)
+// += column sums, planes as launch_split_planes_masked writes them. Shapes or
+// alignments the fused kernel does not take run the two launches instead.
+int launch_split_planes_colsum(const float* dy, const float* mask, void* hi, void* lo,
+                               uint32_t M, int D, int Dp, size_t ldp, int c0, float* db,
+                               float* ws, cudaStream_t s) {
+  if (D > Dp || D <= 0 || c0 < 0 || static_cast<size_t>(c0) + Dp > ldp) return PA_ERR_SHAPE;
+  uint32_t R = 1;
+  const uint32_t rows_per = colsum_chunks(M, static_cast<uint32_t>(D), &R);
+  if (!ws || D % 4 != 0 || Dp % 4 != 0 || c0 % 4 != 0 || ldp % 4 != 0 || !al16(dy) ||
+      (mask && !al16(mask)) || !al16(ws) || R < 2) {
+    const int st = launch_split_planes_masked(dy, mask, hi, lo, M, D, Dp, ldp, c0, s);
+    if (st != PA_OK) return st;
+    return launch_bias_grad_masked(dy, mask, db, M, static_cast<uint32_t>(D), ws, s);
+  }
+  split_colsum_kernel<<<dim3((Dp + 127) / 128, R), 256, 0, s>>>(
+      dy, mask, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), ws, M,
+      static_cast<uint32_t>(D), static_cast<uint32_t>(Dp), ldp, static_cast<uint32_t>(c0),
+      rows_per);
+  bias_grad_kernel<<<(D + 31) / 32, 1024, 0, s>>>(ws, nullptr, db, R, static_cast<uint32_t>(D));
   return done();
 }
 

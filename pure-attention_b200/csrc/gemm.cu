@@ -437,8 +437,9 @@ int split_into(const float* x, const Planes& p, cudaStream_t s) {
 }
 
 // GEMM of `mode` (see launch_gemm_f32) on operands already split into planes.
+// Modes 1 and 2 add into C unless accumulate is 0, when they overwrite it.
 int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int N, int K,
-                const Epilogue& ep, uint32_t* status, cudaStream_t s) {
+                const Epilogue& ep, uint32_t* status, cudaStream_t s, int accumulate = 1) {
   const bool a_mn = (mode == 2), b_mn = (mode != 1);
   // persistent 128 x 256 kernel: maps A hi, A lo, B hi, B lo (A boxes of 128 rows, B of 256)
   {
@@ -454,14 +455,15 @@ int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int
                !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn, 256)) {
       return PA_ERR_ALIGN;
     }
+    const int acc = accumulate ? 1 : 0;
     if (one) {
       if (mode == 0) return run_gemm_persist<false, true, 1>(m, C, N, M, N, K, 0, ep, status, s);
-      if (mode == 1) return run_gemm_persist<false, false, 1>(m, C, N, M, N, K, 1, ep, status, s);
-      return run_gemm_persist<true, true, 1>(m, C, K, N, K, M, 1, ep, status, s);
+      if (mode == 1) return run_gemm_persist<false, false, 1>(m, C, N, M, N, K, acc, ep, status, s);
+      return run_gemm_persist<true, true, 1>(m, C, K, N, K, M, acc, ep, status, s);
     }
     if (mode == 0) return run_gemm_persist<false, true, 3>(m, C, N, M, N, K, 0, ep, status, s);
-    if (mode == 1) return run_gemm_persist<false, false, 3>(m, C, N, M, N, K, 1, ep, status, s);
-    return run_gemm_persist<true, true, 3>(m, C, K, N, K, M, 1, ep, status, s);
+    if (mode == 1) return run_gemm_persist<false, false, 3>(m, C, N, M, N, K, acc, ep, status, s);
+    return run_gemm_persist<true, true, 3>(m, C, K, N, K, M, acc, ep, status, s);
   }
 }
 
@@ -541,7 +543,8 @@ int launch_linear_fwd(const float* x, const float* wt, const float* bias, float*
 
 int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_parts, int n_parts,
                       const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
-                      int OUT, void* ws, uint32_t* status, cudaStream_t s, const void* kept) {
+                      int OUT, void* ws, uint32_t* status, cudaStream_t s, const void* kept,
+                      int dx_accumulate) {
   uint8_t* w = static_cast<uint8_t*>(ws);
   const Planes dy = carve(w, M, OUT), wp = carve(w, IN, OUT);
   Planes xp = carve(w, M, IN);
@@ -550,20 +553,27 @@ int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_pa
     xp = Planes{kp, kp + plane_size(M, IN), M, IN};
   }
   float* bias_ws = reinterpret_cast<float*>(w);  // bias_partials_bytes(M, OUT)
-  // gather the column-block gradients into one pair of planes (row pitch round8(OUT))
+  // gather the column-block gradients into one pair of planes (row pitch
+  // round8(OUT)), with the bias gradient summed in the same pass over dY
   const int part = OUT / n_parts;
+  void* dy_lo = f32_math() == PA_F32_MATH_BF16 ? nullptr : dy.lo;
   for (int p = 0; p < n_parts; ++p) {
     const int width = p + 1 < n_parts ? part : round8(OUT) - p * part;  // last block takes the pad
-    const int st = launch_split_planes_masked(
-        dy_parts[p], relu_out, dy.hi,  // relu_out: single-part projections only
-        f32_math() == PA_F32_MATH_BF16 ? nullptr : dy.lo, static_cast<size_t>(M), part, width,
-        static_cast<size_t>(round8(OUT)), p * part, s);
+    // relu_out: single-part projections only
+    const int st =
+        dbias ? launch_split_planes_colsum(dy_parts[p], relu_out, dy.hi, dy_lo,
+                                           static_cast<uint32_t>(M), part, width,
+                                           static_cast<size_t>(round8(OUT)), p * part,
+                                           dbias + p * part, bias_ws, s)
+              : launch_split_planes_masked(dy_parts[p], relu_out, dy.hi, dy_lo,
+                                           static_cast<size_t>(M), part, width,
+                                           static_cast<size_t>(round8(OUT)), p * part, s);
     if (st != PA_OK) return st;
   }
   if (dx) {
     int st = split_into(wt, wp, s);
     if (st != PA_OK) return st;
-    st = gemm_planes(1, dy, wp, dx, M, IN, OUT, Epilogue{}, status, s);
+    st = gemm_planes(1, dy, wp, dx, M, IN, OUT, Epilogue{}, status, s, dx_accumulate);
     if (st != PA_OK) return st;
   }
   if (dw) {
@@ -572,13 +582,6 @@ int launch_linear_bwd(const float* x, const float* wt, const float* const* dy_pa
     st = gemm_planes(2, xp, dy, dw, M, IN, OUT, Epilogue{}, status, s);
     if (st != PA_OK) return st;
   }
-  if (dbias)
-    for (int p = 0; p < n_parts; ++p) {
-      const int st = launch_bias_grad_masked(dy_parts[p], relu_out, dbias + p * part,
-                                             static_cast<uint32_t>(M), static_cast<uint32_t>(part),
-                                             bias_ws, s);
-      if (st != PA_OK) return st;
-    }
   return PA_OK;
 }
 

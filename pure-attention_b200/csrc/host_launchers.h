@@ -56,6 +56,12 @@ size_t layer_norm_bwd_workspace_bytes(uint32_t M, uint32_t N);
 int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, const float* rs,
                           const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,
                           float* part, int accumulate_dx, cudaStream_t s);
+// Backward of sum = x + r, y = LN(sum): dx (+)= G and dr (+)= G with
+// G = LN_bwd(dy) + dsum (dsum may be null; dx or dr may be null).
+int launch_add_layer_norm_bwd(const float* dy, const float* dsum, const float* x, const float* mu,
+                              const float* rs, const float* g, float* dx, int acc_dx, float* dr,
+                              int acc_dr, float* dg, float* db, uint32_t M, uint32_t N,
+                              float* part, cudaStream_t s);
 
 // elementwise.cu
 int launch_bias_add(const float* a, const float* bias, float* out, uint32_t M, uint32_t N,
@@ -66,6 +72,11 @@ int launch_bias_grad(const float* dy, float* db, uint32_t M, uint32_t N, cudaStr
 size_t bias_grad_workspace_bytes(uint32_t M, uint32_t N);
 int launch_bias_grad_masked(const float* dy, const float* mask, float* db, uint32_t M, uint32_t N,
                             float* ws, cudaStream_t s);
+// launch_split_planes_masked of dy [M, D] and db += its (masked) column sums,
+// in one pass over dy when the shapes allow (ws: bias_grad_workspace_bytes(M, D)).
+int launch_split_planes_colsum(const float* dy, const float* mask, void* hi, void* lo,
+                               uint32_t M, int D, int Dp, size_t ldp, int c0, float* db,
+                               float* ws, cudaStream_t s);
 int launch_split_last_dim(const float* in, float* const* outs, uint32_t parts, uint32_t rows,
                           uint32_t width, cudaStream_t s);
 int launch_concat_last_dim_grad(const float* const* grads, float* grad_in, uint32_t parts,
@@ -92,7 +103,7 @@ int launch_linear_fwd(const float* x, const float* w, const float* bias, float* 
 int launch_linear_bwd(const float* x, const float* w, const float* const* dy_parts, int n_parts,
                       const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
                       int OUT, void* ws, uint32_t* status, cudaStream_t s,
-                      const void* kept = nullptr);
+                      const void* kept = nullptr, int dx_accumulate = 1);
 size_t linear_kept_bytes(int M, int IN, int mode);
 
 // training.cu

@@ -174,6 +174,100 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
   }
 }
 
+// Backward of sum = x + r, y = LN(sum): G = LN_bwd(dY) + dS, with dS the
+// gradient that reached the sum from its other consumers (null: none), goes
+// to both addends' gradients in one pass: dx = G (+ old dx when acc_dx), dr =
+// G (+ old dr when acc_dr); either may be null, and they may be the same
+// buffer (x + x), which then receives 2G. dgamma / dbeta partials as in
+// ln_bwd_kernel. dS and the old gradients are read only when the row is
+// written, so the registers held across the row reductions are ln_bwd_kernel's.
+template <int VPL>
+__global__ void __launch_bounds__(LN_WARPS * 32)
+    add_ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ dsum,
+                      const float* __restrict__ x, const float* __restrict__ mean,
+                      const float* __restrict__ rstd, const float* __restrict__ gamma, float* dx,
+                      int acc_dx, float* dr, int acc_dr, float* __restrict__ part, uint32_t M,
+                      uint32_t N) {
+  extern __shared__ float red[];  // [LN_WARPS][2][N] when part != nullptr
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  const uint32_t nvec = N / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  float4* rg = reinterpret_cast<float4*>(red + static_cast<size_t>(warp) * 2 * N);
+  float4* rb = reinterpret_cast<float4*>(red + static_cast<size_t>(warp) * 2 * N + N);
+  if (part)
+    for (uint32_t c = lane; c < nvec; c += 32) rg[c] = rb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float inv_n = 1.f / N;
+  const float fn = static_cast<float>(N);
+  auto add4 = [](float4 a, const float4 b) {
+    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    return a;
+  };
+  for (uint32_t row = blockIdx.x * LN_WARPS + warp; row < M; row += gridDim.x * LN_WARPS) {
+    const size_t off = static_cast<size_t>(row) * N;
+    const float4* xr = reinterpret_cast<const float4*>(x + off);
+    const float4* dyr = reinterpret_cast<const float4*>(dy + off);
+    const float4* dsr = dsum ? reinterpret_cast<const float4*>(dsum + off) : nullptr;
+    float4* xo = dx ? reinterpret_cast<float4*>(dx + off) : nullptr;
+    float4* ro = dr ? reinterpret_cast<float4*>(dr + off) : nullptr;
+    float4 xv[VPL], dv[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const uint32_t c = lane + 32 * i;
+      const bool in = c < nvec;
+      xv[i] = in ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      dv[i] = in ? dyr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float mu = mean[row], rs = rstd[row];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const uint32_t c = lane + 32 * i;
+      if (c < nvec) {
+        const float4 g = g4[c];
+        const float t0 = dv[i].x * g.x, t1 = dv[i].y * g.y, t2 = dv[i].z * g.z, t3 = dv[i].w * g.w;
+        s1 += (t0 + t1) + (t2 + t3);
+        s2 += (t0 * (xv[i].x - mu) + t1 * (xv[i].y - mu)) + (t2 * (xv[i].z - mu) + t3 * (xv[i].w - mu));
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2) * rs;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const uint32_t c = lane + 32 * i;
+      if (c < nvec) {
+        const float4 g = g4[c];
+        const float h0 = (xv[i].x - mu) * rs, h1 = (xv[i].y - mu) * rs;
+        const float h2 = (xv[i].z - mu) * rs, h3 = (xv[i].w - mu) * rs;
+        if (xo || ro) {
+          float4 o = make_float4((fn * dv[i].x * g.x - s1 - h0 * s2) * rs * inv_n,
+                                 (fn * dv[i].y * g.y - s1 - h1 * s2) * rs * inv_n,
+                                 (fn * dv[i].z * g.z - s1 - h2 * s2) * rs * inv_n,
+                                 (fn * dv[i].w * g.w - s1 - h3 * s2) * rs * inv_n);
+          if (dsr) o = add4(o, dsr[c]);
+          if (xo) xo[c] = acc_dx ? add4(o, xo[c]) : o;
+          if (ro) ro[c] = acc_dr ? add4(o, ro[c]) : o;
+        }
+        if (part) {
+          float4 a = rg[c], b = rb[c];
+          a.x += dv[i].x * h0; a.y += dv[i].y * h1; a.z += dv[i].z * h2; a.w += dv[i].w * h3;
+          b.x += dv[i].x; b.y += dv[i].y; b.z += dv[i].z; b.w += dv[i].w;
+          rg[c] = a;
+          rb[c] = b;
+        }
+      }
+    }
+  }
+  if (!part) return;
+  __syncthreads();
+  float* out = part + static_cast<size_t>(blockIdx.x) * 2 * N;
+  for (uint32_t c = threadIdx.x; c < 2 * N; c += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < LN_WARPS; ++w) acc += red[static_cast<size_t>(w) * 2 * N + c];
+    out[c] = acc;
+  }
+}
+
 // dgamma[c] += sum_b part[b][0][c]; dbeta[c] += sum_b part[b][1][c] (fixed
 // order). CTA = 32 of the 2N columns x 32 lanes over the partial rows.
 __global__ void __launch_bounds__(1024)
@@ -248,6 +342,27 @@ int ln_bwd_launch(const float* dy, const float* x, const float* mu, const float*
   return PA_OK;
 }
 
+template <int VPL>
+int add_ln_bwd_launch(const float* dy, const float* dsum, const float* x, const float* mu,
+                      const float* rs, const float* g, float* dx, int acc_dx, float* dr, int acc_dr,
+                      float* dg, float* db, uint32_t M, uint32_t N, float* part, cudaStream_t s) {
+  const uint32_t blocks = ln_bwd_blocks(M, N);
+  const size_t smem = static_cast<size_t>(LN_WARPS) * 2 * N * sizeof(float);
+  float* p = (dg || db) ? part : nullptr;
+  static std::atomic<uint64_t> attr{0};
+  if (!ensure_smem_attr(add_ln_bwd_kernel<VPL>, static_cast<int>(LN_WARPS * 2 * 128 * VPL * 4),
+                        attr))
+    return PA_ERR_LAUNCH;
+  add_ln_bwd_kernel<VPL><<<blocks, LN_WARPS * 32, p ? smem : 0, s>>>(
+      dy, dsum, x, mu, rs, g, dx, acc_dx, dr, acc_dr, p, M, N);
+  if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
+  if (dg || db) {
+    ln_param_reduce_kernel<<<(2 * N + 31) / 32, 1024, 0, s>>>(part, dg, db, blocks, N);
+    if (cudaGetLastError() != cudaSuccess) return PA_ERR_LAUNCH;
+  }
+  return PA_OK;
+}
+
 }  // namespace
 
 // r == nullptr: y = LN(x); else sum = x + r and y = LN(sum).
@@ -274,6 +389,21 @@ int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, cons
   if (N <= 256) return ln_bwd_launch<2>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
   if (N <= 512) return ln_bwd_launch<4>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
   if (N <= 1024) return ln_bwd_launch<8>(dy, x, mu, rs, g, dx, dg, db, M, N, part, acc, s);
+  return PA_ERR_UNSUPPORTED;
+}
+
+int launch_add_layer_norm_bwd(const float* dy, const float* dsum, const float* x, const float* mu,
+                              const float* rs, const float* g, float* dx, int acc_dx, float* dr,
+                              int acc_dr, float* dg, float* db, uint32_t M, uint32_t N,
+                              float* part, cudaStream_t s) {
+  if (N <= 128)
+    return add_ln_bwd_launch<1>(dy, dsum, x, mu, rs, g, dx, acc_dx, dr, acc_dr, dg, db, M, N, part, s);
+  if (N <= 256)
+    return add_ln_bwd_launch<2>(dy, dsum, x, mu, rs, g, dx, acc_dx, dr, acc_dr, dg, db, M, N, part, s);
+  if (N <= 512)
+    return add_ln_bwd_launch<4>(dy, dsum, x, mu, rs, g, dx, acc_dx, dr, acc_dr, dg, db, M, N, part, s);
+  if (N <= 1024)
+    return add_ln_bwd_launch<8>(dy, dsum, x, mu, rs, g, dx, acc_dx, dr, acc_dr, dg, db, M, N, part, s);
   return PA_ERR_UNSUPPORTED;
 }
 

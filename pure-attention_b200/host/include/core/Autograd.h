@@ -116,4 +116,44 @@ struct LayerNormFunction : public Function {
   std::vector<std::shared_ptr<Tensor>> inputs() const override { return {input, gamma, beta}; }
 };
 
+// Backward of core::add_layer_norm: sum = x + r, out = LayerNorm(sum). This
+// node is sum's grad_fn, so it runs after every consumer of sum; out's grad_fn
+// is a LayerNormOutFunction, which runs after every consumer of out and hands
+// out's gradient to this node. The node then writes G = LN_bwd(dout) + dsum
+// (dsum: the gradient sum received from its other consumers) straight into
+// x's and r's gradients (pa_add_layer_norm_bwd): the sum's own gradient is
+// never formed, and no separate add pass runs.
+struct AddLayerNormFunction : public Function {
+  std::shared_ptr<Tensor> x_input;
+  std::shared_ptr<Tensor> r_input;
+  std::shared_ptr<Tensor> gamma;
+  std::shared_ptr<Tensor> beta;
+  std::shared_ptr<Tensor> mean;
+  std::shared_ptr<Tensor> rstd;
+  std::weak_ptr<Tensor> sum_output;
+  uint32_t M;
+  uint32_t N;
+  // out, set by out's node in the current backward when a gradient reached it
+  std::shared_ptr<Tensor> pending_out;
+  AddLayerNormFunction(const std::shared_ptr<Tensor>& x, const std::shared_ptr<Tensor>& r,
+                       const std::shared_ptr<Tensor>& g, const std::shared_ptr<Tensor>& b,
+                       const std::shared_ptr<Tensor>& sum, const std::shared_ptr<Tensor>& m,
+                       const std::shared_ptr<Tensor>& rs, uint32_t m_size, uint32_t n_size);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override {
+    return {x_input, r_input, gamma, beta};
+  }
+};
+
+// out's node in core::add_layer_norm: holds the sum (whose values the
+// backward reads) and passes out's gradient to the sum's AddLayerNormFunction,
+// which runs after it.
+struct LayerNormOutFunction : public Function {
+  std::shared_ptr<Tensor> sum;
+  std::weak_ptr<Tensor> output;
+  LayerNormOutFunction(const std::shared_ptr<Tensor>& s, const std::shared_ptr<Tensor>& out);
+  void apply_backward() override;
+  std::vector<std::shared_ptr<Tensor>> inputs() const override { return {sum}; }
+};
+
 }  // namespace core

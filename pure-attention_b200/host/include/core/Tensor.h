@@ -1,7 +1,11 @@
 // core::Tensor - fp32 device tensor with an optional gradient and a link to the
 // graph node that produced it. Same interface as the reference's
 // include/core/Tensor.h:22-53; storage is stream-ordered (cudaMallocAsync on
-// the context stream) and gradients start at zero.
+// the context stream) and gradients start at zero. A leaf's gradient is zeroed
+// when it is allocated; an op output's is zeroed only when something first
+// reads it or adds to it, and a graph node that writes every element of it
+// first overwrites it instead, so most activations' gradients are written
+// once and never memset.
 #pragma once
 #include <cstdint>
 #include <functional>
@@ -31,7 +35,15 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
 
   bool requires_grad() const { return requires_gradient; }
   bool leaf() const { return is_leaf; }
-  float32_t* get_gradient_ptr() const { return gradient_ptr; }
+  // The gradient buffer, zeroed first if nothing has written it yet.
+  float32_t* get_gradient_ptr() const;
+  // For a graph node that writes the whole gradient: the buffer, and in
+  // *unwritten whether nothing has written it yet - its contents are then
+  // undefined (it stands for zero), and the node must overwrite every element
+  // rather than add. Afterwards the gradient counts as written.
+  float32_t* gradient_for_write(bool* unwritten) const;
+  // True while the gradient stands for zero without having been written.
+  bool gradient_unwritten() const { return grad_unwritten; }
   void set_grad_fn(std::shared_ptr<Function> fn);
   std::shared_ptr<Function> grad_fn() const { return grad_function; }
   void zero_grad() const;
@@ -62,6 +74,7 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
   bool requires_gradient = false;
   bool is_leaf = true;
   bool owns_gradient = true;
+  mutable bool grad_unwritten = false;
   std::shared_ptr<Function> grad_function;
 };
 

@@ -1,6 +1,7 @@
 #include "core/Autograd.h"
 
 #include <stdexcept>
+#include <string>
 
 #include "device_util.h"
 
@@ -9,6 +10,26 @@ namespace core {
 namespace {
 cudaStream_t stream() { return CudaContext::getStream(); }
 size_t rows_of(const Tensor& t) { return t.numel() / last_dim(t); }
+
+// The gradient that reached an output, or null when none did (the tensor has
+// expired, has no gradient, or nothing has written its gradient: zero).
+const float* grad_in(const std::shared_ptr<Tensor>& t) {
+  if (!t || !t->requires_grad() || t->gradient_unwritten()) return nullptr;
+  return t->get_gradient_ptr();
+}
+
+// t.grad += src (n floats), as a copy when nothing has written t.grad yet.
+void add_into(const Tensor& t, const float* src, size_t n, const char* what) {
+  bool unwritten = false;
+  float* dst = t.gradient_for_write(&unwritten);
+  if (unwritten) {
+    if (cudaMemcpyAsync(dst, src, n * sizeof(float), cudaMemcpyDeviceToDevice, stream()) !=
+        cudaSuccess)
+      throw std::runtime_error(std::string(what) + ": cudaMemcpyAsync failed");
+    return;
+  }
+  check_status(pa_grad_accumulate(src, dst, n, ps(stream())), what);
+}
 }  // namespace
 
 MatMulFunction::MatMulFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> w,
@@ -18,7 +39,7 @@ MatMulFunction::MatMulFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor
 // X [..., in] flattened to M rows, W [in, out]: dX += dY W^T, dW += X^T dY.
 void MatMulFunction::apply_backward() {
   auto Y = Y_output.lock();
-  if (!Y || !Y->get_gradient_ptr()) return;
+  if (!grad_in(Y)) return;
   const int in = static_cast<int>(W_input->get_shape()[0]);
   const int out = static_cast<int>(W_input->get_shape()[1]);
   const int M = static_cast<int>(rows_of(*X_input));
@@ -41,17 +62,13 @@ AddFunction::AddFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor> bias
 
 void AddFunction::apply_backward() {
   auto Y = Y_output.lock();
-  if (!Y || !Y->get_gradient_ptr()) return;
+  const float* dy = grad_in(Y);
+  if (!dy) return;
   const size_t n = Y->numel();
-  if (X_input->requires_grad())
-    check_status(pa_grad_accumulate(Y->get_gradient_ptr(), X_input->get_gradient_ptr(), n,
-                                    ps(stream())),
-                 "add grad");
+  if (X_input->requires_grad()) add_into(*X_input, dy, n, "add grad");
   if (bias_input->requires_grad()) {
     if (bias_input->numel() == n) {
-      check_status(pa_grad_accumulate(Y->get_gradient_ptr(), bias_input->get_gradient_ptr(), n,
-                                      ps(stream())),
-                   "add grad");
+      add_into(*bias_input, dy, n, "add grad");
     } else {
       const int N = static_cast<int>(bias_input->numel());
       const int M = static_cast<int>(n / N);
@@ -68,7 +85,7 @@ ReLUFunction::ReLUFunction(std::shared_ptr<Tensor> in, std::shared_ptr<Tensor> o
 
 void ReLUFunction::apply_backward() {
   auto Y = Output.lock();
-  if (!Y || !Y->get_gradient_ptr() || !Input->requires_grad()) return;
+  if (!grad_in(Y) || !Input->requires_grad()) return;
   check_status(pa_relu_bwd(Y->get_gradient_ptr(), Input->get_data_ptr(), Input->get_gradient_ptr(),
                            Input->numel(), ps(stream())),
                "relu backward");
@@ -80,7 +97,7 @@ MSEFunction::MSEFunction(const std::shared_ptr<Tensor>& preds, const std::shared
 
 void MSEFunction::apply_backward() {
   auto L = output_loss.lock();
-  if (!L || !L->get_gradient_ptr() || !predictions->requires_grad()) return;
+  if (!grad_in(L) || !predictions->requires_grad()) return;
   check_status(pa_mse_bwd(predictions->get_data_ptr(), targets->get_data_ptr(),
                           L->get_gradient_ptr(), predictions->get_gradient_ptr(),
                           predictions->numel(), ps(stream())),
@@ -94,34 +111,24 @@ LinearFunction::LinearFunction(std::shared_ptr<Tensor> x, std::shared_ptr<Tensor
       Outputs(outs.begin(), outs.end()), relu(relu_) {}
 
 // dX += dY W^T, dW += X^T dY, dbias += column sums of dY, with dY the column
-// blocks' gradients (a block whose tensor has expired contributes zero).
+// blocks' gradients (a block whose tensor has expired, or that no gradient
+// reached, contributes zero). dX is written outright when nothing has written
+// it yet.
 void LinearFunction::apply_backward() {
   const int K = static_cast<int>(W_input->get_shape()[0]);
   const int N = static_cast<int>(W_input->get_shape()[1]);
   const int M = static_cast<int>(rows_of(*X_input));
   const int parts = static_cast<int>(Outputs.size());
   const size_t part_bytes = static_cast<size_t>(M) * (N / parts) * sizeof(float);
-  float* dX = X_input->requires_grad() ? X_input->get_gradient_ptr() : nullptr;
-  float* dW = W_input->requires_grad() ? W_input->get_gradient_ptr() : nullptr;
-  float* db = bias_input->requires_grad() ? bias_input->get_gradient_ptr() : nullptr;
-  if (relu) {  // the saved output's sign masks its gradient inside the call
-    auto Y = Outputs[0].lock();
-    if (!Y || !Y->get_gradient_ptr()) return;
-    Scratch ws(pa_linear_workspace_size(M, K, N), stream());
-    const float* dy = Y->get_gradient_ptr();
-    check_status(pa_linear_bwd_kept(X_input->get_data_ptr(), W_input->get_data_ptr(), kept.get(),
-                                    kept_bytes, kept_mode, Y->get_data_ptr(), &dy, 1, dX, dW, db,
-                                    M, K, N, ws.get(), ws.size(), ps(stream())),
-                 "linear + ReLU backward");
-    return;
-  }
   std::vector<const float*> grads;
   std::vector<std::unique_ptr<Scratch>> zeros;
+  std::shared_ptr<Tensor> Y0;
   bool any = false;
   for (auto& w : Outputs) {
     auto t = w.lock();
-    if (t && t->get_gradient_ptr()) {
-      grads.push_back(t->get_gradient_ptr());
+    if (!Y0) Y0 = t;
+    if (const float* g = grad_in(t)) {
+      grads.push_back(g);
       any = true;
     } else {
       zeros.push_back(std::make_unique<Scratch>(part_bytes, stream()));
@@ -130,11 +137,18 @@ void LinearFunction::apply_backward() {
     }
   }
   if (!any) return;
+  // the saved ReLU output's sign masks its gradient inside the call
+  const float* y = relu ? Y0->get_data_ptr() : nullptr;
+  bool dx_unwritten = false;
+  float* dX = X_input->requires_grad() ? X_input->gradient_for_write(&dx_unwritten) : nullptr;
+  float* dW = W_input->requires_grad() ? W_input->get_gradient_ptr() : nullptr;
+  float* db = bias_input->requires_grad() ? bias_input->get_gradient_ptr() : nullptr;
   Scratch ws(pa_linear_workspace_size(M, K, N), stream());
   check_status(pa_linear_bwd_kept(X_input->get_data_ptr(), W_input->get_data_ptr(), kept.get(),
-                                  kept_bytes, kept_mode, nullptr, grads.data(), parts, dX, dW, db,
-                                  M, K, N, ws.get(), ws.size(), ps(stream())),
-               "linear backward");
+                                  kept_bytes, kept_mode, y, grads.data(), parts, dX, dW, db, M, K,
+                                  N, dx_unwritten ? PA_LINEAR_DX_OVERWRITE : 0, ws.get(),
+                                  ws.size(), ps(stream())),
+               relu ? "linear + ReLU backward" : "linear backward");
 }
 
 SplitFunction::SplitFunction(std::shared_ptr<Tensor> in, std::vector<std::shared_ptr<Tensor>> outs)
@@ -146,7 +160,7 @@ void SplitFunction::apply_backward() {
   uint32_t width = 0;
   for (auto& w : Outputs) {
     auto t = w.lock();
-    grads.push_back(t ? t->get_gradient_ptr() : nullptr);  // expired part: zero gradient
+    grads.push_back(grad_in(t));  // expired or unreached part: zero gradient
     if (t) width = static_cast<uint32_t>(last_dim(*t));
   }
   if (width == 0) return;
@@ -164,11 +178,14 @@ FlashAttentionFunction::FlashAttentionFunction(const std::shared_ptr<Tensor>& q,
                                                const std::shared_ptr<Tensor>& lcache, int heads)
     : Q_input(q), K_input(k), V_input(v), O_output(o), L_cache(lcache), num_heads(heads) {}
 
-// Gradients are added straight into Q/K/V's grads (accumulate = 1): no
-// temporaries, unlike the reference's three cudaMallocAsync'd buffers.
+// Gradients go straight into Q/K/V's grads: written outright when nothing
+// has written any of them yet (accumulate = 0), else added (accumulate = 1,
+// after zeroing those still unwritten). No temporaries, unlike the
+// reference's three cudaMallocAsync'd buffers.
 void FlashAttentionFunction::apply_backward() {
   auto O = O_output.lock();
-  if (!O || !O->get_gradient_ptr()) return;
+  const float* dO = grad_in(O);
+  if (!dO) return;
   const auto sh = Q_input->get_shape();
   pa_attn_desc d{static_cast<int32_t>(sh[0]), static_cast<int32_t>(sh[1]), num_heads,
                  static_cast<int32_t>(sh[2]) / num_heads, PA_F32, 0.f};
@@ -179,13 +196,26 @@ void FlashAttentionFunction::apply_backward() {
                    ? 0
                    : n * sizeof(float),
                stream());
-  auto g = [&](const std::shared_ptr<Tensor>& t) {
-    return t->requires_grad() ? static_cast<void*>(t->get_gradient_ptr()) : sink.get();
-  };
+  const std::shared_ptr<Tensor>* qkv[3] = {&Q_input, &K_input, &V_input};
+  void* dst[3];
+  bool unwritten[3] = {false, false, false};
+  bool all_unwritten = true;
+  for (int i = 0; i < 3; ++i) {
+    const Tensor& t = **qkv[i];
+    if (t.requires_grad()) {
+      dst[i] = t.gradient_for_write(&unwritten[i]);
+      all_unwritten = all_unwritten && unwritten[i];
+    } else {
+      dst[i] = sink.get();
+    }
+  }
+  if (!all_unwritten)
+    for (int i = 0; i < 3; ++i)
+      if (unwritten[i]) cudaMemsetAsync(dst[i], 0, n * sizeof(float), stream());
   check_status(pa_attn_bwd(&d, Q_input->get_data_ptr(), K_input->get_data_ptr(),
-                           V_input->get_data_ptr(), O->get_data_ptr(), O->get_gradient_ptr(),
-                           L_cache->get_data_ptr(), g(Q_input), g(K_input), g(V_input), 1, ws.get(),
-                           ws.size(), ps(stream())),
+                           V_input->get_data_ptr(), O->get_data_ptr(), dO,
+                           L_cache->get_data_ptr(), dst[0], dst[1], dst[2], all_unwritten ? 0 : 1,
+                           ws.get(), ws.size(), ps(stream())),
                "FlashAttention Backward");
 }
 
@@ -200,19 +230,68 @@ LayerNormFunction::LayerNormFunction(const std::shared_ptr<Tensor>& inp,
 
 // dX is accumulated by the kernel into the input's gradient, which may
 // already hold a residual branch's contribution (the reference's node
-// overwrites it, source/core/Autograd.cpp:257-280).
+// overwrites it, source/core/Autograd.cpp:257-280), or written outright when
+// nothing has written that gradient yet.
 void LayerNormFunction::apply_backward() {
   auto Y = output.lock();
-  if (!Y || !Y->get_gradient_ptr()) return;
+  const float* dy = grad_in(Y);
+  if (!dy) return;
   Scratch ws(pa_layer_norm_bwd_workspace_size(M, N), stream());
-  check_status(pa_layer_norm_bwd_accumulate(
-                   Y->get_gradient_ptr(), input->get_data_ptr(), mean->get_data_ptr(),
-                   rstd->get_data_ptr(), gamma->get_data_ptr(),
-                   input->requires_grad() ? input->get_gradient_ptr() : nullptr,
-                   gamma->requires_grad() ? gamma->get_gradient_ptr() : nullptr,
-                   beta->requires_grad() ? beta->get_gradient_ptr() : nullptr, M, N, ws.get(),
-                   ws.size(), ps(stream())),
+  bool unwritten = false;
+  float* dx = input->requires_grad() ? input->gradient_for_write(&unwritten) : nullptr;
+  float* dg = gamma->requires_grad() ? gamma->get_gradient_ptr() : nullptr;
+  float* db = beta->requires_grad() ? beta->get_gradient_ptr() : nullptr;
+  auto fn = unwritten ? pa_layer_norm_bwd : pa_layer_norm_bwd_accumulate;
+  check_status(fn(dy, input->get_data_ptr(), mean->get_data_ptr(), rstd->get_data_ptr(),
+                  gamma->get_data_ptr(), dx, dg, db, M, N, ws.get(), ws.size(), ps(stream())),
                "LayerNorm backward");
+}
+
+AddLayerNormFunction::AddLayerNormFunction(
+    const std::shared_ptr<Tensor>& x, const std::shared_ptr<Tensor>& r,
+    const std::shared_ptr<Tensor>& g, const std::shared_ptr<Tensor>& b,
+    const std::shared_ptr<Tensor>& sum, const std::shared_ptr<Tensor>& m,
+    const std::shared_ptr<Tensor>& rs, uint32_t m_size, uint32_t n_size)
+    : x_input(x), r_input(r), gamma(g), beta(b), mean(m), rstd(rs), sum_output(sum), M(m_size),
+      N(n_size) {}
+
+void AddLayerNormFunction::apply_backward() {
+  auto S = sum_output.lock();
+  std::shared_ptr<Tensor> out = std::move(pending_out);
+  pending_out.reset();
+  const float* dsum = grad_in(S);
+  const float* dy = grad_in(out);
+  if (!dy && !dsum) return;
+  const size_t n = static_cast<size_t>(M) * N;
+  if (!dy) {  // only the sum's own consumers: each addend receives their gradient
+    if (x_input->requires_grad()) add_into(*x_input, dsum, n, "add grad");
+    if (r_input->requires_grad()) add_into(*r_input, dsum, n, "add grad");
+    return;
+  }
+  bool ux = false, ur = false;
+  float* dx = x_input->requires_grad() ? x_input->gradient_for_write(&ux) : nullptr;
+  float* dr = r_input->requires_grad() ? r_input->gradient_for_write(&ur) : nullptr;
+  float* dg = gamma->requires_grad() ? gamma->get_gradient_ptr() : nullptr;
+  float* db = beta->requires_grad() ? beta->get_gradient_ptr() : nullptr;
+  const int flags = (dx && !ux ? PA_ADD_LN_ACC_DX : 0) | (dr && !ur ? PA_ADD_LN_ACC_DR : 0);
+  Scratch ws(pa_layer_norm_bwd_workspace_size(M, N), stream());
+  // out's node holds the sum, so its values are alive whenever out's gradient is
+  if (!S) throw std::runtime_error("Add+LayerNorm backward: the sum has expired");
+  check_status(pa_add_layer_norm_bwd(dy, dsum, S->get_data_ptr(), mean->get_data_ptr(),
+                                     rstd->get_data_ptr(), gamma->get_data_ptr(), dx, dr, dg, db,
+                                     M, N, flags, ws.get(), ws.size(), ps(stream())),
+               "Add+LayerNorm backward");
+}
+
+LayerNormOutFunction::LayerNormOutFunction(const std::shared_ptr<Tensor>& s,
+                                           const std::shared_ptr<Tensor>& out)
+    : sum(s), output(out) {}
+
+void LayerNormOutFunction::apply_backward() {
+  auto Y = output.lock();
+  if (!grad_in(Y)) return;
+  if (auto* node = dynamic_cast<AddLayerNormFunction*>(sum->grad_fn().get()))
+    node->pending_out = Y;
 }
 
 }  // namespace core

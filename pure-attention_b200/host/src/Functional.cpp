@@ -59,15 +59,17 @@ void pop_grad_zeros(const std::shared_ptr<Tensor>& A, const cudaStream_t& stream
   pop_grad_zeros(A.get(), stream);
 }
 void pop_grad_zeros(Tensor* A, const cudaStream_t& stream) {
-  if (A->get_gradient_ptr())
-    cudaMemsetAsync(A->get_gradient_ptr(), 0, A->numel() * sizeof(float), stream);
+  bool unwritten = false;
+  if (float* g = A->gradient_for_write(&unwritten))
+    cudaMemsetAsync(g, 0, A->numel() * sizeof(float), stream);
 }
 void pop_grad_ones(const std::shared_ptr<Tensor>& A, const cudaStream_t& stream) {
   pop_grad_ones(A.get(), stream);
 }
 void pop_grad_ones(Tensor* A, const cudaStream_t& stream) {
-  if (A->get_gradient_ptr())
-    check_status(pa_fill(A->get_gradient_ptr(), A->numel(), 1.0f, ps(stream)), "fill");
+  bool unwritten = false;
+  if (float* g = A->gradient_for_write(&unwritten))
+    check_status(pa_fill(g, A->numel(), 1.0f, ps(stream)), "fill");
 }
 void pop_data_normal(const std::shared_ptr<Tensor>& A, float std_dev, const cudaStream_t& stream) {
   check_status(pa_fill_normal(A->get_data_ptr(), A->numel(), std_dev, CudaContext::nextSeed(),
@@ -236,10 +238,13 @@ std::pair<std::shared_ptr<Tensor>, std::shared_ptr<Tensor>> add_layer_norm(
                                      output->get_data_ptr(), mean->get_data_ptr(),
                                      rstd->get_data_ptr(), M, N, epsilon, ps(stream)),
                "Add+LayerNorm");
-  if (gs) sum->set_grad_fn(std::make_shared<AddFunction>(x, r, sum));
-  if (g)
+  if (gs) {  // one backward pass writes both addends' gradients
+    sum->set_grad_fn(std::make_shared<AddLayerNormFunction>(x, r, gamma, beta, sum, mean, rstd, M, N));
+    output->set_grad_fn(std::make_shared<LayerNormOutFunction>(sum, output));
+  } else if (g) {  // only gamma / beta need gradients
     output->set_grad_fn(
         std::make_shared<LayerNormFunction>(sum, gamma, beta, output, mean, rstd, M, N));
+  }
   return {sum, output};
 }
 

@@ -32,8 +32,27 @@ Tensor::Tensor(const std::vector<uint32_t>& shape_, bool requires_gradient_, boo
   data_ptr = device_alloc(size, s);
   if (requires_gradient) {
     gradient_ptr = device_alloc(size, s);
-    cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), s);  // gradients start at zero
+    if (is_leaf)
+      cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), s);  // gradients start at zero
+    else
+      grad_unwritten = true;  // zeroed (or overwritten) on first use
   }
+}
+
+float32_t* Tensor::get_gradient_ptr() const {
+  if (grad_unwritten) {
+    grad_unwritten = false;
+    if (cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), CudaContext::getStream()) !=
+        cudaSuccess)
+      throw std::runtime_error("gradient: cudaMemsetAsync failed");
+  }
+  return gradient_ptr;
+}
+
+float32_t* Tensor::gradient_for_write(bool* unwritten) const {
+  *unwritten = grad_unwritten;
+  grad_unwritten = false;
+  return gradient_ptr;
 }
 
 Tensor::~Tensor() {
@@ -64,7 +83,7 @@ std::vector<float32_t> Tensor::to_host() const {
 
 std::vector<float32_t> Tensor::grad_to_host() const {
   std::vector<float32_t> out(size, 0.f);
-  if (!gradient_ptr) return out;
+  if (!gradient_ptr || grad_unwritten) return out;
   const cudaStream_t s = CudaContext::getStream();
   if (cudaMemcpyAsync(out.data(), gradient_ptr, size * sizeof(float32_t), cudaMemcpyDeviceToHost,
                       s) != cudaSuccess ||
@@ -86,12 +105,13 @@ void Tensor::set_gradient_storage(float32_t* external) {
   if (gradient_ptr && owns_gradient) cudaFreeAsync(gradient_ptr, s);
   gradient_ptr = external;
   owns_gradient = false;
+  grad_unwritten = false;
   if (cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), s) != cudaSuccess)
     throw std::runtime_error("set_gradient_storage: cudaMemsetAsync failed");
 }
 
 void Tensor::zero_grad() const {
-  if (gradient_ptr)
+  if (gradient_ptr && !grad_unwritten)
     cudaMemsetAsync(gradient_ptr, 0, size * sizeof(float32_t), CudaContext::getStream());
 }
 
@@ -100,8 +120,10 @@ void Tensor::backward(bool seed_with_ones) const { backward(seed_with_ones, Leaf
 void Tensor::backward(bool seed_with_ones, const LeafHook& leaf_ready) const {
   if (!requires_gradient)
     throw std::runtime_error("Called backward() on a tensor that does not require gradients.");
-  if (seed_with_ones)
+  if (seed_with_ones) {
+    grad_unwritten = false;
     check_status(pa_fill(gradient_ptr, size, 1.0f, ps(CudaContext::getStream())), "backward seed");
+  }
   if (!grad_function) return;
   // Post-order DFS over the graph: a node is appended after every node that
   // produces one of its inputs, so the reversed list runs each node only once

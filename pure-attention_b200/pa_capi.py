@@ -26,7 +26,7 @@ EXPORTS = [
     "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_add_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
-    "pa_layer_norm_bwd_accumulate",
+    "pa_layer_norm_bwd_accumulate", "pa_add_layer_norm_bwd",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
     "pa_linear_relu_bwd", "pa_linear_kept_size", "pa_linear_fwd_keep", "pa_linear_bwd_kept",
@@ -73,6 +73,7 @@ _SIGS = {
     "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
     "pa_layer_norm_bwd": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
     "pa_layer_norm_bwd_accumulate": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
+    "pa_add_layer_norm_bwd": (_int, [_vp] * 10 + [_u32, _u32, _int, _vp, _sz, _vp]),
     "pa_matmul_workspace_size": (_sz, [_int] * 3),
     "pa_matmul": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_matmul_grad_x": (_int, [_vp] * 3 + [_int] * 3 + [_vp, _sz, _vp]),
@@ -83,7 +84,7 @@ _SIGS = {
     "pa_linear_kept_size": (_sz, [_int, _int]),
     "pa_linear_fwd_keep": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp)] + [_int] * 5 + [_vp, _sz, _vp, _sz, _vp]),
     "pa_linear_bwd_kept": (_int, [_vp, _vp, _vp, _sz, _int, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp]
-                           + [_int] * 3 + [_vp, _sz, _vp]),
+                           + [_int] * 4 + [_vp, _sz, _vp]),
     "pa_linear_fwd": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp), _int, _int, _int, _int, _vp, _sz, _vp]),
     "pa_linear_bwd": (_int, [_vp, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp, _int, _int, _int,
                              _vp, _sz, _vp]),
@@ -278,6 +279,22 @@ def layer_norm_bwd(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, workspace, strea
     _check(name, st)
 
 
+def add_layer_norm_bwd(dy, dsum, s, mean, rstd, gamma, dx, dr, dgamma, dbeta, workspace,
+                       acc_dx=False, acc_dr=False, stream=None):
+    """Backward of sum = x + r, y = LayerNorm(sum): with G = LN_bwd(dy) + dsum
+    (dsum may be None), dx and dr get G (added to their contents with acc_dx /
+    acc_dr); dgamma, dbeta accumulate. Any output may be None."""
+    M = s.numel() // s.shape[-1]
+    N = s.shape[-1]
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    opt = lambda t: _ptr(t) if t is not None else None
+    flags = (1 if acc_dx else 0) | (2 if acc_dr else 0)
+    _check("pa_add_layer_norm_bwd", load().pa_add_layer_norm_bwd(
+        _ptr(dy), opt(dsum), _ptr(s), _ptr(mean), _ptr(rstd), _ptr(gamma), opt(dx), opt(dr),
+        opt(dgamma), opt(dbeta), M, N, flags, opt(workspace), ws_bytes,
+        _stream() if stream is None else stream))
+
+
 def matmul_workspace_size(M, N, K):
     return load().pa_matmul_workspace_size(M, N, K)
 
@@ -406,15 +423,16 @@ def linear_fwd_keep(x, w, bias, outs, M, in_features, out_features, kept, relu=F
 
 
 def linear_bwd_kept(x, w, kept, kept_mode, y, dy_parts, dx, dw, dbias, M, in_features, out_features,
-                    workspace=None, stream=None):
-    """linear_bwd (y None) / linear_relu_bwd (y = ReLU output) using the kept planes of x."""
+                    workspace=None, stream=None, dx_overwrite=False):
+    """linear_bwd (y None) / linear_relu_bwd (y = ReLU output) using the kept planes of x;
+    dx_overwrite: dx = dY w^T instead of dx += dY w^T."""
     ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
     arr = (_vp * len(dy_parts))(*[_ptr(t) for t in dy_parts])
     opt = lambda t: _ptr(t) if t is not None else None
     _check("pa_linear_bwd_kept", load().pa_linear_bwd_kept(
         _ptr(x), _ptr(w), _ptr(kept), kept.numel() * kept.element_size(), F32_MATH[kept_mode],
         opt(y), arr, len(dy_parts), opt(dx), opt(dw), opt(dbias), M, in_features, out_features,
-        _ptr(ws), nb, _stream() if stream is None else stream))
+        1 if dx_overwrite else 0, _ptr(ws), nb, _stream() if stream is None else stream))
 
 
 def split_last_dim(inp, outs, rows, width, stream=None):

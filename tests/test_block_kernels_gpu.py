@@ -133,6 +133,50 @@ def test_add_layer_norm_matches_oracle(M, N):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M,N", [(16384, 1024), (37, 128), (5, 12)])
+def test_add_layer_norm_bwd_matches_oracle(M, N):
+    """pa_add_layer_norm_bwd: G = LN_bwd(dy) + dsum written to both addends'
+    gradients (overwritten or accumulated per flag), dgamma / dbeta as the
+    plain LayerNorm backward's bits; dx and dr may be one buffer (x + x)."""
+    import oracle
+    import pa_capi
+    x, r = seeded_normal(M + 30, (M, N)), seeded_normal(M + 31, (M, N))
+    gamma = 1.0 + 0.1 * seeded_normal(N + 32, (N,))
+    beta = 0.1 * seeded_normal(N + 33, (N,))
+    dy, dsum = seeded_normal(M + 34, (M, N)), seeded_normal(M + 35, (M, N))
+    s, y = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+    mean, rstd = torch.empty(M, device="cuda"), torch.empty(M, device="cuda")
+    pa_capi.add_layer_norm_fwd(_cu(x), _cu(r), s, _cu(gamma), _cu(beta), y, mean, rstd)
+    odx, odg, odb = oracle.layer_norm_bwd(dy, _np(s), _np(mean), _np(rstd), gamma)
+    G = odx + dsum
+    ws = torch.empty(pa_capi.layer_norm_bwd_workspace_size(M, N), dtype=torch.uint8, device="cuda")
+    dx0, dr0 = seeded_normal(M + 36, (M, N)), seeded_normal(M + 37, (M, N))
+    dg0, db0 = seeded_normal(38, (N,)), seeded_normal(39, (N,))
+    dx = torch.full((M, N), float("nan"), device="cuda")  # overwritten
+    dr = _cu(dr0)                                         # accumulated
+    dg, db = _cu(dg0), _cu(db0)
+    pa_capi.add_layer_norm_bwd(_cu(dy), _cu(dsum), s, mean, rstd, _cu(gamma), dx, dr, dg, db, ws,
+                               acc_dx=False, acc_dr=True)
+    assert pa_capi.device_status() == 0
+    assert rel_err(_np(dx), G) < 1e-4
+    assert rel_err(_np(dr), dr0 + G) < 1e-4
+    # parameter gradients: the same bits as the plain LayerNorm backward
+    dg2, db2 = _cu(dg0), _cu(db0)
+    pa_capi.layer_norm_bwd(_cu(dy), s, mean, rstd, _cu(gamma), None, dg2, db2, ws)
+    assert torch.equal(dg, dg2) and torch.equal(db, db2)
+    # without dsum, and x + x: one buffer receives both addends' gradient
+    both = _cu(dx0)
+    pa_capi.add_layer_norm_bwd(_cu(dy), None, s, mean, rstd, _cu(gamma), both, both, None, None, None,
+                               acc_dx=True, acc_dr=True)
+    assert rel_err(_np(both), dx0 + 2 * odx) < 1e-4
+    fresh = torch.full((M, N), float("nan"), device="cuda")
+    pa_capi.add_layer_norm_bwd(_cu(dy), None, s, mean, rstd, _cu(gamma), fresh, fresh, None, None, None,
+                               acc_dx=False, acc_dr=True)
+    assert rel_err(_np(fresh), 2 * odx) < 1e-4
+    assert pa_capi.device_status() == 0
+
+
+@pytest.mark.gpu
 def test_layer_norm_backward_is_deterministic():
     import pa_capi
     M, N = 4096, 512
@@ -381,6 +425,44 @@ def test_linear_relu_matches_oracle(math_mode):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("math_mode", ["split3", "bf16"])
+@pytest.mark.parametrize("M,IN,OUT,n,relu", [(16384, 128, 3072, 3, False), (16384, 128, 4096, 1, True),
+                                             (3000, 64, 200, 1, False), (40, 64, 96, 3, False)])
+def test_linear_bwd_bias_grad_same_bits_as_column_sum_kernel(M, IN, OUT, n, relu, math_mode):
+    """The projection backward sums the bias gradient in the same pass that
+    gathers dY into bf16 planes; its chunked column sums are the two-stage
+    pa_bias_grad_ws kernel's, so db matches that kernel bit for bit (masked
+    by the ReLU output when there is one), and dX matches the oracle."""
+    import oracle
+    import pa_capi
+    x, w = seeded_normal(51, (M, IN)), seeded_normal(52, (IN, OUT), 0.1)
+    parts = [seeded_normal(60 + c, (M, OUT // n)) for c in range(n)]
+    y = np.maximum(seeded_normal(59, (M, OUT)), 0.0) if relu else None
+    db0 = seeded_normal(53, (OUT,))
+    pa_capi.set_f32_math(math_mode)
+    try:
+        db, dx = _cu(db0), torch.zeros(M, IN, device="cuda")
+        if relu:
+            pa_capi.linear_relu_bwd(_cu(x), _cu(w), _cu(y), _cu(parts[0]), dx, None, db, M, IN, OUT)
+        else:
+            pa_capi.linear_bwd(_cu(x), _cu(w), [_cu(p) for p in parts], dx, None, db, M, IN, OUT)
+        assert pa_capi.device_status() == 0
+        ref = _cu(db0)
+        W = OUT // n
+        ws = torch.empty(pa_capi.bias_grad_workspace_size(M, W), dtype=torch.uint8, device="cuda")
+        for c in range(n):
+            d = np.where(y > 0, parts[c], 0.0).astype(np.float32) if relu else parts[c]
+            pa_capi.bias_grad(_cu(d), ref[c * W:(c + 1) * W], M, W, workspace=ws)
+        assert torch.equal(db, ref)
+        dz = np.concatenate([np.where(y > 0, p, 0.0) if relu else p for p in parts], axis=1)
+        rb = _rb if math_mode == "bf16" else (lambda a: a)
+        tol = BF16_MATH_TOL if math_mode == "bf16" else GEMM_TOL
+        assert rel_err(_np(dx), oracle.matmul_grad_x(rb(dz), rb(w), np.zeros((M, IN)))) < tol
+    finally:
+        pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
 def test_adam_multi_tensor_matches_single_tensor_updates():
     """pa_adam_step_multi over 100 tensors (three launches of up to 48; sizes
     ragged, empty, one element and several chunks) equals pa_adam_step per
@@ -447,3 +529,35 @@ def test_linear_kept_planes_match_plain_calls(fwd_mode, bwd_mode):
     finally:
         pa_capi.set_f32_math("split3")
     assert pa_capi.device_status() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,IN,OUT,relu", [(16384, 1024, 4096, True), (1000, 200, 96, False)])
+def test_linear_bwd_dx_overwrite(M, IN, OUT, relu):
+    """PA_LINEAR_DX_OVERWRITE writes dX = dY W^T over whatever the buffer held
+    (NaN here): the values of accumulating into zeros (which may split K into
+    slices added in any order, so within fp32 reordering: 1e-5), the other
+    gradients untouched by the flag."""
+    import pa_capi
+    x, w, bias = seeded_normal(71, (M, IN)), seeded_normal(72, (IN, OUT), 0.05), seeded_normal(73, (OUT,))
+    dy = seeded_normal(74, (M, OUT))
+    ws = torch.empty(pa_capi.linear_workspace_size(M, IN, OUT), dtype=torch.uint8, device="cuda")
+    pa_capi.set_f32_math("bf16")
+    try:
+        kept = torch.empty(pa_capi.linear_kept_size(M, IN), dtype=torch.uint8, device="cuda")
+        y = torch.empty(M, OUT, device="cuda")
+        pa_capi.linear_fwd_keep(_cu(x), _cu(w), _cu(bias), [y], M, IN, OUT, kept, relu=relu, workspace=ws)
+        grads = []
+        for overwrite in (False, True):
+            dx = torch.full((M, IN), float("nan"), device="cuda") if overwrite else torch.zeros(M, IN, device="cuda")
+            dw, db = torch.zeros(IN, OUT, device="cuda"), torch.zeros(OUT, device="cuda")
+            pa_capi.linear_bwd_kept(_cu(x), _cu(w), kept, "bf16", y if relu else None, [_cu(dy)], dx, dw, db,
+                                    M, IN, OUT, workspace=ws, dx_overwrite=overwrite)
+            grads.append((dx, dw, db))
+        assert pa_capi.device_status() == 0
+        assert not torch.isnan(grads[1][0]).any()
+        for a, b in zip(*grads):
+            assert rel_err(_np(b), _np(a)) < 1e-5
+        assert torch.equal(grads[0][2], grads[1][2])  # bias gradient: fixed-order sums
+    finally:
+        pa_capi.set_f32_math("split3")

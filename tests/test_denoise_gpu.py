@@ -281,9 +281,18 @@ def test_gradient_arenas_reduce_in_place(dn):
         for _ in range(2):
             la, lb = a.step(x, t), b.step(x, t)
             assert abs(la - lb) <= 1e-6 * abs(la)
-        for p, q in zip(a.params, b.params):
-            assert rel_err(_h(q), _h(p)) < 1e-5
-            if np.linalg.norm(_g(p)) > 0:
-                assert rel_err(_g(q), _g(p)) < 1e-4
+        # The key slice of each in-projection bias has a gradient that is zero in
+        # exact arithmetic (softmax ignores a constant added to a query's scores),
+        # so it holds rounding noise, which Adam turns into steps of +-lr: it is
+        # left out of the comparison.
+        E, per_layer = SMALL["embed"], len(a.params) // SMALL["layers"]
+        for i, (p, q) in enumerate(zip(a.params, b.params)):
+            hp, hq, gp, gq = _h(p), _h(q), _g(p), _g(q)
+            if i % per_layer == 1:  # MultiheadAttention.in_proj_bias [1, 3E]: q, k, v slices
+                keep = np.r_[0:E, 2 * E:3 * E]
+                hp, hq, gp, gq = hp[..., keep], hq[..., keep], gp[..., keep], gq[..., keep]
+            assert rel_err(hq, hp) < 1e-5, i
+            if np.linalg.norm(gp) > 0:
+                assert rel_err(gq, gp) < 1e-4, i
     finally:
         dist.destroy_process_group()

@@ -100,6 +100,70 @@ def test_fused_add_layer_norm_matches_unfused_graph(pa):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("case", ["out_only", "sum_only", "same_input", "chained"])
+def test_fused_add_layer_norm_gradient_paths_match_torch(pa, case):
+    """The Add+LayerNorm node against torch float64 on each path its backward
+    takes: only the norm feeds the loss (no gradient reaches the sum
+    directly), only the sum does (no LayerNorm backward), x + x (one
+    buffer receives both addends' gradient), and two chained blocks with an
+    intermediate gradient read back (a gradient written once, never zeroed)."""
+    import torch.nn.functional as F
+    x, r, t = (seeded_normal(60 + i, (4, 16, 32)) for i in range(3))
+    g0 = (1.0 + 0.1 * seeded_normal(63, (32,))).astype(np.float32)
+    b0 = (0.1 * seeded_normal(64, (32,))).astype(np.float32)
+    ln, ln2 = pa.LayerNorm(32), pa.LayerNorm(32)
+    for m in (ln, ln2):
+        m.gamma.to_device(g0.tolist())
+        m.beta.to_device(b0.tolist())
+    X = _t(pa, x, True)
+    R = X if case == "same_input" else _t(pa, r, True)
+    s, y = ln.forward_add(X, R)
+    T = _t(pa, t)
+    if case == "sum_only":
+        loss = pa.MSE()(s, T)
+    elif case == "chained":
+        s2, y2 = ln2.forward_add(s, y)
+        loss = pa.MSE()(y2, T)
+    else:
+        loss = pa.MSE()(y, T)
+    loss.backward()
+    tx = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    tr = tx if case == "same_input" else torch.tensor(r, dtype=torch.float64, requires_grad=True)
+    tg = torch.tensor(g0, dtype=torch.float64, requires_grad=True)
+    tb = torch.tensor(b0, dtype=torch.float64, requires_grad=True)
+    ts = tx + tr
+    ts.retain_grad()
+    ty = F.layer_norm(ts, (32,), tg, tb, 1e-5)
+    tt = torch.tensor(t, dtype=torch.float64)
+    if case == "sum_only":
+        tl = torch.mean((ts - tt) ** 2)
+    elif case == "chained":
+        ty.retain_grad()
+        tl = torch.mean((F.layer_norm(ts + ty, (32,), tg, tb, 1e-5) - tt) ** 2)
+    else:
+        tl = torch.mean((ty - tt) ** 2)
+    tl.backward()
+    assert abs(_h(loss)[0] - tl.item()) < 1e-5 * abs(tl.item())
+    assert rel_err(_g(X), tx.grad.numpy()) < 1e-4
+    if case != "same_input":
+        assert rel_err(_g(R), tr.grad.numpy()) < 1e-4
+    if case == "sum_only":
+        assert not _g(ln.gamma).any() and not _g(ln.beta).any()
+    elif case == "chained":
+        # y's gradient was written once by the second block's node and is readable
+        assert rel_err(_g(y), ty.grad.numpy()) < 1e-4
+        for a, b, want in ((ln.gamma, ln2.gamma, tg), (ln.beta, ln2.beta, tb)):
+            assert rel_err(_g(a).ravel() + _g(b).ravel(), want.grad.numpy()) < 1e-4
+    else:
+        assert rel_err(_g(ln.gamma).ravel(), tg.grad.numpy()) < 1e-4
+        assert rel_err(_g(ln.beta).ravel(), tb.grad.numpy()) < 1e-4
+    # the sum's gradient is never formed by the fused node: it reads as zero
+    # unless a consumer of the sum wrote it (the second block, or the loss)
+    if case in ("out_only", "same_input"):
+        assert not _g(s).any()
+
+
+@pytest.mark.gpu
 def test_backward_leaf_hook_reports_final_gradients(pa):
     """backward(seed, hook) calls hook(t) once per gradient-requiring leaf
     (every parameter of a denoise layer and the input), after the last node
