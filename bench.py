@@ -892,7 +892,7 @@ def run_kernels(args):
     wsg = torch.empty(pa_capi.linear_workspace_size(Mg, IN, OUT), dtype=torch.uint8, device="cuda")
     ms_g = timed(lambda: pa_capi.linear_fwd(xg, wg, bg, [yg], Mg, IN, OUT, wsg))
     fl = 2 * Mg * IN * OUT
-    rows.append({"kernel": "split_planes_kernel x2 + gemm_persist_kernel (pa_linear_fwd)",
+    rows.append({"kernel": "split_planes_kernel x2 + gemm_pair_kernel (pa_linear_fwd)",
                  "shape": f"{Mg}x{IN} @ {IN}x{OUT} fp32 in/out, bf16 products", "bound": "tensor",
                  "us": round(ms_g * 1e3, 2), "algorithmic_flops": fl,
                  "achieved_tflops": round(fl / (ms_g * 1e-3) / 1e12, 1),

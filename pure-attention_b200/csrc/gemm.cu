@@ -25,14 +25,15 @@
 // incoming gradient by the saved output while gathering it (no ReLU passes,
 // no pre-activation tensor).
 //
-// One persistent CTA per SM walks 128 x 256 output tiles (work units: tiles,
-// or tiles x K slices for accumulating GEMMs that would fill the GPU badly);
-// K in blocks of 64 through a TMA ring of bf16 planes; the fp32 accumulator is
-// double-buffered in TMEM so the epilogue of one unit overlaps the MMAs of the
-// next; the epilogue stages 128 x 32 chunks in shared memory for TMA stores or
-// TMA add-reductions.
-//   warp 0     TMA producer
-//   warp 1     TMEM allocator + MMA issuer
+// Persistent clusters of two CTAs (one MMA unit, tcgen05 cta_group::2) walk
+// 256 x 256 output tiles (work units: tiles, or tiles x K slices for
+// accumulating GEMMs that would fill the GPU badly); K in blocks of 64
+// through a TMA ring of bf16 planes; the fp32 accumulator is double-buffered
+// in TMEM so the epilogue of one unit overlaps the MMAs of the next; the
+// epilogue stages 128 x 32 chunks in shared memory for TMA stores or TMA
+// add-reductions. In each CTA:
+//   warp 0     TMA producer (its own 128 rows of A, 128 columns of B)
+//   warp 1     TMEM allocator; in the even CTA also the MMA issuer
 //   warps 4-7  epilogue: TMEM -> registers (+ bias, ReLU) -> shared -> TMA
 #include <cuda_bf16.h>
 #include "host_launchers.h"
@@ -44,62 +45,74 @@ namespace {
 constexpr int GB = 128;          // output tile rows (the tile is GB x PB_N)
 constexpr int GK = 64;           // K block (one 128-byte swizzle row of bf16)
 
-// ---------------------------------------------------------------- persistent GEMM
-// One CTA per SM walks the work units (unit i, i + gridDim.x, ...; M-tile index
-// fastest). K in blocks of 64 through a TMA ring: per stage A 128 x 64 and
-// B 256 x 64 bf16 (48 KB) for one product (bf16 math, 4 stages), or the hi and
-// lo planes of both (96 KB) for three (split3, 2 stages). The fp32 accumulator
-// is double-buffered in TMEM (2 x 256 columns): the epilogue warps drain unit
-// i while the MMA warp accumulates unit i + 1. Every MMA is M=128 N=256 K=16,
-// the full-rate shape (a 128 x 128 tile leaves the tensor core idle during
-// each epilogue and reads twice the operand bytes per FLOP: 1.3-1.5x slower
-// at the training step's shapes).
-// Epilogue with tma_out: each 128 x 32 chunk is staged in shared memory
-// (128-byte swizzled, two buffers) and written by one TMA store - or, when
-// accumulating, one TMA add-reduction - per chunk, so the stores are whole
-// 128-byte row segments instead of one row per thread. Without tma_out
+// Output tiles are 256 x 256 (a CTA pair) walked by persistent pairs; K in
+// blocks of 64. The fp32 accumulator is double-buffered in TMEM (2 x 256
+// columns per CTA): the epilogue warps drain unit i while the MMAs accumulate
+// unit i + 1. Epilogue with tma_out: each 128 x 32 chunk is staged in shared
+// memory (128-byte swizzled, two buffers) and written by one TMA store - or,
+// when accumulating, one TMA add-reduction - per chunk, so the stores are
+// whole 128-byte row segments instead of one row per thread. Without tma_out
 // (unaligned outputs, column blocks not multiples of 32) each thread stores
-// its own row.
-constexpr int PB_N = 256;
-constexpr int PB_A = GB * GK * 2;    // 16 KB: one A plane of one stage
-constexpr int PB_B = PB_N * GK * 2;  // 32 KB: one B plane
-constexpr int PB_STG = 128 * 32 * 4;  // one 128-row x 32-column fp32 output chunk (16 KB)
-// NT = 1: planes A, B per stage, 4 stages; NT = 3 (hi/lo): A hi, A lo, B hi, B lo, 2 stages.
+// its own row. The bias of the tile's 256 columns is staged in shared memory
+// once per tile.
+constexpr int PB_N = 256;              // output tile columns
+constexpr int PB_A = GB * GK * 2;      // 16 KB: one A plane of one stage (128 rows)
+constexpr int PB_STG = 128 * 32 * 4;   // one 128-row x 32-column fp32 output chunk (16 KB)
+
+// ---------------------------------------------------------------- paired GEMM
+// Two CTAs of a cluster act as one MMA unit (tcgen05 cta_group::2) on a
+// 256 x 256 output tile: per K block each CTA loads its 128 rows of A and its
+// 128 of the tile's 256 columns of B, and the even CTA's MMAs (M=256 N=256
+// K=16) read both CTAs' shared memory and leave each CTA's 128 output rows in
+// its own TMEM. Per SM that is 32 KB of operands per K block for the MMA work
+// the one-CTA 128 x 256 tile needs 48 KB for, so the same shared memory holds
+// a ring half again as deep in time (6 stages in bf16 math, 3 of hi/lo planes
+// in split3) and the L2 reads per FLOP drop by a third. Both CTAs' TMA loads
+// count towards the even CTA's full barrier (cta_group::2 loads: no
+// multicast, each CTA fetches its own tiles); one commit, multicast to both
+// CTAs, frees a stage in both, and another hands an accumulator to both
+// epilogues, which report back to the even CTA (4 warps each).
+constexpr int PP_BH = 128 * GK * 2;  // 16 KB: this CTA's 128 columns of one B plane
 template <int NT>
-struct PersistCfg {
+struct PairCfg {
   static constexpr int NP = NT == 3 ? 2 : 1;
-  static constexpr int STAGE = NP * (PB_A + PB_B);
-  static constexpr int STAGES = NT == 3 ? 2 : 4;
+  static constexpr int STAGE = NP * (PB_A + PP_BH);
+  static constexpr int STAGES = NT == 3 ? 3 : 6;
   static constexpr int SMEM = STAGES * STAGE + 2 * PB_STG + 1024;
 };
 
 template <bool A_MN, bool B_MN, int NT>
-__global__ void __launch_bounds__(256, 1)
-    gemm_persist_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAl,
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAl,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBl,
                      const __grid_constant__ CUtensorMap mC0, const __grid_constant__ CUtensorMap mC1,
                      const __grid_constant__ CUtensorMap mC2, int tma_out, int ksplit,
                      float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
                      const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
                      int nsplit, int relu, uint32_t* status) {
-  using P = PersistCfg<NT>;
-  constexpr int PB_STAGES = P::STAGES, PB_STAGE = P::STAGE, NP = P::NP;
+  using P = PairCfg<NT>;
+  constexpr int ST = P::STAGES, STG = P::STAGE, NP = P::NP;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bars[2 * PB_STAGES + 4];
+  __shared__ uint64_t bars[2 * ST + 4];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
-  if (cta_aborted(status, &abort_flag)) return;
+  __shared__ __align__(16) float bias_s[PB_N];  // the current tile's bias (0 past Nout)
+  // No early return: both CTAs must take part in the paired TMEM allocation
+  // and the cluster barriers. A status word set by an earlier failure skips
+  // the work loops (a pair that disagrees on it ends in bounded waits).
+  const bool skip = cta_aborted(status, &abort_flag);
   uint8_t* smem = align1024(smem_raw);
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
   auto full = [&](int s) { return smem_u32(&bars[s]); };
-  auto empty = [&](int s) { return smem_u32(&bars[PB_STAGES + s]); };
-  auto acc_full = [&](int b) { return smem_u32(&bars[2 * PB_STAGES + b]); };
-  auto acc_empty = [&](int b) { return smem_u32(&bars[2 * PB_STAGES + 2 + b]); };
+  auto empty = [&](int s) { return smem_u32(&bars[ST + s]); };
+  auto acc_full = [&](int b) { return smem_u32(&bars[2 * ST + b]); };
+  auto acc_empty = [&](int b) { return smem_u32(&bars[2 * ST + 2 + b]); };  // the even CTA's
   const int warp = warp_id();
-  const int tiles_m = (Mout + GB - 1) / GB;
-  // work unit u = (tile u / ksplit, K slice u % ksplit); slices > 1 only when
-  // accumulating through TMA add-reductions
+  const int tiles_m = (Mout + 2 * GB - 1) / (2 * GB);
   const int units = tiles_m * ((Nout + PB_N - 1) / PB_N) * ksplit;
   const int nk_all = (Kred + GK - 1) / GK;
+  const int cl = static_cast<int>(blockIdx.x) / 2, ncl = static_cast<int>(gridDim.x) / 2;
   auto kslice = [&](int u, int& kb0, int& kb1) {
     const int sl = u % ksplit;
     kb0 = static_cast<int>((static_cast<long long>(nk_all) * sl) / ksplit);
@@ -107,118 +120,129 @@ __global__ void __launch_bounds__(256, 1)
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PB_STAGES; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 128);
+      mbar_init(acc_empty(b), 8);  // lane 0 of the four epilogue warps of both CTAs
     }
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&tmem_slot), 512);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(&tmem_slot), 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (elect_one()) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (!skip && elect_one()) {
       int g = 0;  // k-blocks loaded so far: ring slot and phase
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      for (int u = cl; ok && u < units; u += ncl) {
         const int tile = u / ksplit;
-        const int m0 = (tile % tiles_m) * GB, n0 = (tile / tiles_m) * PB_N;
+        const int m0 = (tile % tiles_m) * 2 * GB + static_cast<int>(rank) * GB;
+        const int n0 = (tile / tiles_m) * PB_N + static_cast<int>(rank) * 128;
         int kb0, kb1;
         kslice(u, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int s = g % PB_STAGES;
-          if (g >= PB_STAGES && !(ok = mbar_wait(empty(s), ((g / PB_STAGES) - 1) & 1, status)))
-            break;
-          mbar_arrive_expect_tx(full(s), PB_STAGE);
-          // stage: A planes (hi[, lo]) then B planes
-          const uint32_t st0 = smem_u32(smem + s * PB_STAGE);
+          const int s = g % ST;
+          // both CTAs' MMAs on this slot are done (the commit reaches both)
+          if (g >= ST && !(ok = mbar_wait(empty(s), ((g / ST) - 1) & 1, status))) break;
+          if (even) mbar_arrive_expect_tx(full(s), 2 * STG);
+          const uint32_t bar = mapa_shared(full(s), 0);
+          const uint32_t st0 = smem_u32(smem + s * STG);
 #pragma unroll
           for (int pl = 0; pl < NP; ++pl) {
-            const uint32_t da = st0 + pl * PB_A, db = st0 + NP * PB_A + pl * PB_B;
+            const uint32_t da = st0 + pl * PB_A, db = st0 + NP * PB_A + pl * PP_BH;
             const CUtensorMap* ma = pl ? &mAl : &mA;
             const CUtensorMap* mb = pl ? &mBl : &mB;
             if (A_MN) {  // two 64-wide M groups of 64 K rows
-              tma_load_2d(da, ma, full(s), m0, kb * GK);
-              tma_load_2d(da + PB_A / 2, ma, full(s), m0 + 64, kb * GK);
+              tma_load_2d_pair(da, ma, bar, m0, kb * GK);
+              tma_load_2d_pair(da + PB_A / 2, ma, bar, m0 + 64, kb * GK);
             } else {
-              tma_load_2d(da, ma, full(s), kb * GK, m0);
+              tma_load_2d_pair(da, ma, bar, kb * GK, m0);
             }
-            if (B_MN) {  // four 64-wide N groups of 64 K rows
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                tma_load_2d(db + q * (PB_B / 4), mb, full(s), n0 + 64 * q, kb * GK);
+            if (B_MN) {  // two 64-wide N groups of 64 K rows
+              tma_load_2d_pair(db, mb, bar, n0, kb * GK);
+              tma_load_2d_pair(db + PP_BH / 2, mb, bar, n0 + 64, kb * GK);
             } else {
-              tma_load_2d(db, mb, full(s), kb * GK, n0);
+              tma_load_2d_pair(db, mb, bar, kb * GK, n0);
             }
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      constexpr uint32_t idesc = make_idesc(128, PB_N, 1, A_MN, B_MN);
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (even && !skip && elect_one()) {
+      constexpr uint32_t idesc = make_idesc(2 * GB, PB_N, 1, A_MN, B_MN);
       const uint32_t s0 = smem_u32(smem);
       int g = 0, it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++it) {
+      for (int u = cl; ok && u < units; u += ncl, ++it) {
         const int b = it & 1;
         int kb0, kb1;
         kslice(u, kb0, kb1);
-        // the epilogue has drained this accumulator buffer (unit it - 2)
-        if (it >= 2 && !(ok = mbar_wait(acc_empty(b), ((it >> 1) - 1) & 1, status))) break;
+        // both epilogues have drained this accumulator buffer (unit it - 2)
+        if (it >= 2 && !(ok = mbar_wait_cluster(acc_empty(b), ((it >> 1) - 1) & 1, status))) break;
         tc_fence_after();
         const uint32_t d = tmem + b * PB_N;
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int s = g % PB_STAGES;
-          if (!(ok = mbar_wait(full(s), (g / PB_STAGES) & 1, status))) break;
+          const int s = g % ST;
+          if (!(ok = mbar_wait_cluster(full(s), (g / ST) & 1, status))) break;
           tc_fence_after();
 #pragma unroll
           for (int term = 0; term < NT; ++term) {
             // planes (A, B) of each term: (hi, hi), (hi, lo), (lo, hi)
-            const uint32_t sa = s0 + s * PB_STAGE + (term == 2 ? PB_A : 0);
-            const uint32_t sb = s0 + s * PB_STAGE + NP * PB_A + (term == 1 ? PB_B : 0);
+            const uint32_t sa = s0 + s * STG + (term == 2 ? PB_A : 0);
+            const uint32_t sb = s0 + s * STG + NP * PB_A + (term == 1 ? PP_BH : 0);
 #pragma unroll
             for (int ks = 0; ks < GK / 16; ++ks) {
               const uint64_t da = A_MN ? make_sdesc(sa + ks * 2048, PB_A / 2, 1024)
                                        : make_sdesc(sa + ks * 32, 16, 1024);
-              const uint64_t db = B_MN ? make_sdesc(sb + ks * 2048, PB_B / 4, 1024)
+              const uint64_t db = B_MN ? make_sdesc(sb + ks * 2048, PP_BH / 2, 1024)
                                        : make_sdesc(sb + ks * 32, 16, 1024);
-              umma_f16_ss(d, da, db, idesc, (kb > kb0 || term > 0 || ks > 0) ? 1u : 0u);
+              umma_f16_ss_pair(d, da, db, idesc, (kb > kb0 || term > 0 || ks > 0) ? 1u : 0u);
             }
           }
-          umma_commit(empty(s));
+          umma_commit_pair(empty(s));
         }
-        if (ok) umma_commit(acc_full(b));
+        if (ok) umma_commit_pair(acc_full(b));
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------ epilogue (both CTAs)
     const int r = threadIdx.x - 128;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const bool leader = threadIdx.x == 128;
-    uint8_t* stg = smem + PB_STAGES * PB_STAGE;
+    uint8_t* stg = smem + ST * STG;
     int q = 0;  // staged chunks so far (buffer q & 1)
     int it = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    for (int u = cl; !skip && u < units; u += ncl, ++it) {
       const int tile = u / ksplit;
       const int b = it & 1;
-      bool ok = mbar_wait_warp(acc_full(b), (it >> 1) & 1, status);
-      if (tma_out) ok = named_bar_and(1, 128, ok);  // the four warps leave together
+      bool ok = mbar_wait_cluster_warp(acc_full(b), (it >> 1) & 1, status);
+      ok = named_bar_and(1, 128, ok);  // the four warps leave together
       if (!ok) break;
       tc_fence_after();
-      const int row = (tile % tiles_m) * GB + r, n0 = (tile / tiles_m) * PB_N;
+      const int row0 = (tile % tiles_m) * 2 * GB + static_cast<int>(rank) * GB;
+      const int row = row0 + r, n0 = (tile / tiles_m) * PB_N;
+      if (bias) {
+        // every thread is past the previous tile's reads of bias_s (the barrier
+        // above), so it can be refilled; the barrier below publishes it
+#pragma unroll
+        for (int h = 0; h < PB_N / 128; ++h) {
+          const int col = n0 + r + 128 * h;
+          bias_s[r + 128 * h] = col < Nout ? bias[col] : 0.f;
+        }
+        named_bar_sync(1, 128);
+      }
       // Output column `col` goes to C[row * ldc + col], or with nsplit > 0 to
       // part p = col / nsplit (C, C1, C2) at [row * nsplit + col - p * nsplit].
       auto dst_of = [&](int col) -> float* {
@@ -232,44 +256,43 @@ __global__ void __launch_bounds__(256, 1)
         uint32_t v[32];
         tmem_ld32(tmem + b * PB_N + c * 32 + lane_base, v);
         tmem_ld_wait();
-        if (c == PB_N / 32 - 1) {  // the buffer is free for tile it + 2
+        if (c == PB_N / 32 - 1) {  // the buffer is free for tile it + 2 (in both CTAs)
           tc_fence_before();
-          mbar_arrive(acc_empty(b));
+          __syncwarp();
+          if (lane_id() == 0) mbar_arrive_cluster(mapa_shared(acc_empty(b), 0));
         }
         const int col0 = n0 + c * 32;
         if (tma_out) {
-          if (col0 >= Nout) continue;  // uniform over the epilogue warps
+          // uniform over the epilogue warps (an odd CTA past the last row stores nothing)
+          if (col0 >= Nout || row0 >= Mout) continue;
           const int buf = q++ & 1;
           if (leader) bulk_wait_read<1>();  // the store of two chunks ago has read this buffer
           named_bar_sync(1, 128);
           uint8_t* srow = stg + buf * PB_STG;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
-                                   __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+          for (int e = 0; e < 8; ++e) {
+            float4 f = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                   __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
             if (bias) {
-              const int cb = col0 + 4 * u;
-              f.x += cb < Nout ? bias[cb] : 0.f;
-              f.y += cb + 1 < Nout ? bias[cb + 1] : 0.f;
-              f.z += cb + 2 < Nout ? bias[cb + 2] : 0.f;
-              f.w += cb + 3 < Nout ? bias[cb + 3] : 0.f;
+              const float4 bb = reinterpret_cast<const float4*>(bias_s)[c * 8 + e];
+              f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
             }
             if (relu) {
               f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
               f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
             }
-            *reinterpret_cast<float4*>(srow + sw128_offset(r, 16 * u)) = f;
+            *reinterpret_cast<float4*>(srow + sw128_offset(r, 16 * e)) = f;
           }
           fence_proxy_async_smem();
           named_bar_sync(1, 128);
           if (leader) {
             const int p = nsplit > 0 ? col0 / nsplit : 0;
             const CUtensorMap* map = p == 0 ? &mC0 : (p == 1 ? &mC1 : &mC2);
-            const int x = col0 - p * (nsplit > 0 ? nsplit : 0), y = row - r;
+            const int x = col0 - p * (nsplit > 0 ? nsplit : 0);
             if (accumulate)
-              tma_reduce_add_2d(map, smem_u32(srow), x, y);
+              tma_reduce_add_2d(map, smem_u32(srow), x, row0);
             else
-              tma_store_2d(map, smem_u32(srow), x, y);
+              tma_store_2d(map, smem_u32(srow), x, row0);
             tma_store_commit();
           }
           continue;
@@ -279,16 +302,15 @@ __global__ void __launch_bounds__(256, 1)
         const bool one_part = nsplit <= 0 || (col0 % nsplit) + 32 <= nsplit;
         const int ld = nsplit > 0 ? nsplit : ldc;
         const bool vec = (col0 + 32 <= Nout) && one_part && ((ld & 3) == 0) &&
-                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) &&
-                         (!bias || (reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0);
+                         ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
         if (vec) {
           float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            float4 f = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
-                                   __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+          for (int e = 0; e < 8; ++e) {
+            float4 f = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                   __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
             if (bias) {
-              const float4 bb = *reinterpret_cast<const float4*>(bias + col0 + 4 * u);
+              const float4 bb = reinterpret_cast<const float4*>(bias_s)[c * 8 + e];
               f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
             }
             if (relu) {
@@ -296,10 +318,10 @@ __global__ void __launch_bounds__(256, 1)
               f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
             }
             if (accumulate) {
-              const float4 p = d4[u];
+              const float4 p = d4[e];
               f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
             }
-            d4[u] = f;
+            d4[e] = f;
           }
         } else {
 #pragma unroll
@@ -307,7 +329,7 @@ __global__ void __launch_bounds__(256, 1)
             const int col = col0 + e;
             if (col < Nout) {
               float* de = dst_of(col);
-              float f = __uint_as_float(v[e]) + (bias ? bias[col] : 0.f);
+              float f = __uint_as_float(v[e]) + (bias ? bias_s[c * 32 + e] : 0.f);
               if (relu) f = fmaxf(f, 0.f);
               *de = f + (accumulate ? *de : 0.f);
             }
@@ -318,10 +340,10 @@ __global__ void __launch_bounds__(256, 1)
     if (leader) bulk_wait_all();  // staged chunks fully written before the CTA ends
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // the other CTA no longer reaches into this one's barriers or TMEM
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -352,10 +374,6 @@ struct Epilogue {
   int relu = 0;  // max(0, .) after the bias (forward projections only)
 };
 
-
-int sm_count() { return device_sm_count(); }
-
-// bf16 math: maps over the hi planes, A boxes of 128 rows and B boxes of 256.
 // fp32 [rows, cols] output with row pitch ld, as 128-row x 32-column TMA boxes.
 bool out_map(CUtensorMap* m, const float* base, int rows, int cols, int ld) {
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
@@ -365,15 +383,15 @@ bool out_map(CUtensorMap* m, const float* base, int rows, int cols, int ld) {
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// The paired kernel: the same work units over 256-row tiles, one CTA pair per
+// two SMs (as many pairs as the device holds at once).
 template <bool A_MN, bool B_MN, int NT>
-int run_gemm_persist(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred,
-                     int accumulate, const Epilogue& ep, uint32_t* status, cudaStream_t s) {
+int run_gemm_pair(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, int Kred,
+                  int accumulate, const Epilogue& ep, uint32_t* status, cudaStream_t s) {
   const CUtensorMap& mA = m[0];
   static std::atomic<uint64_t> attr{0};
-  if (!ensure_smem_attr(gemm_persist_kernel<A_MN, B_MN, NT>, PersistCfg<NT>::SMEM, attr))
+  if (!ensure_smem_attr(gemm_pair_kernel<A_MN, B_MN, NT>, PairCfg<NT>::SMEM, attr))
     return PA_ERR_LAUNCH;
-  // TMA-store epilogue when every output is 16-byte aligned with a 16-byte row
-  // pitch and column blocks hold whole 32-column chunks
   CUtensorMap mc[3];
   const bool al = [&] {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -392,17 +410,33 @@ int run_gemm_persist(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout
     return true;
   }();
   if (!al) mc[0] = mc[1] = mc[2] = mA;  // unused
-  const int tiles = ((Mout + GB - 1) / GB) * ((Nout + PB_N - 1) / PB_N);
-  // Accumulating GEMMs (dX, dW) through the TMA path may split K so that the
-  // work units fill whole waves of CTAs: the slices add into C in any order,
-  // so their results can differ in the last bits from run to run.
+  const int dev = current_device();
+  if (dev < 0) return PA_ERR_DEVICE;
+  static std::atomic<int> max_pairs[kMaxDevices];
+  const int pairs = cached_per_device(max_pairs, dev, [] {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 1024, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = PairCfg<NT>::SMEM;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<A_MN, B_MN, NT>, &cfg) != cudaSuccess ||
+        n <= 0) {
+      cudaGetLastError();  // clear a failed query; fall back to one pair per two SMs
+      n = device_sm_count() / 2;
+    }
+    return n;
+  });
+  const int tiles = ((Mout + 2 * GB - 1) / (2 * GB)) * ((Nout + PB_N - 1) / PB_N);
+  // Accumulating GEMMs through the TMA path may split K so that the work units
+  // fill whole waves of pairs: the slices add into C in any order, so their
+  // results can differ in the last bits from run to run.
   int ksplit = 1;
   if (accumulate && al && !ep.bias && !ep.relu) {
-    const int nk = (Kred + GK - 1) / GK, sms = sm_count();
+    const int nk = (Kred + GK - 1) / GK;
     double best = 0.0;
     for (int sp = 1; sp <= 16 && nk / sp >= 4; ++sp) {
-      const int units = tiles * sp, waves = (units + sms - 1) / sms;
-      const double eff = static_cast<double>(units) / (static_cast<double>(waves) * sms);
+      const int units = tiles * sp, waves = (units + pairs - 1) / pairs;
+      const double eff = static_cast<double>(units) / (static_cast<double>(waves) * pairs);
       if (eff > best + 0.02) {
         best = eff;
         ksplit = sp;
@@ -410,8 +444,8 @@ int run_gemm_persist(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout
     }
   }
   const int units = tiles * ksplit;
-  const int grid = units < sm_count() ? units : sm_count();
-  gemm_persist_kernel<A_MN, B_MN, NT><<<grid, 256, PersistCfg<NT>::SMEM, s>>>(
+  const int grid = 2 * (units < pairs ? units : pairs);
+  gemm_pair_kernel<A_MN, B_MN, NT><<<grid, 256, PairCfg<NT>::SMEM, s>>>(
       m[0], m[1], m[2], m[3], mc[0], mc[1], mc[2], al ? 1 : 0, ksplit, C, ldc, Mout, Nout, Kred,
       accumulate, ep.bias, ep.c1, ep.c2, ep.nsplit, ep.relu, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
@@ -441,29 +475,30 @@ int split_into(const float* x, const Planes& p, cudaStream_t s) {
 int gemm_planes(int mode, const Planes& a, const Planes& b, float* C, int M, int N, int K,
                 const Epilogue& ep, uint32_t* status, cudaStream_t s, int accumulate = 1) {
   const bool a_mn = (mode == 2), b_mn = (mode != 1);
-  // persistent 128 x 256 kernel: maps A hi, A lo, B hi, B lo (A boxes of 128 rows, B of 256)
+  // paired 256 x 256 kernel: maps A hi, A lo, B hi, B lo (K-major boxes of 128 rows:
+  // each CTA loads its 128 rows of A and its 128 columns of B)
   {
     const bool one = f32_math() == PA_F32_MATH_BF16;
     CUtensorMap m[4];
     if (!plane_map(&m[0], a.hi, a.rows, a.cols, a_mn, 128) ||
-        !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn, 256))
+        !plane_map(&m[2], b.hi, b.rows, b.cols, b_mn, 128))
       return PA_ERR_ALIGN;
     if (one) {
       m[1] = m[0];
       m[3] = m[2];
     } else if (!plane_map(&m[1], a.lo, a.rows, a.cols, a_mn, 128) ||
-               !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn, 256)) {
+               !plane_map(&m[3], b.lo, b.rows, b.cols, b_mn, 128)) {
       return PA_ERR_ALIGN;
     }
     const int acc = accumulate ? 1 : 0;
     if (one) {
-      if (mode == 0) return run_gemm_persist<false, true, 1>(m, C, N, M, N, K, 0, ep, status, s);
-      if (mode == 1) return run_gemm_persist<false, false, 1>(m, C, N, M, N, K, acc, ep, status, s);
-      return run_gemm_persist<true, true, 1>(m, C, K, N, K, M, acc, ep, status, s);
+      if (mode == 0) return run_gemm_pair<false, true, 1>(m, C, N, M, N, K, 0, ep, status, s);
+      if (mode == 1) return run_gemm_pair<false, false, 1>(m, C, N, M, N, K, acc, ep, status, s);
+      return run_gemm_pair<true, true, 1>(m, C, K, N, K, M, acc, ep, status, s);
     }
-    if (mode == 0) return run_gemm_persist<false, true, 3>(m, C, N, M, N, K, 0, ep, status, s);
-    if (mode == 1) return run_gemm_persist<false, false, 3>(m, C, N, M, N, K, acc, ep, status, s);
-    return run_gemm_persist<true, true, 3>(m, C, K, N, K, M, acc, ep, status, s);
+    if (mode == 0) return run_gemm_pair<false, true, 3>(m, C, N, M, N, K, 0, ep, status, s);
+    if (mode == 1) return run_gemm_pair<false, false, 3>(m, C, N, M, N, K, acc, ep, status, s);
+    return run_gemm_pair<true, true, 3>(m, C, K, N, K, M, acc, ep, status, s);
   }
 }
 
