@@ -110,6 +110,17 @@ int pa_attn_bwd(const pa_attn_desc* desc, const void* q, const void* k, const vo
                 const void* o, const void* dO, const float* lse, void* dq, void* dk, void* dv,
                 int accumulate, void* workspace, size_t workspace_bytes, pa_stream_t stream);
 
+/* pa_attn_bwd for PA_F32 tensors that reuses the bf16 operand planes of q, k, v
+ * which pa_attn_fwd left in its workspace (`fwd_workspace`, made under f32 math
+ * mode `fwd_mode`, and not written since): only dO is converted. A bf16-math
+ * forward at head_dim 64 kept no lo planes, so a split3 backward converts q, k,
+ * v again. With dtype PA_BF16 or a NULL fwd_workspace this is pa_attn_bwd. No
+ * counterpart in the reference, whose backward reads its fp32 inputs again. */
+int pa_attn_bwd_kept(const pa_attn_desc* desc, const void* q, const void* k, const void* v,
+                     const void* o, const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                     int accumulate, const void* fwd_workspace, size_t fwd_workspace_bytes,
+                     int fwd_mode, void* workspace, size_t workspace_bytes, pa_stream_t stream);
+
 /* Backward without a caller workspace, for callers that cannot allocate device
  * memory (e.g. plugins whose host framework owns all GPU memory, or runtimes
  * that forbid allocations once a model is resident). No counterpart in the

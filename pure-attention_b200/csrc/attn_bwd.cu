@@ -1348,9 +1348,13 @@ size_t attn_bwd_workspace_bytes_f32(const AttnShape& sh) {
   return 8 * plane + stats_bytes(sh, Dp, sh.D == 64);
 }
 
+// kept: the forward's workspace (launch_attn_fwd_f32), which holds the planes
+// of q, k, v in the same layout as planes 0-5 here (hi of operand i at 2i, lo
+// at 2i + 1); then only dO is converted. kept_lo: it holds the lo planes too.
 int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v,
                         const void* o, const void* dO, const float* lse, void* dq, void* dk,
-                        void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream) {
+                        void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream,
+                        const void* kept, bool kept_lo) {
   const int Dp = f32_plane_dim(sh.D);
   if (Dp != 64) return PA_ERR_UNSUPPORTED;
   const size_t rows = static_cast<size_t>(sh.B) * sh.L * sh.H;
@@ -1361,12 +1365,19 @@ int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const
   AttnShape ps = sh;
   ps.D = Dp;
   CUtensorMap m[8];
-  if (sh.D == 64 && f32_math() == PA_F32_MATH_BF16) {
+  const bool bf16_math = sh.D == 64 && f32_math() == PA_F32_MATH_BF16;
+  // planes of operand i: from the forward's kept workspace (q, k, v) or converted here
+  uint8_t* kp = const_cast<uint8_t*>(static_cast<const uint8_t*>(kept));
+  const bool use_kept = kp && (bf16_math || kept_lo);
+  auto planes_of = [&](int i) { return (use_kept && i < 3 ? kp : w) + (2 * i) * plane; };
+  if (bf16_math) {
     // one bf16 plane per operand, the bf16 d64 kernel with fp32 dK / dV
     for (int i = 0; i < 4; ++i) {
-      uint8_t* hi = w + (2 * i) * plane;
-      const int st = launch_split_planes(src[i], hi, nullptr, rows, sh.D, Dp, stream);
-      if (st != PA_OK) return st;
+      uint8_t* hi = planes_of(i);
+      if (!(use_kept && i < 3)) {
+        const int st = launch_split_planes(src[i], hi, nullptr, rows, sh.D, Dp, stream);
+        if (st != PA_OK) return st;
+      }
       if (!make_qkv_map(&m[i], hi, ps, 128)) return PA_ERR_ALIGN;
       m[4 + i] = m[i];
     }
@@ -1374,10 +1385,12 @@ int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const
                                      status, stream);
   }
   for (int i = 0; i < 4; ++i) {
-    uint8_t* hi = w + (2 * i) * plane;
-    uint8_t* lo = w + (2 * i + 1) * plane;
-    const int st = launch_split_planes(src[i], hi, lo, rows, sh.D, Dp, stream);
-    if (st != PA_OK) return st;
+    uint8_t* hi = planes_of(i);
+    uint8_t* lo = hi + plane;
+    if (!(use_kept && i < 3)) {
+      const int st = launch_split_planes(src[i], hi, lo, rows, sh.D, Dp, stream);
+      if (st != PA_OK) return st;
+    }
     if (!make_qkv_map(&m[i], hi, ps, 128) || !make_qkv_map(&m[4 + i], lo, ps, 128))
       return PA_ERR_ALIGN;
   }

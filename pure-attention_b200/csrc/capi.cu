@@ -171,6 +171,35 @@ int pa_attn_bwd(const pa_attn_desc* desc, const void* q, const void* k, const vo
                                  status, s);
 }
 
+int pa_attn_bwd_kept(const pa_attn_desc* desc, const void* q, const void* k, const void* v,
+                     const void* o, const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                     int accumulate, const void* fwd_workspace, size_t fwd_workspace_bytes,
+                     int fwd_mode, void* workspace, size_t workspace_bytes, pa_stream_t stream) {
+  if (!desc) return PA_ERR_NULL;
+  if (desc->dtype != PA_F32 || !fwd_workspace)
+    return pa_attn_bwd(desc, q, k, v, o, dO, lse, dq, dk, dv, accumulate, workspace,
+                       workspace_bytes, stream);
+  pa::AttnShape sh;
+  int st = check_attn(desc, &sh);
+  if (st != PA_OK) return st;
+  if (fwd_mode != PA_F32_MATH_SPLIT3 && fwd_mode != PA_F32_MATH_BF16) return PA_ERR_SHAPE;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv) return PA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dO) ||
+      !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
+    return PA_ERR_ALIGN;
+  const size_t need = pa_attn_bwd_workspace_size(desc);
+  if (!workspace || workspace_bytes < need) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PA_ERR_ALIGN;
+  if (fwd_workspace_bytes < pa_attn_fwd_workspace_size(desc)) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(fwd_workspace) & 255u) != 0) return PA_ERR_ALIGN;
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  // a bf16-math forward at head dim 64 kept only the hi planes
+  const bool kept_lo = !(desc->head_dim == 64 && fwd_mode == PA_F32_MATH_BF16);
+  return pa::launch_attn_bwd_f32(sh, q, k, v, o, dO, lse, dq, dk, dv, accumulate, workspace,
+                                 status, static_cast<cudaStream_t>(stream), fwd_workspace, kept_lo);
+}
+
 int pa_attn_delta(const pa_attn_desc* desc, const void* dO, const void* o, float* delta,
                   pa_stream_t stream) {
   pa::AttnShape sh;

@@ -37,7 +37,8 @@ int launch_attn_bwd_bf16(const AttnShape& sh, const void* q, const void* k, cons
                          void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream);
 int launch_attn_bwd_f32(const AttnShape& sh, const void* q, const void* k, const void* v,
                         const void* o, const void* dO, const float* lse, void* dq, void* dk,
-                        void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream);
+                        void* dv, int accumulate, void* ws, uint32_t* status, cudaStream_t stream,
+                        const void* kept = nullptr, bool kept_lo = false);
 int launch_attn_delta_bf16(const AttnShape& sh, const void* dO, const void* o, float* delta,
                            cudaStream_t stream);
 int launch_attn_delta_f32(const AttnShape& sh, const void* dO, const void* o, float* delta,

@@ -183,6 +183,13 @@ PYBIND11_MODULE(PureAttention, m) {
   });
   m.def("set_seed", &CudaContext::setSeed, "Seed of fill_normal and layer initialisation",
         py::arg("seed"));
+  m.def("set_stream", [](uintptr_t handle) {
+    CudaContext::setStream(reinterpret_cast<cudaStream_t>(handle));
+  }, "Stream every operator, allocation and gradient of this module runs on from now on "
+     "(a cudaStream_t handle, e.g. torch.cuda.Stream().cuda_stream; 0 = the legacy default "
+     "stream). A non-default stream lets a step be captured into a CUDA graph.",
+     py::arg("handle"));
+  m.def("get_stream", []() { return reinterpret_cast<uintptr_t>(CudaContext::getStream()); });
   m.def("device_status", []() { return pa_device_status(CudaContext::getStream(), 1); },
         "Synchronise and return the kernels' status word (0 = ok)");
 }

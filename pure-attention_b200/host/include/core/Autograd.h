@@ -90,6 +90,11 @@ struct FlashAttentionFunction : public Function {
   std::weak_ptr<Tensor> O_output;
   std::shared_ptr<Tensor> L_cache;
   int num_heads;
+  // the forward's workspace, holding the bf16 planes of Q, K, V it converted,
+  // with the f32 math mode they were made under (the backward converts only dO)
+  std::shared_ptr<void> kept;
+  size_t kept_bytes = 0;
+  int kept_mode = 0;
   FlashAttentionFunction(const std::shared_ptr<Tensor>& q, const std::shared_ptr<Tensor>& k,
                          const std::shared_ptr<Tensor>& v, const std::shared_ptr<Tensor>& o,
                          const std::shared_ptr<Tensor>& lcache, int heads);

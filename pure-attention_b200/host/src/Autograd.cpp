@@ -181,7 +181,8 @@ FlashAttentionFunction::FlashAttentionFunction(const std::shared_ptr<Tensor>& q,
 // Gradients go straight into Q/K/V's grads: written outright when nothing
 // has written any of them yet (accumulate = 0), else added (accumulate = 1,
 // after zeroing those still unwritten). No temporaries, unlike the
-// reference's three cudaMallocAsync'd buffers.
+// reference's three cudaMallocAsync'd buffers. Q, K, V's bf16 planes come from
+// the forward's kept workspace; only dO is converted.
 void FlashAttentionFunction::apply_backward() {
   auto O = O_output.lock();
   const float* dO = grad_in(O);
@@ -212,10 +213,11 @@ void FlashAttentionFunction::apply_backward() {
   if (!all_unwritten)
     for (int i = 0; i < 3; ++i)
       if (unwritten[i]) cudaMemsetAsync(dst[i], 0, n * sizeof(float), stream());
-  check_status(pa_attn_bwd(&d, Q_input->get_data_ptr(), K_input->get_data_ptr(),
-                           V_input->get_data_ptr(), O->get_data_ptr(), dO,
-                           L_cache->get_data_ptr(), dst[0], dst[1], dst[2], all_unwritten ? 0 : 1,
-                           ws.get(), ws.size(), ps(stream())),
+  check_status(pa_attn_bwd_kept(&d, Q_input->get_data_ptr(), K_input->get_data_ptr(),
+                                V_input->get_data_ptr(), O->get_data_ptr(), dO,
+                                L_cache->get_data_ptr(), dst[0], dst[1], dst[2],
+                                all_unwritten ? 0 : 1, kept.get(), kept_bytes, kept_mode,
+                                ws.get(), ws.size(), ps(stream())),
                "FlashAttention Backward");
 }
 

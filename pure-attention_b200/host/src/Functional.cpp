@@ -185,14 +185,30 @@ void flash_attention(const std::shared_ptr<Tensor>& Q, const std::shared_ptr<Ten
       std::vector<uint32_t>{sh[0] * static_cast<uint32_t>(num_heads), sh[1]}, false, false);
   pa_attn_desc d{static_cast<int32_t>(sh[0]), static_cast<int32_t>(sh[1]), num_heads,
                  static_cast<int32_t>(sh[2]) / num_heads, PA_F32, 0.f};
-  Scratch ws(pa_attn_fwd_workspace_size(&d), stream);
+  // With gradients, the workspace (Q, K, V's bf16 operand planes) stays with
+  // the graph node, so the backward does not convert them again.
+  const size_t ws_bytes = pa_attn_fwd_workspace_size(&d);
+  std::shared_ptr<void> ws;
+  if (ws_bytes) {
+    void* p = nullptr;
+    retain_pool_memory();
+    if (cudaMallocAsync(&p, ws_bytes, stream) != cudaSuccess)
+      throw std::runtime_error("FlashAttention: cannot allocate the workspace");
+    ws = std::shared_ptr<void>(p, [](void* q) { cudaFreeAsync(q, CudaContext::getStream()); });
+  }
   const int st = pa_attn_fwd(&d, Q->get_data_ptr(), K->get_data_ptr(), V->get_data_ptr(),
-                             O->get_data_ptr(), L_cache->get_data_ptr(), ws.get(), ws.size(),
+                             O->get_data_ptr(), L_cache->get_data_ptr(), ws.get(), ws_bytes,
                              ps(stream));
   if (st == PA_ERR_UNSUPPORTED)
     throw std::runtime_error("FlashAttention: Unsupported Head Dimension");
   check_status(st, "FlashAttention");
-  if (g) O->set_grad_fn(std::make_shared<FlashAttentionFunction>(Q, K, V, O, L_cache, num_heads));
+  if (g) {
+    auto node = std::make_shared<FlashAttentionFunction>(Q, K, V, O, L_cache, num_heads);
+    node->kept = ws;
+    node->kept_bytes = ws_bytes;
+    node->kept_mode = pa_get_f32_math();
+    O->set_grad_fn(node);
+  }
 }
 
 std::shared_ptr<Tensor> layer_norm(const std::shared_ptr<Tensor>& input,

@@ -23,7 +23,7 @@ STATUS = {
 EXPORTS = [
     "pa_abi_version", "pa_status_string", "pa_device_status", "pa_wait_selftest", "pa_set_f32_math",
     "pa_get_f32_math",
-    "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_noalloc",
+    "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_kept", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
     "pa_layer_norm_fwd", "pa_add_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
     "pa_layer_norm_bwd_accumulate", "pa_add_layer_norm_bwd",
@@ -66,6 +66,7 @@ _SIGS = {
     "pa_attn_fwd": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "pa_attn_bwd_workspace_size": (_sz, [ctypes.POINTER(AttnDesc)]),
     "pa_attn_bwd": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp, _sz, _vp]),
+    "pa_attn_bwd_kept": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp, _sz, _int, _vp, _sz, _vp]),
     "pa_attn_bwd_noalloc": (_int, [ctypes.POINTER(AttnDesc)] + [_vp] * 9 + [_int, _vp]),
     "pa_attn_delta": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp]),
     "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
@@ -208,6 +209,19 @@ def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, workspace, accumulate=False, desc=
                             _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), int(bool(accumulate)),
                             _ptr(workspace), ws_bytes, _stream() if stream is None else stream)
     _check("pa_attn_bwd", st)
+
+
+def attn_bwd_kept(q, k, v, o, dO, lse, dq, dk, dv, fwd_workspace, fwd_mode, workspace,
+                  accumulate=False, desc=None, stream=None):
+    """attn_bwd reusing the q, k, v planes an fp32 attn_fwd left in its workspace
+    (made under f32 math mode fwd_mode, 'split3' or 'bf16')."""
+    d = desc or attn_desc(q)
+    st = load().pa_attn_bwd_kept(
+        ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(dq),
+        _ptr(dk), _ptr(dv), int(bool(accumulate)), _ptr(fwd_workspace),
+        fwd_workspace.numel() * fwd_workspace.element_size(), F32_MATH[fwd_mode], _ptr(workspace),
+        workspace.numel() * workspace.element_size(), _stream() if stream is None else stream)
+    _check("pa_attn_bwd_kept", st)
 
 
 # Scratch limit of pa_attn_bwd_noalloc (PA_ATTN_BWD_NOALLOC_MAX_WORKSPACE).

@@ -319,3 +319,35 @@ def test_attention_f32_tensors_bf16_math(B, L, H, D, bf16_math):
     assert pa_capi.device_status() == 0
     f = lambda t: t.cpu().numpy().astype(np.float64)
     _check(tuple(rounded), (f(o), f(lse), f(dq), f(dk), f(dv)), accumulate=True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fwd_mode,bwd_mode", [("bf16", "bf16"), ("split3", "split3"),
+                                               ("split3", "bf16"), ("bf16", "split3")])
+def test_attention_f32_backward_with_kept_planes(fwd_mode, bwd_mode):
+    """pa_attn_bwd_kept reuses the q, k, v planes the fp32 forward left in its
+    workspace: the same results as pa_attn_bwd (dK, dV bit for bit; dQ within
+    the fp32 reduction order of its accumulator), also when the math mode
+    changed in between (split3 planes serve bf16; bf16 planes make a split3
+    backward convert q, k, v again)."""
+    import pa_capi
+    B, L, H, D = 2, 384, 3, 64
+    shape = (B, L, H, D)
+    tq, tk, tv, tg = (torch.from_numpy(seeded_normal(40 + i, shape, 0.5)).cuda() for i in range(4))
+    d = pa_capi.attn_desc(tq)
+    o, lse = torch.empty_like(tq), torch.empty(B * H, L, device="cuda")
+    try:
+        pa_capi.set_f32_math(fwd_mode)
+        fws = torch.empty(pa_capi.attn_fwd_workspace_size(d), dtype=torch.uint8, device="cuda")
+        pa_capi.attn_fwd(tq, tk, tv, o, lse, workspace=fws)
+        pa_capi.set_f32_math(bwd_mode)
+        ws = torch.empty(pa_capi.attn_bwd_workspace_size(d), dtype=torch.uint8, device="cuda")
+        got = [torch.full_like(tq, float("nan")) for _ in range(3)]
+        pa_capi.attn_bwd_kept(tq, tk, tv, o, tg, lse, *got, fws, fwd_mode, ws)
+        want = [torch.full_like(tq, float("nan")) for _ in range(3)]
+        pa_capi.attn_bwd(tq, tk, tv, o, tg, lse, *want, ws)
+        assert pa_capi.device_status() == 0
+    finally:
+        pa_capi.set_f32_math("split3")
+    assert torch.equal(got[1], want[1]) and torch.equal(got[2], want[2])
+    assert rel_err(got[0].cpu().numpy(), want[0].cpu().numpy()) < 1e-6
