@@ -763,8 +763,10 @@ def run_train(args):
     ms_ar = None
     if tr.reducer is not None:
         ms_ar = timed(lambda i: tr.reducer())
-    # the same step with fp32-level products (side figure)
+    # the same step with fp32-level products (side figure; one untimed step
+    # first, which captures its graph on one GPU)
     tr.math = "split3"
+    tr.step_resident()
     ms_split3 = timed(lambda i: tr.step_resident())
     status = pa.device_status()
     if dist is not None:
@@ -786,7 +788,8 @@ def run_train(args):
         "data": "synthetic denoise sequences (4 sinusoids lifted by a fixed Linear(1->1024) + noise)",
         "config": {"workload": "denoise transformer training step", **TRAIN,
                    "global_batch": TRAIN["batch"] * world, "parallelism": "dp%d" % world,
-                   "params": tr.num_parameters},
+                   "params": tr.num_parameters,
+                   "cuda_graph": bool(tr.graph and tr.reducer is None)},
         "model_tflops_per_gpu": round(tflops, 1),
         "model_flops_per_gpu_step": flops,
         "frac_of_sustained_peak": round(tflops / (peak_sus or peak), 4),

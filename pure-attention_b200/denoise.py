@@ -31,6 +31,16 @@ master weights and fp32 Adam.
 Stream order: the operators run on the CUDA legacy default stream, which is
 also torch's default stream, so the torch copies and process-group collectives
 issued from the same thread are ordered with them without host syncs.
+
+CUDA graph (one GPU, no gradient all-reduce): the first step on an input
+buffer captures zero_grad, forward, MSE and backward - about 340 kernel
+launches, the stream-ordered allocations and frees of the step's activations
+and the loss copied into a persistent scalar - into a CUDA graph on a side
+stream; later steps replay it and run Adam after it. Replay removes the host
+work and the launch gaps between the kernels. The side stream waits for the
+default stream before each step and the default stream for it after, so
+callers see the same order as eager steps. A graph is kept per input buffer
+and f32 math mode (the mode is fixed at capture).
 """
 import math
 
@@ -296,7 +306,7 @@ class DenoiseTrainer:
 
     def __init__(self, layers=6, embed=1024, heads=16, ffn=4096, seq=2048, batch=8, lr=1e-4,
                  seed=5, bucket_bytes=25 << 20, group=None, math="split3", tail_bytes=0,
-                 tail_bucket_bytes=None):
+                 tail_bucket_bytes=None, graph=None):
         import torch.distributed as dist
         self.shape = (batch, seq, embed)
         self.math = math
@@ -318,6 +328,13 @@ class DenoiseTrainer:
             self.reducer = GradAllReduce.for_tensors(self.params, bucket_bytes, group, tail_bytes,
                                                      tail_bucket_bytes)
         self.overlap = True  # all-reduce each bucket while the rest of the backward runs
+        # replay the forward + backward as a CUDA graph (default: on one GPU)
+        self.graph = (self.reducer is None) if graph is None else bool(graph)
+        if self.graph and self.reducer is not None:
+            raise ValueError("graph replay runs without a gradient all-reduce")
+        self._graphs = {}  # (input tensor, math) -> torch.cuda.CUDAGraph
+        self._gstream = None
+        self._loss = None
 
     def _leaf_ready(self, t):
         self.reducer.ready(t.grad_view().__cuda_array_interface__["data"][0])
@@ -332,8 +349,53 @@ class DenoiseTrainer:
         self.x_dev.view(x_host.shape).copy_(x_host, non_blocking=True)
         self.t_dev.view(t_host.shape).copy_(t_host, non_blocking=True)
 
+    def _forward_backward(self):
+        """zero_grad, forward, MSE, backward into self._loss (graph capture body:
+        every tensor of the step is freed before it returns)."""
+        import pa_capi
+        self.opt.zero_grad()
+        out = self.model.forward(self.x)
+        loss = self.criterion(out, self.t)
+        loss.backward()
+        lib, st = pa_capi.load(), pa.get_stream()
+        dst = self._loss.__cuda_array_interface__["data"][0]
+        if (lib.pa_fill(dst, 1, 0.0, st) != 0 or
+                lib.pa_grad_accumulate(loss.__cuda_array_interface__["data"][0], dst, 1, st) != 0):
+            raise RuntimeError("DenoiseTrainer: loss copy failed")
+        del out, loss
+
+    def _step_graph(self):
+        torch = _torch()
+        if self._gstream is None:
+            self._gstream = torch.cuda.Stream()
+            self._loss = pa.Tensor([1], False)
+        main, s = torch.cuda.current_stream(), self._gstream
+        prev = pa.get_stream()
+        s.wait_stream(main)  # inputs and earlier steps first
+        pa.set_stream(s.cuda_stream)
+        try:
+            key = (id(self.x), self.math)
+            g = self._graphs.get(key)
+            with torch.cuda.stream(s):
+                if g is None:
+                    for k in [k for k in self._graphs if k[0] == key[0]]:
+                        del self._graphs[k]  # a graph of the same input in another math mode
+                    self._forward_backward()  # eager once: first-use setup outside the capture
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=s):
+                        self._forward_backward()
+                    self._graphs[key] = g
+                g.replay()
+                self.opt.step()
+        finally:
+            pa.set_stream(prev)
+        main.wait_stream(s)
+        return self._loss
+
     def step_resident(self):
         pa.set_float32_math(self.math)
+        if self.graph and self.reducer is None:
+            return self._step_graph()
         self.opt.zero_grad()
         out = self.model.forward(self.x)
         loss = self.criterion(out, self.t)

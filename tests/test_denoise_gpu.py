@@ -172,6 +172,32 @@ def test_pipelined_train_loop_matches_step_by_step(dn):
     assert b.train(seq[:1])[0] > 0 and len(b.train([])) == 0
 
 
+@pytest.mark.gpu
+def test_graph_replay_takes_the_eager_steps(dn):
+    """On one GPU the trainer captures its forward + backward into a CUDA graph
+    once per input buffer and math mode and replays it: the same losses as a
+    trainer launching every kernel (graph=False) - the first one bit for bit -
+    also after the math mode changes (a new capture)."""
+    lift = dn.embedding(SMALL["embed"], 5)
+    rng = np.random.default_rng(21)
+    data = [tuple(_pinned(a) for a in dn.denoise_batch(rng, SMALL["batch"], SMALL["seq"], lift))
+            for _ in range(2)]
+    a = dn.DenoiseTrainer(lr=1e-3, graph=False, **SMALL)
+    b = dn.DenoiseTrainer(lr=1e-3, **SMALL)
+    assert b.graph and not a.graph
+    la = [a.step(*data[i % 2]) for i in range(4)]
+    lb = [b.step(*data[i % 2]) for i in range(4)]
+    assert len(b._graphs) == 1
+    assert lb[0] == la[0]
+    np.testing.assert_allclose(lb, la, rtol=1e-5)
+    a.math = b.math = "bf16"
+    la2 = [a.step(*data[i % 2]) for i in range(2)]
+    lb2 = [b.step(*data[i % 2]) for i in range(2)]
+    assert len(b._graphs) == 1 and list(b._graphs)[0][1] == "bf16"
+    np.testing.assert_allclose(lb2, la2, rtol=1e-4)
+    assert b.train(data)[1] > 0 and len(b._graphs) == 2  # the second input buffer
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
