@@ -126,6 +126,9 @@ def parse():
                     help="--train: the gradients backward finishes last (this many MB) go into "
                          "smaller buckets of --tail-bucket-mb")
     ap.add_argument("--tail-bucket-mb", type=float, default=4.0)
+    ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto",
+                    help="--train: replay forward + backward as a CUDA graph (auto: on one GPU; "
+                         "on: also with the gradient all-reduce captured)")
     return ap.parse_args()
 
 
@@ -715,7 +718,8 @@ def run_train(args):
     import denoise
     peak, peak_sus, _, peak_src = peaks()
     mb = lambda x: int(x * (1 << 20))
-    tr = denoise.DenoiseTrainer(lr=1e-4, math="bf16", bucket_bytes=mb(args.bucket_mb),
+    graph = {"auto": None, "on": True, "off": False}[args.graph]
+    tr = denoise.DenoiseTrainer(lr=1e-4, math="bf16", bucket_bytes=mb(args.bucket_mb), graph=graph,
                                 tail_bytes=mb(args.tail_mb),
                                 tail_bucket_bytes=mb(args.tail_bucket_mb) if args.tail_mb else None,
                                 **TRAIN)
@@ -769,6 +773,7 @@ def run_train(args):
     tr.step_resident()
     ms_split3 = timed(lambda i: tr.step_resident())
     status = pa.device_status()
+    tr.release_graphs()
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:
@@ -789,7 +794,7 @@ def run_train(args):
         "config": {"workload": "denoise transformer training step", **TRAIN,
                    "global_batch": TRAIN["batch"] * world, "parallelism": "dp%d" % world,
                    "params": tr.num_parameters,
-                   "cuda_graph": bool(tr.graph and tr.reducer is None)},
+                   "cuda_graph": bool(tr.graph and (tr.reducer is None or graph is not None))},
         "model_tflops_per_gpu": round(tflops, 1),
         "model_flops_per_gpu_step": flops,
         "frac_of_sustained_peak": round(tflops / (peak_sus or peak), 4),

@@ -32,7 +32,8 @@ Stream order: the operators run on the CUDA legacy default stream, which is
 also torch's default stream, so the torch copies and process-group collectives
 issued from the same thread are ordered with them without host syncs.
 
-CUDA graph (one GPU, no gradient all-reduce): the first step on an input
+CUDA graph (graph=True, the default; with a gradient all-reduce its
+overlapped NCCL buckets are captured with the backward): the first step on an input
 buffer captures zero_grad, forward, MSE and backward - about 340 kernel
 launches, the stream-ordered allocations and frees of the step's activations
 and the loss copied into a persistent scalar - into a CUDA graph on a side
@@ -211,7 +212,9 @@ class GradAllReduce:
             raise ValueError("one key per gradient")
         self.where = {keys[i]: b for b, idx in enumerate(plan) for i in idx}
         cuda = grads[0].device.type == "cuda"
-        self.comm = torch.cuda.Stream(device=grads[0].device) if cuda else None
+        # high priority: a bucket's all-reduce kernel takes SMs as soon as the
+        # backward's kernels free some, instead of queueing behind the next ones
+        self.comm = torch.cuda.Stream(device=grads[0].device, priority=-1) if cuda else None
         self.pending = None
 
     @classmethod
@@ -328,10 +331,9 @@ class DenoiseTrainer:
             self.reducer = GradAllReduce.for_tensors(self.params, bucket_bytes, group, tail_bytes,
                                                      tail_bucket_bytes)
         self.overlap = True  # all-reduce each bucket while the rest of the backward runs
-        # replay the forward + backward as a CUDA graph (default: on one GPU)
-        self.graph = (self.reducer is None) if graph is None else bool(graph)
-        if self.graph and self.reducer is not None:
-            raise ValueError("graph replay runs without a gradient all-reduce")
+        # replay the forward + backward as a CUDA graph (with a gradient
+        # all-reduce, its overlapped NCCL buckets are captured with the backward)
+        self.graph = True if graph is None else bool(graph)
         self._graphs = {}  # (input tensor, math) -> torch.cuda.CUDAGraph
         self._gstream = None
         self._loss = None
@@ -356,7 +358,12 @@ class DenoiseTrainer:
         self.opt.zero_grad()
         out = self.model.forward(self.x)
         loss = self.criterion(out, self.t)
-        loss.backward()
+        if self.reducer is not None:
+            self.reducer.begin()
+            loss.backward(True, self._leaf_ready)
+            self.reducer.finish()
+        else:
+            loss.backward()
         lib, st = pa_capi.load(), pa.get_stream()
         dst = self._loss.__cuda_array_interface__["data"][0]
         if (lib.pa_fill(dst, 1, 0.0, st) != 0 or
@@ -392,9 +399,14 @@ class DenoiseTrainer:
         main.wait_stream(s)
         return self._loss
 
+    def release_graphs(self):
+        """Drop the captured graphs (before destroying a process group whose
+        collectives they hold)."""
+        self._graphs.clear()
+
     def step_resident(self):
         pa.set_float32_math(self.math)
-        if self.graph and self.reducer is None:
+        if self.graph:
             return self._step_graph()
         self.opt.zero_grad()
         out = self.model.forward(self.x)

@@ -235,6 +235,7 @@ def _dp_worker(rank, world, port, out_dir):
         th.cuda.synchronize()
         np.savez(os.path.join(out_dir, "dp%d.npz" % rank),
                  *[d.device_view(p).cpu().numpy() for p in tr.params], *grads)
+        tr.release_graphs()  # its graph holds NCCL calls: dropped before the group
     finally:
         dist.destroy_process_group()
 
@@ -278,12 +279,14 @@ def test_two_rank_data_parallel_matches_one_rank(dn, tmp_path):
 
 
 @pytest.mark.gpu
-def test_gradient_arenas_reduce_in_place(dn):
+@pytest.mark.parametrize("graph", [False, True])
+def test_gradient_arenas_reduce_in_place(dn, graph):
     """GradAllReduce.for_tensors moves every parameter's gradient into one flat
     arena per bucket (the first layers' gradients, finished last, in small tail
     buckets) and all-reduces each arena in place. With a one-rank NCCL group
     the average is the identity, so a trainer whose gradients live in the
-    arenas takes the same steps as one without a reducer - up to the last bits
+    arenas takes the same steps as one without a reducer, launched eagerly or
+    replayed as a CUDA graph that holds the all-reduces - up to the last bits
     that differ between any two runs (the split-K weight-gradient GEMMs and
     the dQ reductions add their parts in no fixed order)."""
     import torch.distributed as dist
@@ -293,8 +296,8 @@ def test_gradient_arenas_reduce_in_place(dn):
         x, t = dn.denoise_batch(np.random.default_rng(13), SMALL["batch"], SMALL["seq"],
                                 dn.embedding(SMALL["embed"], 5))
         x, t = _pinned(x), _pinned(t)
-        a = dn.DenoiseTrainer(lr=1e-3, **SMALL)
-        b = dn.DenoiseTrainer(lr=1e-3, **SMALL)
+        a = dn.DenoiseTrainer(lr=1e-3, graph=graph, **SMALL)
+        b = dn.DenoiseTrainer(lr=1e-3, graph=graph, **SMALL)
         assert a.reducer is None and b.reducer is None  # one rank: no reducer by default
         b.reducer = dn.GradAllReduce.for_tensors(b.params, bucket_bytes=1 << 16,
                                                  tail_bytes=1 << 16, tail_bucket_bytes=1 << 14)
@@ -307,6 +310,7 @@ def test_gradient_arenas_reduce_in_place(dn):
         for _ in range(2):
             la, lb = a.step(x, t), b.step(x, t)
             assert abs(la - lb) <= 1e-6 * abs(la)
+        assert len(b._graphs) == (1 if graph else 0)  # graph: the NCCL buckets captured too
         # The key slice of each in-projection bias has a gradient that is zero in
         # exact arithmetic (softmax ignores a constant added to a query's scores),
         # so it holds rounding noise, which Adam turns into steps of +-lr: it is
@@ -321,4 +325,7 @@ def test_gradient_arenas_reduce_in_place(dn):
             if np.linalg.norm(gp) > 0:
                 assert rel_err(gq, gp) < 1e-4, i
     finally:
+        for name in ("a", "b"):
+            if name in locals():
+                locals()[name].release_graphs()  # graphs holding NCCL calls go first
         dist.destroy_process_group()
