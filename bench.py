@@ -794,7 +794,7 @@ def run_train(args):
         "config": {"workload": "denoise transformer training step", **TRAIN,
                    "global_batch": TRAIN["batch"] * world, "parallelism": "dp%d" % world,
                    "params": tr.num_parameters,
-                   "cuda_graph": bool(tr.graph and (tr.reducer is None or graph is not None))},
+                   "cuda_graph": bool(tr.graph)},
         "model_tflops_per_gpu": round(tflops, 1),
         "model_flops_per_gpu_step": flops,
         "frac_of_sustained_peak": round(tflops / (peak_sus or peak), 4),

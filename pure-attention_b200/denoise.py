@@ -212,9 +212,7 @@ class GradAllReduce:
             raise ValueError("one key per gradient")
         self.where = {keys[i]: b for b, idx in enumerate(plan) for i in idx}
         cuda = grads[0].device.type == "cuda"
-        # high priority: a bucket's all-reduce kernel takes SMs as soon as the
-        # backward's kernels free some, instead of queueing behind the next ones
-        self.comm = torch.cuda.Stream(device=grads[0].device, priority=-1) if cuda else None
+        self.comm = torch.cuda.Stream(device=grads[0].device) if cuda else None
         self.pending = None
 
     @classmethod
