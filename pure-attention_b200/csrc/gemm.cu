@@ -89,7 +89,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                      const __grid_constant__ CUtensorMap mC2, int tma_out, int ksplit,
                      float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
                      const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
-                     int nsplit, int relu, uint32_t* status) {
+                     int nsplit, int relu, int n_fast, uint32_t* status) {
   using P = PairCfg<NT>;
   constexpr int ST = P::STAGES, STG = P::STAGE, NP = P::NP;
   extern __shared__ uint8_t smem_raw[];
@@ -110,7 +110,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   auto acc_empty = [&](int b) { return smem_u32(&bars[2 * ST + 2 + b]); };  // the even CTA's
   const int warp = warp_id();
   const int tiles_m = (Mout + 2 * GB - 1) / (2 * GB);
-  const int units = tiles_m * ((Nout + PB_N - 1) / PB_N) * ksplit;
+  const int tiles_n = (Nout + PB_N - 1) / PB_N;
+  const int units = tiles_m * tiles_n * ksplit;
+  // Tile order: consecutive units (which run at the same time) share the
+  // operand indexed by the slow index, so with n_fast the A rows of a tile
+  // come from DRAM once and serve its column tiles from L2 (A the larger
+  // operand); else the B columns do.
+  auto tile_m = [&](int tile) { return n_fast ? tile / tiles_n : tile % tiles_m; };
+  auto tile_n = [&](int tile) { return n_fast ? tile % tiles_n : tile / tiles_m; };
   const int nk_all = (Kred + GK - 1) / GK;
   const int cl = static_cast<int>(blockIdx.x) / 2, ncl = static_cast<int>(gridDim.x) / 2;
   auto kslice = [&](int u, int& kb0, int& kb1) {
@@ -146,8 +153,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       bool ok = true;
       for (int u = cl; ok && u < units; u += ncl) {
         const int tile = u / ksplit;
-        const int m0 = (tile % tiles_m) * 2 * GB + static_cast<int>(rank) * GB;
-        const int n0 = (tile / tiles_m) * PB_N + static_cast<int>(rank) * 128;
+        const int m0 = tile_m(tile) * 2 * GB + static_cast<int>(rank) * GB;
+        const int n0 = tile_n(tile) * PB_N + static_cast<int>(rank) * 128;
         int kb0, kb1;
         kslice(u, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
@@ -231,8 +238,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       ok = named_bar_and(1, 128, ok);  // the four warps leave together
       if (!ok) break;
       tc_fence_after();
-      const int row0 = (tile % tiles_m) * 2 * GB + static_cast<int>(rank) * GB;
-      const int row = row0 + r, n0 = (tile / tiles_m) * PB_N;
+      const int row0 = tile_m(tile) * 2 * GB + static_cast<int>(rank) * GB;
+      const int row = row0 + r, n0 = tile_n(tile) * PB_N;
       if (bias) {
         // every thread is past the previous tile's reads of bias_s (the barrier
         // above), so it can be refilled; the barrier below publishes it
@@ -445,9 +452,11 @@ int run_gemm_pair(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, i
   }
   const int units = tiles * ksplit;
   const int grid = 2 * (units < pairs ? units : pairs);
+  // walk N fastest when A (Mout x Kred) is the larger operand: it then streams once
+  const int n_fast = Mout > Nout ? 1 : 0;
   gemm_pair_kernel<A_MN, B_MN, NT><<<grid, 256, PairCfg<NT>::SMEM, s>>>(
       m[0], m[1], m[2], m[3], mc[0], mc[1], mc[2], al ? 1 : 0, ksplit, C, ldc, Mout, Nout, Kred,
-      accumulate, ep.bias, ep.c1, ep.c2, ep.nsplit, ep.relu, status);
+      accumulate, ep.bias, ep.c1, ep.c2, ep.nsplit, ep.relu, n_fast, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
