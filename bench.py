@@ -120,7 +120,7 @@ def parse():
                          "fwd / add+fwd / bwd / bwd-accumulate, multi-tensor Adam, the attention "
                          "backward's prep and dQ-convert kernels) and the projection GEMM timed "
                          "alone with CUDA events, as achieved GB/s (or TFLOP/s) against the peak")
-    ap.add_argument("--bucket-mb", type=float, default=25.0,
+    ap.add_argument("--bucket-mb", type=float, default=100.0,
                     help="--train: gradient bucket size of the all-reduce")
     ap.add_argument("--tail-mb", type=float, default=0.0,
                     help="--train: the gradients backward finishes last (this many MB) go into "

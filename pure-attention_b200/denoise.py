@@ -189,7 +189,7 @@ class GradAllReduce:
     and finish() makes the default stream wait for them.
     """
 
-    def __init__(self, grads, bucket_bytes=25 << 20, group=None, keys=None, tail_bytes=0,
+    def __init__(self, grads, bucket_bytes=100 << 20, group=None, keys=None, tail_bytes=0,
                  tail_bucket_bytes=None, arenas=None, plan=None):
         torch = _torch()
         import torch.distributed as dist
@@ -216,7 +216,7 @@ class GradAllReduce:
         self.pending = None
 
     @classmethod
-    def for_tensors(cls, tensors, bucket_bytes=25 << 20, group=None, tail_bytes=0,
+    def for_tensors(cls, tensors, bucket_bytes=100 << 20, group=None, tail_bytes=0,
                     tail_bucket_bytes=None):
         """Reducer over the gradients of PureAttention tensors, which are moved
         (Tensor.set_grad_storage, zeroed) into one flat arena per bucket: each
@@ -306,7 +306,7 @@ class DenoiseTrainer:
     """
 
     def __init__(self, layers=6, embed=1024, heads=16, ffn=4096, seq=2048, batch=8, lr=1e-4,
-                 seed=5, bucket_bytes=25 << 20, group=None, math="split3", tail_bytes=0,
+                 seed=5, bucket_bytes=100 << 20, group=None, math="split3", tail_bytes=0,
                  tail_bucket_bytes=None, graph=None):
         import torch.distributed as dist
         self.shape = (batch, seq, embed)
