@@ -266,6 +266,22 @@ int pa_linear_fwd_keep(const float* X, const float* W, const float* bias, float*
                        int n_outs, int relu, int M, int in_features, int out_features, void* kept,
                        size_t kept_bytes, void* workspace, size_t workspace_bytes,
                        pa_stream_t stream);
+/* pa_linear_fwd_keep with X's planes possibly made already and Y's planes
+ * written too, so a projection that reads Y next needs no conversion of it:
+ *  - flags & PA_LINEAR_KEPT_VALID: `kept` already holds X's planes, made under
+ *    f32 math mode kept_mode (e.g. the y_planes of the projection that
+ *    produced X); X is not converted again where they serve the current mode;
+ *  - y_planes (n_outs = 1; may be NULL): Y's bf16 planes, in the layout of
+ *    `kept` for a projection with in_features = out_features (256-byte
+ *    aligned, pa_linear_kept_size(M, out_features) bytes): hi = bf16(Y) and,
+ *    under split3 math, lo = bf16(Y - hi), written by the GEMM epilogue from
+ *    the same values as Y. */
+#define PA_LINEAR_KEPT_VALID 1
+int pa_linear_fwd_planes(const float* X, const float* W, const float* bias, float* const* outs,
+                         int n_outs, int relu, int M, int in_features, int out_features, void* kept,
+                         size_t kept_bytes, int kept_mode, int flags, void* y_planes,
+                         size_t y_planes_bytes, void* workspace, size_t workspace_bytes,
+                         pa_stream_t stream);
 /* pa_linear_bwd (Y = NULL) or pa_linear_relu_bwd (Y = the ReLU output,
  * n_parts = 1) reading X's planes from `kept`, written by pa_linear_fwd_keep
  * under f32 math mode `kept_mode`. Where they cannot serve the current mode

@@ -408,6 +408,36 @@ int pa_linear_fwd_keep(const float* X, const float* W, const float* bias, float*
                                workspace, status, static_cast<cudaStream_t>(stream), kept);
 }
 
+int pa_linear_fwd_planes(const float* X, const float* W, const float* bias, float* const* outs,
+                         int n_outs, int relu, int M, int in_features, int out_features, void* kept,
+                         size_t kept_bytes, int kept_mode, int flags, void* y_planes,
+                         size_t y_planes_bytes, void* workspace, size_t workspace_bytes,
+                         pa_stream_t stream) {
+  if (!X || !W || !outs || !kept) return PA_ERR_NULL;
+  const int st = linear_check(M, in_features, out_features, n_outs, workspace, workspace_bytes);
+  if (st != PA_OK) return st;
+  if (relu && n_outs != 1) return PA_ERR_SHAPE;
+  if ((flags & ~PA_LINEAR_KEPT_VALID) != 0) return PA_ERR_SHAPE;
+  const int mode = pa::f32_math();
+  if (kept_bytes < pa::linear_kept_bytes(M, in_features, mode)) return PA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(kept) & 255u) != 0) return PA_ERR_ALIGN;
+  if (y_planes) {
+    if (n_outs != 1) return PA_ERR_SHAPE;
+    if (y_planes_bytes < pa::linear_kept_bytes(M, out_features, mode)) return PA_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(y_planes) & 255u) != 0) return PA_ERR_ALIGN;
+  }
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i]) return PA_ERR_NULL;
+  // planes made under bf16 math have no lo plane: a split3 call converts X again
+  const bool valid = (flags & PA_LINEAR_KEPT_VALID) &&
+                     (mode == PA_F32_MATH_BF16 || kept_mode == PA_F32_MATH_SPLIT3);
+  uint32_t* status = status_word();
+  if (!status) return PA_ERR_DEVICE;
+  return pa::launch_linear_fwd(X, W, bias, outs, n_outs, M, in_features, out_features, relu ? 1 : 0,
+                               workspace, status, static_cast<cudaStream_t>(stream), kept,
+                               valid ? 1 : 0, y_planes);
+}
+
 int pa_linear_bwd_kept(const float* X, const float* W, const void* kept, size_t kept_bytes,
                        int kept_mode, const float* Y, const float* const* dy_parts, int n_parts,
                        float* dX, float* dW, float* dbias, int M, int in_features,

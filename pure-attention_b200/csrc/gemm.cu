@@ -89,7 +89,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                      const __grid_constant__ CUtensorMap mC2, int tma_out, int ksplit,
                      float* __restrict__ C, int ldc, int Mout, int Nout, int Kred, int accumulate,
                      const float* __restrict__ bias, float* __restrict__ C1, float* __restrict__ C2,
-                     int nsplit, int relu, int n_fast, uint32_t* status) {
+                     int nsplit, int relu, int n_fast, __nv_bfloat16* __restrict__ yp_hi,
+                     __nv_bfloat16* __restrict__ yp_lo, int yp_ld, uint32_t* status) {
   using P = PairCfg<NT>;
   constexpr int ST = P::STAGES, STG = P::STAGE, NP = P::NP;
   extern __shared__ uint8_t smem_raw[];
@@ -269,6 +270,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if (lane_id() == 0) mbar_arrive_cluster(mapa_shared(acc_empty(b), 0));
         }
         const int col0 = n0 + c * 32;
+        // this row's 32 values of the chunk, with the bias and the ReLU
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float4 f = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                 __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+          if (bias) {
+            const float4 bb = reinterpret_cast<const float4*>(bias_s)[c * 8 + e];
+            f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
+          }
+          if (relu) {
+            f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
+            f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
+          }
+          v[4 * e] = __float_as_uint(f.x); v[4 * e + 1] = __float_as_uint(f.y);
+          v[4 * e + 2] = __float_as_uint(f.z); v[4 * e + 3] = __float_as_uint(f.w);
+        }
+        // the output's bf16 operand planes (hi = bf16(y), lo = bf16(y - hi)), for a
+        // projection that reads this output next: 64 contiguous bytes per row
+        if (yp_hi && row < Mout && col0 < Nout) {
+          __nv_bfloat16* ph = yp_hi + static_cast<size_t>(row) * yp_ld + col0;
+          __nv_bfloat16* pl = yp_lo ? yp_lo + static_cast<size_t>(row) * yp_ld + col0 : nullptr;
+          if (col0 + 32 <= Nout) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t h[4], l[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float a = __uint_as_float(v[8 * e + 2 * k]);
+                const float b2 = __uint_as_float(v[8 * e + 2 * k + 1]);
+                h[k] = pack_bf16x2(a, b2);
+                l[k] = pack_bf16x2(a - __uint_as_float(h[k] << 16),
+                                   b2 - __uint_as_float(h[k] & 0xffff0000u));
+              }
+              reinterpret_cast<uint4*>(ph)[e] = make_uint4(h[0], h[1], h[2], h[3]);
+              if (pl) reinterpret_cast<uint4*>(pl)[e] = make_uint4(l[0], l[1], l[2], l[3]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {  // constant indices: v stays in registers
+              if (col0 + e < Nout) {
+                const float a = __uint_as_float(v[e]);
+                const __nv_bfloat16 h = __float2bfloat16_rn(a);
+                ph[e] = h;
+                if (pl) pl[e] = __float2bfloat16_rn(a - __bfloat162float(h));
+              }
+            }
+          }
+        }
         if (tma_out) {
           // uniform over the epilogue warps (an odd CTA past the last row stores nothing)
           if (col0 >= Nout || row0 >= Mout) continue;
@@ -277,19 +326,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           named_bar_sync(1, 128);
           uint8_t* srow = stg + buf * PB_STG;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float4 f = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                   __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
-            if (bias) {
-              const float4 bb = reinterpret_cast<const float4*>(bias_s)[c * 8 + e];
-              f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
-            }
-            if (relu) {
-              f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
-              f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
-            }
-            *reinterpret_cast<float4*>(srow + sw128_offset(r, 16 * e)) = f;
-          }
+          for (int e = 0; e < 8; ++e)
+            *reinterpret_cast<uint4*>(srow + sw128_offset(r, 16 * e)) =
+                make_uint4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
           fence_proxy_async_smem();
           named_bar_sync(1, 128);
           if (leader) {
@@ -316,14 +355,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           for (int e = 0; e < 8; ++e) {
             float4 f = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
                                    __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
-            if (bias) {
-              const float4 bb = reinterpret_cast<const float4*>(bias_s)[c * 8 + e];
-              f.x += bb.x; f.y += bb.y; f.z += bb.z; f.w += bb.w;
-            }
-            if (relu) {
-              f.x = fmaxf(f.x, 0.f); f.y = fmaxf(f.y, 0.f);
-              f.z = fmaxf(f.z, 0.f); f.w = fmaxf(f.w, 0.f);
-            }
             if (accumulate) {
               const float4 p = d4[e];
               f.x += p.x; f.y += p.y; f.z += p.z; f.w += p.w;
@@ -336,9 +367,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             const int col = col0 + e;
             if (col < Nout) {
               float* de = dst_of(col);
-              float f = __uint_as_float(v[e]) + (bias ? bias_s[c * 32 + e] : 0.f);
-              if (relu) f = fmaxf(f, 0.f);
-              *de = f + (accumulate ? *de : 0.f);
+              *de = __uint_as_float(v[e]) + (accumulate ? *de : 0.f);
             }
           }
         }
@@ -379,6 +408,10 @@ struct Epilogue {
   float* c2 = nullptr;
   int nsplit = 0;
   int relu = 0;  // max(0, .) after the bias (forward projections only)
+  // the output's bf16 planes as well (lo: split3 only; row pitch round8(Nout)),
+  // for a single-output forward projection
+  void* y_hi = nullptr;
+  void* y_lo = nullptr;
 };
 
 // fp32 [rows, cols] output with row pitch ld, as 128-row x 32-column TMA boxes.
@@ -456,7 +489,9 @@ int run_gemm_pair(const CUtensorMap* m, float* C, int ldc, int Mout, int Nout, i
   const int n_fast = Mout > Nout ? 1 : 0;
   gemm_pair_kernel<A_MN, B_MN, NT><<<grid, 256, PairCfg<NT>::SMEM, s>>>(
       m[0], m[1], m[2], m[3], mc[0], mc[1], mc[2], al ? 1 : 0, ksplit, C, ldc, Mout, Nout, Kred,
-      accumulate, ep.bias, ep.c1, ep.c2, ep.nsplit, ep.relu, n_fast, status);
+      accumulate, ep.bias, ep.c1, ep.c2, ep.nsplit, ep.relu, n_fast,
+      static_cast<__nv_bfloat16*>(ep.y_hi), static_cast<__nv_bfloat16*>(ep.y_lo), round8(Nout),
+      status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
@@ -565,12 +600,12 @@ size_t linear_kept_bytes(int M, int IN, int mode) {
 
 int launch_linear_fwd(const float* x, const float* wt, const float* bias, float* const* outs,
                       int n_outs, int M, int IN, int OUT, int relu, void* ws, uint32_t* status,
-                      cudaStream_t s, void* kept) {
+                      cudaStream_t s, void* kept, int kept_valid, void* y_planes) {
   uint8_t* w = static_cast<uint8_t*>(ws);
   uint8_t* kp = static_cast<uint8_t*>(kept);
   const Planes a = kept ? Planes{kp, kp + plane_size(M, IN), M, IN} : carve(w, M, IN);
   const Planes b = carve(w, IN, OUT);
-  int st = split_into(x, a, s);
+  int st = kept && kept_valid ? PA_OK : split_into(x, a, s);  // valid: X's planes are there
   if (st != PA_OK) return st;
   st = split_into(wt, b, s);
   if (st != PA_OK) return st;
@@ -581,6 +616,11 @@ int launch_linear_fwd(const float* x, const float* wt, const float* bias, float*
     ep.nsplit = OUT / n_outs;
     ep.c1 = outs[1];
     ep.c2 = n_outs > 2 ? outs[2] : nullptr;
+  }
+  if (y_planes) {  // Y's planes in the kept layout of a projection that reads Y next
+    uint8_t* yp = static_cast<uint8_t*>(y_planes);
+    ep.y_hi = yp;
+    ep.y_lo = f32_math() == PA_F32_MATH_BF16 ? nullptr : yp + plane_size(M, OUT);
   }
   return gemm_planes(0, a, b, outs[0], M, OUT, IN, ep, status, s);
 }

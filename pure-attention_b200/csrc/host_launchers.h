@@ -98,9 +98,12 @@ size_t linear_workspace_bytes(int M, int IN, int OUT);
 // whose sign masks dy.
 // kept (optional): X's operand planes, written by the forward (linear_kept_bytes
 // for the math mode) and read by the backward instead of converting X again.
+// kept: X's planes (written here, or already there when kept_valid); y_planes:
+// Y's planes too (single output), in the kept layout of a projection reading Y.
 int launch_linear_fwd(const float* x, const float* w, const float* bias, float* const* outs,
                       int n_outs, int M, int IN, int OUT, int relu, void* ws, uint32_t* status,
-                      cudaStream_t s, void* kept = nullptr);
+                      cudaStream_t s, void* kept = nullptr, int kept_valid = 0,
+                      void* y_planes = nullptr);
 int launch_linear_bwd(const float* x, const float* w, const float* const* dy_parts, int n_parts,
                       const float* relu_out, float* dx, float* dw, float* dbias, int M, int IN,
                       int OUT, void* ws, uint32_t* status, cudaStream_t s,

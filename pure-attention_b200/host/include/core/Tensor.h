@@ -66,6 +66,15 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
   using LeafHook = std::function<void(const std::shared_ptr<Tensor>&)>;
   void backward(bool seed_with_ones, const LeafHook& leaf_ready) const;
 
+  // bf16 operand planes of this tensor's data, written by the op that produced
+  // it (a projection's epilogue) under f32 math mode operand_planes_mode, in
+  // the layout a projection reading the tensor keeps for its backward; that
+  // projection takes them instead of converting the tensor. to_device drops
+  // them; other writes into the data must reset them too.
+  std::shared_ptr<void> operand_planes;
+  size_t operand_planes_bytes = 0;
+  int operand_planes_mode = -1;
+
  private:
   float32_t* data_ptr = nullptr;
   float32_t* gradient_ptr = nullptr;

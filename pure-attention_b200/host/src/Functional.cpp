@@ -114,30 +114,54 @@ void linear(const std::shared_ptr<Tensor>& A, const std::shared_ptr<Tensor>& W,
     outs.push_back(mine.back()->get_data_ptr());
   }
   Scratch ws(pa_linear_workspace_size(M, K, N), stream);
-  std::shared_ptr<LinearFunction> node;
-  if (g) {
-    // the backward needs X's operand planes again: keep the forward's in the node
-    node = std::make_shared<LinearFunction>(A, W, bias, mine, relu);
-    node->kept_bytes = pa_linear_kept_size(M, K);
-    node->kept_mode = pa_get_f32_math();
-    void* p = nullptr;
-    retain_pool_memory();
-    if (cudaMallocAsync(&p, node->kept_bytes, stream) != cudaSuccess)
-      throw std::runtime_error("Linear: cannot allocate the kept operand planes");
-    node->kept = std::shared_ptr<void>(p, [](void* q) { cudaFreeAsync(q, CudaContext::getStream()); });
-    check_status(pa_linear_fwd_keep(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
-                                    outs.data(), static_cast<int>(num_parts), relu ? 1 : 0, M, K, N,
-                                    p, node->kept_bytes, ws.get(), ws.size(), ps(stream)),
+  // X's operand planes: from X's producer where they serve this math mode (no
+  // conversion), else converted here; with gradients the node keeps them for
+  // the backward. A hidden layer (Linear + ReLU) also writes its output's
+  // planes for the projection that reads it next.
+  const int mode = pa_get_f32_math();
+  const size_t need = pa_linear_kept_size(M, K);
+  const bool have = A->operand_planes && A->operand_planes_bytes >= need &&
+                    (mode == PA_F32_MATH_BF16 || A->operand_planes_mode == PA_F32_MATH_SPLIT3);
+  std::shared_ptr<void> kept;
+  size_t kept_bytes = need;
+  int kept_mode = mode;
+  if (have) {
+    kept = A->operand_planes;
+    kept_bytes = A->operand_planes_bytes;
+    kept_mode = A->operand_planes_mode;
+  } else if (g || relu) {
+    kept = device_buffer(kept_bytes, stream, "Linear");
+  }
+  std::shared_ptr<void> y_planes;
+  size_t y_bytes = 0;
+  if (relu) {
+    y_bytes = pa_linear_kept_size(M, N);
+    y_planes = device_buffer(y_bytes, stream, "Linear + ReLU");
+  }
+  if (kept) {
+    check_status(pa_linear_fwd_planes(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
+                                      outs.data(), static_cast<int>(num_parts), relu ? 1 : 0, M, K,
+                                      N, kept.get(), kept_bytes, kept_mode,
+                                      have ? PA_LINEAR_KEPT_VALID : 0, y_planes.get(), y_bytes,
+                                      ws.get(), ws.size(), ps(stream)),
                  relu ? "Linear + ReLU" : "Linear");
-  } else if (relu) {
-    check_status(pa_linear_relu_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
-                                    outs[0], M, K, N, ws.get(), ws.size(), ps(stream)),
-                 "Linear + ReLU");
   } else {
     check_status(pa_linear_fwd(A->get_data_ptr(), W->get_data_ptr(), bias->get_data_ptr(),
                                outs.data(), static_cast<int>(num_parts), M, K, N, ws.get(),
                                ws.size(), ps(stream)),
                  "Linear");
+  }
+  if (y_planes) {
+    mine[0]->operand_planes = y_planes;
+    mine[0]->operand_planes_bytes = y_bytes;
+    mine[0]->operand_planes_mode = mode;
+  }
+  std::shared_ptr<LinearFunction> node;
+  if (g) {
+    node = std::make_shared<LinearFunction>(A, W, bias, mine, relu);
+    node->kept = kept;
+    node->kept_bytes = kept_bytes;
+    node->kept_mode = kept_mode;
   }
   if (g) {
     for (auto& p : mine) p->set_grad_fn(node);

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include "core/Context.h"
@@ -54,6 +55,16 @@ class Scratch {
 };
 
 inline pa_stream_t ps(cudaStream_t s) { return static_cast<pa_stream_t>(s); }
+
+// Stream-ordered device memory owned by a shared_ptr (freed on the context
+// stream when the last owner lets go).
+inline std::shared_ptr<void> device_buffer(size_t bytes, cudaStream_t s, const char* what) {
+  void* p = nullptr;
+  retain_pool_memory();
+  if (cudaMallocAsync(&p, bytes, s) != cudaSuccess)
+    throw std::runtime_error(std::string(what) + ": cannot allocate device memory");
+  return std::shared_ptr<void>(p, [](void* q) { cudaFreeAsync(q, CudaContext::getStream()); });
+}
 
 inline size_t last_dim(const Tensor& t) {
   const auto sh = t.get_shape();

@@ -29,7 +29,7 @@ EXPORTS = [
     "pa_layer_norm_bwd_accumulate", "pa_add_layer_norm_bwd",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
-    "pa_linear_relu_bwd", "pa_linear_kept_size", "pa_linear_fwd_keep", "pa_linear_bwd_kept",
+    "pa_linear_relu_bwd", "pa_linear_kept_size", "pa_linear_fwd_keep", "pa_linear_fwd_planes", "pa_linear_bwd_kept",
     "pa_bias_add", "pa_add", "pa_grad_accumulate", "pa_bias_grad", "pa_bias_grad_workspace_size", "pa_bias_grad_ws",
     "pa_split_last_dim", "pa_concat_last_dim_grad",
     "pa_relu_fwd", "pa_relu_bwd", "pa_mse_fwd", "pa_mse_fwd_workspace_size", "pa_mse_fwd_ws", "pa_mse_bwd", "pa_adam_step", "pa_adam_step_multi",
@@ -84,6 +84,7 @@ _SIGS = {
     "pa_linear_relu_bwd": (_int, [_vp] * 7 + [_int] * 3 + [_vp, _sz, _vp]),
     "pa_linear_kept_size": (_sz, [_int, _int]),
     "pa_linear_fwd_keep": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp)] + [_int] * 5 + [_vp, _sz, _vp, _sz, _vp]),
+    "pa_linear_fwd_planes": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp)] + [_int] * 5 + [_vp, _sz, _int, _int, _vp, _sz, _vp, _sz, _vp]),
     "pa_linear_bwd_kept": (_int, [_vp, _vp, _vp, _sz, _int, _vp, ctypes.POINTER(_vp), _int, _vp, _vp, _vp]
                            + [_int] * 4 + [_vp, _sz, _vp]),
     "pa_linear_fwd": (_int, [_vp, _vp, _vp, ctypes.POINTER(_vp), _int, _int, _int, _int, _vp, _sz, _vp]),
@@ -433,6 +434,20 @@ def linear_fwd_keep(x, w, bias, outs, M, in_features, out_features, kept, relu=F
     _check("pa_linear_fwd_keep", load().pa_linear_fwd_keep(
         _ptr(x), _ptr(w), _ptr(bias) if bias is not None else None, arr, len(outs), int(relu), M,
         in_features, out_features, _ptr(kept), kept.numel() * kept.element_size(), _ptr(ws), nb,
+        _stream() if stream is None else stream))
+
+
+def linear_fwd_planes(x, w, bias, outs, M, in_features, out_features, kept, kept_mode="bf16",
+                      kept_valid=False, y_planes=None, relu=False, workspace=None, stream=None):
+    """linear_fwd_keep with X's planes already in `kept` (kept_valid, made under
+    kept_mode) and, optionally, Y's planes written to y_planes."""
+    ws, nb = _linear_ws(M, in_features, out_features, workspace, x.device)
+    arr = (_vp * len(outs))(*[_ptr(o) for o in outs])
+    yb = 0 if y_planes is None else y_planes.numel() * y_planes.element_size()
+    _check("pa_linear_fwd_planes", load().pa_linear_fwd_planes(
+        _ptr(x), _ptr(w), _ptr(bias) if bias is not None else None, arr, len(outs), int(relu), M,
+        in_features, out_features, _ptr(kept), kept.numel() * kept.element_size(),
+        F32_MATH[kept_mode], 1 if kept_valid else 0, _ptr(y_planes), yb, _ptr(ws), nb,
         _stream() if stream is None else stream))
 
 

@@ -561,3 +561,38 @@ def test_linear_bwd_dx_overwrite(M, IN, OUT, relu):
         assert torch.equal(grads[0][2], grads[1][2])  # bias gradient: fixed-order sums
     finally:
         pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("math_mode", ["bf16", "split3"])
+@pytest.mark.parametrize("M,IN,HID,OUT", [(4096, 256, 1024, 256), (300, 64, 200, 72)])
+def test_linear_output_planes_feed_the_next_projection(math_mode, M, IN, HID, OUT):
+    """pa_linear_fwd_planes writes the hidden layer's bf16 planes from its GEMM
+    epilogue: byte for byte the planes the next projection would make from the
+    stored output, so that projection, taking them as kept (PA_LINEAR_KEPT_VALID),
+    gives the same output bits as converting them itself."""
+    import pa_capi
+    x, w1, b1 = seeded_normal(81, (M, IN)), seeded_normal(82, (IN, HID), 0.1), seeded_normal(83, (HID,))
+    w2, b2 = seeded_normal(84, (HID, OUT), 0.05), seeded_normal(85, (OUT,))
+    pa_capi.set_f32_math(math_mode)
+    try:
+        kept1 = torch.empty(pa_capi.linear_kept_size(M, IN), dtype=torch.uint8, device="cuda")
+        yp = torch.zeros(pa_capi.linear_kept_size(M, HID), dtype=torch.uint8, device="cuda")
+        h = torch.empty(M, HID, device="cuda")
+        pa_capi.linear_fwd_planes(_cu(x), _cu(w1), _cu(b1), [h], M, IN, HID, kept1, math_mode,
+                                  y_planes=yp, relu=True)
+        h_ref = torch.empty_like(h)
+        pa_capi.linear_relu_fwd(_cu(x), _cu(w1), _cu(b1), h_ref, M, IN, HID)
+        assert torch.equal(h, h_ref)
+        # the planes the next projection makes from h itself
+        kept2 = torch.zeros_like(yp)
+        y_conv = torch.empty(M, OUT, device="cuda")
+        pa_capi.linear_fwd_keep(h, _cu(w2), _cu(b2), [y_conv], M, HID, OUT, kept2)
+        assert torch.equal(yp, kept2)
+        y_taken = torch.empty_like(y_conv)
+        pa_capi.linear_fwd_planes(h, _cu(w2), _cu(b2), [y_taken], M, HID, OUT, yp, math_mode,
+                                  kept_valid=True)
+        assert torch.equal(y_taken, y_conv)
+        assert pa_capi.device_status() == 0
+    finally:
+        pa_capi.set_f32_math("split3")
