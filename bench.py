@@ -869,7 +869,32 @@ def run_kernels(args):
     hbm_row("ln_bwd_kernel (accumulate into dX) + reduce", f"M{M} N{N} fp32", 4 * e + 8 * M,
             timed(lambda: pa_capi.layer_norm_bwd(dy, x, mu, rs, gam, dx, dg, db, ws,
                                                  accumulate=True)))
-    del x, r, dy, y, s, dx
+    # backward of the residual add + LayerNorm: read dY, the sum and the sum's own
+    # gradient, write both addends' gradients (overwritten)
+    dr = torch.empty_like(x)
+    hbm_row("add_ln_bwd_kernel + ln_param_reduce_kernel", f"M{M} N{N} fp32", 5 * e + 8 * M,
+            timed(lambda: pa_capi.add_layer_norm_bwd(dy, r, x, mu, rs, gam, dx, dr, dg, db, ws)))
+    del x, r, dy, y, s, dx, dr
+
+    # projection backward with the ReLU mask at the FFN's first layer (bf16 math): the
+    # dY gather with the bias-gradient sums (split_colsum_kernel) and the two GEMMs;
+    # the ncu capture of this call isolates the gather
+    pa_capi.set_f32_math("bf16")
+    Mf, INf, OUTf = 16384, 1024, 4096
+    xf, wf, yf, dyf = rnd(Mf, INf), rnd(INf, OUTf) * 0.03, rnd(Mf, OUTf).relu_(), rnd(Mf, OUTf)
+    dxf, dwf, dbf = torch.zeros(Mf, INf, device="cuda"), torch.zeros(INf, OUTf, device="cuda"), \
+        torch.zeros(OUTf, device="cuda")
+    wsf = torch.empty(pa_capi.linear_workspace_size(Mf, INf, OUTf), dtype=torch.uint8, device="cuda")
+    ms_f = timed(lambda: pa_capi.linear_relu_bwd(xf, wf, yf, dyf, dxf, dwf, dbf, Mf, INf, OUTf, wsf))
+    fl_f = 2 * 2 * Mf * INf * OUTf
+    rows.append({"kernel": "pa_linear_relu_bwd (split_colsum_kernel + bias_grad_kernel + split_planes x2 + "
+                           "gemm_pair_kernel x2)",
+                 "shape": f"{Mf}x{INf} -> {OUTf}, ReLU mask, bf16 products", "bound": "tensor",
+                 "us": round(ms_f * 1e3, 2), "algorithmic_flops": fl_f,
+                 "achieved_tflops": round(fl_f / (ms_f * 1e-3) / 1e12, 1),
+                 "gather_algorithmic_bytes": 10 * Mf * OUTf})
+    pa_capi.set_f32_math("split3")
+    del xf, wf, yf, dyf, dxf, dwf, dbf, wsf
 
     # multi-tensor Adam over the training step's 75.6 M parameters (48 tensors of its shapes)
     shapes = [(1024, 3072), (3072,), (1024, 1024), (1024,), (1024, 4096), (4096,), (4096, 1024),
