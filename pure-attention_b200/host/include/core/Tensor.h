@@ -71,9 +71,9 @@ class Tensor : public std::enable_shared_from_this<Tensor> {
   // the layout a projection reading the tensor keeps for its backward; that
   // projection takes them instead of converting the tensor. to_device drops
   // them; other writes into the data must reset them too.
-  std::shared_ptr<void> operand_planes;
-  size_t operand_planes_bytes = 0;
-  int operand_planes_mode = -1;
+  mutable std::shared_ptr<void> operand_planes;
+  mutable size_t operand_planes_bytes = 0;
+  mutable int operand_planes_mode = -1;
 
  private:
   float32_t* data_ptr = nullptr;

@@ -64,7 +64,7 @@ Tensor::~Tensor() {
 void Tensor::to_device(const std::vector<float32_t>& host_data) const {
   if (host_data.size() != size)
     throw std::length_error("Size mismatch: CPU array has different size to GPU tensor.");
-  const_cast<Tensor*>(this)->operand_planes.reset();  // they described the old values
+  operand_planes.reset();  // they described the old values
   const cudaStream_t s = CudaContext::getStream();
   if (cudaMemcpyAsync(data_ptr, host_data.data(), size * sizeof(float32_t), cudaMemcpyHostToDevice,
                       s) != cudaSuccess ||
