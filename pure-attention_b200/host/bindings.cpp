@@ -1,6 +1,7 @@
 // PureAttention Python module: the reference's surface (bindings.cpp:37-125)
 // over the B200 host layer. Names, signatures and defaults match; additions
-// are set_seed, device_status and Tensor.zero_grad.
+// include set_seed, device_status, set_stream, flash_attention and
+// Tensor.zero_grad.
 #include <pybind11/pybind11.h>
 #include <string>
 #include <pybind11/functional.h>
@@ -183,6 +184,13 @@ PYBIND11_MODULE(PureAttention, m) {
   });
   m.def("set_seed", &CudaContext::setSeed, "Seed of fill_normal and layer initialisation",
         py::arg("seed"));
+  m.def("flash_attention", [](const std::shared_ptr<Tensor>& q, const std::shared_ptr<Tensor>& k,
+                              const std::shared_ptr<Tensor>& v, int num_heads) {
+    std::shared_ptr<Tensor> o;
+    core::flash_attention(q, k, v, o, num_heads, CudaContext::getStream());
+    return o;
+  }, "core::flash_attention: softmax(q k^T / sqrt(d)) v per head of [N, L, E] fp32 tensors, with "
+     "its graph node", py::arg("q"), py::arg("k"), py::arg("v"), py::arg("num_heads"));
   m.def("set_stream", [](uintptr_t handle) {
     CudaContext::setStream(reinterpret_cast<cudaStream_t>(handle));
   }, "Stream every operator, allocation and gradient of this module runs on from now on "

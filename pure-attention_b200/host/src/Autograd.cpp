@@ -198,6 +198,20 @@ void FlashAttentionFunction::apply_backward() {
                    : n * sizeof(float),
                stream());
   const std::shared_ptr<Tensor>* qkv[3] = {&Q_input, &K_input, &V_input};
+  if (Q_input == K_input || K_input == V_input || Q_input == V_input) {
+    // one tensor in two or three roles (self-attention on x itself): the kernels
+    // write dQ, dK, dV concurrently, so they go to separate buffers first
+    Scratch g3(3 * n * sizeof(float), stream());
+    float* gp = static_cast<float*>(g3.get());
+    check_status(pa_attn_bwd_kept(&d, Q_input->get_data_ptr(), K_input->get_data_ptr(),
+                                  V_input->get_data_ptr(), O->get_data_ptr(), dO,
+                                  L_cache->get_data_ptr(), gp, gp + n, gp + 2 * n, 0, kept.get(),
+                                  kept_bytes, kept_mode, ws.get(), ws.size(), ps(stream())),
+                 "FlashAttention Backward");
+    for (int i = 0; i < 3; ++i)
+      if ((*qkv[i])->requires_grad()) add_into(**qkv[i], gp + i * n, n, "FlashAttention Backward");
+    return;
+  }
   void* dst[3];
   bool unwritten[3] = {false, false, false};
   bool all_unwritten = true;

@@ -284,3 +284,54 @@ def test_pre_ln_mha_block_matches_oracle(pa):
     print("pre-LN block relative errors:", errs)
     for name, e in errs.items():
         assert e < F32_TOL, (name, e)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("same", [True, False])
+def test_flash_attention_node_with_one_tensor_in_several_roles(pa, same):
+    """flash_attention(x, x, x) (self-attention on x itself) gives x the sum of
+    its three gradients, as torch does; with three tensors each gets its own
+    (fp32 tensors, split3 products: within 1e-3 of float64)."""
+    import torch.nn.functional as F
+    N, L, E, H = 2, 96, 64, 2
+    x, k2, v2, t = (seeded_normal(90 + i, (N, L, E), 0.5) for i in range(4))
+    X = _t(pa, x, True)
+    K = X if same else _t(pa, k2, True)
+    V = X if same else _t(pa, v2, True)
+    o = pa.flash_attention(X, K, V, H)
+    loss = pa.MSE()(o, _t(pa, t))
+    loss.backward()
+    tx = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    tk = tx if same else torch.tensor(k2, dtype=torch.float64, requires_grad=True)
+    tv = tx if same else torch.tensor(v2, dtype=torch.float64, requires_grad=True)
+    sp = lambda a: a.view(N, L, H, E // H).transpose(1, 2)
+    to = F.scaled_dot_product_attention(sp(tx), sp(tk), sp(tv)).transpose(1, 2).reshape(N, L, E)
+    tl = torch.mean((to - torch.tensor(t, dtype=torch.float64)) ** 2)
+    tl.backward()
+    assert rel_err(_h(o), to.detach().numpy()) < F32_TOL
+    assert rel_err(_g(X), tx.grad.numpy()) < F32_TOL
+    if not same:
+        assert rel_err(_g(K), tk.grad.numpy()) < F32_TOL
+        assert rel_err(_g(V), tv.grad.numpy()) < F32_TOL
+
+
+@pytest.mark.gpu
+def test_input_shared_by_two_projections_gets_both_gradients(pa):
+    """x feeds two Linear layers: the first projection backward writes x's
+    gradient outright (nothing had written it), the second adds to it - the
+    sum of both, as torch gives."""
+    x, t = seeded_normal(95, (128, 48)), seeded_normal(96, (128, 32))
+    l1, l2 = pa.Linear(48, 32), pa.Linear(48, 32, True)
+    w1, w2 = _h(l1.weight), _h(l2.weight)
+    X = _t(pa, x, True)
+    loss = pa.MSE()(pa.add(l1.forward(X), l2.forward(X)), _t(pa, t))
+    loss.backward()
+    tx = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    tw1, tw2 = (torch.tensor(w, dtype=torch.float64, requires_grad=True) for w in (w1, w2))
+    ty = tx @ tw1 + torch.relu(tx @ tw2)
+    tl = torch.mean((ty - torch.tensor(t, dtype=torch.float64)) ** 2)
+    tl.backward()
+    assert abs(_h(loss)[0] - tl.item()) < 1e-5 * abs(tl.item())
+    assert rel_err(_g(X), tx.grad.numpy()) < 1e-4
+    assert rel_err(_g(l1.weight), tw1.grad.numpy()) < 1e-4
+    assert rel_err(_g(l2.weight), tw2.grad.numpy()) < 1e-4
