@@ -162,6 +162,20 @@ int pa_add_layer_norm_fwd(const float* x, const float* r, float* sum, const floa
                           const float* beta, float* y, float* mean, float* rstd, uint32_t M,
                           uint32_t N, float epsilon, pa_stream_t stream);
 
+/* pa_layer_norm_fwd (r and sum NULL) or pa_add_layer_norm_fwd that also writes
+ * y's bf16 operand planes, so a projection that reads y next takes them
+ * (pa_linear_fwd_planes with PA_LINEAR_KEPT_VALID) instead of converting y.
+ * The planes are made under the calling thread's f32 math mode, in the layout
+ * of `kept` for a projection with in_features = N: hi = bf16(y) and, under
+ * split3 math, lo = bf16(y - hi), from the same values as y. y_planes:
+ * 256-byte aligned, at least pa_linear_kept_size(M, N) bytes. The reference
+ * has no counterpart: its LayerNorm writes fp32 only and every matmul reads
+ * fp32. */
+int pa_layer_norm_fwd_planes(const float* x, const float* r, float* sum, const float* gamma,
+                             const float* beta, float* y, float* mean, float* rstd, uint32_t M,
+                             uint32_t N, float epsilon, void* y_planes, size_t y_planes_bytes,
+                             pa_stream_t stream);
+
 size_t pa_layer_norm_bwd_workspace_size(uint32_t M, uint32_t N);
 
 /* dx (overwritten), dgamma and dbeta (accumulated); a NULL output is skipped.

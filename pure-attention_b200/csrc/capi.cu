@@ -245,6 +245,30 @@ int pa_add_layer_norm_fwd(const float* x, const float* r, float* sum, const floa
                                    static_cast<cudaStream_t>(stream));
 }
 
+int pa_layer_norm_fwd_planes(const float* x, const float* r, float* sum, const float* gamma,
+                             const float* beta, float* y, float* mean, float* rstd, uint32_t M,
+                             uint32_t N, float epsilon, void* y_planes, size_t y_planes_bytes,
+                             pa_stream_t stream) {
+  if (!x || !gamma || !beta || !y || !mean || !rstd || !y_planes) return PA_ERR_NULL;
+  if (!r != !sum) return PA_ERR_NULL;
+  if (M == 0 || N == 0 || M > 0x7fffffffu || N > 0x7fffffffu) return PA_ERR_SHAPE;
+  if (N % 4 != 0) return PA_ERR_UNSUPPORTED;
+  if (!al16(x) || !al16(gamma) || !al16(beta) || !al16(y) || (r && (!al16(r) || !al16(sum))) ||
+      (reinterpret_cast<uintptr_t>(y_planes) & 255u) != 0)
+    return PA_ERR_ALIGN;
+  if (r && (sum == x || sum == r)) return PA_ERR_SHAPE;
+  const int mode = pa::f32_math();
+  if (y_planes_bytes < pa::linear_kept_bytes(static_cast<int>(M), static_cast<int>(N), mode))
+    return PA_ERR_SHAPE;
+  uint8_t* hi = static_cast<uint8_t*>(y_planes);
+  uint8_t* lo = mode == PA_F32_MATH_BF16
+                    ? nullptr
+                    : hi + pa::linear_kept_bytes(static_cast<int>(M), static_cast<int>(N),
+                                                 PA_F32_MATH_BF16);  // one plane
+  return pa::launch_layer_norm_fwd(x, r, sum, gamma, beta, y, mean, rstd, M, N, epsilon,
+                                   static_cast<cudaStream_t>(stream), hi, lo, (N + 7) / 8 * 8);
+}
+
 size_t pa_layer_norm_bwd_workspace_size(uint32_t M, uint32_t N) {
   return pa::layer_norm_bwd_workspace_bytes(M, N);
 }

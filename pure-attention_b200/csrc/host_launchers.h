@@ -49,10 +49,13 @@ int launch_attn_delta_f32(const AttnShape& sh, const void* dO, const void* o, fl
 namespace pa {
 
 // layernorm.cu
-// r == nullptr: y = LN(x); else sum = x + r and y = LN(sum)
+// r == nullptr: y = LN(x); else sum = x + r and y = LN(sum). ph (and pl):
+// y's bf16 hi (and lo) operand planes, row pitch pld = N rounded up to 8
+// (zero padding), written from the same values as y.
 int launch_layer_norm_fwd(const float* x, const float* r, float* sum, const float* g,
                           const float* b, float* y, float* mu, float* rs, uint32_t M, uint32_t N,
-                          float eps, cudaStream_t s);
+                          float eps, cudaStream_t s, void* ph = nullptr, void* pl = nullptr,
+                          uint32_t pld = 0);
 size_t layer_norm_bwd_workspace_bytes(uint32_t M, uint32_t N);
 int launch_layer_norm_bwd(const float* dy, const float* x, const float* mu, const float* rs,
                           const float* g, float* dx, float* dg, float* db, uint32_t M, uint32_t N,

@@ -36,7 +36,8 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
     ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ r,
                   float* __restrict__ sum, const float* __restrict__ gamma,
                   const float* __restrict__ beta, float* __restrict__ y, float* __restrict__ mean,
-                  float* __restrict__ rstd, uint32_t M, uint32_t N, float eps) {
+                  float* __restrict__ rstd, uint32_t M, uint32_t N, float eps,
+                  uint32_t* __restrict__ ph, uint32_t* __restrict__ pl, uint32_t pld) {
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t nvec = N / 4;
   for (uint32_t row = blockIdx.x * LN_WARPS + threadIdx.x / 32; row < M;
@@ -75,13 +76,27 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
     float4* yr = reinterpret_cast<float4*>(y + static_cast<size_t>(row) * N);
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
     const float4* b4 = reinterpret_cast<const float4*>(beta);
+    // operand planes: bf16 pairs, row pitch pld bf16 values (2 words per float4)
+    const size_t prow = static_cast<size_t>(row) * (pld / 2);
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const uint32_t c = lane + 32 * i;
       if (c < nvec) {
         const float4 g = g4[c], bb = b4[c];
-        yr[c] = make_float4(g.x * (v[i].x - mu) * rs + bb.x, g.y * (v[i].y - mu) * rs + bb.y,
-                            g.z * (v[i].z - mu) * rs + bb.z, g.w * (v[i].w - mu) * rs + bb.w);
+        const float4 o = make_float4(g.x * (v[i].x - mu) * rs + bb.x, g.y * (v[i].y - mu) * rs + bb.y,
+                                     g.z * (v[i].z - mu) * rs + bb.z, g.w * (v[i].w - mu) * rs + bb.w);
+        yr[c] = o;
+        if (ph) {  // hi = bf16(y), lo = bf16(y - hi), from the values just stored
+          const uint32_t h0 = pack_bf16x2(o.x, o.y), h1 = pack_bf16x2(o.z, o.w);
+          *reinterpret_cast<uint2*>(ph + prow + 2 * c) = make_uint2(h0, h1);
+          if (pl)
+            *reinterpret_cast<uint2*>(pl + prow + 2 * c) =
+                make_uint2(pack_bf16x2(o.x - __uint_as_float(h0 << 16), o.y - __uint_as_float(h0 & 0xffff0000u)),
+                           pack_bf16x2(o.z - __uint_as_float(h1 << 16), o.w - __uint_as_float(h1 & 0xffff0000u)));
+        }
+      } else if (ph && c == nvec && 4 * nvec < pld) {  // the pitch's zero padding (N % 8 == 4)
+        *reinterpret_cast<uint2*>(ph + prow + 2 * c) = make_uint2(0u, 0u);
+        if (pl) *reinterpret_cast<uint2*>(pl + prow + 2 * c) = make_uint2(0u, 0u);
       }
     }
   }
@@ -302,13 +317,17 @@ uint32_t ln_bwd_blocks(uint32_t M, uint32_t N) {
 
 template <int VPL>
 int ln_fwd_launch(const float* x, const float* r, float* sum, const float* g, const float* b,
-                  float* y, float* mu, float* rs, uint32_t M, uint32_t N, float eps, cudaStream_t s) {
+                  float* y, float* mu, float* rs, uint32_t M, uint32_t N, float eps, void* ph,
+                  void* pl, uint32_t pld, cudaStream_t s) {
   const uint32_t blocks = (M + LN_WARPS - 1) / LN_WARPS;
+  uint32_t* h = static_cast<uint32_t*>(ph);
+  uint32_t* l = static_cast<uint32_t*>(pl);
   if (r)
-    ln_fwd_kernel<VPL, true><<<blocks, LN_WARPS * 32, 0, s>>>(x, r, sum, g, b, y, mu, rs, M, N, eps);
+    ln_fwd_kernel<VPL, true><<<blocks, LN_WARPS * 32, 0, s>>>(x, r, sum, g, b, y, mu, rs, M, N, eps,
+                                                              h, l, pld);
   else
     ln_fwd_kernel<VPL, false><<<blocks, LN_WARPS * 32, 0, s>>>(x, nullptr, nullptr, g, b, y, mu, rs,
-                                                               M, N, eps);
+                                                               M, N, eps, h, l, pld);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
@@ -368,13 +387,14 @@ int add_ln_bwd_launch(const float* dy, const float* dsum, const float* x, const 
 // r == nullptr: y = LN(x); else sum = x + r and y = LN(sum).
 int launch_layer_norm_fwd(const float* x, const float* r, float* sum, const float* g,
                           const float* b, float* y, float* mu, float* rs, uint32_t M, uint32_t N,
-                          float eps, cudaStream_t s) {
-  if (N <= 128) return ln_fwd_launch<1>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 256) return ln_fwd_launch<2>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 512) return ln_fwd_launch<4>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 1024) return ln_fwd_launch<8>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 2048) return ln_fwd_launch<16>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
-  if (N <= 4096) return ln_fwd_launch<32>(x, r, sum, g, b, y, mu, rs, M, N, eps, s);
+                          float eps, cudaStream_t s, void* ph, void* pl, uint32_t pld) {
+  if (ph && (pld < N || pld > N + 4 || pld % 4 != 0)) return PA_ERR_SHAPE;
+  if (N <= 128) return ln_fwd_launch<1>(x, r, sum, g, b, y, mu, rs, M, N, eps, ph, pl, pld, s);
+  if (N <= 256) return ln_fwd_launch<2>(x, r, sum, g, b, y, mu, rs, M, N, eps, ph, pl, pld, s);
+  if (N <= 512) return ln_fwd_launch<4>(x, r, sum, g, b, y, mu, rs, M, N, eps, ph, pl, pld, s);
+  if (N <= 1024) return ln_fwd_launch<8>(x, r, sum, g, b, y, mu, rs, M, N, eps, ph, pl, pld, s);
+  if (N <= 2048) return ln_fwd_launch<16>(x, r, sum, g, b, y, mu, rs, M, N, eps, ph, pl, pld, s);
+  if (N <= 4096) return ln_fwd_launch<32>(x, r, sum, g, b, y, mu, rs, M, N, eps, ph, pl, pld, s);
   return PA_ERR_UNSUPPORTED;
 }
 

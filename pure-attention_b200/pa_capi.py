@@ -25,7 +25,7 @@ EXPORTS = [
     "pa_get_f32_math",
     "pa_attn_fwd_workspace_size", "pa_attn_fwd", "pa_attn_bwd_workspace_size", "pa_attn_bwd", "pa_attn_bwd_kept", "pa_attn_bwd_noalloc",
     "pa_attn_delta",
-    "pa_layer_norm_fwd", "pa_add_layer_norm_fwd", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
+    "pa_layer_norm_fwd", "pa_add_layer_norm_fwd", "pa_layer_norm_fwd_planes", "pa_layer_norm_bwd_workspace_size", "pa_layer_norm_bwd",
     "pa_layer_norm_bwd_accumulate", "pa_add_layer_norm_bwd",
     "pa_matmul_workspace_size", "pa_matmul", "pa_matmul_grad_x", "pa_matmul_grad_w",
     "pa_linear_workspace_size", "pa_linear_fwd", "pa_linear_bwd", "pa_linear_relu_fwd",
@@ -71,6 +71,7 @@ _SIGS = {
     "pa_attn_delta": (_int, [ctypes.POINTER(AttnDesc), _vp, _vp, _vp, _vp]),
     "pa_layer_norm_fwd": (_int, [_vp] * 6 + [_u32, _u32, _flt, _vp]),
     "pa_add_layer_norm_fwd": (_int, [_vp] * 8 + [_u32, _u32, _flt, _vp]),
+    "pa_layer_norm_fwd_planes": (_int, [_vp] * 8 + [_u32, _u32, _flt, _vp, _sz, _vp]),
     "pa_layer_norm_bwd_workspace_size": (_sz, [_u32, _u32]),
     "pa_layer_norm_bwd": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
     "pa_layer_norm_bwd_accumulate": (_int, [_vp] * 8 + [_u32, _u32, _vp, _sz, _vp]),
@@ -275,6 +276,21 @@ def add_layer_norm_fwd(x, r, out_sum, gamma, beta, y, mean, rstd, eps=1e-5, stre
                                       _ptr(y), _ptr(mean), _ptr(rstd), M, N, float(eps),
                                       _stream() if stream is None else stream)
     _check("pa_add_layer_norm_fwd", st)
+
+
+def layer_norm_fwd_planes(x, gamma, beta, y, mean, rstd, y_planes, r=None, out_sum=None, eps=1e-5,
+                          stream=None):
+    """layer_norm_fwd (r None) or add_layer_norm_fwd that also writes y's bf16
+    operand planes into y_planes (uint8, >= linear_kept_size(M, N) bytes) under
+    the current f32 math mode."""
+    M = x.numel() // x.shape[-1]
+    N = x.shape[-1]
+    st = load().pa_layer_norm_fwd_planes(_ptr(x), _ptr(r) if r is not None else None,
+                                         _ptr(out_sum) if out_sum is not None else None, _ptr(gamma),
+                                         _ptr(beta), _ptr(y), _ptr(mean), _ptr(rstd), M, N, float(eps),
+                                         _ptr(y_planes), y_planes.numel() * y_planes.element_size(),
+                                         _stream() if stream is None else stream)
+    _check("pa_layer_norm_fwd_planes", st)
 
 
 def layer_norm_bwd_workspace_size(M, N):

@@ -596,3 +596,69 @@ def test_linear_output_planes_feed_the_next_projection(math_mode, M, IN, HID, OU
         assert pa_capi.device_status() == 0
     finally:
         pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("math_mode", ["bf16", "split3"])
+@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("M,N,OUT", [(4096, 1024, 512), (300, 100, 72), (5, 12, 8)])
+def test_layer_norm_output_planes_feed_the_next_projection(math_mode, residual, M, N, OUT):
+    """pa_layer_norm_fwd_planes writes y, mean and rstd bit for bit as the plain
+    (add +) LayerNorm forward, and y's bf16 planes byte for byte as the next
+    projection would make them from y (zero padding of the row pitch included);
+    that projection, taking them as kept (PA_LINEAR_KEPT_VALID), gives the same
+    output bits as converting y itself."""
+    import pa_capi
+    x, r = seeded_normal(M + 91, (M, N)), seeded_normal(M + 92, (M, N))
+    gamma = 1.0 + 0.1 * seeded_normal(N + 93, (N,))
+    beta = 0.1 * seeded_normal(N + 94, (N,))
+    w, b = seeded_normal(95, (N, OUT), 0.05), seeded_normal(96, (OUT,))
+    pa_capi.set_f32_math(math_mode)
+    try:
+        xs, rs_, g, bt = _cu(x), _cu(r), _cu(gamma), _cu(beta)
+        y, mean, rstd = (torch.empty(M, N, device="cuda"), torch.empty(M, device="cuda"),
+                         torch.empty(M, device="cuda"))
+        s = torch.empty(M, N, device="cuda") if residual else None
+        yp = torch.full((pa_capi.linear_kept_size(M, N),), 0x5A, dtype=torch.uint8, device="cuda")
+        pa_capi.layer_norm_fwd_planes(xs, g, bt, y, mean, rstd, yp, r=rs_ if residual else None,
+                                      out_sum=s)
+        y2, m2, r2 = torch.empty_like(y), torch.empty_like(mean), torch.empty_like(rstd)
+        if residual:
+            s2 = torch.empty_like(y)
+            pa_capi.add_layer_norm_fwd(xs, rs_, s2, g, bt, y2, m2, r2)
+            assert torch.equal(s, s2)
+        else:
+            pa_capi.layer_norm_fwd(xs, g, bt, y2, m2, r2)
+        assert torch.equal(y, y2) and torch.equal(mean, m2) and torch.equal(rstd, r2)
+        kept = torch.full_like(yp, 0x5A)
+        out_conv = torch.empty(M, OUT, device="cuda")
+        pa_capi.linear_fwd_keep(y, _cu(w), _cu(b), [out_conv], M, N, OUT, kept)
+        assert torch.equal(yp, kept)
+        out_taken = torch.empty_like(out_conv)
+        pa_capi.linear_fwd_planes(y, _cu(w), _cu(b), [out_taken], M, N, OUT, yp, math_mode,
+                                  kept_valid=True)
+        assert torch.equal(out_taken, out_conv)
+        assert pa_capi.device_status() == 0
+    finally:
+        pa_capi.set_f32_math("split3")
+
+
+@pytest.mark.gpu
+def test_layer_norm_planes_reject_bad_arguments():
+    """Too small a plane buffer, a misaligned one, or a residual without its sum
+    are refused before any launch."""
+    import pa_capi
+    M, N = 64, 128
+    x = torch.randn(M, N, device="cuda")
+    g, b = torch.ones(N, device="cuda"), torch.zeros(N, device="cuda")
+    y, mean, rstd = torch.empty_like(x), torch.empty(M, device="cuda"), torch.empty(M, device="cuda")
+    n = pa_capi.linear_kept_size(M, N)
+    buf = torch.empty(n + 512, dtype=torch.uint8, device="cuda")
+    with pytest.raises(pa_capi.PaError):
+        pa_capi.layer_norm_fwd_planes(x, g, b, y, mean, rstd, buf[:n - 256])
+    with pytest.raises(pa_capi.PaError):
+        pa_capi.layer_norm_fwd_planes(x, g, b, y, mean, rstd, buf[16:16 + n])
+    with pytest.raises(pa_capi.PaError):
+        pa_capi.layer_norm_fwd_planes(x, g, b, y, mean, rstd, buf[:n], r=x)
+    pa_capi.layer_norm_fwd_planes(x, g, b, y, mean, rstd, buf[:n])
+    assert pa_capi.device_status() == 0
