@@ -119,6 +119,48 @@ def test_attention_bf16_headline_shape_slices():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_bf16_uneven_work_per_cta(D):
+    """B=3, H=13, L=1000 (ragged last tiles): 156 forward units of 256 query
+    rows over 148 CTAs and, at d=64, 156 backward items over 74 CTA pairs, so
+    some CTAs carry their ring slots and barrier phases into a second or third
+    item. Every output element is written (the gradients start as NaN); four
+    heads match the float64 oracle; and each checked head, run again alone as
+    a one-head problem, gives bit-identical O, LSE, dK and dV (dQ is reduced
+    in no fixed order: within one bf16 ulp per element, plus 1e-5 of max |dQ|
+    where the reduction cancels)."""
+    import pa_capi
+    B, L, H = 3, 1000, 13
+    inputs, outs = _run(B, L, H, D, seed=17 + D)
+    for t in outs:
+        assert np.isfinite(t).all()
+    heads = [(0, 0), (1, 7), (2, 11), (2, 12)]
+    _check(inputs, outs, heads=heads)
+    o, lse, dq, dk, dv = outs
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)
+    for (b, h) in heads:
+        sl = (slice(b, b + 1), slice(None), slice(h, h + 1), slice(None))
+        q1, k1, v1, g1 = (torch.from_numpy(np.ascontiguousarray(x[sl]).astype(np.float32))
+                          .to(torch.bfloat16).cuda() for x in inputs)
+        o1 = torch.empty_like(q1)
+        lse1 = torch.empty(1, L, dtype=torch.float32, device="cuda")
+        pa_capi.attn_fwd(q1, k1, v1, o1, lse1)
+        d1 = pa_capi.attn_desc(q1)
+        ws1 = torch.empty(pa_capi.attn_bwd_workspace_size(d1), dtype=torch.uint8, device="cuda")
+        dq1, dk1, dv1 = (torch.empty_like(q1) for _ in range(3))
+        pa_capi.attn_bwd(q1, k1, v1, o1, g1, lse1, dq1, dk1, dv1, ws1)
+        assert pa_capi.device_status() == 0
+        np.testing.assert_array_equal(f(o1), o[sl])
+        np.testing.assert_array_equal(lse1.cpu().numpy().astype(np.float64)[0], lse[b * H + h])
+        np.testing.assert_array_equal(f(dk1), dk[sl])
+        np.testing.assert_array_equal(f(dv1), dv[sl])
+        a, r = f(dq1), dq[sl]
+        # one bf16 ulp, plus fp32 reduction-order noise where dQ cancels to near 0
+        assert np.all(np.abs(a - r) <= np.maximum(np.abs(a), np.abs(r)) * 2.0 ** -7
+                      + 1e-5 * np.max(np.abs(r)))
+
+
+@pytest.mark.gpu
 def test_attention_bf16_d128_two_heads_oracle():
     """d = 128 at L = 2048 (all heads) against the oracle."""
     inputs, outs = _run(1, 2048, 2, 128, seed=4)
