@@ -236,10 +236,14 @@ void flash_attention(const std::shared_ptr<Tensor>& Q, const std::shared_ptr<Ten
 }
 
 // A LayerNorm output's operand planes (pa_layer_norm_fwd_planes), attached to
-// it so that a projection reading it converts nothing.
+// it so that a projection reading it converts nothing. NULL where the plane
+// layout cannot describe the shape (more than INT_MAX rows or columns): the
+// norm then writes y alone and a projection converts it.
 static std::shared_ptr<void> ln_planes(const std::shared_ptr<Tensor>& out, uint32_t M, uint32_t N,
                                        const cudaStream_t& stream) {
+  if (M > 0x7fffffffu || N > 0x7fffffffu) return nullptr;
   const size_t bytes = pa_linear_kept_size(static_cast<int>(M), static_cast<int>(N));
+  if (bytes == 0) return nullptr;
   auto planes = device_buffer(bytes, stream, "LayerNorm");
   out->operand_planes = planes;
   out->operand_planes_bytes = bytes;
@@ -261,11 +265,15 @@ std::shared_ptr<Tensor> layer_norm(const std::shared_ptr<Tensor>& input,
   auto rstd = std::make_shared<Tensor>(std::vector<uint32_t>{M}, false);
   // y's bf16 operand planes from the same pass, for the projection that reads y next
   auto planes = ln_planes(output, M, N, stream);
-  check_status(pa_layer_norm_fwd_planes(input->get_data_ptr(), nullptr, nullptr,
-                                        gamma->get_data_ptr(), beta->get_data_ptr(),
-                                        output->get_data_ptr(), mean->get_data_ptr(),
-                                        rstd->get_data_ptr(), M, N, epsilon, planes.get(),
-                                        output->operand_planes_bytes, ps(stream)),
+  check_status(planes ? pa_layer_norm_fwd_planes(input->get_data_ptr(), nullptr, nullptr,
+                                                 gamma->get_data_ptr(), beta->get_data_ptr(),
+                                                 output->get_data_ptr(), mean->get_data_ptr(),
+                                                 rstd->get_data_ptr(), M, N, epsilon, planes.get(),
+                                                 output->operand_planes_bytes, ps(stream))
+                      : pa_layer_norm_fwd(input->get_data_ptr(), gamma->get_data_ptr(),
+                                          beta->get_data_ptr(), output->get_data_ptr(),
+                                          mean->get_data_ptr(), rstd->get_data_ptr(), M, N, epsilon,
+                                          ps(stream)),
                "LayerNorm");
   if (g)
     output->set_grad_fn(
@@ -290,11 +298,17 @@ std::pair<std::shared_ptr<Tensor>, std::shared_ptr<Tensor>> add_layer_norm(
   auto mean = std::make_shared<Tensor>(std::vector<uint32_t>{M}, false);
   auto rstd = std::make_shared<Tensor>(std::vector<uint32_t>{M}, false);
   auto planes = ln_planes(output, M, N, stream);
-  check_status(pa_layer_norm_fwd_planes(x->get_data_ptr(), r->get_data_ptr(), sum->get_data_ptr(),
-                                        gamma->get_data_ptr(), beta->get_data_ptr(),
-                                        output->get_data_ptr(), mean->get_data_ptr(),
-                                        rstd->get_data_ptr(), M, N, epsilon, planes.get(),
-                                        output->operand_planes_bytes, ps(stream)),
+  check_status(planes ? pa_layer_norm_fwd_planes(x->get_data_ptr(), r->get_data_ptr(),
+                                                 sum->get_data_ptr(), gamma->get_data_ptr(),
+                                                 beta->get_data_ptr(), output->get_data_ptr(),
+                                                 mean->get_data_ptr(), rstd->get_data_ptr(), M, N,
+                                                 epsilon, planes.get(), output->operand_planes_bytes,
+                                                 ps(stream))
+                      : pa_add_layer_norm_fwd(x->get_data_ptr(), r->get_data_ptr(),
+                                              sum->get_data_ptr(), gamma->get_data_ptr(),
+                                              beta->get_data_ptr(), output->get_data_ptr(),
+                                              mean->get_data_ptr(), rstd->get_data_ptr(), M, N,
+                                              epsilon, ps(stream)),
                "Add+LayerNorm");
   if (gs) {  // one backward pass writes both addends' gradients
     sum->set_grad_fn(std::make_shared<AddLayerNormFunction>(x, r, gamma, beta, sum, mean, rstd, M, N));
