@@ -77,6 +77,16 @@ def test_layer_norm_and_matmul_validation_without_gpu():
     assert lib.pa_add_layer_norm_fwd(16, 32, 48, 16, 16, 16, 16, 16, 4, 6, 1e-5, None) == 4
     assert lib.pa_add_layer_norm_fwd(16, 36, 48, 16, 16, 16, 16, 16, 4, 8, 1e-5, None) == 3
     assert lib.pa_add_layer_norm_fwd(16, 32, 16, 16, 16, 16, 16, 16, 4, 8, 1e-5, None) == 1
+    # the same with the output's operand planes: planes NULL, r without sum, too few plane
+    # bytes, planes not 256-byte aligned, N not a multiple of 4
+    pl = lib.pa_layer_norm_fwd_planes
+    need = lib.pa_linear_kept_size(4, 8)
+    assert need > 0
+    assert pl(16, None, None, 16, 16, 16, 16, 16, 4, 8, 1e-5, None, need, None) == 8
+    assert pl(16, 32, None, 16, 16, 16, 16, 16, 4, 8, 1e-5, 256, need, None) == 8
+    assert pl(16, None, None, 16, 16, 16, 16, 16, 4, 8, 1e-5, 256, need - 1, None) == 1
+    assert pl(16, None, None, 16, 16, 16, 16, 16, 4, 8, 1e-5, 272, need, None) == 3
+    assert pl(16, None, None, 16, 16, 16, 16, 16, 4, 6, 1e-5, 256, need, None) == 4
     assert lib.pa_matmul(16, 16, 16, 0, 4, 4, None, 0, None) == 1
     assert lib.pa_matmul_grad_x(None, 16, 16, 4, 4, 4, None, 0, None) == 8
     assert lib.pa_matmul_grad_w(16, 16, 16, 4, 4, 4, None, 0, None) == 7   # no workspace
